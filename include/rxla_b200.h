@@ -1,0 +1,273 @@
+/*
+ * rxla_b200.h — C ABI of the B200 (sm_100a) W8 decode hot path.
+ *
+ * This library replaces, for one path only, the device work that rxla hands
+ * to XLA through PJRT: the int8-weight linear layers (QuantizedLinear) and the
+ * grouped-query KV-cache attention of decoder-LLM decode.  Every entry point
+ * is plain `extern "C"`: raw device pointers, sizes, a CUDA stream passed as
+ * `void*`, and an `int32_t` status.  No C++ or torch types cross the ABI.
+ *
+ * Conventions
+ *  - Ownership: the caller owns every tensor buffer (device pointers).  The
+ *    library allocates only inside `*_create` objects (decoder runner, comm)
+ *    and never on a launch path.
+ *  - Streams: every launch is ordered on the given stream (NULL = legacy
+ *    default stream).  Nothing synchronises implicitly.
+ *  - Errors: 0 is success.  Failures return the negated absl/PJRT status class
+ *    (the same classes rxla maps to `PjrtErrorCode`,
+ *    crates/rxla-pjrt/src/runtime.rs:49-107).  A thread-local message is
+ *    available from rxla_b200_last_error_message().  Nothing aborts or traps.
+ *  - Threading: launches on distinct streams may come from distinct threads.
+ *    A decoder or comm handle is used by one thread at a time.
+ *  - Dtypes: bf16 tensors are raw IEEE bfloat16 (uint16_t storage).
+ *
+ * Reference interfaces replaced (paths inside the rxla project):
+ *  - crates/rxla-nn/src/layers.rs:231-298   QuantizedLinear / apply_quantized_linear
+ *  - crates/rxla-nn/src/layers.rs:784-793   Cx::quantized_linear(out, group)
+ *  - crates/rxla-core/src/nn.rs:286-310     Tensor::linear (x · Wᵀ)
+ *  - crates/rxla-core/src/attention.rs:83-252  grouped_query_attention / SDPA
+ *  - crates/rxla-core/src/attention.rs:14-67   causal masks (decode form)
+ *  - crates/rxla-core/src/kv_cache.rs:53-112   KvCache::update_at(_checked)
+ *  - crates/rxla-core/src/rotary.rs:17-74      rotary_embedding(_angles), SplitHalf
+ *  - crates/rxla-core/src/ops.rs:929-945       Tensor::rms_norm
+ *  - crates/rxla-nn/src/applied.rs:222-237     BoundModel::run (decoder step)
+ *  - crates/rxla-core/src/state.rs:1200-1228   Session::run (stateful step)
+ *  - crates/rxla-pjrt/src/distributed.rs:40-120 distributed rendezvous (comm)
+ */
+#ifndef RXLA_B200_H_
+#define RXLA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RXLA_B200_ABI_VERSION 1
+
+/* Status codes: negated absl status classes, as PjrtErrorCode uses them
+ * (crates/rxla-pjrt/src/runtime.rs:49-107). */
+typedef enum rxla_b200_status {
+  RXLA_B200_OK = 0,
+  RXLA_B200_INVALID_ARGUMENT = -3,
+  RXLA_B200_DEADLINE_EXCEEDED = -4, /* a bounded device wait ran out */
+  RXLA_B200_NOT_FOUND = -5,
+  RXLA_B200_RESOURCE_EXHAUSTED = -8,
+  RXLA_B200_FAILED_PRECONDITION = -9,
+  RXLA_B200_OUT_OF_RANGE = -11,
+  RXLA_B200_UNIMPLEMENTED = -12,
+  RXLA_B200_INTERNAL = -13,
+  RXLA_B200_UNAVAILABLE = -14 /* CUDA / NCCL runtime failure */
+} rxla_b200_status;
+
+/* Element types used at the boundary (rxla DType subset). */
+typedef enum rxla_b200_dtype {
+  RXLA_B200_F32 = 0,
+  RXLA_B200_BF16 = 1,
+  RXLA_B200_U8 = 2,
+  RXLA_B200_I32 = 3
+} rxla_b200_dtype;
+
+/* Linear epilogues. */
+typedef enum rxla_b200_epilogue {
+  /* y[m,n] = out                                                         */
+  RXLA_B200_EPI_STORE = 0,
+  /* y[m,n] (f32, in place) += bf16(out): the residual add of a decoder block */
+  RXLA_B200_EPI_RESIDUAL_ADD = 1,
+  /* weight holds 2n rows [gate; up]; y[m,i] = silu(gate_i) * up_i, both
+   * rounded to bf16 first (crates/rxla-models/src/qwen3_5/layers.rs:270-293) */
+  RXLA_B200_EPI_SWIGLU = 2
+} rxla_b200_epilogue;
+
+/* KV update policy of the decode attention (crates/rxla-core/src/kv_cache.rs). */
+typedef enum rxla_b200_kv_update {
+  /* update_at: an out-of-range start is clamped to the last slot (:43-68) */
+  RXLA_B200_KV_CLAMP = 0,
+  /* update_at_checked: an out-of-range start leaves the cache unchanged and
+   * reports accepted = 0 (:70-112) */
+  RXLA_B200_KV_CHECKED = 1
+} rxla_b200_kv_update;
+
+/* ---------------------------------------------------------------- library */
+
+int32_t rxla_b200_abi_version(void);
+/* Thread-local message of the last failing call on this thread ("" if none). */
+const char* rxla_b200_last_error_message(void);
+/* Number of SMs, and whether the device is sm_100 (B200 class). */
+int32_t rxla_b200_device_info(int32_t device, int32_t* sm_count, int32_t* cc_major,
+                              int32_t* cc_minor);
+
+/* ------------------------------------------------------- W8A16 linear layer
+ *
+ * Replaces QuantizedLinear::apply (crates/rxla-nn/src/layers.rs:257-298) with
+ * the layer compute dtype BF16 (crates/rxla-nn/src/lib.rs:487-500):
+ *
+ *   y = bf16(x) · ((weight - 128) ⊙ scale[n, k / group])ᵀ
+ *
+ * weight : u8 [n_rows, k] row-major, signed int8 stored as value + 128
+ *          (benchmarks/quantize_qwen3_5_w8.py:33-44); n_rows = n, or 2n for
+ *          RXLA_B200_EPI_SWIGLU.
+ * scale  : f32 [n_rows, k / group_size]; group_size must divide k
+ *          (layers.rs:266-275); group_size == k is per-output-channel.
+ * x      : [m, k], RXLA_B200_BF16 or RXLA_B200_F32 (rounded to bf16 on load).
+ * y      : [m, n], RXLA_B200_BF16 or RXLA_B200_F32.  The dot product is
+ *          accumulated in fp32 and rounded to bf16 (the reference's bf16 dot
+ *          output) before it is stored, widened, added or gated.
+ * m == 0 or n == 0 is a no-op.  Sizes are checked; a bad size returns
+ * RXLA_B200_INVALID_ARGUMENT without launching anything.
+ */
+int32_t rxla_b200_w8a16_linear(const void* x, int32_t x_dtype, const uint8_t* weight,
+                               const float* scale, int64_t group_size, int64_t m, int64_t n,
+                               int64_t k, void* y, int32_t y_dtype, int32_t epilogue,
+                               void* stream);
+
+/* Dense bf16-weight linear y = bf16(x) · wᵀ (the tied bf16 LM head of a
+ * decoder whose embedding stays bf16; crates/rxla-core/src/nn.rs:286-310).
+ * weight bf16 [n, k]; same x / y / epilogue rules as above (SWIGLU excluded). */
+int32_t rxla_b200_bf16_linear(const void* x, int32_t x_dtype, const uint16_t* weight,
+                              int64_t m, int64_t n, int64_t k, void* y, int32_t y_dtype,
+                              int32_t epilogue, void* stream);
+
+/* ----------------------------------------------- paged GQA decode attention
+ *
+ * One decode step for `batch` sequences: per-head RMSNorm of q and of the new
+ * k (optional), RoPE (SplitHalf, crates/rxla-core/src/rotary.rs:29-74) at
+ * position ctx_lens[b], append of the new k/v into the paged bf16 cache
+ * (KvCache::update_at / update_at_checked semantics), then
+ * softmax(q·Kᵀ·scale + causal mask)·V over the cache with consecutive query
+ * heads sharing a kv head (crates/rxla-core/src/attention.rs:73-135).
+ *
+ * Cache layout: k_pages / v_pages bf16 [num_pages, kv_heads, page_size,
+ * head_dim]; page_table int32 [batch, max_pages_per_seq] maps the p-th page of
+ * sequence b; capacity of sequence b = pages_per_seq[b] * page_size (or
+ * max_pages_per_seq * page_size when pages_per_seq is NULL).
+ */
+typedef struct rxla_b200_paged_decode_args {
+  uint32_t struct_size; /* sizeof(rxla_b200_paged_decode_args) */
+  int32_t batch, q_heads, kv_heads, head_dim;
+  /* new-token projections (bf16), row stride in elements; q [batch, q_heads*d],
+   * k/v [batch, kv_heads*d] — a fused QKV output passes offsets into one row. */
+  const uint16_t* q;
+  const uint16_t* k_new;
+  const uint16_t* v_new;
+  int64_t q_row_stride, kv_row_stride;
+  /* optional per-head RMSNorm weights [head_dim] (f32), NULL = no norm */
+  const float* q_norm_weight;
+  const float* k_norm_weight;
+  float norm_eps;
+  /* RoPE: inv_freq f32 [rotary_dim/2] (host-computed θ^(-2i/rotary_dim)),
+   * NULL or rotary_dim == 0 = no rotation; rotation covers dims [0, rotary_dim) */
+  const float* inv_freq;
+  int32_t rotary_dim;
+  float scale; /* 0 => 1/sqrt(head_dim) (attention.rs:190) */
+  /* paged cache */
+  uint16_t* k_pages;
+  uint16_t* v_pages;
+  int64_t num_pages;
+  int32_t page_size; /* must be 16 */
+  int32_t max_pages_per_seq;
+  const int32_t* page_table;    /* [batch, max_pages_per_seq] */
+  const int32_t* pages_per_seq; /* [batch] or NULL */
+  const int32_t* ctx_lens;      /* [batch] tokens already cached = new position */
+  int32_t kv_update;            /* rxla_b200_kv_update */
+  int32_t advance_ctx;          /* nonzero: ctx_lens[b] += accepted (in place) */
+  int32_t* accepted;            /* optional [batch] out: 1 written, 0 rejected */
+  /* output [batch, q_heads*head_dim] bf16 */
+  uint16_t* out;
+  /* scratch for split-K partials; size from rxla_b200_paged_decode_workspace_size */
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t max_context; /* upper bound of ctx_lens[b]+1, sizes the split grid */
+} rxla_b200_paged_decode_args;
+
+/* Bytes of workspace the decode attention needs for this shape.  The first
+ * 4*batch*kv_heads bytes are counters that must be zero before the first call
+ * (cudaMemset once); every call leaves them zero again. */
+int32_t rxla_b200_paged_decode_workspace_size(int32_t batch, int32_t q_heads,
+                                              int32_t kv_heads, int32_t head_dim,
+                                              int32_t max_context, size_t* bytes);
+
+int32_t rxla_b200_paged_decode_attention(const rxla_b200_paged_decode_args* args,
+                                         void* stream);
+
+/* ------------------------------------------------------- small fused ops */
+
+/* y[r, :] = bf16(x[r,:] * rsqrt(mean(x²) + eps) * w)  (ops.rs:929-945,
+ * then the bf16 cast of the consuming linear).  x f32 [rows, width]. */
+int32_t rxla_b200_rms_norm_bf16(const float* x, const float* weight, int64_t rows,
+                                int64_t width, float eps, uint16_t* y, void* stream);
+
+/* Greedy sampling: out[r] = first index of the maximum of logits[r, :]
+ * (f32 [rows, vocab]), the ArgMax of crates/rxla-core/src/dtype_rules.rs:26. */
+int32_t rxla_b200_argmax(const float* logits, int64_t rows, int64_t vocab, int32_t* out,
+                         void* stream);
+
+/* ---------------------------------------------------------- decoder runner
+ *
+ * A Qwen3-style W8 decoder (plain q_proj, per-head q_norm / k_norm, full
+ * RoPE, SwiGLU MLP, tied LM head, greedy argmax) composed from the ops above
+ * — the composition of crates/rxla-models/src/qwen3_5/{mod.rs,layers.rs}
+ * restricted to full-attention layers.  It owns its weights and its paged KV
+ * cache; one step is captured once into a CUDA graph and replayed.
+ */
+typedef struct rxla_b200_decoder_config {
+  uint32_t struct_size; /* sizeof(rxla_b200_decoder_config) */
+  int32_t layers, hidden, q_heads, kv_heads, head_dim, intermediate, vocab;
+  float rms_eps, rope_theta;
+  int32_t embedding_dtype; /* RXLA_B200_U8 (W8 tied head) or RXLA_B200_BF16 */
+  int32_t group_size;      /* 0 = per-output-channel */
+  int32_t max_batch, max_context;
+  int32_t tp_rank, tp_size; /* tensor parallel shard of this process */
+} rxla_b200_decoder_config;
+
+typedef struct rxla_b200_decoder rxla_b200_decoder;
+typedef struct rxla_b200_comm rxla_b200_comm;
+
+int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* config, int32_t device,
+                                 rxla_b200_comm* comm, rxla_b200_decoder** out);
+int32_t rxla_b200_decoder_destroy(rxla_b200_decoder* decoder);
+/* Device pointer, byte size and dtype of a named parameter of this shard.
+ * Names follow the checkpoint layout, e.g. "embed_tokens.weight",
+ * "layers.3.self_attn.q_proj.weight", "layers.3.mlp.down_proj.scale",
+ * "layers.3.input_layernorm.weight", "norm.weight". */
+int32_t rxla_b200_decoder_parameter(rxla_b200_decoder* decoder, const char* name,
+                                    void** device_ptr, int64_t* bytes, int32_t* dtype);
+/* Fill every parameter with seeded synthetic values on the device. */
+int32_t rxla_b200_decoder_init_synthetic(rxla_b200_decoder* decoder, uint64_t seed);
+/* Drop all cached context of every sequence. */
+int32_t rxla_b200_decoder_reset(rxla_b200_decoder* decoder, void* stream);
+/* One decode step of `batch` sequences: tokens (device int32 [batch]) at the
+ * next position of each sequence.  Writes the greedy next token (device
+ * int32 [batch]) and, if logits is non-NULL, the f32 logits [batch, vocab]
+ * of this shard.  Stream-ordered; replays a captured CUDA graph. */
+int32_t rxla_b200_decoder_step(rxla_b200_decoder* decoder, const int32_t* tokens,
+                               int32_t batch, int32_t* next_tokens, float* logits,
+                               void* stream);
+/* Host-buffer convenience for one step: copies tokens in and next tokens out
+ * through pinned staging on `stream` and synchronises it. */
+int32_t rxla_b200_decoder_step_host(rxla_b200_decoder* decoder, const int32_t* tokens_host,
+                                    int32_t batch, int32_t* next_tokens_host, void* stream);
+/* Current context length of each sequence (device int32 [max_batch]). */
+int32_t rxla_b200_decoder_context_lengths(rxla_b200_decoder* decoder, const int32_t** lens);
+
+/* ---------------------------------------------------- tensor-parallel comm
+ *
+ * Replaces the PJRT distributed client + KV-store rendezvous
+ * (crates/rxla-pjrt/src/distributed.rs:40-120): rank 0 creates an id, the
+ * caller moves its bytes to every rank (any host store), every rank inits.
+ */
+#define RXLA_B200_COMM_ID_BYTES 128
+int32_t rxla_b200_comm_unique_id(uint8_t id[RXLA_B200_COMM_ID_BYTES]);
+int32_t rxla_b200_comm_init(const uint8_t id[RXLA_B200_COMM_ID_BYTES], int32_t rank,
+                            int32_t world_size, int32_t device, rxla_b200_comm** out);
+int32_t rxla_b200_comm_destroy(rxla_b200_comm* comm);
+/* In-place bf16 or f32 sum all-reduce of `count` elements on `stream`. */
+int32_t rxla_b200_allreduce(rxla_b200_comm* comm, void* buffer, int64_t count,
+                            int32_t dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RXLA_B200_H_ */
