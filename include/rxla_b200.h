@@ -44,6 +44,12 @@
 extern "C" {
 #endif
 
+/* Every declaration below is an exported symbol of librxla_b200.so (the
+ * library is built with hidden visibility for everything else). */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
 #define RXLA_B200_ABI_VERSION 1
 
 /* Status codes: negated absl status classes, as PjrtErrorCode uses them
@@ -94,9 +100,13 @@ typedef enum rxla_b200_kv_update {
 int32_t rxla_b200_abi_version(void);
 /* Thread-local message of the last failing call on this thread ("" if none). */
 const char* rxla_b200_last_error_message(void);
-/* Number of SMs, and whether the device is sm_100 (B200 class). */
+/* Number of SMs and compute capability of `device`. */
 int32_t rxla_b200_device_info(int32_t device, int32_t* sm_count, int32_t* cc_major,
                               int32_t* cc_minor);
+/* Status word the kernels of the current device set when a bounded device-side
+ * wait runs out (RXLA_B200_DEADLINE_EXCEEDED) — kernels return instead of
+ * hanging.  0 when nothing went wrong; nonzero `reset` clears it. */
+int32_t rxla_b200_device_status(int32_t reset);
 
 /* ------------------------------------------------------- W8A16 linear layer
  *
@@ -111,9 +121,13 @@ int32_t rxla_b200_device_info(int32_t device, int32_t* sm_count, int32_t* cc_maj
  * scale  : f32 [n_rows, k / group_size]; group_size must divide k
  *          (layers.rs:266-275); group_size == k is per-output-channel.
  * x      : [m, k], RXLA_B200_BF16 or RXLA_B200_F32 (rounded to bf16 on load).
- * y      : [m, n], RXLA_B200_BF16 or RXLA_B200_F32.  The dot product is
- *          accumulated in fp32 and rounded to bf16 (the reference's bf16 dot
- *          output) before it is stored, widened, added or gated.
+ * y      : [m, n].  The dot product is accumulated in fp32.
+ *          EPI_STORE + BF16 y: stores bf16(dot), the reference's bf16 dot
+ *          output (widen it to get the reference's F32 boundary value).
+ *          EPI_STORE + F32 y: stores the fp32 dot unrounded (an F32-output
+ *          dot, as the tied LM head of qwen3_5/mod.rs:157-173).
+ *          EPI_RESIDUAL_ADD (F32 y): y += bf16(dot).
+ *          EPI_SWIGLU: y = silu(bf16(gate)) * bf16(up), BF16 or F32 y.
  * m == 0 or n == 0 is a no-op.  Sizes are checked; a bad size returns
  * RXLA_B200_INVALID_ARGUMENT without launching anything.
  */
@@ -265,6 +279,10 @@ int32_t rxla_b200_comm_destroy(rxla_b200_comm* comm);
 /* In-place bf16 or f32 sum all-reduce of `count` elements on `stream`. */
 int32_t rxla_b200_allreduce(rxla_b200_comm* comm, void* buffer, int64_t count,
                             int32_t dtype, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,170 @@
+// capi.cu — library-level entry points: errors, device info, small fused ops.
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace rxla {
+
+static thread_local std::string t_last_error;
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+
+int32_t fail(int32_t code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+int32_t cuda_fail(cudaError_t err, const char* what) {
+  t_last_error = std::string(what) + ": " + cudaGetErrorName(err) + " (" +
+                 cudaGetErrorString(err) + ")";
+  return err == cudaErrorMemoryAllocation ? RXLA_B200_RESOURCE_EXHAUSTED : RXLA_B200_UNAVAILABLE;
+}
+
+int sm_count(int device) {
+  static int cache[64] = {};
+  if (device < 0 || device >= 64) return 148;
+  if (cache[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0)
+      v = 148;
+    cache[device] = v;
+  }
+  return cache[device];
+}
+
+int32_t read_device_status(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_rxla_device_status, sizeof(int)) != cudaSuccess)
+    return RXLA_B200_UNAVAILABLE;
+  if (reset && v != 0) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_rxla_device_status, &z, sizeof(int));
+  }
+  return v;
+}
+
+// ------------------------------------------------------------ RMSNorm -> bf16
+// One CTA per row: f32 sum of squares, then x * rsqrt(mean + eps) * w rounded
+// to bf16 (crates/rxla-core/src/ops.rs:929-945 followed by the consuming
+// linear's bf16 cast).
+__global__ void rms_norm_bf16_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                     int64_t width, float eps, __nv_bfloat16* __restrict__ y) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const float* xr = x + blockIdx.x * width;
+  float ss = 0.0f;
+  for (int64_t c = threadIdx.x; c < width; c += blockDim.x) ss += xr[c] * xr[c];
+  __shared__ float red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float mean = red[0] / (float)width;
+  const float rs = 1.0f / sqrtf(mean + eps);
+  for (int64_t c = threadIdx.x; c < width; c += blockDim.x)
+    y[blockIdx.x * width + c] = __float2bfloat16_rn((xr[c] * rs) * w[c]);
+}
+
+// ------------------------------------------------------------------- argmax
+// First index of the maximum (ties -> lowest index), one CTA per row.
+__global__ void argmax_kernel(const float* __restrict__ logits, int64_t vocab,
+                              int32_t* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const float* r = logits + blockIdx.x * vocab;
+  float best = -INFINITY;
+  int32_t idx = 0x7fffffff;
+  for (int64_t c = threadIdx.x; c < vocab; c += blockDim.x) {
+    float v = r[c];
+    if (v > best || (v == best && (int32_t)c < idx)) {
+      best = v;
+      idx = (int32_t)c;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int32_t si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    int32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ob > best || (ob == best && oi < idx)) {
+      best = ob;
+      idx = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sb[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    best = threadIdx.x < nw ? sb[threadIdx.x] : -INFINITY;
+    idx = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      int32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ob > best || (ob == best && oi < idx)) {
+        best = ob;
+        idx = oi;
+      }
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+  }
+}
+
+}  // namespace rxla
+
+extern "C" int32_t rxla_b200_abi_version(void) { return RXLA_B200_ABI_VERSION; }
+
+extern "C" const char* rxla_b200_last_error_message(void) { return rxla::t_last_error.c_str(); }
+
+extern "C" int32_t rxla_b200_device_info(int32_t device, int32_t* sm, int32_t* major,
+                                         int32_t* minor) {
+  cudaDeviceProp prop;
+  RXLA_CUDA_CHECK(cudaGetDeviceProperties(&prop, device));
+  if (sm) *sm = prop.multiProcessorCount;
+  if (major) *major = prop.major;
+  if (minor) *minor = prop.minor;
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_device_status(int32_t reset) {
+  return rxla::read_device_status(reset != 0);
+}
+
+extern "C" int32_t rxla_b200_rms_norm_bf16(const float* x, const float* weight, int64_t rows,
+                                           int64_t width, float eps, uint16_t* y, void* stream) {
+  using namespace rxla;
+  RXLA_REQUIRE(rows >= 0 && width > 0, "rms_norm_bf16: rows >= 0 and width > 0");
+  RXLA_REQUIRE(eps > 0.0f && eps == eps && eps < INFINITY,
+               "rms_norm_bf16: epsilon must be finite and positive (ops.rs:930)");
+  if (rows == 0) return RXLA_B200_OK;
+  RXLA_REQUIRE(x && weight && y, "rms_norm_bf16: null pointer");
+  cudaError_t e = launch_pdl(rms_norm_bf16_kernel, dim3((unsigned)rows), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), x, weight, width, eps,
+                             reinterpret_cast<__nv_bfloat16*>(y));
+  if (e != cudaSuccess) return cuda_fail(e, "rms_norm_bf16 launch");
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_argmax(const float* logits, int64_t rows, int64_t vocab,
+                                    int32_t* out, void* stream) {
+  using namespace rxla;
+  RXLA_REQUIRE(rows >= 0 && vocab > 0 && vocab <= INT32_MAX, "argmax: bad shape");
+  if (rows == 0) return RXLA_B200_OK;
+  RXLA_REQUIRE(logits && out, "argmax: null pointer");
+  cudaError_t e = launch_pdl(argmax_kernel, dim3((unsigned)rows), dim3(1024), 0,
+                             static_cast<cudaStream_t>(stream), logits, vocab, out);
+  if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+  return RXLA_B200_OK;
+}

@@ -1,0 +1,7 @@
+// librxla_b200.cu — single translation unit of the library (one device
+// module, so the device status word and kernels share one symbol space).
+#include <algorithm>
+
+#include "capi.cu"
+#include "w8_linear.cu"
+#include "dense_linear.cu"

@@ -1,0 +1,161 @@
+"""Host-side mirror of rxla's operator surface for the W8 decode hot path.
+
+Names, argument meaning and error behaviour follow the reference (paths inside
+the rxla project); the arithmetic runs in librxla_b200 on the tensors' CUDA
+device, with torch used only for device memory and streams.
+
+  QuantizedLinear / quantized_linear   crates/rxla-nn/src/layers.rs:231-298,784-793
+  linear (bf16 weight)                 crates/rxla-core/src/nn.rs:286-310
+  rms_norm                             crates/rxla-core/src/ops.rs:929-945
+  PagedKvCache / decode_attention      crates/rxla-core/src/kv_cache.rs:7-112,
+                                       crates/rxla-core/src/attention.rs:83-252,
+                                       crates/rxla-core/src/rotary.rs:17-74
+  rope_inv_freq                        crates/rxla-models/src/qwen3_5/mod.rs:211-228
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import RxlaError
+
+
+class InvalidLayerInput(ValueError):
+    """Mirror of rxla_nn::Error::InvalidLayerInput (crates/rxla-nn/src/layers.rs:258-275)."""
+
+
+def _stream(stream) -> ctypes.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def _ptr(t) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+_DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+
+
+def quantized_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
+                     group_size: int | None = None, *, out_dtype=torch.bfloat16,
+                     epilogue: int = _lib.EPI_STORE, out: torch.Tensor | None = None,
+                     stream=None) -> torch.Tensor:
+    """W8A16 linear through rxla_b200_w8a16_linear.
+
+    x [..., K] bf16/f32, weight u8 [N, K] (value + 128; [2N, K] = [gate; up] for
+    EPI_SWIGLU), scale f32 [N_rows, K / group].  Returns y [..., N] in out_dtype
+    (bf16: the bf16 dot; f32: the unrounded fp32 dot), or accumulates into the
+    f32 `out` for EPI_RESIDUAL_ADD.
+    """
+    if x.dtype not in _DT or weight.dtype != torch.uint8 or scale.dtype != torch.float32:
+        raise InvalidLayerInput("QuantizedLinear needs bf16/f32 x, u8 weight, f32 scale")
+    if x.dim() == 0:
+        raise InvalidLayerInput("QuantizedLinear needs an input with rank at least one")
+    k = x.shape[-1]
+    rows = weight.shape[0]
+    if weight.dim() != 2 or weight.shape[1] != k:
+        raise InvalidLayerInput("weight must be [out_features, in_features]")
+    group = k if group_size is None else int(group_size)
+    if group <= 0 or k % group != 0:
+        raise InvalidLayerInput("positive widths and a group size dividing the input width")
+    if scale.numel() != rows * (k // group):
+        raise InvalidLayerInput("scale must be [out_features, in_features / group_size]")
+    n = rows // 2 if epilogue == _lib.EPI_SWIGLU else rows
+    lead = x.shape[:-1]
+    m = int(np.prod(lead)) if len(lead) else 1
+    x2 = x.reshape(m, k)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    if out is None:
+        if epilogue == _lib.EPI_RESIDUAL_ADD:
+            raise InvalidLayerInput("the residual epilogue needs `out` (f32) to add into")
+        out = torch.empty(*lead, n, dtype=out_dtype, device=x.device)
+    _lib.call("rxla_b200_w8a16_linear", _ptr(x2), _DT[x.dtype], _ptr(weight),
+              _ptr(scale), group, m, n, k, _ptr(out), _DT[out.dtype], epilogue, _stream(stream))
+    return out
+
+
+class QuantizedLinear:
+    """rxla_nn::QuantizedLinear::new(out_features, group_size) (layers.rs:231-256).
+
+    `apply(params, name, input)` reads `{name}.weight` (u8 [out, in]) and
+    `{name}.scale` (f32 [out, in/group]) from `params` and returns the F32
+    boundary value of the bf16-compute layer, as apply_quantized_linear does
+    with layer compute dtype BF16 (layers.rs:289-297).
+    """
+
+    def __init__(self, out_features: int, group_size: int):
+        self.out_features = int(out_features)
+        self.group_size = int(group_size)
+
+    def apply(self, params, name: str, input: torch.Tensor) -> torch.Tensor:
+        if input.dtype != torch.float32 or input.dim() == 0:
+            raise InvalidLayerInput("an F32 input with rank at least one")
+        k = input.shape[-1]
+        if (self.out_features <= 0 or self.group_size <= 0 or k <= 0
+                or k % self.group_size != 0):
+            raise InvalidLayerInput("positive widths and a group size dividing the input width")
+        w = params[f"{name}.weight"]
+        s = params[f"{name}.scale"]
+        if tuple(w.shape) != (self.out_features, k) or w.dtype != torch.uint8:
+            raise InvalidLayerInput(f"{name}.weight must be U8 [{self.out_features}, {k}]")
+        y = quantized_linear(input, w, s, self.group_size, out_dtype=torch.bfloat16)
+        return y.float()
+
+
+def bf16_linear(x: torch.Tensor, weight: torch.Tensor, *, out_dtype=torch.float32,
+                epilogue: int = _lib.EPI_STORE, out=None, stream=None) -> torch.Tensor:
+    """y = bf16(x) · weightᵀ with a bf16 weight [N, K] (rxla_b200_bf16_linear)."""
+    k = x.shape[-1]
+    n = weight.shape[0]
+    lead = x.shape[:-1]
+    m = int(np.prod(lead)) if len(lead) else 1
+    x2 = x.reshape(m, k).contiguous()
+    if out is None:
+        out = torch.empty(*lead, n, dtype=out_dtype, device=x.device)
+    _lib.call("rxla_b200_bf16_linear", _ptr(x2), _DT[x.dtype], _ptr(weight), m, n, k,
+              _ptr(out), _DT[out.dtype], epilogue, _stream(stream))
+    return out
+
+
+def rms_norm_bf16(x: torch.Tensor, weight: torch.Tensor, epsilon: float,
+                  out=None, stream=None) -> torch.Tensor:
+    """bf16(x * rsqrt(mean(x²) + eps) * w) over the last axis (ops.rs:929-945)."""
+    if not (epsilon > 0 and math.isfinite(epsilon)):
+        raise InvalidLayerInput("RMSNorm requires a finite positive epsilon")
+    width = x.shape[-1]
+    rows = x.numel() // width
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    _lib.call("rxla_b200_rms_norm_bf16", _ptr(x), _ptr(weight), rows, width,
+              ctypes.c_float(epsilon), _ptr(out), _stream(stream))
+    return out
+
+
+def argmax(logits: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    v = logits.shape[-1]
+    rows = logits.numel() // v
+    if out is None:
+        out = torch.empty(logits.shape[:-1], dtype=torch.int32, device=logits.device)
+    _lib.call("rxla_b200_argmax", _ptr(logits), rows, v, _ptr(out), _stream(stream))
+    return out
+
+
+def rope_inv_freq(theta: float, rotary_dim: int) -> np.ndarray:
+    """θ^(-2i/rotary_dim) in f32, as qwen3_5/mod.rs:213-222 computes it on the host."""
+    i = np.arange(rotary_dim // 2, dtype=np.float32)
+    return np.power(np.float32(theta), (np.float32(-2.0) * i) / np.float32(rotary_dim),
+                    dtype=np.float32)
+
+
+def device_status(reset: bool = False) -> int:
+    return int(_lib.load().rxla_b200_device_status(int(reset)))
+
+
+__all__ = ["QuantizedLinear", "quantized_linear", "bf16_linear", "rms_norm_bf16", "argmax",
+           "rope_inv_freq", "device_status", "InvalidLayerInput", "RxlaError"]

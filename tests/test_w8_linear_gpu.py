@@ -1,0 +1,153 @@
+"""W8A16 linear parity on the GPU, through the C ABI (rxla_b200_w8a16_linear).
+
+Checked against the CPU oracle on the same seeded inputs:
+  * exact algebra (oracle mode 2, f64, scale factored): the kernel's fp32
+    accumulation of exact bf16(x)·q products then one bf16 rounding —
+    |Δ| <= 2^-8·|ref| + 2^-20·Σ|x·q·s|;
+  * the reference's own rounding points (mode 1: bf16(W_deq)) —
+    |Δ| <= 2^-8·|ref| + 2^-8·Σ|x·q·s|, the bound of W_deq's bf16 rounding.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from rxla_b200 import _lib, nn
+
+pytestmark = pytest.mark.gpu
+
+
+def _bound(x, w, s, group):
+    k = x.shape[1]
+    q = np.abs(w.astype(np.float64) - 128.0)
+    xa = np.abs(oracle.bf16_round(x).astype(np.float64))
+    sg = np.repeat(s.astype(np.float64), group, axis=1) if s.shape[1] > 1 else s.astype(np.float64)
+    return xa @ (q * sg).T if s.shape[1] > 1 else (xa @ q.T) * s.reshape(1, -1)
+
+
+def _case(m, n, k, group, seed):
+    x = oracle.bf16_round(oracle.normal(m * k, seed).reshape(m, k))
+    w = (oracle.randint(n * k, seed + 1, -127, 128).reshape(n, k) + 128).astype(np.uint8)
+    s = oracle.uniform(n * (k // group), seed + 2, 1e-3, 1e-2).reshape(n, k // group)
+    return x, w, s
+
+
+def _run(x, w, s, group, x_dtype=torch.bfloat16, out_dtype=torch.bfloat16, dev="cuda"):
+    xt = torch.from_numpy(x).to(dev).to(x_dtype)
+    wt = torch.from_numpy(w).to(dev)
+    st = torch.from_numpy(np.ascontiguousarray(s)).to(dev)
+    y = nn.quantized_linear(xt, wt, st, group, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    return y.float().cpu().numpy()
+
+
+def _check(y, x, w, s, group, bf16_out=True):
+    exact = oracle.w8_linear(x, w, s, group, mode=2).astype(np.float64)
+    ref = oracle.w8_linear(x, w, s, group, mode=1).astype(np.float64)
+    bound = _bound(x, w, s, group)
+    rel = 2.0 ** -8 if bf16_out else 2.0 ** -20
+    err_exact = np.abs(y - exact) - (rel * np.abs(exact) + 2.0 ** -20 * bound)
+    assert err_exact.max() <= 0, f"exact-algebra excess {err_exact.max()}"
+    err_ref = np.abs(y - ref) - (2.0 ** -8 * np.abs(ref) + 2.0 ** -8 * bound)
+    assert err_ref.max() <= 0, f"reference excess {err_ref.max()}"
+
+
+@pytest.mark.parametrize("m", [1, 2, 7, 8, 9, 16, 17, 32, 33, 70])
+def test_sweep_shapes_small(cuda, m):
+    x, w, s = _case(m, 200, 1024, 1024, seed=10 + m)
+    _check(_run(x, w, s, 1024), x, w, s, 1024)
+
+
+@pytest.mark.parametrize("n,k", [(4096, 4096), (6144, 4096), (4096, 12288), (12288, 4096)])
+@pytest.mark.parametrize("m", [1, 8, 32])
+def test_config2_shapes(cuda, n, k, m):
+    """(N,K) sweep, per-channel scales, M in {1,8,32}."""
+    x, w, s = oracle.linear_sweep_case(m, n, k, seed=n + k + m)
+    _check(_run(x, w, s, k), x, w, s, k)
+
+
+@pytest.mark.parametrize("group", [64, 128, 512])
+def test_grouped_scales(cuda, group):
+    x, w, s = _case(5, 300, 1024, group, seed=group)
+    _check(_run(x, w, s, group), x, w, s, group)
+
+
+@pytest.mark.parametrize("n,k,group", [(37, 48, 16), (5, 64, 32), (1, 64, 64), (3, 1000, 8)])
+def test_odd_shapes_generic_path(cuda, n, k, group):
+    """Shapes off the fast path (K % 64 != 0, small groups) use the generic kernel."""
+    x, w, s = _case(3, n, k, group, seed=n * k)
+    _check(_run(x, w, s, group), x, w, s, group)
+
+
+def test_f32_input_and_output(cuda):
+    x, w, s = _case(4, 256, 512, 512, seed=5)
+    x32 = oracle.normal(4 * 512, 99).reshape(4, 512)  # f32, rounded to bf16 by the kernel
+    y = _run(x32, w, s, 512, x_dtype=torch.float32, out_dtype=torch.float32)
+    _check(y, x32, w, s, 512, bf16_out=False)
+
+
+def test_residual_epilogue(cuda):
+    x, w, s = _case(3, 512, 1024, 1024, seed=21)
+    h = oracle.normal(3 * 512, 22).reshape(3, 512)
+    ht = torch.from_numpy(h).cuda()
+    nn.quantized_linear(torch.from_numpy(x).cuda().bfloat16(), torch.from_numpy(w).cuda(),
+                        torch.from_numpy(s).cuda(), 1024, epilogue=_lib.EPI_RESIDUAL_ADD, out=ht)
+    y = _run(x, w, s, 1024)  # bf16 dot
+    expect = (h + y).astype(np.float32)
+    np.testing.assert_array_equal(ht.cpu().numpy(), expect)
+
+
+@pytest.mark.parametrize("m,n,k,group", [(1, 1536, 512, 512), (8, 3000, 1024, 128), (20, 700, 2048, 2048)])
+def test_swiglu_epilogue(cuda, m, n, k, group):
+    x, w, s = _case(m, 2 * n, k, group, seed=m + n)
+    xt = torch.from_numpy(x).cuda().bfloat16()
+    y = nn.quantized_linear(xt, torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda(), group,
+                            epilogue=_lib.EPI_SWIGLU).float().cpu().numpy()
+    exact = oracle.w8_linear(x, w, s, group, mode=2).astype(np.float64)
+    bound = _bound(x, w, s, group)
+    g_ex, u_ex = exact[:, :n], exact[:, n:]
+    # each of gate / up: one bf16 rounding + fp32 accumulation error
+    dg = 2.0 ** -8 * np.abs(g_ex) + 2.0 ** -20 * bound[:, :n]
+    du = 2.0 ** -8 * np.abs(u_ex) + 2.0 ** -20 * bound[:, n:]
+    gate = g_ex
+    sig = 1.0 / (1.0 + np.exp(-gate))
+    expect = gate * sig * u_ex
+    dsilu = np.abs(sig * (1.0 + gate * (1.0 - sig)))  # |d silu / d g|
+    tol = dsilu * dg * (np.abs(u_ex) + du) + np.abs(gate * sig) * du + 2.0 ** -8 * np.abs(expect)
+    excess = np.abs(y - expect) - 1.01 * tol
+    assert excess.max() <= 1e-7, f"swiglu excess {excess.max()}"
+
+
+def test_deterministic(cuda):
+    x, w, s = _case(8, 4096, 4096, 4096, seed=77)
+    a = _run(x, w, s, 4096)
+    b = _run(x, w, s, 4096)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_quantized_linear_layer_mirror(cuda):
+    """QuantizedLinear.apply: F32 in, F32 out (the bf16 dot widened), reference errors."""
+    x, w, s = _case(6, 64, 256, 32, seed=3)
+    params = {"proj.weight": torch.from_numpy(w).cuda(), "proj.scale": torch.from_numpy(s).cuda()}
+    y = nn.QuantizedLinear(64, 32).apply(params, "proj", torch.from_numpy(x).cuda())
+    assert y.dtype == torch.float32 and tuple(y.shape) == (6, 64)
+    _check(y.cpu().numpy(), x, w, s, 32)
+    with pytest.raises(nn.InvalidLayerInput):
+        nn.QuantizedLinear(64, 48).apply(params, "proj", torch.from_numpy(x).cuda())
+    with pytest.raises(nn.InvalidLayerInput):
+        nn.QuantizedLinear(64, 32).apply(params, "proj", torch.from_numpy(x).cuda().bfloat16())
+
+
+def test_invalid_sizes_rejected_without_launch(cuda):
+    x = torch.zeros(2, 64, device="cuda", dtype=torch.bfloat16)
+    w = torch.zeros(8, 64, device="cuda", dtype=torch.uint8)
+    s = torch.ones(8, 1, device="cuda")
+    y = torch.empty(2, 8, device="cuda", dtype=torch.bfloat16)
+    lib = _lib.load()
+    st = lib.rxla_b200_w8a16_linear(x.data_ptr(), _lib.BF16, w.data_ptr(), s.data_ptr(), 48, 2, 8,
+                                    64, y.data_ptr(), _lib.BF16, 0, None)
+    assert st == _lib.INVALID_ARGUMENT
+    assert b"group_size" in lib.rxla_b200_last_error_message()
+    assert lib.rxla_b200_w8a16_linear(None, _lib.BF16, None, None, 64, 0, 8, 64, None, _lib.BF16,
+                                      0, None) == _lib.OK  # m == 0 is a no-op
+    assert nn.device_status() == 0
