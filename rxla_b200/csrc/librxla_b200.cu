@@ -5,3 +5,4 @@
 #include "capi.cu"
 #include "w8_linear.cu"
 #include "dense_linear.cu"
+#include "attention.cu"

@@ -153,9 +153,91 @@ def rope_inv_freq(theta: float, rotary_dim: int) -> np.ndarray:
                     dtype=np.float32)
 
 
+class PagedKvCache:
+    """Paged bf16 K/V cache on the device: [num_pages, kv_heads, 16, head_dim] each.
+
+    The device-side counterpart of rxla_core::KvCache (crates/rxla-core/src/kv_cache.rs:7-112)
+    for decode: `page_table[b, i]` is the i-th page of sequence b, `ctx_lens[b]` the
+    number of cached tokens, i.e. the position of the next token.
+    """
+
+    PAGE = 16
+
+    def __init__(self, *, batch: int, kv_heads: int, head_dim: int, max_context: int,
+                 num_pages: int | None = None, device="cuda"):
+        self.batch, self.kv_heads, self.head_dim = batch, kv_heads, head_dim
+        self.max_context = max_context
+        self.max_pages = (max_context + self.PAGE - 1) // self.PAGE
+        self.num_pages = num_pages or batch * self.max_pages
+        shape = (self.num_pages, kv_heads, self.PAGE, head_dim)
+        self.k = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.page_table = torch.arange(batch * self.max_pages, dtype=torch.int32,
+                                       device=device).reshape(batch, self.max_pages) % self.num_pages
+        self.ctx_lens = torch.zeros(batch, dtype=torch.int32, device=device)
+        self.pages_per_seq = None
+
+
+def paged_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_context) -> int:
+    n = ctypes.c_size_t()
+    _lib.call("rxla_b200_paged_decode_workspace_size", batch, q_heads, kv_heads, head_dim,
+              max_context, ctypes.byref(n))
+    return int(n.value)
+
+
+def paged_decode_attention(q, k_new, v_new, cache: PagedKvCache, *, q_heads: int,
+                           q_norm_weight=None, k_norm_weight=None, eps: float = 1e-6,
+                           inv_freq=None, rotary_dim: int = 0, scale: float = 0.0,
+                           kv_update: int = _lib.KV_CLAMP, advance_ctx: bool = False,
+                           accepted=None, out=None, workspace=None, stream=None):
+    """One decode step of GQA over the paged cache (rxla_b200_paged_decode_attention).
+
+    q [batch, q_heads*D], k_new / v_new [batch, kv_heads*D] (bf16 views with a row
+    stride, e.g. slices of a fused QKV output).  Returns out [batch, q_heads*D] bf16.
+    """
+    batch, hkv, d = cache.batch, cache.kv_heads, cache.head_dim
+    if out is None:
+        out = torch.empty(batch, q_heads * d, dtype=torch.bfloat16, device=q.device)
+    if workspace is None:
+        workspace = torch.zeros(paged_decode_workspace_size(batch, q_heads, hkv, d,
+                                                            cache.max_context),
+                                dtype=torch.uint8, device=q.device)
+    a = _lib.PagedDecodeArgs()
+    a.struct_size = ctypes.sizeof(_lib.PagedDecodeArgs)
+    a.batch, a.q_heads, a.kv_heads, a.head_dim = batch, q_heads, hkv, d
+    a.q, a.k_new, a.v_new = q.data_ptr(), k_new.data_ptr(), v_new.data_ptr()
+    a.q_row_stride = q.stride(0)
+    a.kv_row_stride = k_new.stride(0)
+    if k_new.stride(0) != v_new.stride(0):
+        raise InvalidLayerInput("k_new and v_new must share a row stride")
+    a.q_norm_weight = 0 if q_norm_weight is None else q_norm_weight.data_ptr()
+    a.k_norm_weight = 0 if k_norm_weight is None else k_norm_weight.data_ptr()
+    a.norm_eps = eps
+    a.inv_freq = 0 if inv_freq is None else inv_freq.data_ptr()
+    a.rotary_dim = rotary_dim
+    a.scale = scale
+    a.k_pages, a.v_pages = cache.k.data_ptr(), cache.v.data_ptr()
+    a.num_pages = cache.num_pages
+    a.page_size = PagedKvCache.PAGE
+    a.max_pages_per_seq = cache.page_table.shape[1]
+    a.page_table = cache.page_table.data_ptr()
+    a.pages_per_seq = 0 if cache.pages_per_seq is None else cache.pages_per_seq.data_ptr()
+    a.ctx_lens = cache.ctx_lens.data_ptr()
+    a.kv_update = kv_update
+    a.advance_ctx = int(advance_ctx)
+    a.accepted = 0 if accepted is None else accepted.data_ptr()
+    a.out = out.data_ptr()
+    a.workspace = workspace.data_ptr()
+    a.workspace_bytes = workspace.numel()
+    a.max_context = cache.max_context
+    _lib.call("rxla_b200_paged_decode_attention", ctypes.byref(a), _stream(stream))
+    return out
+
+
 def device_status(reset: bool = False) -> int:
     return int(_lib.load().rxla_b200_device_status(int(reset)))
 
 
 __all__ = ["QuantizedLinear", "quantized_linear", "bf16_linear", "rms_norm_bf16", "argmax",
-           "rope_inv_freq", "device_status", "InvalidLayerInput", "RxlaError"]
+           "rope_inv_freq", "device_status", "InvalidLayerInput", "RxlaError", "PagedKvCache",
+           "paged_decode_attention", "paged_decode_workspace_size"]
