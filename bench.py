@@ -1,0 +1,368 @@
+"""Benchmark: W8 decode tokens/s of the 8B-shaped decoder.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one GPU): the 8B-shaped Qwen3-style W8 decoder (36 layers, hidden
+4096, 32 q / 8 kv heads, head_dim 128, SwiGLU 12288, vocab 151936, int8
+per-channel weights, synthetic seeded values), a 2048-token random prompt fed
+through the decoder, then greedy decode steps.  A "step" is one decode step
+at batch 1 (the headline `value`); the same is measured at batch 64.
+
+N > 1 (torchrun, one process per GPU): N independent replicas of the batch-1
+workload (no data-path collective); value = tokens of all ranks / max-over-
+ranks time ("scaling": "weak").
+
+`--impl reference`: the reference path's CPU restatement (oracle/, the
+reference's Rust/XLA stack cannot run here) timed on all host cores, rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIG4 = dict(layers=36, hidden=4096, q_heads=32, kv_heads=8, head_dim=128, intermediate=12288,
+               vocab=151936, rms_eps=1e-6, rope_theta=1e6)
+PROMPT = 2048
+METRIC = "W8 decode tokens/sec"
+UNIT = "tokens/s"
+
+
+def step_bytes(cfg, batch, ctx):
+    """Algorithmic HBM bytes of one decode step: every weight byte once, the
+    visible KV cache once, plus the per-token activations (negligible)."""
+    H, D, I, V = cfg["hidden"], cfg["head_dim"], cfg["intermediate"], cfg["vocab"]
+    hq, hkv = cfg["q_heads"], cfg["kv_heads"]
+    per_layer = (hq + 2 * hkv) * D * H + H * hq * D + 2 * I * H + H * I
+    weights = cfg["layers"] * per_layer + V * H
+    kv = cfg["layers"] * batch * (ctx + 1) * hkv * D * 2 * 2
+    return weights, kv
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during timing."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9
+                          for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(ROOT / "MEASURED_PEAKS.json") as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ CPU legs
+
+def cpu_decode_sample(threads_note=True):
+    """Time the CPU oracle on a bounded sample of the config-4 decoder.
+
+    Sample: the decoder with 2 of the 36 layers (full 151936-token tied head),
+    4 decode steps after 4 prompt tokens; the per-layer time is
+    (step - head) / 2 and a full token costs 36 layers + head.
+    """
+    import numpy as np
+    import oracle
+    cfg = dict(CONFIG4, layers=2)
+    dec = oracle.Decoder(**cfg, max_batch=1, max_context=32)
+    dec.init_synthetic(0)
+    tok = np.array([1], np.int32)
+    for _ in range(4):
+        _, tok = dec.step(tok)
+    t0 = time.perf_counter()
+    n = 3
+    for _ in range(n):
+        _, tok = dec.step(tok)
+    t_step = (time.perf_counter() - t0) / n
+    emb_w = dec.parameter("embed_tokens.weight").reshape(CONFIG4["vocab"], CONFIG4["hidden"])
+    emb_s = dec.parameter("embed_tokens.scale").reshape(CONFIG4["vocab"], 1)
+    x = np.ones((1, CONFIG4["hidden"]), np.float32)
+    t0 = time.perf_counter()
+    oracle.w8_linear(x, emb_w, emb_s, CONFIG4["hidden"], mode=2)
+    t_head = time.perf_counter() - t0
+    dec.close()
+    t_layer = max(t_step - t_head, 1e-9) / 2
+    t_token = CONFIG4["layers"] * t_layer + t_head
+    return {"value": 1.0 / t_token, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"oracle C restatement, 2 of 36 layers + full head, {n} timed decode steps "
+                      f"(step {t_step:.3f}s, head {t_head:.3f}s), extrapolated to 36 layers"}
+
+
+# --------------------------------------------------------------- our path
+
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    from rxla_b200 import _lib
+    from rxla_b200.decoder import Decoder
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    lib = _lib.load()
+    cfg = dict(CONFIG4)
+    max_ctx = PROMPT + args.warmup + args.steps + 32
+    b64 = 64 if (world == 1 and not args.no_batch64) else 1
+    dec = Decoder(**cfg, embedding_dtype="u8", max_batch=b64, max_context=max_ctx,
+                  device=local_rank)
+    dec.init_synthetic(1234)
+
+    tin = ctypes.c_void_p(dec.tokens_in_ptr)
+    tout = ctypes.c_void_p(dec.tokens_out_ptr)
+
+    def prompt_fill(batch):
+        dec.reset(sptr)
+        prompt = torch.randint(0, cfg["vocab"], (PROMPT, batch), dtype=torch.int32, device=dev,
+                               generator=torch.Generator(device=dev).manual_seed(1))
+        for t in range(PROMPT):
+            _lib.call("rxla_b200_decoder_step", dec.handle, ctypes.c_void_p(prompt[t].data_ptr()),
+                      batch, tout, None, sptr)
+        torch.cuda.synchronize()
+
+    def greedy(batch, n):
+        for _ in range(n):
+            _lib.call("rxla_b200_decoder_step", dec.handle, tout, batch, tout, None, sptr)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def timed(batch, n):
+        greedy(batch, args.warmup)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        greedy(batch, n)
+        e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    sampler = ClockSampler(local_rank)
+    # ---- batch 1 (headline)
+    prompt_fill(1)
+    sampler.start()
+    ms1 = timed(1, args.steps)
+    ctx_b1 = PROMPT + args.warmup + args.steps // 2
+    # ---- end to end through the host-buffer C ABI: H2D tokens, D2H next tokens
+    host_tok = np.zeros(1, np.int32)
+    dec.step_host(host_tok)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host_tok = dec.step_host(host_tok)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    # ---- batch 64
+    res64 = None
+    if b64 == 64:
+        prompt_fill(64)
+        n64 = max(8, min(args.steps, 64))
+        ms64 = timed(64, n64)
+        w, kv = step_bytes(cfg, 64, PROMPT + args.warmup + n64 // 2)
+        res64 = {"value": 64 * n64 / (ms64 / 1e3), "ms_per_step": ms64 / n64, "steps": n64,
+                 "step_gbs": (w + kv) / (ms64 / n64 * 1e-3) / 1e9}
+    clocks = sampler.stop()
+
+    # ---- roofline of the dominant kernel: the W8 linear, all launches of one
+    # batch-1 step (qkv, o, gate/up, down per layer + tied head) replayed in a graph
+    roof = gemv_roofline(dec, cfg, dev, stream, lib)
+    status = lib.rxla_b200_device_status(0)
+    dec.close()
+
+    weights, kv1 = step_bytes(cfg, 1, ctx_b1)
+    tok_s = world * args.steps / (ms1 / 1e3)
+    out = {
+        "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms1 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8 weights, bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded random W8 weights, random 2048-token prompt)",
+        "config": {"workload": "config4: 8B-shaped W8 decoder, batch 1 decode after a 2048-token prompt",
+                   "model": "qwen3-style-8B-shape", "layers": 36, "hidden": 4096, "vocab": 151936,
+                   "global_batch": world, "seq_len": PROMPT, "parallelism": f"replicas x{world}",
+                   "l2": "inputs > L2 (7.6 GB of weights per step)"},
+        "step_gbs": (weights + kv1) / (ms1 / args.steps * 1e-3) / 1e9,
+        "step_frac_of_hbm": (weights + kv1) / (ms1 / args.steps * 1e-3) / 1e9 / measured_peaks()[0],
+        "batch64": res64,
+        "e2e": {"value": world * args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4},
+        "roofline": roof,
+        "clocks": clocks,
+        "gpu_launches": args.steps * (1 + 36 * 7 + 3),
+        "device_status": status,
+    }
+    return out
+
+
+def gemv_roofline(dec, cfg, dev, stream, lib):
+    """Time every W8 linear of one batch-1 step, replayed as one CUDA graph.
+
+    Algorithmic bytes per launch = N·K weights + 4·N scales + 2·K (x) + output;
+    achieved = Σ bytes / Σ time of the launches (bytes-weighted mean)."""
+    import torch
+    H, D, I, V = cfg["hidden"], cfg["head_dim"], cfg["intermediate"], cfg["vocab"]
+    qkv_rows = (cfg["q_heads"] + 2 * cfg["kv_heads"]) * D
+    x = torch.zeros(1, max(H, I, cfg["q_heads"] * D), dtype=torch.bfloat16, device=dev)
+    ybf = torch.empty(1, max(qkv_rows, I), dtype=torch.bfloat16, device=dev)
+    yf = torch.zeros(1, max(H, V), dtype=torch.float32, device=dev)
+    s = ctypes.c_void_p(stream.cuda_stream)
+    launches = []
+    for l in range(cfg["layers"]):
+        p = f"layers.{l}."
+        launches.append((p + "self_attn.qkv", qkv_rows, H, ybf, 1, 0))
+        launches.append((p + "self_attn.o_proj", H, cfg["q_heads"] * D, yf, 0, 1))
+        launches.append((p + "mlp.gate_up", I, H, ybf, 1, 2))
+        launches.append((p + "mlp.down_proj", H, I, yf, 0, 1))
+    launches.append(("embed_tokens", V, H, yf, 0, 0))
+    total_bytes = 0
+    calls = []
+    for name, n, k, y, ybf16, epi in launches:
+        w, _, _ = dec.parameter(name + ".weight")
+        sc, _, _ = dec.parameter(name + ".scale")
+        rows = 2 * n if epi == 2 else n
+        total_bytes += rows * k + 4 * rows + 2 * k + (2 if ybf16 else 4) * n * (2 if epi == 1 else 1)
+        calls.append((x.data_ptr(), w, sc, k, n, k, y.data_ptr(), 1 if ybf16 else 0, epi))
+
+    def run():
+        for xp, w, sc, g, n, k, yp, ybf16, epi in calls:
+            st = lib.rxla_b200_w8a16_linear(xp, 1, w, sc, g, 1, n, k, yp, ybf16, epi,
+                                            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            assert st == 0
+    run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    peak, kind = measured_peaks()
+    achieved = total_bytes / sec / 1e9
+    return {"bound": "hbm", "kernel": "w8_skinny_kernel (all W8 linears of one batch-1 step)",
+            "achieved": achieved, "peak": peak, "peak_kind": kind, "unit": "GB/s",
+            "frac": achieved / peak, "traffic": None, "launches": len(calls),
+            "avg_launch_us": sec / len(calls) * 1e6, "bytes_per_step": total_bytes}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-batch64", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = []
+        res = None
+        for _ in range(max(1, min(args.steps, 2))):
+            res = cpu_decode_sample()
+            steps.append(res["value"])
+        value = statistics.median(steps)
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                "impl": "reference", "scaling": "weak", "vs_baseline": None,
+                "dtype": "u8 weights, f32 activations (CPU restatement)",
+                "data": "synthetic", "config": {"workload": "config4: 8B-shaped W8 decoder, batch 1 decode"},
+                "cpu_baseline": {**res, "value": value},
+                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import torch
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    out = run_ours(args, rank, world, local_rank)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_decode_sample()
+    if world > 1:
+        import torch
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

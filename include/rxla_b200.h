@@ -247,7 +247,13 @@ int32_t rxla_b200_decoder_destroy(rxla_b200_decoder* decoder);
  * "layers.3.input_layernorm.weight", "norm.weight". */
 int32_t rxla_b200_decoder_parameter(rxla_b200_decoder* decoder, const char* name,
                                     void** device_ptr, int64_t* bytes, int32_t* dtype);
-/* Fill every parameter with seeded synthetic values on the device. */
+/* Copy `bytes` of host memory into the named parameter (sizes must match):
+ * the loading path for checkpoint tensors. Synchronous. */
+int32_t rxla_b200_decoder_set_parameter(rxla_b200_decoder* decoder, const char* name,
+                                        const void* host, int64_t bytes);
+/* Fill every parameter with seeded synthetic values on the device: W8 weights
+ * N(0, 0.02) quantized per row (clip 4.5σ), norms 1 + N(0, 0.02), bf16
+ * embedding N(0, 0.02). */
 int32_t rxla_b200_decoder_init_synthetic(rxla_b200_decoder* decoder, uint64_t seed);
 /* Drop all cached context of every sequence. */
 int32_t rxla_b200_decoder_reset(rxla_b200_decoder* decoder, void* stream);
@@ -262,6 +268,16 @@ int32_t rxla_b200_decoder_step(rxla_b200_decoder* decoder, const int32_t* tokens
  * through pinned staging on `stream` and synchronises it. */
 int32_t rxla_b200_decoder_step_host(rxla_b200_decoder* decoder, const int32_t* tokens_host,
                                     int32_t batch, int32_t* next_tokens_host, void* stream);
+/* Device buffers the step reads and writes: tokens in (int32 [max_batch]),
+ * next tokens out (int32 [max_batch]) and logits (f32 [max_batch, vocab]).
+ * Passing tokens_in / tokens_out to rxla_b200_decoder_step skips its copies. */
+int32_t rxla_b200_decoder_io(rxla_b200_decoder* decoder, int32_t** tokens_in,
+                             int32_t** tokens_out, float** logits);
+/* The paged K/V cache of one layer (session state, like Session::state of
+ * crates/rxla-core/src/state.rs): bf16 [max_batch * pages_per_seq, kv_heads,
+ * 16, head_dim] each; sequence b owns pages [b * pages_per_seq, (b+1) * ...). */
+int32_t rxla_b200_decoder_kv_cache(rxla_b200_decoder* decoder, int32_t layer, void** k_pages,
+                                   void** v_pages, int64_t* bytes);
 /* Current context length of each sequence (device int32 [max_batch]). */
 int32_t rxla_b200_decoder_context_lengths(rxla_b200_decoder* decoder, const int32_t** lens);
 

@@ -83,6 +83,7 @@ def lib() -> ctypes.CDLL:
         "oracle_decoder_reset": (None, [_vp]),
         "oracle_decoder_step": (None, [_vp, _i32p, _i32, _f32p, _i32p]),
         "oracle_decoder_context": (_i32, [_vp, _i32]),
+        "oracle_decoder_kv": (None, [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
         "oracle_num_threads": (_i32, []),
     }
     for name, (res, args) in sig.items():
@@ -284,7 +285,7 @@ class _DecCfg(ctypes.Structure):
                 ("layers", "hidden", "q_heads", "kv_heads", "head_dim", "intermediate", "vocab")] + \
                [("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float)] + \
                [(n, ctypes.c_int32) for n in
-                ("embedding_bf16", "group_size", "max_batch", "max_context")]
+                ("embedding_bf16", "group_size", "max_batch", "max_context", "linear_mode")]
 
 
 class Decoder:
@@ -292,10 +293,12 @@ class Decoder:
 
     def __init__(self, *, layers, hidden, q_heads, kv_heads, head_dim, intermediate, vocab,
                  rms_eps=1e-6, rope_theta=1e6, embedding_bf16=False, group_size=0,
-                 max_batch=1, max_context=256):
+                 max_batch=1, max_context=256, linear_mode=1):
+        """linear_mode 1: the reference's QuantizedLinear rounding (bf16(W_deq));
+        3: exact q with the scale on the fp32 dot (the CUDA kernel's algebra)."""
         self.cfg = _DecCfg(layers, hidden, q_heads, kv_heads, head_dim, intermediate, vocab,
                            rms_eps, rope_theta, int(embedding_bf16), group_size, max_batch,
-                           max_context)
+                           max_context, linear_mode)
         self.vocab = vocab
         self._h = lib().oracle_decoder_create(ctypes.byref(self.cfg))
 
@@ -324,6 +327,17 @@ class Decoder:
 
     def init_synthetic(self, seed: int):
         lib().oracle_decoder_init_synthetic(self._h, seed)
+
+    def kv_cache(self, layer: int):
+        """Dense bf16 K/V of one layer: [max_batch, kv_heads, max_context, head_dim] each."""
+        k, v = ctypes.c_void_p(), ctypes.c_void_p()
+        lib().oracle_decoder_kv(self._h, layer, ctypes.byref(k), ctypes.byref(v))
+        c = self.cfg
+        n = c.max_batch * c.kv_heads * c.max_context * c.head_dim
+        shape = (c.max_batch, c.kv_heads, c.max_context, c.head_dim)
+        kk = np.frombuffer((ctypes.c_uint16 * n).from_address(k.value), np.uint16).reshape(shape)
+        vv = np.frombuffer((ctypes.c_uint16 * n).from_address(v.value), np.uint16).reshape(shape)
+        return kk, vv
 
     def reset(self):
         lib().oracle_decoder_reset(self._h)

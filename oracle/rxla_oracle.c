@@ -125,7 +125,7 @@ void oracle_w8_linear(const float* x, int64_t m, int64_t k, const uint8_t* w,
     float* wrow = (float*)malloc(sizeof(float) * (size_t)k);
 #pragma omp for schedule(static)
     for (int64_t r = 0; r < n; ++r) {
-      if (mode == 2) {
+      if (mode == 2 || mode == 3) {
         for (int64_t mm = 0; mm < m; ++mm) {
           double acc = 0.0;
           for (int64_t g = 0; g < groups; ++g) {
@@ -136,20 +136,27 @@ void oracle_w8_linear(const float* x, int64_t m, int64_t k, const uint8_t* w,
             }
             acc += part * (double)scale[r * groups + g];
           }
-          y[mm * n + r] = (float)acc;
+          y[mm * n + r] = mode == 3 ? oracle_bf16_round((float)acc) : (float)acc;
         }
         continue;
       }
       /* layers.rs:277-288: cast(F32) -> add(-128) -> mul(scale) in f32 */
       for (int64_t c = 0; c < k; ++c) {
         float wd = (float)((int32_t)w[r * k + c] - 128) * scale[r * groups + c / group];
-        wrow[c] = (mode == 1) ? oracle_bf16_round(wd) : wd;
+        wrow[c] = (mode == 1 || mode == 4) ? oracle_bf16_round(wd) : wd;
       }
       for (int64_t mm = 0; mm < m; ++mm) {
-        double acc = 0.0;
-        for (int64_t c = 0; c < k; ++c) acc += (double)xr[mm * k + c] * (double)wrow[c];
-        float out = (float)acc;
-        y[mm * n + r] = (mode == 1) ? oracle_bf16_round(out) : out;
+        float out;
+        if (mode == 4) { /* mode 1 with an fp32 running sum (noise-floor probe) */
+          float facc = 0.0f;
+          for (int64_t c = 0; c < k; ++c) facc += xr[mm * k + c] * wrow[c];
+          out = facc;
+        } else {
+          double acc = 0.0;
+          for (int64_t c = 0; c < k; ++c) acc += (double)xr[mm * k + c] * (double)wrow[c];
+          out = (float)acc;
+        }
+        y[mm * n + r] = (mode == 1 || mode == 4) ? oracle_bf16_round(out) : out;
       }
     }
     free(wrow);
@@ -555,6 +562,13 @@ void oracle_decoder_reset(oracle_decoder* dec) {
 
 int32_t oracle_decoder_context(oracle_decoder* dec, int32_t b) { return dec->ctx[b]; }
 
+void oracle_decoder_kv(oracle_decoder* dec, int32_t layer, uint16_t** k, uint16_t** v) {
+  size_t per = (size_t)dec->cfg.max_batch * dec->cfg.kv_heads * dec->cfg.max_context *
+               dec->cfg.head_dim;
+  *k = dec->k_cache + (size_t)layer * per;
+  *v = dec->v_cache + (size_t)layer * per;
+}
+
 static float silu_f32(float g) {
   /* crates/rxla-core/src/ops.rs:336-341: x * sigmoid(x), sigmoid with a
    * nonpositive exponent argument */
@@ -578,7 +592,9 @@ static void dec_w8(oracle_decoder* dec, const char* prefix, const float* x, int6
   snprintf(nm, sizeof(nm), "%s.scale", prefix);
   oracle_param* s = find_param(dec, nm);
   int64_t group = dec->cfg.group_size > 0 ? dec->cfg.group_size : k;
-  oracle_w8_linear(x, m, k, (const uint8_t*)w->data, (const float*)s->data, n, group, 1, y);
+  oracle_w8_linear(x, m, k, (const uint8_t*)w->data, (const float*)s->data, n, group,
+                   dec->cfg.linear_mode == 3 || dec->cfg.linear_mode == 4 ? dec->cfg.linear_mode : 1,
+                   y);
 }
 
 void oracle_decoder_step(oracle_decoder* dec, const int32_t* tokens, int32_t batch,

@@ -46,7 +46,10 @@ void oracle_quantize_w8(const float* w, int64_t n, int64_t k, int64_t group, uin
  * mode 1: compute dtype BF16 (:289-297): x -> bf16, W_deq (f32) -> bf16, dot,
  *         output rounded to bf16 (the dot's dtype), widened to f32.
  * mode 2: the kernel's algebra without roundings of W: Σ_g s_g Σ bf16(x)·(q-128),
- *         f64 throughout, f32 out (used to bound the kernel's accumulation error). */
+ *         f64 throughout, f32 out (used to bound the kernel's accumulation error).
+ * mode 3: mode 2 with the output rounded to bf16.
+ * mode 4: mode 1 with an fp32 running sum in index order (a second valid
+ *         implementation of the reference's arithmetic: the noise floor). */
 void oracle_w8_linear(const float* x, int64_t m, int64_t k, const uint8_t* w,
                       const float* scale, int64_t n, int64_t group, int32_t mode, float* y);
 
@@ -117,6 +120,10 @@ typedef struct oracle_decoder_config {
   int32_t embedding_bf16; /* 1: bf16 embedding + bf16 tied head; 0: W8 */
   int32_t group_size;     /* 0 = per channel */
   int32_t max_batch, max_context;
+  /* QuantizedLinear arithmetic: 1 = the reference's (bf16(W_deq), output bf16),
+   * 3 = exact q with the scale applied to the fp32 dot, output bf16,
+   * 4 = the reference's with an fp32 running sum */
+  int32_t linear_mode;
 } oracle_decoder_config;
 
 typedef struct oracle_decoder oracle_decoder;
@@ -134,6 +141,8 @@ void oracle_decoder_reset(oracle_decoder* dec);
 void oracle_decoder_step(oracle_decoder* dec, const int32_t* tokens, int32_t batch,
                          float* logits, int32_t* next_tokens);
 int32_t oracle_decoder_context(oracle_decoder* dec, int32_t b);
+/* Dense bf16 cache of one layer: [max_batch][kv_heads][max_context][head_dim]. */
+void oracle_decoder_kv(oracle_decoder* dec, int32_t layer, uint16_t** k, uint16_t** v);
 
 /* Number of OpenMP threads the oracle uses (for the CPU baseline report). */
 int32_t oracle_num_threads(void);

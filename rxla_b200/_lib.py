@@ -99,10 +99,15 @@ SIGNATURES = {
     "rxla_b200_decoder_parameter": (_i32, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp),
                                            ctypes.POINTER(_i64), ctypes.POINTER(_i32)]),
     "rxla_b200_decoder_init_synthetic": (_i32, [_vp, _u64]),
+    "rxla_b200_decoder_set_parameter": (_i32, [_vp, ctypes.c_char_p, _vp, _i64]),
+    "rxla_b200_decoder_io": (_i32, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                                    ctypes.POINTER(_vp)]),
     "rxla_b200_decoder_reset": (_i32, [_vp, _vp]),
     "rxla_b200_decoder_step": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
     "rxla_b200_decoder_step_host": (_i32, [_vp, _vp, _i32, _vp, _vp]),
     "rxla_b200_decoder_context_lengths": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "rxla_b200_decoder_kv_cache": (_i32, [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                                          ctypes.POINTER(_i64)]),
     "rxla_b200_comm_unique_id": (_i32, [_vp]),
     "rxla_b200_comm_init": (_i32, [_vp, _i32, _i32, _i32, ctypes.POINTER(_vp)]),
     "rxla_b200_comm_destroy": (_i32, [_vp]),

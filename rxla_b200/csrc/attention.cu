@@ -25,8 +25,9 @@
 //    bf16 hi + lo so q·k keeps fp32 accuracy against the bf16 cache;
 //  * S^T = K·Q^T with tokens on the mma M side (16 per page) and the G query
 //    heads of the kv head on the N side; online softmax per head column;
-//    P^T is moved into the B-fragment layout with movmatrix.trans and
-//    O^T += V^T·P^T (V^T from ldmatrix.trans of the swizzled tile);
+//    P^T (split into bf16 hi + lo, so the weights keep f32 accuracy) is moved
+//    into the B-fragment layout with movmatrix.trans and O^T += V^T·P^T (V^T
+//    from ldmatrix.trans of the swizzled tile);
 //  * the CTA owning the new slot writes k/v to the cache and patches the row
 //    into its loaded tile; every CTA fences and then triggers dependent
 //    launches, so later kernels (including the next step's attention, whose
@@ -392,9 +393,14 @@ __global__ void __launch_bounds__(17 * 32, 1)
         o[mt][2] *= alpha[0];
         o[mt][3] *= alpha[1];
       }
-      // P^T (tokens x heads) -> B fragment of O^T += V^T · P^T
-      const uint32_t b0 = movmatrix_t(pack_bf16x2(pv0[0], pv0[1]));
-      const uint32_t b1 = movmatrix_t(pack_bf16x2(pv1[0], pv1[1]));
+      // P^T (tokens x heads) -> B fragments of O^T += V^T · P^T; P = hi + lo
+      // in bf16 keeps the f32 softmax weights (the reference's F32 attention)
+      const float h00 = bf16_round(pv0[0]), h01 = bf16_round(pv0[1]);
+      const float h10 = bf16_round(pv1[0]), h11 = bf16_round(pv1[1]);
+      const uint32_t b0 = movmatrix_t(pack_bf16x2(h00, h01));
+      const uint32_t b1 = movmatrix_t(pack_bf16x2(h10, h11));
+      const uint32_t c0 = movmatrix_t(pack_bf16x2(pv0[0] - h00, pv0[1] - h01));
+      const uint32_t c1 = movmatrix_t(pack_bf16x2(pv1[0] - h10, pv1[1] - h11));
       const uint32_t vbase = smem_u32(vt);
 #pragma unroll
       for (int mt = 0; mt < D / 16; ++mt) {
@@ -402,6 +408,7 @@ __global__ void __launch_bounds__(17 * 32, 1)
         uint32_t a[4];
         ldsm_x4_t(a, vbase + swz(r0 + rr + ((mi >> 1) << 3), mt * 16 + ((mi & 1) << 3), rows));
         mma_bf16_16816(o[mt], a, b0, b1);
+        mma_bf16_16816(o[mt], a, c0, c1);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -543,9 +550,13 @@ extern "C" int32_t rxla_b200_paged_decode_workspace_size(int32_t batch, int32_t 
   return RXLA_B200_OK;
 }
 
-extern "C" int32_t rxla_b200_paged_decode_attention(const rxla_b200_paged_decode_args* a,
-                                                    void* stream) {
-  using namespace rxla;
+namespace rxla {
+namespace attn {
+// Validate, plan and launch.  `ctx_stable`: no kernel between the last write
+// of ctx_lens and this one may still be running, so pages can be fetched
+// before griddepcontrol.wait (the decoder runner advances ctx_lens only at
+// the end of a step).
+int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx_stable) {
   RXLA_REQUIRE(a && a->struct_size >= sizeof(rxla_b200_paged_decode_args),
                "paged_decode: args struct missing or too small");
   const int D = a->head_dim;
@@ -617,7 +628,7 @@ extern "C" int32_t rxla_b200_paged_decode_attention(const rxla_b200_paged_decode
   p.ws_ml = p.ws_o + part * D;
   p.stage_bytes = 2 * a->kv_heads * attn::kPage * D * 2;
   p.batch = a->batch;
-  p.ctx_stable = 0;  // a standalone call cannot know who wrote ctx_lens last
+  p.ctx_stable = ctx_stable ? 1 : 0;
   p.stages = (int)std::min<int64_t>(attn::kMaxStages, (200 * 1024) / p.stage_bytes);
   if (p.stages < 2) p.stages = 2;
 
@@ -630,7 +641,7 @@ extern "C" int32_t rxla_b200_paged_decode_attention(const rxla_b200_paged_decode
   const size_t smem = 2048 + (size_t)p.stages * p.stage_bytes;
   const dim3 grid(p.max_splits, a->batch);
   const dim3 block((a->kv_heads + 1) * 32);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaStream_t s = s_in;
   cudaError_t e;
   if (D == 128) {
     e = cudaFuncSetAttribute(attn::paged_decode_kernel<128>,
@@ -645,4 +656,12 @@ extern "C" int32_t rxla_b200_paged_decode_attention(const rxla_b200_paged_decode
   }
   if (e != cudaSuccess) return cuda_fail(e, "paged decode attention launch");
   return RXLA_B200_OK;
+}
+}  // namespace attn
+}  // namespace rxla
+
+extern "C" int32_t rxla_b200_paged_decode_attention(const rxla_b200_paged_decode_args* args,
+                                                    void* stream) {
+  // a standalone call cannot know which kernel last wrote ctx_lens
+  return rxla::attn::launch(args, static_cast<cudaStream_t>(stream), false);
 }

@@ -75,8 +75,10 @@ __global__ void rms_norm_bf16_kernel(const float* __restrict__ x, const float* _
 
 // ------------------------------------------------------------------- argmax
 // First index of the maximum (ties -> lowest index), one CTA per row.
+// `advance` (optional): ctx_lens[row] += 1 once the row's token is chosen —
+// the decoder runner's end-of-step position update.
 __global__ void argmax_kernel(const float* __restrict__ logits, int64_t vocab,
-                              int32_t* __restrict__ out) {
+                              int32_t* __restrict__ out, int32_t* __restrict__ advance) {
   pdl_launch_dependents();
   pdl_wait();
   const float* r = logits + blockIdx.x * vocab;
@@ -118,7 +120,10 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int64_t vocab,
         idx = oi;
       }
     }
-    if (threadIdx.x == 0) out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+    if (threadIdx.x == 0) {
+      out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+      if (advance) advance[blockIdx.x] += 1;
+    }
   }
 }
 
@@ -164,7 +169,8 @@ extern "C" int32_t rxla_b200_argmax(const float* logits, int64_t rows, int64_t v
   if (rows == 0) return RXLA_B200_OK;
   RXLA_REQUIRE(logits && out, "argmax: null pointer");
   cudaError_t e = launch_pdl(argmax_kernel, dim3((unsigned)rows), dim3(1024), 0,
-                             static_cast<cudaStream_t>(stream), logits, vocab, out);
+                             static_cast<cudaStream_t>(stream), logits, vocab, out,
+                             (int32_t*)nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
   return RXLA_B200_OK;
 }

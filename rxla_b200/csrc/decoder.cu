@@ -1,0 +1,682 @@
+// decoder.cu — Qwen3-style W8 decoder runner (one decode step per call).
+//
+// Composition (crates/rxla-models/src/qwen3_5/mod.rs:199-273 and layers.rs,
+// restricted to full-attention layers, with the Qwen3 differences: plain
+// q_proj, per-head q_norm / k_norm, full RoPE, tied LM head):
+//
+//   h = embed(token)                                   (W8: (u8-128)*scale, or bf16)
+//   per layer:
+//     x  = bf16(rms_norm(h, input_layernorm))
+//     qkv = W8(x, [q_proj; k_proj; v_proj])             (one fused GEMV)
+//     a  = attention(q_norm/k_norm, RoPE, append, GQA)  (paged bf16 cache)
+//     h += bf16(W8(a, o_proj))
+//     x  = bf16(rms_norm(h, post_attention_layernorm))
+//     g  = silu(bf16(W8(x, gate))) * bf16(W8(x, up))    (one fused GEMV)
+//     h += bf16(W8(g, down_proj))
+//   logits = bf16(rms_norm(h, norm)) · Eᵀ  (f32, unrounded), token = argmax
+//
+// The residual stream is f32; every linear computes in bf16 with fp32
+// accumulation (the layer compute dtype BF16 of crates/rxla-nn/src/layers.rs:
+// 289-297).  A step is 7 kernels per layer + 4, all launched with
+// programmatic dependent launch and captured once per batch size into a CUDA
+// graph; ctx_lens (the next position of each sequence) changes only in the
+// final argmax kernel, so the attention kernels may prefetch cache pages
+// before griddepcontrol.wait.
+//
+// Tensor parallelism (tp_size > 1): each rank holds its q/kv heads, its
+// slices of gate/up rows and the matching columns of o_proj/down_proj; the
+// row-parallel partial sums are all-reduced before the residual add.
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace rxla {
+
+int32_t comm_allreduce_f32(rxla_b200_comm* comm, float* buf, int64_t count, cudaStream_t s);
+
+namespace attn {
+int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable);
+}
+
+namespace dec {
+
+__device__ __forceinline__ uint64_t mix64(uint64_t x) {
+  uint64_t z = x + 0x9e3779b97f4a7c15ull;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+
+// standard normal from a counter (Box-Muller on two 24-bit uniforms)
+__device__ __forceinline__ float normal_at(uint64_t seed, uint64_t i) {
+  const uint64_t r = mix64(seed ^ mix64(i));
+  const float u1 = ((float)(r >> 40) + 1.0f) * (1.0f / 16777217.0f);
+  const float u2 = (float)((r >> 16) & 0xffffff) * (1.0f / 16777216.0f);
+  return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+// Synthetic W8 weights: N(0, 0.02) quantized symmetrically per row with the
+// clip at 4.5σ (scale = 0.02·4.5/127): q = clamp(round(z·127/4.5)).
+__global__ void fill_w8_kernel(uint8_t* w, float* scale, int64_t rows, int64_t k, int64_t groups,
+                               uint64_t seed) {
+  const int64_t n = rows * k;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float q = rintf(normal_at(seed, (uint64_t)i) * (127.0f / 4.5f));
+    q = fminf(127.0f, fmaxf(-127.0f, q));
+    w[i] = (uint8_t)((int)q + 128);
+    if (i < rows * groups) scale[i] = 0.02f * 4.5f / 127.0f;
+  }
+}
+
+__global__ void fill_norm_kernel(float* w, int64_t n, uint64_t seed) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    w[i] = bf16_round(1.0f + 0.02f * normal_at(seed, (uint64_t)i));
+}
+
+__global__ void fill_bf16_kernel(__nv_bfloat16* w, int64_t n, uint64_t seed) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    w[i] = __float2bfloat16_rn(0.02f * normal_at(seed, (uint64_t)i));
+}
+
+// h[b, :] = embedding row of tokens[b] (token ids clamped into [0, vocab),
+// as a gather clamps its indices).
+__global__ void embed_kernel(const int32_t* __restrict__ tokens, const uint8_t* __restrict__ w8,
+                             const float* __restrict__ scale, const __nv_bfloat16* __restrict__ wb,
+                             int64_t vocab, int64_t hidden, int64_t groups, int64_t group,
+                             float* __restrict__ h) {
+  pdl_launch_dependents();
+  pdl_wait();
+  int64_t t = tokens[blockIdx.x];
+  t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+  for (int64_t j = threadIdx.x; j < hidden; j += blockDim.x) {
+    float v;
+    if (w8) v = (float)((int)w8[t * hidden + j] - 128) * scale[t * groups + j / group];
+    else v = __bfloat162float(wb[t * hidden + j]);
+    h[blockIdx.x * hidden + j] = v;
+  }
+}
+
+// h[b, :] += bf16(partial[b, :]) (tensor-parallel residual add after the
+// all-reduce of the row-parallel partial sums).
+__global__ void residual_add_kernel(const float* __restrict__ part, float* __restrict__ h,
+                                    int64_t n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    h[i] = h[i] + bf16_round(part[i]);
+}
+
+struct Param {
+  std::string name;
+  void* ptr;
+  int64_t bytes;
+  int32_t dtype;
+};
+
+struct Layer {
+  float* ln1;
+  float* ln2;
+  uint8_t* wqkv;
+  float* sqkv;
+  float* qn;
+  float* kn;
+  uint8_t* wo;
+  float* so;
+  uint8_t* wgu;
+  float* sgu;
+  uint8_t* wd;
+  float* sd;
+  uint16_t* kc;
+  uint16_t* vc;
+};
+
+}  // namespace dec
+}  // namespace rxla
+
+struct rxla_b200_decoder {
+  rxla_b200_decoder_config cfg;
+  int device = 0;
+  rxla_b200_comm* comm = nullptr;
+  // shard sizes
+  int hq = 0, hkv = 0, inter = 0, vocab = 0, groups_h = 1, groups_i = 1, groups_o = 1;
+  int64_t qkv_rows = 0;
+  int group_h = 0, group_i = 0, group_o = 0;  // group sizes per input width
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<rxla::dec::Param> params;
+  std::vector<rxla::dec::Layer> layers;
+  uint8_t* emb_w8 = nullptr;
+  float* emb_scale = nullptr;
+  uint16_t* emb_bf16 = nullptr;
+  float* final_norm = nullptr;
+  // cache
+  int max_pages = 0;
+  int32_t* page_table = nullptr;
+  int32_t* ctx = nullptr;
+  // activations
+  float* h = nullptr;
+  uint16_t* xn = nullptr;
+  uint16_t* qkv = nullptr;
+  uint16_t* att = nullptr;
+  uint16_t* act = nullptr;
+  float* part = nullptr;
+  float* logits = nullptr;
+  int32_t* tok_in = nullptr;
+  int32_t* tok_out = nullptr;
+  float* inv_freq = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  int32_t* host_pinned = nullptr;
+  std::map<int, cudaGraphExec_t> graphs;
+};
+
+namespace rxla {
+namespace dec {
+
+static int32_t alloc_dev(void** p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "decoder allocation");
+  return RXLA_B200_OK;
+}
+
+// One decode step for `batch` sequences, enqueued on `s` (graph-capturable).
+static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
+  const auto& c = d->cfg;
+  const int64_t H = c.hidden, D = c.head_dim;
+  cudaError_t e = launch_pdl(embed_kernel, dim3(batch), dim3(256), 0, s, (const int32_t*)d->tok_in,
+                             (const uint8_t*)d->emb_w8, (const float*)d->emb_scale,
+                             (const __nv_bfloat16*)d->emb_bf16, (int64_t)c.vocab, H,
+                             (int64_t)d->groups_h, (int64_t)d->group_h, d->h);
+  if (e != cudaSuccess) return cuda_fail(e, "embed launch");
+  const bool tp = c.tp_size > 1;
+  const int64_t qd = (int64_t)d->hq * D, kd = (int64_t)d->hkv * D;
+  for (int l = 0; l < c.layers; ++l) {
+    const Layer& L = d->layers[l];
+    int32_t st = rxla_b200_rms_norm_bf16(d->h, L.ln1, batch, H, c.rms_eps, d->xn, s);
+    if (st) return st;
+    st = rxla_b200_w8a16_linear(d->xn, RXLA_B200_BF16, L.wqkv, L.sqkv, d->group_h, batch,
+                                d->qkv_rows, H, d->qkv, RXLA_B200_BF16, RXLA_B200_EPI_STORE, s);
+    if (st) return st;
+    rxla_b200_paged_decode_args a{};
+    a.struct_size = sizeof(a);
+    a.batch = batch;
+    a.q_heads = d->hq;
+    a.kv_heads = d->hkv;
+    a.head_dim = (int32_t)D;
+    a.q = d->qkv;
+    a.k_new = d->qkv + qd;
+    a.v_new = d->qkv + qd + kd;
+    a.q_row_stride = d->qkv_rows;
+    a.kv_row_stride = d->qkv_rows;
+    a.q_norm_weight = L.qn;
+    a.k_norm_weight = L.kn;
+    a.norm_eps = c.rms_eps;
+    a.inv_freq = d->inv_freq;
+    a.rotary_dim = (int32_t)D;
+    a.scale = 0.0f;
+    a.k_pages = L.kc;
+    a.v_pages = L.vc;
+    a.num_pages = (int64_t)c.max_batch * d->max_pages;
+    a.page_size = 16;
+    a.max_pages_per_seq = d->max_pages;
+    a.page_table = d->page_table;
+    a.pages_per_seq = nullptr;
+    a.ctx_lens = d->ctx;
+    a.kv_update = RXLA_B200_KV_CLAMP;
+    a.advance_ctx = 0;
+    a.accepted = nullptr;
+    a.out = d->att;
+    a.workspace = d->ws;
+    a.workspace_bytes = d->ws_bytes;
+    a.max_context = c.max_context;
+    st = attn::launch(&a, s, true);
+    if (st) return st;
+    if (!tp) {
+      st = rxla_b200_w8a16_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd,
+                                  d->h, RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s);
+      if (st) return st;
+    } else {
+      st = rxla_b200_w8a16_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd,
+                                  d->part, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
+      if (st) return st;
+      st = comm_allreduce_f32(d->comm, d->part, batch * H, s);
+      if (st) return st;
+      e = launch_pdl(residual_add_kernel, dim3(std::max(1, (int)((batch * H + 1023) / 1024))),
+                     dim3(1024), 0, s, (const float*)d->part, d->h, (int64_t)batch * H);
+      if (e != cudaSuccess) return cuda_fail(e, "residual add launch");
+    }
+    st = rxla_b200_rms_norm_bf16(d->h, L.ln2, batch, H, c.rms_eps, d->xn, s);
+    if (st) return st;
+    st = rxla_b200_w8a16_linear(d->xn, RXLA_B200_BF16, L.wgu, L.sgu, d->group_h, batch, d->inter,
+                                H, d->act, RXLA_B200_BF16, RXLA_B200_EPI_SWIGLU, s);
+    if (st) return st;
+    if (!tp) {
+      st = rxla_b200_w8a16_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H,
+                                  d->inter, d->h, RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s);
+      if (st) return st;
+    } else {
+      st = rxla_b200_w8a16_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H,
+                                  d->inter, d->part, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
+      if (st) return st;
+      st = comm_allreduce_f32(d->comm, d->part, batch * H, s);
+      if (st) return st;
+      e = launch_pdl(residual_add_kernel, dim3(std::max(1, (int)((batch * H + 1023) / 1024))),
+                     dim3(1024), 0, s, (const float*)d->part, d->h, (int64_t)batch * H);
+      if (e != cudaSuccess) return cuda_fail(e, "residual add launch");
+    }
+  }
+  int32_t st = rxla_b200_rms_norm_bf16(d->h, d->final_norm, batch, H, c.rms_eps, d->xn, s);
+  if (st) return st;
+  if (d->emb_w8)
+    st = rxla_b200_w8a16_linear(d->xn, RXLA_B200_BF16, d->emb_w8, d->emb_scale, d->group_h,
+                                batch, d->vocab, H, d->logits, RXLA_B200_F32, RXLA_B200_EPI_STORE,
+                                s);
+  else
+    st = rxla_b200_bf16_linear(d->xn, RXLA_B200_BF16, d->emb_bf16, batch, d->vocab, H, d->logits,
+                               RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
+  if (st) return st;
+  if (tp) return fail(RXLA_B200_UNIMPLEMENTED, "tensor-parallel LM head argmax");
+  e = launch_pdl(argmax_kernel, dim3(batch), dim3(1024), 0, s, (const float*)d->logits,
+                 (int64_t)d->vocab, d->tok_out, d->ctx);
+  if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+  return RXLA_B200_OK;
+}
+
+}  // namespace dec
+}  // namespace rxla
+
+using namespace rxla;
+
+extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg, int32_t device,
+                                            rxla_b200_comm* comm, rxla_b200_decoder** out) {
+  RXLA_REQUIRE(cfg && out && cfg->struct_size >= sizeof(rxla_b200_decoder_config),
+               "decoder_create: config struct missing or too small");
+  const auto& c = *cfg;
+  RXLA_REQUIRE(c.layers > 0 && c.hidden > 0 && c.q_heads > 0 && c.kv_heads > 0 &&
+                   c.head_dim > 0 && c.intermediate > 0 && c.vocab > 0,
+               "decoder_create: sizes must be positive");
+  RXLA_REQUIRE(c.q_heads % c.kv_heads == 0, "decoder_create: q_heads % kv_heads != 0");
+  RXLA_REQUIRE(c.rms_eps > 0.0f && std::isfinite(c.rms_eps), "decoder_create: bad rms_eps");
+  RXLA_REQUIRE(c.rope_theta > 0.0f && std::isfinite(c.rope_theta), "decoder_create: bad rope_theta");
+  RXLA_REQUIRE(c.embedding_dtype == RXLA_B200_U8 || c.embedding_dtype == RXLA_B200_BF16,
+               "decoder_create: embedding_dtype must be U8 or BF16");
+  RXLA_REQUIRE(c.max_batch > 0 && c.max_context > 0, "decoder_create: max_batch / max_context");
+  const int tp = c.tp_size <= 0 ? 1 : c.tp_size;
+  RXLA_REQUIRE(c.tp_rank >= 0 && c.tp_rank < tp, "decoder_create: tp_rank out of range");
+  RXLA_REQUIRE(c.kv_heads % tp == 0 && c.intermediate % tp == 0,
+               "decoder_create: kv_heads and intermediate must divide by tp_size");
+  RXLA_REQUIRE(tp == 1 || comm, "decoder_create: tensor parallel needs a comm");
+  RXLA_REQUIRE(tp == 1, "decoder_create: tensor-parallel decoding is not available in this build");
+  const int gsz = c.group_size;
+  auto groups_for = [&](int64_t k) -> int64_t { return gsz > 0 ? k / gsz : 1; };
+  RXLA_REQUIRE(gsz <= 0 || (c.hidden % gsz == 0 && (c.q_heads * c.head_dim / tp) % gsz == 0 &&
+                            (c.intermediate / tp) % gsz == 0),
+               "decoder_create: group_size must divide every input width");
+  RXLA_CUDA_CHECK(cudaSetDevice(device));
+
+  auto* d = new rxla_b200_decoder();
+  d->cfg = c;
+  d->cfg.tp_size = tp;
+  d->device = device;
+  d->comm = comm;
+  d->hq = c.q_heads / tp;
+  d->hkv = c.kv_heads / tp;
+  d->inter = c.intermediate / tp;
+  d->vocab = c.vocab;
+  const int64_t H = c.hidden, D = c.head_dim, I = d->inter;
+  d->qkv_rows = (int64_t)(d->hq + 2 * d->hkv) * D;
+  d->groups_h = (int)groups_for(H);
+  d->groups_o = (int)groups_for((int64_t)d->hq * D);
+  d->groups_i = (int)groups_for(I);
+  d->group_h = gsz > 0 ? gsz : (int)H;
+  d->group_o = gsz > 0 ? gsz : (int)(d->hq * D);
+  d->group_i = gsz > 0 ? gsz : (int)I;
+  d->max_pages = (c.max_context + 15) / 16;
+
+  // ---- parameter arena (256-byte aligned views)
+  struct Spec {
+    std::string name;
+    int64_t bytes;
+    int32_t dtype;
+  };
+  std::vector<Spec> specs;
+  auto add = [&](const std::string& n, int64_t bytes, int32_t dt) { specs.push_back({n, bytes, dt}); };
+  const bool w8emb = c.embedding_dtype == RXLA_B200_U8;
+  if (w8emb) {
+    add("embed_tokens.weight", (int64_t)c.vocab * H, RXLA_B200_U8);
+    add("embed_tokens.scale", (int64_t)c.vocab * d->groups_h * 4, RXLA_B200_F32);
+  } else {
+    add("embed_tokens.weight", (int64_t)c.vocab * H * 2, RXLA_B200_BF16);
+  }
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    add(p + "input_layernorm.weight", H * 4, RXLA_B200_F32);
+    add(p + "self_attn.qkv.weight", d->qkv_rows * H, RXLA_B200_U8);
+    add(p + "self_attn.qkv.scale", d->qkv_rows * d->groups_h * 4, RXLA_B200_F32);
+    add(p + "self_attn.q_norm.weight", D * 4, RXLA_B200_F32);
+    add(p + "self_attn.k_norm.weight", D * 4, RXLA_B200_F32);
+    add(p + "self_attn.o_proj.weight", H * d->hq * D, RXLA_B200_U8);
+    add(p + "self_attn.o_proj.scale", H * d->groups_o * 4, RXLA_B200_F32);
+    add(p + "post_attention_layernorm.weight", H * 4, RXLA_B200_F32);
+    add(p + "mlp.gate_up.weight", 2 * I * H, RXLA_B200_U8);
+    add(p + "mlp.gate_up.scale", 2 * I * d->groups_h * 4, RXLA_B200_F32);
+    add(p + "mlp.down_proj.weight", H * I, RXLA_B200_U8);
+    add(p + "mlp.down_proj.scale", H * d->groups_i * 4, RXLA_B200_F32);
+  }
+  add("norm.weight", H * 4, RXLA_B200_F32);
+  size_t total = 0;
+  for (auto& sp : specs) total += (size_t)((sp.bytes + 255) / 256 * 256);
+  int32_t st = dec::alloc_dev(reinterpret_cast<void**>(&d->arena), total);
+  if (st) {
+    delete d;
+    return st;
+  }
+  d->arena_bytes = total;
+  size_t off = 0;
+  for (auto& sp : specs) {
+    d->params.push_back({sp.name, d->arena + off, sp.bytes, sp.dtype});
+    off += (size_t)((sp.bytes + 255) / 256 * 256);
+  }
+  auto find = [&](const std::string& n) -> void* {
+    for (auto& p : d->params)
+      if (p.name == n) return p.ptr;
+    return nullptr;
+  };
+  if (w8emb) {
+    d->emb_w8 = static_cast<uint8_t*>(find("embed_tokens.weight"));
+    d->emb_scale = static_cast<float*>(find("embed_tokens.scale"));
+  } else {
+    d->emb_bf16 = static_cast<uint16_t*>(find("embed_tokens.weight"));
+  }
+  d->final_norm = static_cast<float*>(find("norm.weight"));
+  // ---- KV cache (per layer), page table, activations
+  const int64_t pages = (int64_t)c.max_batch * d->max_pages;
+  const size_t cache_bytes = (size_t)pages * d->hkv * 16 * D * 2;
+  d->layers.resize(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    dec::Layer& L = d->layers[l];
+    L.ln1 = static_cast<float*>(find(p + "input_layernorm.weight"));
+    L.ln2 = static_cast<float*>(find(p + "post_attention_layernorm.weight"));
+    L.wqkv = static_cast<uint8_t*>(find(p + "self_attn.qkv.weight"));
+    L.sqkv = static_cast<float*>(find(p + "self_attn.qkv.scale"));
+    L.qn = static_cast<float*>(find(p + "self_attn.q_norm.weight"));
+    L.kn = static_cast<float*>(find(p + "self_attn.k_norm.weight"));
+    L.wo = static_cast<uint8_t*>(find(p + "self_attn.o_proj.weight"));
+    L.so = static_cast<float*>(find(p + "self_attn.o_proj.scale"));
+    L.wgu = static_cast<uint8_t*>(find(p + "mlp.gate_up.weight"));
+    L.sgu = static_cast<float*>(find(p + "mlp.gate_up.scale"));
+    L.wd = static_cast<uint8_t*>(find(p + "mlp.down_proj.weight"));
+    L.sd = static_cast<float*>(find(p + "mlp.down_proj.scale"));
+    st = dec::alloc_dev(reinterpret_cast<void**>(&L.kc), cache_bytes);
+    if (!st) st = dec::alloc_dev(reinterpret_cast<void**>(&L.vc), cache_bytes);
+    if (st) {
+      rxla_b200_decoder_destroy(d);
+      return st;
+    }
+  }
+  const int64_t B = c.max_batch;
+  size_t need_ws = 0;
+  rxla_b200_paged_decode_workspace_size(c.max_batch, d->hq, d->hkv, (int32_t)D, c.max_context,
+                                        &need_ws);
+  d->ws_bytes = need_ws;
+  struct A {
+    void** p;
+    size_t bytes;
+  } acts[] = {
+      {(void**)&d->page_table, (size_t)B * d->max_pages * 4},
+      {(void**)&d->ctx, (size_t)B * 4},
+      {(void**)&d->h, (size_t)B * H * 4},
+      {(void**)&d->xn, (size_t)B * H * 2},
+      {(void**)&d->qkv, (size_t)B * d->qkv_rows * 2},
+      {(void**)&d->att, (size_t)B * d->hq * D * 2},
+      {(void**)&d->act, (size_t)B * I * 2},
+      {(void**)&d->part, (size_t)B * H * 4},
+      {(void**)&d->logits, (size_t)B * c.vocab * 4},
+      {(void**)&d->tok_in, (size_t)B * 4},
+      {(void**)&d->tok_out, (size_t)B * 4},
+      {(void**)&d->inv_freq, (size_t)D * 2},
+      {&d->ws, need_ws},
+  };
+  for (auto& a : acts) {
+    st = dec::alloc_dev(a.p, std::max<size_t>(a.bytes, 256));
+    if (st) {
+      rxla_b200_decoder_destroy(d);
+      return st;
+    }
+  }
+  if (cudaMallocHost(reinterpret_cast<void**>(&d->host_pinned), (size_t)B * 8) != cudaSuccess) {
+    rxla_b200_decoder_destroy(d);
+    return fail(RXLA_B200_RESOURCE_EXHAUSTED, "decoder_create: pinned staging");
+  }
+  // page table: sequence b owns pages [b * max_pages, (b+1) * max_pages)
+  std::vector<int32_t> pt((size_t)B * d->max_pages);
+  for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int32_t)i;
+  // RoPE frequencies on the host in f32, as qwen3_5/mod.rs:213-222 computes them
+  std::vector<float> inv((size_t)D / 2);
+  for (int64_t i = 0; i < D / 2; ++i)
+    inv[(size_t)i] = std::pow(c.rope_theta, (-2.0f * (float)i) / (float)D);
+  if (cudaMemcpy(d->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(d->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(d->ctx, 0, (size_t)B * 4) != cudaSuccess ||
+      cudaMemset(d->ws, 0, need_ws) != cudaSuccess ||
+      cudaMemset(d->arena, 0, d->arena_bytes) != cudaSuccess) {
+    rxla_b200_decoder_destroy(d);
+    return fail(RXLA_B200_UNAVAILABLE, "decoder_create: initial copies failed");
+  }
+  for (auto& L : d->layers) {
+    cudaMemset(L.kc, 0, cache_bytes);
+    cudaMemset(L.vc, 0, cache_bytes);
+  }
+  RXLA_CUDA_CHECK(cudaDeviceSynchronize());
+  *out = d;
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_decoder_destroy(rxla_b200_decoder* d) {
+  if (!d) return RXLA_B200_OK;
+  cudaSetDevice(d->device);
+  for (auto& g : d->graphs) cudaGraphExecDestroy(g.second);
+  for (auto& L : d->layers) {
+    cudaFree(L.kc);
+    cudaFree(L.vc);
+  }
+  void* ptrs[] = {d->arena, d->page_table, d->ctx, d->h, d->xn, d->qkv, d->att, d->act,
+                  d->part, d->logits, d->tok_in, d->tok_out, d->inv_freq, d->ws};
+  for (void* p : ptrs) cudaFree(p);
+  if (d->host_pinned) cudaFreeHost(d->host_pinned);
+  delete d;
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_decoder_parameter(rxla_b200_decoder* d, const char* name,
+                                               void** ptr, int64_t* bytes, int32_t* dtype) {
+  RXLA_REQUIRE(d && name && ptr, "decoder_parameter: null argument");
+  const std::string n(name);
+  const auto& c = d->cfg;
+  const int64_t H = c.hidden, D = c.head_dim;
+  // q_proj / k_proj / v_proj are row ranges of the fused qkv weight, gate/up of gate_up
+  auto sub = [&](const std::string& fused, int64_t row0, int64_t rows, int64_t row_bytes) -> int32_t {
+    for (auto& p : d->params)
+      if (p.name == fused) {
+        *ptr = static_cast<uint8_t*>(p.ptr) + row0 * row_bytes;
+        if (bytes) *bytes = rows * row_bytes;
+        if (dtype) *dtype = p.dtype;
+        return RXLA_B200_OK;
+      }
+    return fail(RXLA_B200_NOT_FOUND, "decoder_parameter: no parameter " + n);
+  };
+  for (auto& p : d->params)
+    if (p.name == n) {
+      *ptr = p.ptr;
+      if (bytes) *bytes = p.bytes;
+      if (dtype) *dtype = p.dtype;
+      return RXLA_B200_OK;
+    }
+  const auto dot = n.rfind('.');
+  const auto proj = n.rfind('.', dot - 1);
+  if (dot != std::string::npos && proj != std::string::npos) {
+    const std::string prefix = n.substr(0, proj), which = n.substr(proj + 1, dot - proj - 1),
+                      kind = n.substr(dot + 1);
+    const bool is_w = kind == "weight", is_s = kind == "scale";
+    if (is_w || is_s) {
+      const int64_t rb_w = H, rb_s = (int64_t)d->groups_h * 4;
+      const int64_t rb = is_w ? rb_w : rb_s;
+      const int64_t qd = (int64_t)d->hq * D, kd = (int64_t)d->hkv * D;
+      if (which == "q_proj") return sub(prefix + ".qkv." + kind, 0, qd, rb);
+      if (which == "k_proj") return sub(prefix + ".qkv." + kind, qd, kd, rb);
+      if (which == "v_proj") return sub(prefix + ".qkv." + kind, qd + kd, kd, rb);
+      if (which == "gate_proj") return sub(prefix + ".gate_up." + kind, 0, d->inter, rb);
+      if (which == "up_proj") return sub(prefix + ".gate_up." + kind, d->inter, d->inter, rb);
+    }
+  }
+  return fail(RXLA_B200_NOT_FOUND, "decoder_parameter: no parameter " + n);
+}
+
+extern "C" int32_t rxla_b200_decoder_set_parameter(rxla_b200_decoder* d, const char* name,
+                                                   const void* host, int64_t bytes) {
+  RXLA_REQUIRE(d && name && host, "decoder_set_parameter: null argument");
+  void* ptr = nullptr;
+  int64_t have = 0;
+  int32_t dt = 0;
+  int32_t st = rxla_b200_decoder_parameter(d, name, &ptr, &have, &dt);
+  if (st) return st;
+  RXLA_REQUIRE(have == bytes, std::string("decoder_set_parameter: ") + name + " holds " +
+                                  std::to_string(have) + " bytes, got " + std::to_string(bytes));
+  RXLA_CUDA_CHECK(cudaSetDevice(d->device));
+  RXLA_CUDA_CHECK(cudaMemcpy(ptr, host, (size_t)bytes, cudaMemcpyHostToDevice));
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_decoder_init_synthetic(rxla_b200_decoder* d, uint64_t seed) {
+  RXLA_REQUIRE(d, "decoder_init_synthetic: null decoder");
+  RXLA_CUDA_CHECK(cudaSetDevice(d->device));
+  const int grid = sm_count(d->device) * 8;
+  uint64_t idx = 0;
+  for (size_t i = 0; i < d->params.size(); ++i, ++idx) {
+    auto& p = d->params[i];
+    const uint64_t s = seed * 1000003ull + idx;
+    if (p.dtype == RXLA_B200_U8) {
+      // the scale is the next parameter; rows = scale elements / groups
+      auto& sc = d->params[i + 1];
+      const int64_t k = (p.name.find("down_proj") != std::string::npos)
+                            ? d->inter
+                            : (p.name.find("o_proj") != std::string::npos ? (int64_t)d->hq * d->cfg.head_dim
+                                                                           : d->cfg.hidden);
+      const int64_t rows = p.bytes / k;
+      const int64_t groups = sc.bytes / 4 / rows;
+      dec::fill_w8_kernel<<<grid, 256>>>(static_cast<uint8_t*>(p.ptr), static_cast<float*>(sc.ptr),
+                                         rows, k, groups, s);
+    } else if (p.dtype == RXLA_B200_BF16) {
+      dec::fill_bf16_kernel<<<grid, 256>>>(static_cast<__nv_bfloat16*>(p.ptr), p.bytes / 2, s);
+    } else if (p.name.find(".scale") == std::string::npos) {
+      dec::fill_norm_kernel<<<grid, 256>>>(static_cast<float*>(p.ptr), p.bytes / 4, s);
+    }
+  }
+  RXLA_CUDA_CHECK(cudaGetLastError());
+  RXLA_CUDA_CHECK(cudaDeviceSynchronize());
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_decoder_reset(rxla_b200_decoder* d, void* stream) {
+  RXLA_REQUIRE(d, "decoder_reset: null decoder");
+  RXLA_CUDA_CHECK(cudaMemsetAsync(d->ctx, 0, (size_t)d->cfg.max_batch * 4,
+                                  static_cast<cudaStream_t>(stream)));
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_decoder_kv_cache(rxla_b200_decoder* d, int32_t layer, void** k,
+                                              void** v, int64_t* bytes) {
+  RXLA_REQUIRE(d && layer >= 0 && layer < d->cfg.layers, "decoder_kv_cache: bad layer");
+  if (k) *k = d->layers[layer].kc;
+  if (v) *v = d->layers[layer].vc;
+  if (bytes)
+    *bytes = (int64_t)d->cfg.max_batch * d->max_pages * d->hkv * 16 * d->cfg.head_dim * 2;
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_decoder_context_lengths(rxla_b200_decoder* d, const int32_t** lens) {
+  RXLA_REQUIRE(d && lens, "decoder_context_lengths: null argument");
+  *lens = d->ctx;
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_decoder_step(rxla_b200_decoder* d, const int32_t* tokens,
+                                          int32_t batch, int32_t* next_tokens, float* logits,
+                                          void* stream) {
+  RXLA_REQUIRE(d && tokens && next_tokens, "decoder_step: null argument");
+  RXLA_REQUIRE(batch > 0 && batch <= d->cfg.max_batch, "decoder_step: batch out of range");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  RXLA_CUDA_CHECK(cudaSetDevice(d->device));
+  if (tokens != d->tok_in)
+    RXLA_CUDA_CHECK(cudaMemcpyAsync(d->tok_in, tokens, (size_t)batch * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+  auto it = d->graphs.find(batch);
+  if (it == d->graphs.end()) {
+    // first use of this batch size: one eager step (sets kernel attributes and
+    // resolves driver entry points outside capture) would advance the state,
+    // so capture directly on a private stream and launch the graph.
+    cudaStream_t cs;
+    RXLA_CUDA_CHECK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+    int32_t st = e == cudaSuccess ? dec::enqueue_step(d, batch, cs) : cuda_fail(e, "begin capture");
+    cudaError_t e2 = cudaStreamEndCapture(cs, &graph);
+    cudaStreamDestroy(cs);
+    if (st) {
+      if (graph) cudaGraphDestroy(graph);
+      return st;
+    }
+    if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
+    it = d->graphs.emplace(batch, exec).first;
+  }
+  RXLA_CUDA_CHECK(cudaGraphLaunch(it->second, s));
+  if (next_tokens != d->tok_out)
+    RXLA_CUDA_CHECK(cudaMemcpyAsync(next_tokens, d->tok_out, (size_t)batch * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+  if (logits)
+    RXLA_CUDA_CHECK(cudaMemcpyAsync(logits, d->logits, (size_t)batch * d->vocab * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_decoder_step_host(rxla_b200_decoder* d, const int32_t* tokens_host,
+                                               int32_t batch, int32_t* next_tokens_host,
+                                               void* stream) {
+  RXLA_REQUIRE(d && tokens_host && next_tokens_host, "decoder_step_host: null argument");
+  RXLA_REQUIRE(batch > 0 && batch <= d->cfg.max_batch, "decoder_step_host: batch out of range");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::memcpy(d->host_pinned, tokens_host, (size_t)batch * 4);
+  RXLA_CUDA_CHECK(cudaMemcpyAsync(d->tok_in, d->host_pinned, (size_t)batch * 4,
+                                  cudaMemcpyHostToDevice, s));
+  int32_t st = rxla_b200_decoder_step(d, d->tok_in, batch, d->tok_out, nullptr, stream);
+  if (st) return st;
+  RXLA_CUDA_CHECK(cudaMemcpyAsync(d->host_pinned + d->cfg.max_batch, d->tok_out, (size_t)batch * 4,
+                                  cudaMemcpyDeviceToHost, s));
+  RXLA_CUDA_CHECK(cudaStreamSynchronize(s));
+  std::memcpy(next_tokens_host, d->host_pinned + d->cfg.max_batch, (size_t)batch * 4);
+  return RXLA_B200_OK;
+}
+
+// Device buffers of the step's inputs and outputs (write tokens_in directly to
+// skip the copy in rxla_b200_decoder_step).
+extern "C" int32_t rxla_b200_decoder_io(rxla_b200_decoder* d, int32_t** tokens_in,
+                                        int32_t** tokens_out, float** logits) {
+  RXLA_REQUIRE(d, "decoder_io: null decoder");
+  if (tokens_in) *tokens_in = d->tok_in;
+  if (tokens_out) *tokens_out = d->tok_out;
+  if (logits) *logits = d->logits;
+  return RXLA_B200_OK;
+}

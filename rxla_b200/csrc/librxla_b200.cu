@@ -6,3 +6,5 @@
 #include "w8_linear.cu"
 #include "dense_linear.cu"
 #include "attention.cu"
+#include "decoder.cu"
+#include "comm.cu"

@@ -1,10 +1,10 @@
 // w8_linear.cu — W8A16 linear for decode shapes (M <= 32 tokens per pass).
 //
 // Replaces QuantizedLinear::apply (crates/rxla-nn/src/layers.rs:257-298) with
-// BF16 layer compute: y = bf16(x) · ((W - 128) ⊙ scale)ᵀ, fp32 accumulate,
-// the dot rounded to bf16.  The scale is factored out of the dot
-// (Σ_g s_g Σ_k q·x), which is exact in the q and differs from the reference's
-// bf16(W_deq) only by that rounding of W_deq (bounded in the tests).
+// BF16 layer compute, at the reference's rounding points: every weight is
+// dequantized in f32 (q = u8 - 128, exact; q·s rounded once to f32), rounded
+// to bf16 (the cast of W_deq, :293-296), multiplied with bf16(x) exactly and
+// accumulated in fp32; the dot is rounded to bf16.
 //
 // Design (HBM-bound: one byte of weight per multiply-add at M = 1):
 //  * persistent grid, one CTA per SM; CTA c owns output rows
@@ -21,16 +21,15 @@
 //    are in flight while the previous kernel finishes; x (the previous
 //    kernel's output) is then copied once into shared memory;
 //  * 16 consumer warps split each stage into 64-column boxes of 16 rows and
-//    feed mma.sync m16n8k16 (fp16 in, fp32 accumulate) with weight rows on
+//    feed mma.sync m16n8k16 (bf16 in, fp32 accumulate) with weight rows on
 //    the M side and tokens on the N side, so there is no cross-lane reduction
-//    over K.  u8 -> fp16 is exact and costs one PRMT + one HSUB2 per two
-//    weights (0x64bb is 1024 + b; minus 1152 leaves q).  x is converted once
-//    per CTA to fp16 scaled by a per-token power of two 2^-e (max |x| lands in
-//    [2^14, 2^15)): exact for every bf16 value within 2^29 of the token's
-//    maximum; the epilogue multiplies by 2^e.  For SwiGLU, rows 0-7 of the A
-//    tile are gate rows and rows 8-15 the matching up rows.  The K columns are
-//    permuted consistently for A and B: a lane reads 16 contiguous weight
-//    bytes and the 16 matching x values, which covers four k-steps;
+//    over K.  Dequantization runs in registers with packed f32x2 arithmetic:
+//    PRMT makes 2^23 + b, add.f32x2 subtracts 2^23 + 128 (exact q),
+//    mul.f32x2 applies the row's scale (the reference's f32 product) and
+//    cvt.rn.bf16x2 rounds to bf16.  For SwiGLU, rows 0-7 of the A tile are
+//    gate rows and rows 8-15 the matching up rows.  The K columns are permuted
+//    consistently for A and B: a lane reads 16 contiguous weight bytes and the
+//    16 matching x values, which covers four k-steps;
 //  * an epilogue warp sums the 16 warps' partial tiles in a fixed order
 //    (deterministic), scales, rounds to bf16 and stores / adds to the f32
 //    residual / gates with SiLU, double-buffered so the consumers never wait
@@ -69,9 +68,7 @@ struct Params {
   int32_t kc;           // K columns per stage (multiple of 64)
   int32_t k_chunks;     // ceil(k / kc)
   int32_t stages;       // ring depth
-  int32_t x_pitch;      // bytes of one resident token row of raw x
-  int32_t h_pitch;      // bytes of one fp16 token row (== x_pitch for bf16 x)
-  int32_t x16_offset;   // byte offset of the fp16 rows (0: converted in place)
+  int32_t x_pitch;      // bytes of one resident token row of x
   int32_t stage_bytes;  // 16 rows × kc
 };
 
@@ -82,28 +79,32 @@ struct Bars {
   uint64_t grp[2];
   uint64_t epi_full[2];
   uint64_t epi_free[2];
-  float tok_scale[kMaxTokens];    // 2^e per token (epilogue)
-  float tok_max[kConsumerWarps][kMaxTokens];
 };
 static_assert(sizeof(Bars) <= kHeader, "header");
 
-__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                              uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
 }
 
-// Four u8 weights (value b, q = b - 128) -> two f16x2 registers of exact q:
-// lo = (q0, q1), hi = (q2, q3).  0x64bb is the fp16 1024 + b.
-__device__ __forceinline__ void u8x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t bias = 0x64806480u;  // (1152, 1152)
-  uint32_t a = __byte_perm(w, 0x64646464u, 0x4140u);
-  uint32_t b = __byte_perm(w, 0x64646464u, 0x4342u);
-  asm("sub.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(bias));
-  asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(bias));
+// Four u8 weights of one row (value b, q = b - 128) with the row's scale pair
+// (s, s) -> two bf16x2 registers of bf16(f32(q)·s): lo = (w0, w1), hi = (w2, w3).
+__device__ __forceinline__ void deq4(uint32_t w, uint64_t s2, uint32_t& lo, uint32_t& hi) {
+  const uint64_t bias = 0xCB000080CB000080ull;  // (-(2^23 + 128), -(2^23 + 128))
+  uint64_t a = f32x2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u)),
+                     __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541u)));
+  uint64_t c = f32x2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7542u)),
+                     __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7543u)));
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(a) : "l"(bias));
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(c) : "l"(bias));
+  asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(a) : "l"(s2));
+  asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(c) : "l"(s2));
+  float a0, a1, c0, c1;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(c0), "=f"(c1) : "l"(c));
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(a1), "f"(a0));
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(c1), "f"(c0));
 }
 
 // Bounded barrier among the 16 consumer warps (one arrival per warp).
@@ -118,8 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
   Bars& bars = *reinterpret_cast<Bars*>(smem_raw);
   float* red = reinterpret_cast<float*>(smem_raw + kHeader);  // [2][warp][16 rows][8 tokens]
   uint8_t* xs = smem_raw + kHeader + 2 * kRedFloats * 4;
-  uint8_t* xh = xs + p.x16_offset;
-  uint8_t* stages = xs + p.x16_offset + (size_t)p.m * p.h_pitch;
+  uint8_t* stages = xs + (size_t)p.m * p.x_pitch;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -221,14 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
           v += rb[(w2 * kTileRows + row) * kMaxTokens + tok];
           if (swiglu) u += rb[(w2 * kTileRows + row + 8) * kMaxTokens + tok];
         }
-        const float ts = bars.tok_scale[tok];
-        v *= ts;
-        u *= ts;
         const int out_col = r0 + row;
-        if (per_channel) {
-          v *= __ldg(p.scale + out_col);
-          if (swiglu) u *= __ldg(p.scale + p.n + out_col);
-        }
         const int64_t o = (int64_t)tok * p.ldy + out_col;
         if (swiglu) {
           const float r = silu(bf16_round(v)) * bf16_round(u);
@@ -251,56 +244,34 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
 
   // -------------------------------------------------------------- consumers
   if (!mbar_wait(&bars.x_full, 0)) return;
-  const int ctid = threadIdx.x;  // 0 .. 511
-  {
-    // x -> fp16 scaled by 2^-e per token (exact); e from max |x|
-    float mx[kMaxTokens];
-#pragma unroll
-    for (int t = 0; t < kMaxTokens; ++t) mx[t] = 0.0f;
-    for (int t = 0; t < p.m; ++t) {
-      const uint8_t* row = xs + t * p.x_pitch;
-      float v = 0.0f;
-      for (int c = ctid; c < p.k; c += kConsumerWarps * 32) {
-        const float a = p.x_f32 ? reinterpret_cast<const float*>(row)[c]
-                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(row)[c]);
-        v = fmaxf(v, fabsf(bf16_round(a)));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-      mx[t] = v;
-    }
-    if (lane == 0)
-      for (int t = 0; t < kMaxTokens; ++t) bars.tok_max[warp][t] = mx[t];
-    if (!consumer_sync(&bars.grp[0], 0)) return;
-    float inv[kMaxTokens];
-    for (int t = 0; t < p.m; ++t) {
-      float v = 0.0f;
-      for (int w2 = 0; w2 < kConsumerWarps; ++w2) v = fmaxf(v, bars.tok_max[w2][t]);
-      // e with max * 2^-e in [2^14, 2^15); zero / non-finite rows keep e = 0
-      int e = 0;
-      if (v > 0.0f && v < INFINITY) e = ((__float_as_int(v) >> 23) & 0xff) - 127 - 14;
-      e = max(-100, min(100, e));
-      inv[t] = __int_as_float((127 - e) << 23);  // 2^-e (|e| < 127 for finite bf16)
-      if (ctid == 0) bars.tok_scale[t] = __int_as_float((127 + e) << 23);
-    }
-    for (int t = 0; t < p.m; ++t) {
-      const uint8_t* row = xs + t * p.x_pitch;
-      __half* out = reinterpret_cast<__half*>(xh + t * p.h_pitch);
-      for (int c = ctid; c < p.k; c += kConsumerWarps * 32) {
-        const float a = p.x_f32 ? reinterpret_cast<const float*>(row)[c]
-                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(row)[c]);
-        out[c] = __float2half_rn(bf16_round(a) * inv[t]);
-      }
-    }
-    if (!consumer_sync(&bars.grp[1], 0)) return;
-  }
   const bool has_tok = g < p.m;
-  const uint8_t* xrow = xh + g * p.h_pitch;
+  const uint8_t* xrow = xs + g * p.x_pitch;
 
   int it = 0;
   for (int blk = 0; blk < n_blocks; ++blk) {
     const int r0 = r_begin + blk * out_rows;
     const int nr = min(out_rows, r_end - r0);
+    // weight rows of this lane's A fragment: tile rows g and g + 8
+    int ra, rb;
+    bool va, vb;
+    if (swiglu) {
+      va = vb = g < nr;
+      ra = r0 + g;
+      rb = p.n + r0 + g;
+    } else {
+      va = g < nr;
+      vb = g + 8 < nr;
+      ra = r0 + g;
+      rb = r0 + g + 8;
+    }
+    const float* sa = p.scale + (int64_t)ra * p.groups;
+    const float* sb = p.scale + (int64_t)rb * p.groups;
+    uint64_t s2a = 0, s2b = 0;
+    if (per_channel) {
+      const float x0 = va ? __ldg(sa) : 0.0f, x1 = vb ? __ldg(sb) : 0.0f;
+      s2a = f32x2(x0, x0);
+      s2b = f32x2(x1, x1);
+    }
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int kc = 0; kc < p.k_chunks; ++kc, ++it) {
       const int s = it % S;
@@ -308,15 +279,31 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       const int nbox = min(p.kc, p.k - col0) >> 6;
       if (!mbar_wait(&bars.full[s], (it / S) & 1)) return;
       const uint8_t* stage = stages + (size_t)s * p.stage_bytes;
+#pragma unroll 2
       for (int box = warp; box < nbox; box += kConsumerWarps) {
         const int lcol = box * 64 + 16 * q;  // stage-local column of this lane's 16 bytes
         const int gcol = col0 + lcol;        // global K column
+        if (!per_channel) {
+          const int grp = gcol / p.group_size;
+          const float x0 = va ? __ldg(sa + grp) : 0.0f, x1 = vb ? __ldg(sb + grp) : 0.0f;
+          s2a = f32x2(x0, x0);
+          s2b = f32x2(x1, x1);
+        }
         uint32_t bx[8];
         if (has_tok) {
-          const uint4 v0 = *reinterpret_cast<const uint4*>(xrow + gcol * 2);
-          const uint4 v1 = *reinterpret_cast<const uint4*>(xrow + gcol * 2 + 16);
-          bx[0] = v0.x; bx[1] = v0.y; bx[2] = v0.z; bx[3] = v0.w;
-          bx[4] = v1.x; bx[5] = v1.y; bx[6] = v1.z; bx[7] = v1.w;
+          if (p.x_f32) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 v = *reinterpret_cast<const float4*>(xrow + (gcol + 4 * j) * 4);
+              bx[2 * j] = pack_bf16x2(v.x, v.y);
+              bx[2 * j + 1] = pack_bf16x2(v.z, v.w);
+            }
+          } else {
+            const uint4 v0 = *reinterpret_cast<const uint4*>(xrow + gcol * 2);
+            const uint4 v1 = *reinterpret_cast<const uint4*>(xrow + gcol * 2 + 16);
+            bx[0] = v0.x; bx[1] = v0.y; bx[2] = v0.z; bx[3] = v0.w;
+            bx[4] = v1.x; bx[5] = v1.y; bx[6] = v1.z; bx[7] = v1.w;
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 8; ++j) bx[j] = 0u;
@@ -325,35 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
         const uint4 hi = *reinterpret_cast<const uint4*>(stage + (g + 8) * p.kc + lcol);
         const uint32_t wl[4] = {lo.x, lo.y, lo.z, lo.w};
         const uint32_t wh[4] = {hi.x, hi.y, hi.z, hi.w};
-        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int st = 0; st < 4; ++st) {
           uint32_t a[4];
-          u8x4_to_f16x2(wl[st], a[0], a[2]);  // row g: k-low pair, k-high pair
-          u8x4_to_f16x2(wh[st], a[1], a[3]);  // row g+8
-          mma_f16_16816(per_channel ? acc : part, a, bx[2 * st], bx[2 * st + 1]);
-        }
-        if (!per_channel) {
-          // grouped scales: each 64-column box lies inside one group
-          const int grp = gcol / p.group_size;
-          int ra, rb;
-          bool va, vb;
-          if (swiglu) {
-            va = vb = g < nr;
-            ra = r0 + g;
-            rb = p.n + r0 + g;
-          } else {
-            va = g < nr;
-            vb = g + 8 < nr;
-            ra = r0 + g;
-            rb = r0 + g + 8;
-          }
-          const float s0 = va ? __ldg(p.scale + (int64_t)ra * p.groups + grp) : 0.0f;
-          const float s1 = vb ? __ldg(p.scale + (int64_t)rb * p.groups + grp) : 0.0f;
-          acc[0] += s0 * part[0];
-          acc[1] += s0 * part[1];
-          acc[2] += s1 * part[2];
-          acc[3] += s1 * part[3];
+          deq4(wl[st], s2a, a[0], a[2]);  // row g: k-low pair, k-high pair
+          deq4(wh[st], s2b, a[1], a[3]);  // row g+8
+          mma_bf16_16816(acc, a, bx[2 * st], bx[2 * st + 1]);
         }
       }
       __syncwarp();
@@ -394,15 +358,16 @@ __global__ void w8_generic_kernel(const Params p) {
       float tot = 0.0f;
       for (int gi = 0; gi < p.groups; ++gi) {
         float part = 0.0f;
+        const float sc = __ldg(p.scale + (int64_t)row * p.groups + gi);
         for (int c = gi * p.group_size + lane; c < (gi + 1) * p.group_size; c += 32) {
           float xv = p.x_f32 ? static_cast<const float*>(p.x)[(int64_t)tok * p.ldx + c]
                              : __bfloat162float(static_cast<const __nv_bfloat16*>(p.x)[(int64_t)tok * p.ldx + c]);
           xv = bf16_round(xv);
-          part += xv * (float)((int)wr[c] - 128);
+          part += xv * bf16_round(__fmul_rn((float)((int)wr[c] - 128), sc));
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        tot += part * __ldg(p.scale + (int64_t)row * p.groups + gi);
+        tot += part;
       }
       res[half] = tot;
     }
@@ -436,10 +401,7 @@ static int32_t plan_skinny(Params& p, size_t& smem) {
   p.k_chunks = (p.k + kc - 1) / kc;
   p.stage_bytes = kTileRows * kc;
   p.x_pitch = p.k * xe + 16;
-  p.h_pitch = p.k * 2 + 16;
-  p.x16_offset = p.x_f32 ? p.m * p.x_pitch : 0;
-  const size_t fixed =
-      kHeader + 2 * kRedFloats * 4 + (size_t)p.x16_offset + (size_t)p.m * p.h_pitch;
+  const size_t fixed = kHeader + 2 * kRedFloats * 4 + (size_t)p.m * p.x_pitch;
   const size_t budget = 227 * 1024;
   if (fixed + 2 * (size_t)p.stage_bytes > budget) return -1;
   p.stages = (int)std::min<size_t>(kMaxStages, (budget - fixed) / p.stage_bytes);

@@ -3,8 +3,9 @@
 Inputs are seeded bf16 values; the reference is the CPU oracle's restatement
 of the same contract (q/k RMSNorm, SplitHalf RoPE at position ctx_len, KV
 append with clamp / checked semantics, f64 softmax over the bf16 cache).
-Tolerance: the kernel rounds the softmax weights to bf16 for P·V and the
-output to bf16, so |Δ| <= 2^-8·|ref| + 2^-8·Σ_t p_t|v_t| (+1e-6).
+Tolerance: the kernel keeps q and the softmax weights at f32 accuracy
+(bf16 hi + lo splits) and rounds the output to bf16, so the difference is one
+bf16 ulp of the output plus f32-level error: |Δ| <= 2^-7·|ref| + 2^-14·max|v|.
 """
 import numpy as np
 import pytest
@@ -95,7 +96,7 @@ def _abs_weighted_v(c, kp_after, vp_after):
 
 
 def _check_close(got, ref, bound):
-    tol = 2.0 ** -8 * np.abs(ref) + 2.0 ** -8 * bound + 1e-6
+    tol = 2.0 ** -7 * np.abs(ref) + 2.0 ** -14 * bound + 1e-6
     excess = np.abs(got - ref) - tol
     assert excess.max() <= 0, f"excess {excess.max()} at {np.unravel_index(excess.argmax(), excess.shape)}"
 

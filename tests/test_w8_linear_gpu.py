@@ -1,11 +1,10 @@
 """W8A16 linear parity on the GPU, through the C ABI (rxla_b200_w8a16_linear).
 
-Checked against the CPU oracle on the same seeded inputs:
-  * exact algebra (oracle mode 2, f64, scale factored): the kernel's fp32
-    accumulation of exact bf16(x)·q products then one bf16 rounding —
-    |Δ| <= 2^-8·|ref| + 2^-20·Σ|x·q·s|;
-  * the reference's own rounding points (mode 1: bf16(W_deq)) —
-    |Δ| <= 2^-8·|ref| + 2^-8·Σ|x·q·s|, the bound of W_deq's bf16 rounding.
+Checked against the CPU oracle on the same seeded inputs, at the reference's
+own rounding points (oracle mode 1: bf16(x) · bf16(f32(q)·s), f64 sum, bf16
+output).  The kernel forms the same exact products and sums them in fp32, so
+the only difference is the fp32 accumulation: at most one bf16 ulp of the
+output plus that error — |Δ| <= 2^-7·|ref| + 2^-20·Σ|x·q·s|.
 """
 import numpy as np
 import pytest
@@ -42,14 +41,19 @@ def _run(x, w, s, group, x_dtype=torch.bfloat16, out_dtype=torch.bfloat16, dev="
 
 
 def _check(y, x, w, s, group, bf16_out=True):
-    exact = oracle.w8_linear(x, w, s, group, mode=2).astype(np.float64)
-    ref = oracle.w8_linear(x, w, s, group, mode=1).astype(np.float64)
+    ref = oracle.w8_linear(x, w, s, group, mode=1 if bf16_out else 0).astype(np.float64)
+    if not bf16_out:  # unrounded fp32 output: the f64 dot of the same bf16 operands
+        xb = oracle.bf16_round(x).astype(np.float64)
+        groups = s.shape[1]
+        sg = np.repeat(s, w.shape[1] // groups, axis=1)
+        wd = oracle.bf16_round(((w.astype(np.float32) - 128.0) * sg).astype(np.float32))
+        ref = xb @ wd.astype(np.float64).T
     bound = _bound(x, w, s, group)
-    rel = 2.0 ** -8 if bf16_out else 2.0 ** -20
-    err_exact = np.abs(y - exact) - (rel * np.abs(exact) + 2.0 ** -20 * bound)
-    assert err_exact.max() <= 0, f"exact-algebra excess {err_exact.max()}"
-    err_ref = np.abs(y - ref) - (2.0 ** -8 * np.abs(ref) + 2.0 ** -8 * bound)
-    assert err_ref.max() <= 0, f"reference excess {err_ref.max()}"
+    rel = 2.0 ** -7 if bf16_out else 2.0 ** -22
+    excess = np.abs(y - ref) - (rel * np.abs(ref) + 2.0 ** -20 * bound)
+    assert excess.max() <= 0, f"reference-rounding excess {excess.max()}"
+    if bf16_out:  # most outputs are bit-identical to the reference
+        assert np.mean(y == ref) > 0.97, f"only {np.mean(y == ref):.3f} identical"
 
 
 @pytest.mark.parametrize("m", [1, 2, 7, 8, 9, 16, 17, 32, 33, 70])
@@ -103,17 +107,17 @@ def test_swiglu_epilogue(cuda, m, n, k, group):
     xt = torch.from_numpy(x).cuda().bfloat16()
     y = nn.quantized_linear(xt, torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda(), group,
                             epilogue=_lib.EPI_SWIGLU).float().cpu().numpy()
-    exact = oracle.w8_linear(x, w, s, group, mode=2).astype(np.float64)
+    ref = oracle.w8_linear(x, w, s, group, mode=1).astype(np.float64)
     bound = _bound(x, w, s, group)
-    g_ex, u_ex = exact[:, :n], exact[:, n:]
-    # each of gate / up: one bf16 rounding + fp32 accumulation error
-    dg = 2.0 ** -8 * np.abs(g_ex) + 2.0 ** -20 * bound[:, :n]
-    du = 2.0 ** -8 * np.abs(u_ex) + 2.0 ** -20 * bound[:, n:]
+    g_ex, u_ex = ref[:, :n], ref[:, n:]
+    # each of gate / up: at most one bf16 ulp + fp32 accumulation error
+    dg = 2.0 ** -7 * np.abs(g_ex) + 2.0 ** -20 * bound[:, :n]
+    du = 2.0 ** -7 * np.abs(u_ex) + 2.0 ** -20 * bound[:, n:]
     gate = g_ex
     sig = 1.0 / (1.0 + np.exp(-gate))
     expect = gate * sig * u_ex
     dsilu = np.abs(sig * (1.0 + gate * (1.0 - sig)))  # |d silu / d g|
-    tol = dsilu * dg * (np.abs(u_ex) + du) + np.abs(gate * sig) * du + 2.0 ** -8 * np.abs(expect)
+    tol = dsilu * dg * (np.abs(u_ex) + du) + np.abs(gate * sig) * du + 2.0 ** -7 * np.abs(expect)
     excess = np.abs(y - expect) - 1.01 * tol
     assert excess.max() <= 1e-7, f"swiglu excess {excess.max()}"
 
