@@ -205,6 +205,26 @@ int32_t rxla_b200_paged_decode_workspace_size(int32_t batch, int32_t q_heads,
 int32_t rxla_b200_paged_decode_attention(const rxla_b200_paged_decode_args* args,
                                          void* stream);
 
+/* Paged decode attention that allocates nothing, for callers that may not
+ * call cudaMalloc: code running inside another runtime's execute callback
+ * (an XLA FFI custom call, a PJRT plugin, a serving engine's step), whose
+ * runtime owns the device memory, and latency-critical decode loops, where an
+ * allocation can synchronise the device.  No counterpart in the reference
+ * (rxla's XLA path allocates through PJRT).
+ *
+ * Same arguments and results as rxla_b200_paged_decode_attention, except that
+ * args->workspace / workspace_bytes are ignored: the split-K scratch is a
+ * fixed array of RXLA_B200_NOALLOC_SCRATCH_BYTES compiled into the library
+ * (held by every GPU that loads the library until the process exits).  A shape
+ * whose rxla_b200_paged_decode_workspace_size exceeds it returns
+ * RXLA_B200_OUT_OF_RANGE without launching.  The first call on a device looks
+ * up the array's device address (make it before any stream capture); every
+ * call clears the array's split counters on its stream.  All calls share the
+ * one array, so calls that can run at the same time on the GPU race. */
+#define RXLA_B200_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+int32_t rxla_b200_paged_decode_attention_noalloc(const rxla_b200_paged_decode_args* args,
+                                                 void* stream);
+
 /* ------------------------------------------------------- small fused ops */
 
 /* y[r, :] = bf16(x[r,:] * rsqrt(mean(x²) + eps) * w)  (ops.rs:929-945,

@@ -8,3 +8,4 @@
 #include "attention.cu"
 #include "decoder.cu"
 #include "comm.cu"
+#include "noalloc.cu"
