@@ -95,6 +95,13 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def launches_per_step(cfg):
+    """Our kernels in one decode step: embedding, per layer qkv (norm fused),
+    attention, o_proj, gate/up (norm fused), down, and the LM head with the
+    norm and the greedy argmax fused."""
+    return 1 + cfg["layers"] * 5 + 1
+
+
 def measured_peaks():
     try:
         with open(ROOT / "MEASURED_PEAKS.json") as f:
@@ -249,7 +256,7 @@ def run_ours(args, rank, world, local_rank):
                 "d2h_bytes_per_step": 4},
         "roofline": roof,
         "clocks": clocks,
-        "gpu_launches": args.steps * (1 + 36 * 7 + 3),
+        "gpu_launches": args.steps * launches_per_step(cfg),
         "device_status": status,
     }
     return out
@@ -313,6 +320,61 @@ def gemv_roofline(dec, cfg, dev, stream, lib):
             "avg_launch_us": sec / len(calls) * 1e6, "bytes_per_step": total_bytes}
 
 
+def profile_case(what: str):
+    """Small, self-contained cases for ncu captures (no JSON line).
+
+    gemv:      one W8 linear, N=32768 K=4096 M=1 (134 MB of weights > L2), 3 launches
+    step:      the config-4 decoder after a 256-token prompt, 2 decode steps inside
+               the NVTX range "profile"
+    attention: config-3 shaped paged decode attention (batch 8, ctx ~U[512, 8192])
+    """
+    import numpy as np
+    import torch
+    from rxla_b200 import _lib, nn
+    dev = torch.device("cuda:0")
+    if what == "gemv":
+        n, k = 32768, 4096
+        w = torch.randint(0, 256, (n, k), dtype=torch.uint8, device=dev)
+        sc = torch.rand(n, 1, device=dev) * 1e-2
+        x = torch.randn(1, k, device=dev).bfloat16()
+        y = torch.empty(1, n, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            nn.quantized_linear(x, w, sc, k, out=y)
+    elif what == "step":
+        from rxla_b200.decoder import Decoder
+        dec = Decoder(**CONFIG4, embedding_dtype="u8", max_batch=1, max_context=320)
+        dec.init_synthetic(1)
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        tout = ctypes.c_void_p(dec.tokens_out_ptr)
+        for _ in range(256):
+            _lib.call("rxla_b200_decoder_step", dec.handle, tout, 1, tout, None, s)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("profile")
+        for _ in range(2):
+            _lib.call("rxla_b200_decoder_step", dec.handle, tout, 1, tout, None, s)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        dec.close()
+    elif what == "attention":
+        batch, hq, hkv, d, max_ctx = 8, 32, 8, 128, 8192
+        cache = nn.PagedKvCache(batch=batch, kv_heads=hkv, head_dim=d, max_context=max_ctx)
+        cache.k.normal_()
+        cache.v.normal_()
+        g = torch.Generator(device=dev).manual_seed(3)
+        cache.ctx_lens = torch.randint(512, 8192, (batch,), dtype=torch.int32, device=dev,
+                                       generator=g)
+        qkv = torch.randn(batch, (hq + 2 * hkv) * d, device=dev).bfloat16()
+        ws = torch.zeros(nn.paged_decode_workspace_size(batch, hq, hkv, d, max_ctx),
+                         dtype=torch.uint8, device=dev)
+        inv = torch.from_numpy(nn.rope_inv_freq(1e6, d)).to(dev)
+        for _ in range(3):
+            nn.paged_decode_attention(qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d],
+                                      qkv[:, (hq + hkv) * d:], cache, q_heads=hq, inv_freq=inv,
+                                      rotary_dim=d, workspace=ws)
+    torch.cuda.synchronize()
+    print("profile case done:", what)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -321,7 +383,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-batch64", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["gemv", "step", "attention"], default=None,
+                    help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
+    if args.profile:
+        profile_case(args.profile)
+        return
     args.warmup = max(args.warmup, 3)
 
     rank = int(os.environ.get("RANK", "0"))

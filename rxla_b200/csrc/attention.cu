@@ -15,11 +15,11 @@
 // rounded to bf16) and v at slot ctx_len of each sequence.
 //
 // Design (HBM-bound: the whole visible cache is read once):
-//  * CTA = (sequence, split of `pps` pages); warp h = kv head h, a producer
-//    warp streams pages through a shared-memory ring with TMA tensor loads.
-//    One box is [64 dims × kv_heads·16 rows] with 128-byte swizzle, so a page
-//    of K for all kv heads is D/64 requests of up to 16 KB (the TMA engine is
-//    request-rate bound below ~4 KB per request);
+//  * CTA = (split of `pps` pages, kv head, sequence); four compute warps take
+//    the split's pages round-robin while a producer warp streams them through
+//    an 8-stage shared-memory ring with TMA tensor loads (one box is
+//    [64 dims × 16 rows] with 128-byte swizzle).  Splits are sized so the
+//    grid holds a few CTAs per SM at full context, with at most 32 splits;
 //  * q is normalised and rotated lane-locally in the layout of the mma B
 //    fragment (a RoPE pair (i, i + rot/2) lives in one lane), split into
 //    bf16 hi + lo so q·k keeps fp32 accuracy against the bf16 cache;
@@ -32,8 +32,9 @@
 //    into its loaded tile; every CTA fences and then triggers dependent
 //    launches, so later kernels (including the next step's attention, whose
 //    page prefetch runs before griddepcontrol.wait) see the appended rows;
-//  * splits write (O, m, l) partials to the workspace; the last CTA of a
-//    sequence (atomic counter) merges them with log-sum-exp weights and
+//  * the four warps' softmax states merge in shared memory; splits write
+//    (O, m, l) partials to the workspace and the last CTA of a (sequence,
+//    kv head) (atomic counter) merges them with log-sum-exp weights and
 //    resets the counter.  A single split writes the output directly.
 #include <cudaTypedefs.h>
 
@@ -43,7 +44,6 @@ namespace rxla {
 namespace attn {
 
 constexpr int kPage = 16;
-constexpr int kMaxStages = 4;
 
 struct Params {
   const __nv_bfloat16* q;
@@ -119,7 +119,7 @@ __device__ __forceinline__ void finish_cta(const Params& p) {
   __threadfence();
   uint32_t* exits = p.ws_counter + (size_t)p.batch * p.hkv;
   const uint32_t prev = atomicAdd(exits, 1u);
-  if (prev != gridDim.x * gridDim.y - 1) return;
+  if (prev != gridDim.x * gridDim.y * gridDim.z - 1) return;
   __threadfence();
   for (int b = 0; b < p.batch; ++b) {
     const int pos = __ldcg(p.ctx_lens + b);
@@ -131,22 +131,52 @@ __device__ __forceinline__ void finish_cta(const Params& p) {
   *exits = 0u;
 }
 
+// SplitHalf RoPE of q in the mma B-fragment layout: lane (g, q4) holds dims
+// ks*16 + 2*q4 + {0,1,8,9} of k-step ks; dim d pairs with d + 16*HS.
+template <int KS, int HS>
+__device__ __forceinline__ void rope_q(float (&qv)[KS][4], const float2* cs, int q4) {
+#pragma unroll
+  for (int ks = 0; ks < HS; ++ks)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int d = ks * 16 + 2 * q4 + (i & 1) + (i >> 1) * 8;
+      const float2 t = cs[d];
+      const float x0 = qv[ks][i], x1 = qv[ks + HS][i];
+      qv[ks][i] = x0 * t.x - x1 * t.y;
+      qv[ks + HS][i] = x1 * t.x + x0 * t.y;
+    }
+}
+
+constexpr int kComputeWarps = 4;
+constexpr int kStagesV2 = 8;
+
 template <int D>
-__global__ void __launch_bounds__(17 * 32, 1)
+__global__ void __launch_bounds__((kComputeWarps + 1) * 32)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  constexpr int DL = D / 32;     // dims per lane for the new k / v and the merges
+  constexpr int KS = D / 16;     // k-steps of q·kᵀ
+  constexpr int kTile = kPage * D * 2;            // one page of one kv head, bytes
+  constexpr int kStage = 2 * kTile;               // K + V
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
-  uint64_t* empty = full + kMaxStages;
-  // the swizzled ring must start on a 1024-byte boundary
+  uint64_t* empty = full + kStagesV2;
+  float* misc = reinterpret_cast<float*>(empty + kStagesV2);  // 8 floats: flags
+  float2* cs = reinterpret_cast<float2*>(misc + 8);               // [64] cos, sin
+  float* qw = reinterpret_cast<float*>(cs + 64);                  // [128] q norm weight
+  float* kw = qw + 128;                                           // [128] k norm weight
+  // the swizzled ring must start on a 1024-byte boundary, after the above
   const uint32_t base_u32 = smem_u32(smem_raw);
-  uint8_t* ring = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u) + 1024;
+  uint8_t* ring = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u) + 2048;
+  // per-warp softmax states for the in-CTA merge: O [warp][8][D], m/l [warp][8][2]
+  float* st_o = reinterpret_cast<float*>(ring + kStagesV2 * kStage);
+  float* st_ml = st_o + kComputeWarps * 8 * D;
+  float* wts = st_ml + kComputeWarps * 8 * 2;  // cross-split maxima [max_splits][8]
+  float* wls = wts + p.max_splits * 8;           // cross-split sums [max_splits][8]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.y, split = blockIdx.x;
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hkv = p.hkv, G = p.group;
-  const int rows = hkv * kPage;  // rows of one page box (all kv heads)
-  const int S = p.stages;
 
   if (!p.ctx_stable) pdl_wait();
   const int pos = p.ctx_lens[b];
@@ -156,89 +186,122 @@ __global__ void __launch_bounds__(17 * 32, 1)
   const int n_splits = max(1, (n_pages + p.pps - 1) / p.pps);
   const int pg0 = split * p.pps;
   const int pg1 = min(n_pages, pg0 + p.pps);
+  const int n_it = max(0, pg1 - pg0);
   const bool in_range = pos >= 0 && pos < cap;
   const bool accept = cap > 0 && (in_range || p.kv_update == RXLA_B200_KV_CLAMP);
   const int slot = pos < 0 ? 0 : (pos >= cap ? cap - 1 : pos);
   const bool owner = accept && split == (slot / kPage) / p.pps;
 
-  if (split >= n_splits) {  // nothing of this sequence in this split
+  if (split >= n_splits) {  // nothing of this sequence in this split (exit = trigger)
     if (threadIdx.x == 0) finish_cta(p);
-    pdl_launch_dependents();
     return;
   }
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
+    for (int s = 0; s < kStagesV2; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], hkv);
+      mbar_init(&empty[s], 1);
     }
     fence_mbarrier_init();
   }
   __syncthreads();
 
-  if (warp == hkv) {
+  if (warp == kComputeWarps) {
     // ------------------------------------------------------------ producer
     // Pages hold rows appended by earlier kernels only (the new row is patched
     // in from registers); with a stable ctx_lens they are fetched before
     // griddepcontrol.wait.
     if (lane == 0) {
-      const uint32_t bytes = (uint32_t)p.stage_bytes;
-      for (int pg = pg0, it = 0; pg < pg1; ++pg, ++it) {
-        const int s = it % S;
-        if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1)) break;
-        const int page = p.page_table[(int64_t)b * p.max_pages + pg];
-        const int row = page * rows;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        uint8_t* kdst = ring + (size_t)s * p.stage_bytes;
-        uint8_t* vdst = kdst + p.stage_bytes / 2;
+      for (int it = 0; it < n_it; ++it) {
+        const int s = it % kStagesV2;
+        if (it >= kStagesV2 && !mbar_wait(&empty[s], ((it / kStagesV2) - 1) & 1)) break;
+        const int page = p.page_table[(int64_t)b * p.max_pages + pg0 + it];
+        const int row = (page * hkv + h) * kPage;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)kStage);
+        uint8_t* kdst = ring + (size_t)s * kStage;
 #pragma unroll
         for (int j = 0; j < D / 64; ++j) {
-          tma_load_2d(kdst + j * rows * 128, &kmap, 64 * j, row, &full[s]);
-          tma_load_2d(vdst + j * rows * 128, &vmap, 64 * j, row, &full[s]);
+          tma_load_2d(kdst + j * kPage * 128, &kmap, 64 * j, row, &full[s]);
+          tma_load_2d(kdst + kTile + j * kPage * 128, &vmap, 64 * j, row, &full[s]);
         }
       }
     }
   } else {
-    // -------------------------------------------------------- kv-head warps
-    const int h = warp;
+    // ------------------------------------------------------- compute warps
+    const int tid = threadIdx.x;  // 0 .. 127
+    // Position tables (cos, sin of pos·inv_freq) and the norm weights go to
+    // shared memory first; with a stable ctx_lens this overlaps the previous
+    // kernel.  The angle is f32(pos) · inv_freq in f32, as the oracle forms it.
+    if (p.rot > 0 && tid < p.rot / 2) {
+      const float ang = (float)pos * p.inv_freq[tid];
+      cs[tid] = make_float2(cosf(ang), sinf(ang));
+    }
+    if (p.q_norm_w && tid < D) qw[tid] = p.q_norm_w[tid];
+    if (p.k_norm_w && tid < D) kw[tid] = p.k_norm_w[tid];
     if (p.ctx_stable) pdl_wait();  // q / k_new / v_new come from the previous kernel
+    // dependents wait for this grid's completion before reading its output
+    if (tid == 0) pdl_launch_dependents();
     const int g = lane >> 2, q4 = lane & 3;
 
-    // new k / v of this kv head: lane holds dims [DL*lane, DL*lane + DL)
-    constexpr int DL = D / 32;
+    // raw q (lane (g, q4) holds head g, dims ks*16 + 2*q4 + {0,1,8,9}) and,
+    // in the warp that meets the slot's page, the new k / v: all loads first
+    float qv[KS][4];
+    const bool qvalid = g < G;
+    {
+      const __nv_bfloat16* qr =
+          p.q + (int64_t)b * p.q_stride + (int64_t)(h * G + (qvalid ? g : 0)) * D;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        const int d0 = ks * 16 + 2 * q4;
+        const __nv_bfloat162 x0 = *reinterpret_cast<const __nv_bfloat162*>(qr + d0);
+        const __nv_bfloat162 x1 = *reinterpret_cast<const __nv_bfloat162*>(qr + d0 + 8);
+        qv[ks][0] = qvalid ? __low2float(x0) : 0.0f;
+        qv[ks][1] = qvalid ? __high2float(x0) : 0.0f;
+        qv[ks][2] = qvalid ? __low2float(x1) : 0.0f;
+        qv[ks][3] = qvalid ? __high2float(x1) : 0.0f;
+      }
+    }
+    const int slot_pg = slot / kPage;
+    const bool appender = owner && warp == (slot_pg - pg0) % kComputeWarps;
     float kn[DL], vn[DL];
-    if (owner) {
+    if (appender) {
       const __nv_bfloat16* kr = p.k_new + (int64_t)b * p.kv_stride + (int64_t)h * D;
       const __nv_bfloat16* vr = p.v_new + (int64_t)b * p.kv_stride + (int64_t)h * D;
-      float ss = 0.0f;
 #pragma unroll
       for (int i = 0; i < DL; ++i) {
         kn[i] = __bfloat162float(kr[DL * lane + i]);
         vn[i] = __bfloat162float(vr[DL * lane + i]);
-        ss += kn[i] * kn[i];
       }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");  // tables ready
+
+    if (appender) {
+      // k: RMSNorm over the head, RoPE, bf16; appended at the slot and patched
+      // into this warp's tile of the slot's page below
       if (p.k_norm_w) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DL; ++i) ss += kn[i] * kn[i];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float rs = 1.0f / sqrtf(ss / (float)D + p.eps);
 #pragma unroll
-        for (int i = 0; i < DL; ++i) kn[i] = (kn[i] * rs) * p.k_norm_w[DL * lane + i];
+        for (int i = 0; i < DL; ++i) kn[i] = (kn[i] * rs) * kw[DL * lane + i];
       }
       if (p.rot > 0) {
         // partner of dim d < rot/2 is d + rot/2, held by lane + rot/(2·DL)
         const int half = p.rot / 2, off = half / DL;
-        const float fpos = (float)pos;
 #pragma unroll
         for (int i = 0; i < DL; ++i) {
           const int d = DL * lane + i;
           const float up = __shfl_sync(0xffffffffu, kn[i], (lane + off) & 31);
           const float dn = __shfl_sync(0xffffffffu, kn[i], (lane - off) & 31);
           if (d < half) {
-            const float ang = fpos * p.inv_freq[d];
-            kn[i] = kn[i] * cosf(ang) - up * sinf(ang);
+            const float2 t = cs[d];
+            kn[i] = kn[i] * t.x - up * t.y;
           } else if (d < p.rot) {
-            const float ang = fpos * p.inv_freq[d - half];
-            kn[i] = kn[i] * cosf(ang) + dn * sinf(ang);
+            const float2 t = cs[d - half];
+            kn[i] = kn[i] * t.x + dn * t.y;
           }
         }
       }
@@ -247,43 +310,25 @@ __global__ void __launch_bounds__(17 * 32, 1)
         kn[i] = bf16_round(kn[i]);
         vn[i] = bf16_round(vn[i]);
       }
-      // append into the cache (global)
-      const int page = p.page_table[(int64_t)b * p.max_pages + slot / kPage];
+      const int page = p.page_table[(int64_t)b * p.max_pages + slot_pg];
       const int64_t base = (((int64_t)page * hkv + h) * kPage + slot % kPage) * D + DL * lane;
 #pragma unroll
       for (int i = 0; i < DL; ++i) {
         p.k_pages[base + i] = __float2bfloat16_rn(kn[i]);
         p.v_pages[base + i] = __float2bfloat16_rn(vn[i]);
       }
-      __threadfence();
     }
-    // every kv-head warp has appended: let dependent kernels launch
-    asm volatile("bar.sync 1, %0;" ::"r"(hkv * 32) : "memory");
-    if (warp == 0 && lane == 0) pdl_launch_dependents();
 
-    // q of the G heads of this kv head, in B-fragment layout: lane (g, q4)
-    // holds head g, dims ks*16 + 2*q4 + {0,1,8,9} for ks = 0..D/16-1.
-    constexpr int KS = D / 16;
+    // q of the G heads of this kv head in B-fragment layout, normed, rotated
+    // and split into bf16 hi + lo
     uint32_t qhi[KS][2], qlo[KS][2];
     {
-      float qv[KS][4];
-      const bool valid = g < G;
-      const __nv_bfloat16* qr =
-          p.q + (int64_t)b * p.q_stride + (int64_t)(h * G + (valid ? g : 0)) * D;
-      float ss = 0.0f;
-#pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        const int d0 = ks * 16 + 2 * q4;
-        const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(qr + d0);
-        const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(qr + d0 + 8);
-        qv[ks][0] = valid ? __low2float(a) : 0.0f;
-        qv[ks][1] = valid ? __high2float(a) : 0.0f;
-        qv[ks][2] = valid ? __low2float(c) : 0.0f;
-        qv[ks][3] = valid ? __high2float(c) : 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) ss += qv[ks][i] * qv[ks][i];
-      }
       if (p.q_norm_w) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) ss += qv[ks][i] * qv[ks][i];
         ss += __shfl_xor_sync(0xffffffffu, ss, 1);
         ss += __shfl_xor_sync(0xffffffffu, ss, 2);
         const float rs = 1.0f / sqrtf(ss / (float)D + p.eps);
@@ -292,25 +337,17 @@ __global__ void __launch_bounds__(17 * 32, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int d = ks * 16 + 2 * q4 + (i & 1) + (i >> 1) * 8;
-            qv[ks][i] = (qv[ks][i] * rs) * p.q_norm_w[d];
+            qv[ks][i] = (qv[ks][i] * rs) * qw[d];
           }
       }
-      if (p.rot > 0) {
-        const int hs = p.rot / 32;  // k-step distance of a RoPE pair
-        const float fpos = (float)pos;
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-          if (ks >= hs) continue;  // upper halves are rotated with their partner
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int d = ks * 16 + 2 * q4 + (i & 1) + (i >> 1) * 8;
-            const float ang = fpos * p.inv_freq[d];
-            const float c = cosf(ang), sn = sinf(ang);
-            const float a = qv[ks][i], bb = qv[ks + hs][i];
-            qv[ks][i] = a * c - bb * sn;
-            qv[ks + hs][i] = bb * c + a * sn;
-          }
-        }
+      // a RoPE pair (d, d + rot/2) is rot/32 k-steps apart; the distance is a
+      // template argument so qv stays in registers
+      switch (p.rot / 32) {
+        case 1: rope_q<KS, 1>(qv, cs, q4); break;
+        case 2: rope_q<KS, 2>(qv, cs, q4); break;
+        case 3: if constexpr (KS >= 6) rope_q<KS, 3>(qv, cs, q4); break;
+        case 4: if constexpr (KS >= 8) rope_q<KS, 4>(qv, cs, q4); break;
+        default: break;
       }
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
@@ -324,7 +361,7 @@ __global__ void __launch_bounds__(17 * 32, 1)
     }
     const float scale = p.scale;
 
-    // running softmax state of head columns 2*q4, 2*q4+1
+    // running softmax state of head columns 2*q4, 2*q4+1 over this warp's pages
     float m_run[2] = {-INFINITY, -INFINITY};
     float l_part[2] = {0.0f, 0.0f};
     float o[D / 16][4];
@@ -333,32 +370,32 @@ __global__ void __launch_bounds__(17 * 32, 1)
 #pragma unroll
       for (int i = 0; i < 4; ++i) o[mt][i] = 0.0f;
 
-    const int r0 = h * kPage;
-    for (int pg = pg0, it = 0; pg < pg1; ++pg, ++it) {
-      const int s = it % S;
-      if (!mbar_wait(&full[s], (it / S) & 1)) break;
-      uint8_t* kt = ring + (size_t)s * p.stage_bytes;
-      uint8_t* vt = kt + p.stage_bytes / 2;
-      if (owner && pg == slot / kPage) {
+    const int mi = lane >> 3, rr = lane & 7;
+    for (int it = warp; it < n_it; it += kComputeWarps) {
+      const int s = it % kStagesV2;
+      if (!mbar_wait(&full[s], (it / kStagesV2) & 1)) break;
+      const int pg = pg0 + it;
+      uint8_t* kt = ring + (size_t)s * kStage;
+      uint8_t* vt = kt + kTile;
+      if (appender && pg == slot_pg) {
         // patch the appended row into the loaded tile
-        const int r = r0 + slot % kPage;
+        const int r = slot % kPage;
 #pragma unroll
         for (int i = 0; i < DL; i += 2) {
           const int d = DL * lane + i;
-          *reinterpret_cast<uint32_t*>(kt + swz(r, d, rows)) = pack_bf16x2(kn[i], kn[i + 1]);
-          *reinterpret_cast<uint32_t*>(vt + swz(r, d, rows)) = pack_bf16x2(vn[i], vn[i + 1]);
+          *reinterpret_cast<uint32_t*>(kt + swz(r, d, kPage)) = pack_bf16x2(kn[i], kn[i + 1]);
+          *reinterpret_cast<uint32_t*>(vt + swz(r, d, kPage)) = pack_bf16x2(vn[i], vn[i + 1]);
         }
         __syncwarp();
       }
       // ---- S^T (16 tokens x 8 head columns) = K · Q^T
       float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       const uint32_t kbase = smem_u32(kt);
-      const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         // matrices: (tok 0-7, d 0-7), (tok 8-15, d 0-7), (tok 0-7, d 8-15), (tok 8-15, d 8-15)
         uint32_t a[4];
-        ldsm_x4(a, kbase + swz(r0 + rr + ((mi & 1) << 3), ks * 16 + ((mi >> 1) << 3), rows));
+        ldsm_x4(a, kbase + swz(rr + ((mi & 1) << 3), ks * 16 + ((mi >> 1) << 3), kPage));
         mma_bf16_16816(sc, a, qhi[ks][0], qhi[ks][1]);
         mma_bf16_16816(sc, a, qlo[ks][0], qlo[ks][1]);
       }
@@ -406,7 +443,7 @@ __global__ void __launch_bounds__(17 * 32, 1)
       for (int mt = 0; mt < D / 16; ++mt) {
         // A = V^T (16 dims x 16 tokens): (d 0-7,t 0-7), (d 8-15,t 0-7), (d 0-7,t 8-15), (d 8-15,t 8-15)
         uint32_t a[4];
-        ldsm_x4_t(a, vbase + swz(r0 + rr + ((mi >> 1) << 3), mt * 16 + ((mi & 1) << 3), rows));
+        ldsm_x4_t(a, vbase + swz(rr + ((mi >> 1) << 3), mt * 16 + ((mi & 1) << 3), kPage));
         mma_bf16_16816(o[mt], a, b0, b1);
         mma_bf16_16816(o[mt], a, c0, c1);
       }
@@ -414,79 +451,116 @@ __global__ void __launch_bounds__(17 * 32, 1)
       if (lane == 0) mbar_arrive(&empty[s]);
     }
 
-    // ---- finalize this split
-    float l_tot[2];
+    // ---- this warp's state -> shared memory (head column j = 2*q4 + jj)
+    {
+      float* wo = st_o + (size_t)warp * 8 * D;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float l = l_part[j];
-      l += __shfl_xor_sync(0xffffffffu, l, 4);
-      l += __shfl_xor_sync(0xffffffffu, l, 8);
-      l += __shfl_xor_sync(0xffffffffu, l, 16);
-      l_tot[j] = l;
-    }
-    const int hc0 = 2 * q4;  // head columns of this lane
-    if (n_splits == 1) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        if (hc0 + j >= G) continue;
-        const float inv = l_tot[j] > 0.0f ? 1.0f / l_tot[j] : 0.0f;
-        __nv_bfloat16* orow = p.out + (int64_t)b * p.hq * D + (int64_t)(h * G + hc0 + j) * D;
+      for (int jj = 0; jj < 2; ++jj) {
+        float l = l_part[jj];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        const int j = 2 * q4 + jj;
 #pragma unroll
         for (int mt = 0; mt < D / 16; ++mt) {
-          orow[mt * 16 + g] = __float2bfloat16_rn(o[mt][j] * inv);
-          orow[mt * 16 + g + 8] = __float2bfloat16_rn(o[mt][2 + j] * inv);
-        }
-      }
-    } else {
-      // partials of this split, then the last split of (b, h) merges them
-      const int64_t seg = (((int64_t)b * hkv + h) * p.max_splits + split) * G;
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        if (hc0 + j >= G) continue;
-        float* po = p.ws_o + (seg + hc0 + j) * D;
-#pragma unroll
-        for (int mt = 0; mt < D / 16; ++mt) {
-          po[mt * 16 + g] = o[mt][j];
-          po[mt * 16 + g + 8] = o[mt][2 + j];
+          wo[j * D + mt * 16 + g] = o[mt][jj];
+          wo[j * D + mt * 16 + g + 8] = o[mt][2 + jj];
         }
         if (g == 0) {
-          p.ws_ml[(seg + hc0 + j) * 2] = m_run[j];
-          p.ws_ml[(seg + hc0 + j) * 2 + 1] = l_tot[j];
+          st_ml[(warp * 8 + j) * 2] = m_run[jj];
+          st_ml[(warp * 8 + j) * 2 + 1] = l;
         }
       }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
+
+    // ---- merge the 4 warps (in-CTA) -> this split's (O, m, l) per head;
+    // a thread takes 4 consecutive dims of one head
+    const int64_t seg = (((int64_t)b * hkv + h) * p.max_splits + split) * G;
+    for (int e = tid; e < G * D / 4; e += kComputeWarps * 32) {
+      const int j = (4 * e) / D, d = (4 * e) % D;
+      float m = -INFINITY;
+#pragma unroll
+      for (int w2 = 0; w2 < kComputeWarps; ++w2) m = fmaxf(m, st_ml[(w2 * 8 + j) * 2]);
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      float l = 0.0f;
+#pragma unroll
+      for (int w2 = 0; w2 < kComputeWarps; ++w2) {
+        const float mw = st_ml[(w2 * 8 + j) * 2];
+        const float wgt = mw == -INFINITY ? 0.0f : expf(mw - m);
+        const float4 x = *reinterpret_cast<const float4*>(st_o + ((size_t)w2 * 8 + j) * D + d);
+        acc.x += wgt * x.x;
+        acc.y += wgt * x.y;
+        acc.z += wgt * x.z;
+        acc.w += wgt * x.w;
+        l += wgt * st_ml[(w2 * 8 + j) * 2 + 1];
+      }
+      if (n_splits == 1) {
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        uint2 pk;
+        pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+        pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+        *reinterpret_cast<uint2*>(p.out + (int64_t)b * p.hq * D + (int64_t)(h * G + j) * D + d) = pk;
+      } else {
+        *reinterpret_cast<float4*>(p.ws_o + (seg + j) * D + d) = acc;
+        if (d == 0) *reinterpret_cast<float2*>(p.ws_ml + (seg + j) * 2) = make_float2(m, l);
+      }
+    }
+    if (n_splits > 1) {
       __threadfence();
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) {
+      asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
+      if (tid == 0) {
         const uint32_t prev = atomicAdd(&p.ws_counter[b * hkv + h], 1u);
-        last = prev == (uint32_t)(n_splits - 1);
+        misc[0] = prev == (uint32_t)(n_splits - 1) ? 1.0f : 0.0f;
       }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
+      asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
+      if (misc[0] != 0.0f) {
+        // the last split of (b, h) merges all splits' partials: (m, l) of
+        // every split in one round of loads, then up to 8 partial rows in flight
         __threadfence();
-        for (int j = 0; j < G; ++j) {
-          const int64_t segj = ((int64_t)b * hkv + h) * p.max_splits * G + j;
-          float mstar = -INFINITY;
-          for (int sp = 0; sp < n_splits; ++sp)
-            mstar = fmaxf(mstar, __ldcg(p.ws_ml + (segj + (int64_t)sp * G) * 2));
-          float den = 0.0f;
-          float acc[DL];
-#pragma unroll
-          for (int i = 0; i < DL; ++i) acc[i] = 0.0f;
-          for (int sp = 0; sp < n_splits; ++sp) {
-            const int64_t e = segj + (int64_t)sp * G;
-            const float m = __ldcg(p.ws_ml + e * 2), l = __ldcg(p.ws_ml + e * 2 + 1);
-            const float w = (m == -INFINITY) ? 0.0f : expf(m - mstar);
-            den += w * l;
-#pragma unroll
-            for (int i = 0; i < DL; ++i) acc[i] += w * __ldcg(p.ws_o + e * D + lane + 32 * i);
-          }
-          const float inv = den > 0.0f ? 1.0f / den : 0.0f;
-          __nv_bfloat16* orow = p.out + (int64_t)b * p.hq * D + (int64_t)(h * G + j) * D;
-#pragma unroll
-          for (int i = 0; i < DL; ++i) orow[lane + 32 * i] = __float2bfloat16_rn(acc[i] * inv);
+        const int64_t base = ((int64_t)b * hkv + h) * p.max_splits * G;
+        for (int e = tid; e < n_splits * G; e += kComputeWarps * 32) {
+          const int sp = e / G, j = e % G;
+          const float2 ml =
+              __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (base + (int64_t)sp * G + j) * 2));
+          wts[sp * 8 + j] = ml.x;
+          wls[sp * 8 + j] = ml.y;
         }
-        if (lane == 0) p.ws_counter[b * hkv + h] = 0u;
+        asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
+        for (int e = tid; e < G * D / 4; e += kComputeWarps * 32) {
+          const int j = (4 * e) / D, d = (4 * e) % D;
+          float m = -INFINITY;
+          for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, wts[sp * 8 + j]);
+          float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          float l = 0.0f;
+          for (int sp0 = 0; sp0 < n_splits; sp0 += 8) {
+            float4 x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              if (sp0 + u < n_splits)
+                x[u] = __ldcg(reinterpret_cast<const float4*>(
+                    p.ws_o + (base + (int64_t)(sp0 + u) * G + j) * D + d));
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              if (sp0 + u < n_splits) {
+                const float mw = wts[(sp0 + u) * 8 + j];
+                const float wgt = mw == -INFINITY ? 0.0f : expf(mw - m);
+                acc.x += wgt * x[u].x;
+                acc.y += wgt * x[u].y;
+                acc.z += wgt * x[u].z;
+                acc.w += wgt * x[u].w;
+                l += wgt * wls[(sp0 + u) * 8 + j];
+              }
+            }
+          }
+          const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+          uint2 pk;
+          pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+          pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+          *reinterpret_cast<uint2*>(p.out + (int64_t)b * p.hq * D + (int64_t)(h * G + j) * D + d) =
+              pk;
+        }
+        if (tid == 0) p.ws_counter[b * hkv + h] = 0u;
       }
     }
   }
@@ -514,7 +588,7 @@ static int32_t make_page_map(CUtensorMap* map, void* base, int64_t num_pages, in
   if (!fn) return fail(RXLA_B200_UNAVAILABLE, "cuTensorMapEncodeTiled is unavailable");
   const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)(num_pages * hkv * kPage)};
   const cuuint64_t strides[1] = {(cuuint64_t)d * 2};
-  const cuuint32_t box[2] = {64, (cuuint32_t)(hkv * kPage)};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kPage};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -523,11 +597,13 @@ static int32_t make_page_map(CUtensorMap* map, void* base, int64_t num_pages, in
   return RXLA_B200_OK;
 }
 
-// pages per split: enough CTAs for ~4 waves when sequences average half of
-// max_context, at most 16 pages (256 tokens) per split for balance.
-static int pages_per_split(int batch, int max_pages) {
-  int64_t v = ((int64_t)batch * max_pages) / (8 * 148);
-  return (int)std::max<int64_t>(1, std::min<int64_t>(16, v));
+// Pages per split: CTAs are (sequence, kv head, split).  Aim for ~4 CTAs per
+// SM when every sequence is at max_context, with at most 32 pages per split
+// for balance, but never more than 32 splits (the merge depth).
+static int pages_per_split(int batch, int kv_heads, int max_pages) {
+  const int64_t want = ((int64_t)batch * kv_heads * max_pages + 4 * 148 - 1) / (4 * 148);
+  const int64_t depth = ((int64_t)max_pages + 31) / 32;
+  return (int)std::max<int64_t>(1, std::max(depth, std::min<int64_t>(32, want)));
 }
 
 }  // namespace attn
@@ -541,7 +617,7 @@ extern "C" int32_t rxla_b200_paged_decode_workspace_size(int32_t batch, int32_t 
                    head_dim > 0 && max_context >= 0,
                "paged_decode_workspace_size: bad arguments");
   const int max_pages = (max_context + attn::kPage - 1) / attn::kPage;
-  const int pps = attn::pages_per_split(batch, max_pages);
+  const int pps = attn::pages_per_split(batch, kv_heads, max_pages);
   const int64_t splits = std::max(1, (max_pages + pps - 1) / pps);
   const int64_t G = q_heads / kv_heads;
   const int64_t part = (int64_t)batch * kv_heads * splits * G;
@@ -564,7 +640,8 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
                    a->q_heads % a->kv_heads == 0,
                "paged_decode: query heads must be a positive multiple of kv heads (attention.rs:99-112)");
   RXLA_REQUIRE(a->q_heads / a->kv_heads <= 8, "paged_decode: at most 8 query heads per kv head");
-  RXLA_REQUIRE(a->kv_heads <= 16, "paged_decode: at most 16 kv heads per call (shard larger models)");
+  RXLA_REQUIRE(a->kv_heads <= 65535 && a->batch <= 65535,
+               "paged_decode: kv_heads and batch must be <= 65535 (grid dimensions)");
   RXLA_REQUIRE(D == 64 || D == 128, "paged_decode: head_dim must be 64 or 128");
   RXLA_REQUIRE(a->page_size == attn::kPage, "paged_decode: page_size must be 16");
   RXLA_REQUIRE(a->rotary_dim == 0 || a->inv_freq == nullptr ||
@@ -582,6 +659,8 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   RXLA_REQUIRE(a->q_row_stride % 2 == 0 && a->kv_row_stride % 2 == 0 &&
                    (reinterpret_cast<uintptr_t>(a->q) % 4 == 0),
                "paged_decode: q / kv rows must be 4-byte aligned");
+  RXLA_REQUIRE(reinterpret_cast<uintptr_t>(a->out) % 8 == 0,
+               "paged_decode: out must be 8-byte aligned");
   if (a->batch == 0) return RXLA_B200_OK;
   RXLA_REQUIRE(a->q && a->k_new && a->v_new && a->k_pages && a->v_pages && a->page_table &&
                    a->ctx_lens && a->out,
@@ -618,7 +697,7 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   p.hkv = a->kv_heads;
   p.group = a->q_heads / a->kv_heads;
   const int max_pages = (a->max_context + attn::kPage - 1) / attn::kPage;
-  p.pps = attn::pages_per_split(a->batch, max_pages);
+  p.pps = attn::pages_per_split(a->batch, a->kv_heads, max_pages);
   p.max_splits = std::max(1, (max_pages + p.pps - 1) / p.pps);
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   const size_t cnt_bytes = (((size_t)a->batch * a->kv_heads + 1) * 4 + 255) / 256 * 256;
@@ -626,11 +705,10 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   p.ws_o = reinterpret_cast<float*>(ws + cnt_bytes);
   const int64_t part = (int64_t)a->batch * a->kv_heads * p.max_splits * p.group;
   p.ws_ml = p.ws_o + part * D;
-  p.stage_bytes = 2 * a->kv_heads * attn::kPage * D * 2;
+  p.stage_bytes = 2 * attn::kPage * D * 2;
   p.batch = a->batch;
   p.ctx_stable = ctx_stable ? 1 : 0;
-  p.stages = (int)std::min<int64_t>(attn::kMaxStages, (200 * 1024) / p.stage_bytes);
-  if (p.stages < 2) p.stages = 2;
+  p.stages = attn::kStagesV2;
 
   CUtensorMap kmap, vmap;
   int32_t st = attn::make_page_map(&kmap, a->k_pages, a->num_pages, a->kv_heads, D);
@@ -638,9 +716,11 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   st = attn::make_page_map(&vmap, a->v_pages, a->num_pages, a->kv_heads, D);
   if (st != RXLA_B200_OK) return st;
 
-  const size_t smem = 2048 + (size_t)p.stages * p.stage_bytes;
-  const dim3 grid(p.max_splits, a->batch);
-  const dim3 block((a->kv_heads + 1) * 32);
+  const size_t smem = 3072 + (size_t)p.stages * p.stage_bytes +
+                      (size_t)attn::kComputeWarps * 8 * (D + 2) * 4 +
+                      (size_t)p.max_splits * 8 * 2 * 4;
+  const dim3 grid(p.max_splits, a->kv_heads, a->batch);
+  const dim3 block((attn::kComputeWarps + 1) * 32);
   cudaStream_t s = s_in;
   cudaError_t e;
   if (D == 128) {

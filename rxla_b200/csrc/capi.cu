@@ -50,8 +50,8 @@ int32_t read_device_status(bool reset) {
 // linear's bf16 cast).
 __global__ void rms_norm_bf16_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                      int64_t width, float eps, __nv_bfloat16* __restrict__ y) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
   const float* xr = x + blockIdx.x * width;
   float ss = 0.0f;
   for (int64_t c = threadIdx.x; c < width; c += blockDim.x) ss += xr[c] * xr[c];
@@ -79,8 +79,8 @@ __global__ void rms_norm_bf16_kernel(const float* __restrict__ x, const float* _
 // the decoder runner's end-of-step position update.
 __global__ void argmax_kernel(const float* __restrict__ logits, int64_t vocab,
                               int32_t* __restrict__ out, int32_t* __restrict__ advance) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
   const float* r = logits + blockIdx.x * vocab;
   float best = -INFINITY;
   int32_t idx = 0x7fffffff;

@@ -12,7 +12,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "common.cuh"
+#include "internal.cuh"
 
 struct rxla_b200_comm {
   ncclComm_t nccl = nullptr;

@@ -165,7 +165,11 @@ __device__ __forceinline__ void bulk_g2s_nohint(void* dst, const void* src, uint
 }
 
 // Programmatic dependent launch: wait for the previous grid's results, and
-// allow the next grid to start its prologue.
+// allow the next grid to start its prologue.  Every kernel of this library
+// triggers its dependents only after its own griddepcontrol.wait, so when a
+// grid starts, every grid before the one directly preceding it has completed:
+// code before griddepcontrol.wait overlaps only that one grid, and may read
+// anything the grids before it wrote.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -17,11 +17,12 @@
 //
 // The residual stream is f32; every linear computes in bf16 with fp32
 // accumulation (the layer compute dtype BF16 of crates/rxla-nn/src/layers.rs:
-// 289-297).  A step is 7 kernels per layer + 4, all launched with
+// 289-297).  A step is 5 kernels per layer + 2 (W8 embedding), all launched with
 // programmatic dependent launch and captured once per batch size into a CUDA
 // graph; ctx_lens (the next position of each sequence) changes only in the
-// final argmax kernel, so the attention kernels may prefetch cache pages
-// before griddepcontrol.wait.
+// last kernel of the step (the LM head's argmax epilogue), so the attention
+// kernels may prefetch cache pages before griddepcontrol.wait.  The RMSNorms
+// in front of qkv, gate/up and the head run in those GEMVs' prologues.
 //
 // Tensor parallelism (tp_size > 1): each rank holds its q/kv heads, its
 // slices of gate/up rows and the matching columns of o_proj/down_proj; the
@@ -32,15 +33,9 @@
 #include <string>
 #include <vector>
 
-#include "common.cuh"
+#include "internal.cuh"
 
 namespace rxla {
-
-int32_t comm_allreduce_f32(rxla_b200_comm* comm, float* buf, int64_t count, cudaStream_t s);
-
-namespace attn {
-int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable);
-}
 
 namespace dec {
 
@@ -91,8 +86,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const uint8_t* 
                              const float* __restrict__ scale, const __nv_bfloat16* __restrict__ wb,
                              int64_t vocab, int64_t hidden, int64_t groups, int64_t group,
                              float* __restrict__ h) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
   int64_t t = tokens[blockIdx.x];
   t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
   for (int64_t j = threadIdx.x; j < hidden; j += blockDim.x) {
@@ -107,8 +102,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const uint8_t* 
 // all-reduce of the row-parallel partial sums).
 __global__ void residual_add_kernel(const float* __restrict__ part, float* __restrict__ h,
                                     int64_t n) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     h[i] = h[i] + bf16_round(part[i]);
@@ -174,6 +169,10 @@ struct rxla_b200_decoder {
   float* inv_freq = nullptr;
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  // fused LM-head argmax: per-CTA partials and the arrival counter
+  float* arg_val = nullptr;
+  int32_t* arg_idx = nullptr;
+  uint32_t* arg_count = nullptr;
   int32_t* host_pinned = nullptr;
   std::map<int, cudaGraphExec_t> graphs;
 };
@@ -200,10 +199,21 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
   const int64_t qd = (int64_t)d->hq * D, kd = (int64_t)d->hkv * D;
   for (int l = 0; l < c.layers; ++l) {
     const Layer& L = d->layers[l];
-    int32_t st = rxla_b200_rms_norm_bf16(d->h, L.ln1, batch, H, c.rms_eps, d->xn, s);
-    if (st) return st;
-    st = rxla_b200_w8a16_linear(d->xn, RXLA_B200_BF16, L.wqkv, L.sqkv, d->group_h, batch,
-                                d->qkv_rows, H, d->qkv, RXLA_B200_BF16, RXLA_B200_EPI_STORE, s);
+    // qkv = W8(bf16(rms_norm(h) * input_layernorm)), the norm fused in the prologue
+    NormLinearArgs na{};
+    na.h = d->h;
+    na.norm_w = L.ln1;
+    na.eps = c.rms_eps;
+    na.w = L.wqkv;
+    na.scale = L.sqkv;
+    na.group = d->group_h;
+    na.m = batch;
+    na.n = d->qkv_rows;
+    na.k = H;
+    na.y = d->qkv;
+    na.y_dtype = RXLA_B200_BF16;
+    na.epilogue = RXLA_B200_EPI_STORE;
+    int32_t st = w8_norm_linear(na, s);
     if (st) return st;
     rxla_b200_paged_decode_args a{};
     a.struct_size = sizeof(a);
@@ -253,10 +263,14 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
                      dim3(1024), 0, s, (const float*)d->part, d->h, (int64_t)batch * H);
       if (e != cudaSuccess) return cuda_fail(e, "residual add launch");
     }
-    st = rxla_b200_rms_norm_bf16(d->h, L.ln2, batch, H, c.rms_eps, d->xn, s);
-    if (st) return st;
-    st = rxla_b200_w8a16_linear(d->xn, RXLA_B200_BF16, L.wgu, L.sgu, d->group_h, batch, d->inter,
-                                H, d->act, RXLA_B200_BF16, RXLA_B200_EPI_SWIGLU, s);
+    // act = silu(gate) * up of bf16(rms_norm(h) * post_attention_layernorm)
+    na.norm_w = L.ln2;
+    na.w = L.wgu;
+    na.scale = L.sgu;
+    na.n = d->inter;
+    na.y = d->act;
+    na.epilogue = RXLA_B200_EPI_SWIGLU;
+    st = w8_norm_linear(na, s);
     if (st) return st;
     if (!tp) {
       st = rxla_b200_w8a16_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H,
@@ -273,17 +287,35 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
       if (e != cudaSuccess) return cuda_fail(e, "residual add launch");
     }
   }
+  if (tp) return fail(RXLA_B200_UNIMPLEMENTED, "tensor-parallel LM head argmax");
+  if (d->emb_w8) {
+    // tied W8 head: logits = bf16(rms_norm(h) * norm) · Eᵀ (f32), greedy token
+    // and the position advance in the same kernel
+    NormLinearArgs na{};
+    na.h = d->h;
+    na.norm_w = d->final_norm;
+    na.eps = c.rms_eps;
+    na.w = d->emb_w8;
+    na.scale = d->emb_scale;
+    na.group = d->group_h;
+    na.m = batch;
+    na.n = d->vocab;
+    na.k = H;
+    na.y = d->logits;
+    na.y_dtype = RXLA_B200_F32;
+    na.epilogue = kArgmaxEpilogue;
+    na.arg_val = d->arg_val;
+    na.arg_idx = d->arg_idx;
+    na.arg_count = d->arg_count;
+    na.arg_out = d->tok_out;
+    na.arg_advance = d->ctx;
+    return w8_norm_linear(na, s);
+  }
   int32_t st = rxla_b200_rms_norm_bf16(d->h, d->final_norm, batch, H, c.rms_eps, d->xn, s);
   if (st) return st;
-  if (d->emb_w8)
-    st = rxla_b200_w8a16_linear(d->xn, RXLA_B200_BF16, d->emb_w8, d->emb_scale, d->group_h,
-                                batch, d->vocab, H, d->logits, RXLA_B200_F32, RXLA_B200_EPI_STORE,
-                                s);
-  else
-    st = rxla_b200_bf16_linear(d->xn, RXLA_B200_BF16, d->emb_bf16, batch, d->vocab, H, d->logits,
-                               RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
+  st = rxla_b200_bf16_linear(d->xn, RXLA_B200_BF16, d->emb_bf16, batch, d->vocab, H, d->logits,
+                             RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
   if (st) return st;
-  if (tp) return fail(RXLA_B200_UNIMPLEMENTED, "tensor-parallel LM head argmax");
   e = launch_pdl(argmax_kernel, dim3(batch), dim3(1024), 0, s, (const float*)d->logits,
                  (int64_t)d->vocab, d->tok_out, d->ctx);
   if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
@@ -320,6 +352,10 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
   RXLA_REQUIRE(gsz <= 0 || (c.hidden % gsz == 0 && (c.q_heads * c.head_dim / tp) % gsz == 0 &&
                             (c.intermediate / tp) % gsz == 0),
                "decoder_create: group_size must divide every input width");
+  RXLA_REQUIRE(c.hidden % 64 == 0 && (c.q_heads * c.head_dim / tp) % 64 == 0 &&
+                   (c.intermediate / tp) % 64 == 0 && (gsz <= 0 || gsz % 64 == 0),
+               "decoder_create: hidden, q_heads*head_dim, intermediate (and group_size) must be "
+               "multiples of 64");
   RXLA_CUDA_CHECK(cudaSetDevice(device));
 
   auto* d = new rxla_b200_decoder();
@@ -445,6 +481,9 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
       {(void**)&d->tok_out, (size_t)B * 4},
       {(void**)&d->inv_freq, (size_t)D * 2},
       {&d->ws, need_ws},
+      {(void**)&d->arg_val, (size_t)1024 * 8 * 4},
+      {(void**)&d->arg_idx, (size_t)1024 * 8 * 4},
+      {(void**)&d->arg_count, 256},
   };
   for (auto& a : acts) {
     st = dec::alloc_dev(a.p, std::max<size_t>(a.bytes, 256));
@@ -468,6 +507,7 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
       cudaMemcpy(d->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemset(d->ctx, 0, (size_t)B * 4) != cudaSuccess ||
       cudaMemset(d->ws, 0, need_ws) != cudaSuccess ||
+      cudaMemset(d->arg_count, 0, 256) != cudaSuccess ||
       cudaMemset(d->arena, 0, d->arena_bytes) != cudaSuccess) {
     rxla_b200_decoder_destroy(d);
     return fail(RXLA_B200_UNAVAILABLE, "decoder_create: initial copies failed");
@@ -490,7 +530,8 @@ extern "C" int32_t rxla_b200_decoder_destroy(rxla_b200_decoder* d) {
     cudaFree(L.vc);
   }
   void* ptrs[] = {d->arena, d->page_table, d->ctx, d->h, d->xn, d->qkv, d->att, d->act,
-                  d->part, d->logits, d->tok_in, d->tok_out, d->inv_freq, d->ws};
+                  d->part, d->logits, d->tok_in, d->tok_out, d->inv_freq, d->ws,
+                  d->arg_val, d->arg_idx, d->arg_count};
   for (void* p : ptrs) cudaFree(p);
   if (d->host_pinned) cudaFreeHost(d->host_pinned);
   delete d;

@@ -8,8 +8,8 @@ namespace rxla {
 __global__ void bf16_linear_kernel(const void* __restrict__ x, int x_f32,
                                    const __nv_bfloat16* __restrict__ w, int m, int n, int k,
                                    void* __restrict__ y, int y_f32, int epilogue) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;

@@ -1,0 +1,38 @@
+// internal.cuh — library-internal entry points shared by the decoder runner.
+#pragma once
+
+#include "common.cuh"
+
+namespace rxla {
+
+// W8 linear whose x is bf16(rms_norm(h) * norm_w) of the f32 residual h, the
+// norm computed in each CTA's prologue; optionally with the greedy-argmax
+// epilogue of the tied LM head (epilogue = kArgmaxEpilogue).
+struct NormLinearArgs {
+  const float* h;
+  const float* norm_w;
+  float eps;
+  const uint8_t* w;
+  const float* scale;
+  int64_t group, m, n, k;
+  void* y;  // y (STORE / SWIGLU) or logits (argmax; may be null)
+  int32_t y_dtype, epilogue;
+  // argmax scratch and results: per-CTA partials [>= grid][8], a counter that
+  // is zero between launches, the chosen token per row, optional position += 1
+  float* arg_val;
+  int32_t* arg_idx;
+  uint32_t* arg_count;
+  int32_t* arg_out;
+  int32_t* arg_advance;
+};
+
+constexpr int kArgmaxEpilogue = 16;
+
+int32_t w8_norm_linear(const NormLinearArgs& a, cudaStream_t stream);
+int32_t comm_allreduce_f32(rxla_b200_comm* comm, float* buf, int64_t count, cudaStream_t s);
+
+namespace attn {
+int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable);
+}
+
+}  // namespace rxla

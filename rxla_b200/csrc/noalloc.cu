@@ -21,13 +21,9 @@
 // Each call clears the array's split counters on its stream before launching.
 #include <mutex>
 
-#include "common.cuh"
+#include "internal.cuh"
 
 namespace rxla {
-
-namespace attn {
-int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable);
-}
 
 namespace noalloc {
 

@@ -23,10 +23,10 @@
 //  * 16 consumer warps split each stage into 64-column boxes of 16 rows and
 //    feed mma.sync m16n8k16 (bf16 in, fp32 accumulate) with weight rows on
 //    the M side and tokens on the N side, so there is no cross-lane reduction
-//    over K.  Dequantization runs in registers with packed f32x2 arithmetic:
-//    PRMT makes 2^23 + b, add.f32x2 subtracts 2^23 + 128 (exact q),
-//    mul.f32x2 applies the row's scale (the reference's f32 product) and
-//    cvt.rn.bf16x2 rounds to bf16.  For SwiGLU, rows 0-7 of the A tile are
+//    over K.  Dequantization runs in registers: PRMT puts the byte b in a
+//    denormal's mantissa (b·2^-133, exact), one FFMA with s·2^133 and -128·s
+//    rounds (b - 128)·s once (the reference's f32 product), cvt.rn.bf16x2
+//    rounds to bf16: 1.5 integer-pipe + 1 FMA-pipe instruction per weight.  For SwiGLU, rows 0-7 of the A tile are
 //    gate rows and rows 8-15 the matching up rows.  The K columns are permuted
 //    consistently for A and B: a lane reads 16 contiguous weight bytes and the
 //    16 matching x values, which covers four k-steps;
@@ -38,7 +38,7 @@
 
 #include <cuda_fp16.h>
 
-#include "common.cuh"
+#include "internal.cuh"
 
 namespace rxla {
 namespace w8 {
@@ -51,7 +51,17 @@ constexpr int kTileRows = 16;       // A rows per block (16 outputs, or 8 gate +
 constexpr int kMaxStages = 8;
 constexpr int kMaxTokens = 8;       // tokens per pass (one n-tile)
 constexpr int kRedFloats = kConsumerWarps * kTileRows * kMaxTokens;
-constexpr int kHeader = 1024;       // barriers + per-token exponents
+constexpr int kHeader = 1024;       // barriers + norm partials
+
+// Where x comes from.
+enum XMode : int {
+  kXBf16 = 0,  // bf16 [m, k]: bulk-copied into shared memory by the producer
+  kXF32 = 1,   // f32 [m, k]: rounded to bf16 by the consumers (QuantizedLinear's cast)
+  kXNorm = 2   // f32 residual h [m, k]: bf16(rms_norm(h) * norm_w), ops.rs:929-945
+};
+
+// Epilogue codes beyond the public ones (rxla_b200_epilogue).
+constexpr int kEpiArgmax = 16;  // logits (f32, optional) + greedy token per row
 
 struct Params {
   const uint8_t* w;
@@ -64,11 +74,20 @@ struct Params {
   int32_t group_size;
   int64_t ldx, ldy;    // row strides of x and y in elements
   int32_t x_f32, y_f32, epilogue;
+  // fused RMSNorm (kXNorm)
+  const float* norm_w;
+  float norm_eps;
+  // fused greedy argmax (kEpiArgmax): per-CTA partials, arrival counter, result
+  float* arg_val;       // [grid][8]
+  int32_t* arg_idx;     // [grid][8]
+  uint32_t* arg_count;  // one counter, zero between launches
+  int32_t* arg_out;     // [m]
+  int32_t* arg_advance; // optional [m], += 1 per row (decoder position)
   // shared-memory plan (set by the host)
   int32_t kc;           // K columns per stage (multiple of 64)
   int32_t k_chunks;     // ceil(k / kc)
   int32_t stages;       // ring depth
-  int32_t x_pitch;      // bytes of one resident token row of x
+  int32_t x_pitch;      // bytes of one resident bf16 token row of x
   int32_t stage_bytes;  // 16 rows × kc
 };
 
@@ -79,32 +98,49 @@ struct Bars {
   uint64_t grp[2];
   uint64_t epi_full[2];
   uint64_t epi_free[2];
+  float ss[kConsumerWarps][kMaxTokens];  // norm: per-warp sums of squares
 };
 static_assert(sizeof(Bars) <= kHeader, "header");
 
-__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+// Row constants of the exact dequantization below: sbig = s·2^133 and
+// c = -128·s, both exact while s < 2^-5 (larger scales are pre-divided by a
+// power of two and the product multiplied back: `post`).
+struct RowScale {
+  float sbig, c, post;
+};
+
+__device__ __forceinline__ RowScale row_scale(float s) {
+  RowScale r;
+  r.post = 1.0f;
+  if (!(fabsf(s) < 0.03125f) && s == s && fabsf(s) < INFINITY) {
+    const int e = ((__float_as_int(s) >> 23) & 0xff) - 127;  // s in [2^e, 2^(e+1))
+    const int k = e + 6;                                     // s·2^-k < 2^-5
+    s = s * __int_as_float((127 - k) << 23);
+    r.post = __int_as_float((127 + k) << 23);
+  }
+  r.c = -128.0f * s;
+  r.sbig = (s * 0x1p100f) * 0x1p33f;  // s·2^133 (exact: two power-of-two steps)
   return r;
 }
 
-// Four u8 weights of one row (value b, q = b - 128) with the row's scale pair
-// (s, s) -> two bf16x2 registers of bf16(f32(q)·s): lo = (w0, w1), hi = (w2, w3).
-__device__ __forceinline__ void deq4(uint32_t w, uint64_t s2, uint32_t& lo, uint32_t& hi) {
-  const uint64_t bias = 0xCB000080CB000080ull;  // (-(2^23 + 128), -(2^23 + 128))
-  uint64_t a = f32x2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u)),
-                     __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541u)));
-  uint64_t c = f32x2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7542u)),
-                     __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7543u)));
-  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(a) : "l"(bias));
-  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(c) : "l"(bias));
-  asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(a) : "l"(s2));
-  asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(c) : "l"(s2));
-  float a0, a1, c0, c1;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(c0), "=f"(c1) : "l"(c));
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(a1), "f"(a0));
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(c1), "f"(c0));
+// Four u8 weights of one row (value b, q = b - 128) -> two bf16x2 registers of
+// bf16(f32(q)·s), the reference's rounding: lo = (w0, w1), hi = (w2, w3).
+// PRMT places b in the mantissa of a denormal (b·2^-133, exact);
+// fma(b·2^-133, s·2^133, -128·s) rounds (b - 128)·s once, as f32(q)·s does.
+template <bool POST>
+__device__ __forceinline__ void deq4(uint32_t w, const RowScale& r, uint32_t& lo, uint32_t& hi) {
+  float p0 = fmaf(__uint_as_float(__byte_perm(w, 0u, 0x4044u)), r.sbig, r.c);
+  float p1 = fmaf(__uint_as_float(__byte_perm(w, 0u, 0x4144u)), r.sbig, r.c);
+  float p2 = fmaf(__uint_as_float(__byte_perm(w, 0u, 0x4244u)), r.sbig, r.c);
+  float p3 = fmaf(__uint_as_float(__byte_perm(w, 0u, 0x4344u)), r.sbig, r.c);
+  if (POST) {
+    p0 *= r.post;
+    p1 *= r.post;
+    p2 *= r.post;
+    p3 *= r.post;
+  }
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(p1), "f"(p0));
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(p3), "f"(p2));
 }
 
 // Bounded barrier among the 16 consumer warps (one arrival per warp).
@@ -114,18 +150,46 @@ __device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t parity) {
   return mbar_wait(bar, parity);
 }
 
+// One 64-column box of a 16-row tile: 16 B of rows g and g+8 per lane, the
+// lane's 16 x values, four k-steps of m16n8k16.
+template <bool POST>
+__device__ __forceinline__ void box_mma(float (&acc)[4], const uint8_t* stage, int kc_stride,
+                                        int lcol, const uint8_t* xcol, bool has_tok, int g,
+                                        const RowScale& ra, const RowScale& rb) {
+  uint32_t bx[8];
+  if (has_tok) {
+    const uint4 v0 = *reinterpret_cast<const uint4*>(xcol);
+    const uint4 v1 = *reinterpret_cast<const uint4*>(xcol + 16);
+    bx[0] = v0.x; bx[1] = v0.y; bx[2] = v0.z; bx[3] = v0.w;
+    bx[4] = v1.x; bx[5] = v1.y; bx[6] = v1.z; bx[7] = v1.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bx[j] = 0u;
+  }
+  const uint4 lo = *reinterpret_cast<const uint4*>(stage + g * kc_stride + lcol);
+  const uint4 hi = *reinterpret_cast<const uint4*>(stage + (g + 8) * kc_stride + lcol);
+  const uint32_t wl[4] = {lo.x, lo.y, lo.z, lo.w};
+  const uint32_t wh[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+  for (int st = 0; st < 4; ++st) {
+    uint32_t a[4];
+    deq4<POST>(wl[st], ra, a[0], a[2]);  // row g: k-low pair, k-high pair
+    deq4<POST>(wh[st], rb, a[1], a[3]);  // row g+8
+    mma_bf16_16816(acc, a, bx[2 * st], bx[2 * st + 1]);
+  }
+}
+
+template <bool SWIGLU, bool GROUPED, int XMODE>
 __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Bars& bars = *reinterpret_cast<Bars*>(smem_raw);
   float* red = reinterpret_cast<float*>(smem_raw + kHeader);  // [2][warp][16 rows][8 tokens]
-  uint8_t* xs = smem_raw + kHeader + 2 * kRedFloats * 4;
+  uint8_t* xs = smem_raw + kHeader + 2 * kRedFloats * 4;       // bf16 [m][x_pitch]
   uint8_t* stages = xs + (size_t)p.m * p.x_pitch;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const bool swiglu = p.epilogue == RXLA_B200_EPI_SWIGLU;
-  const int xe = p.x_f32 ? 4 : 2;
-  const int out_rows = swiglu ? kTileRows / 2 : kTileRows;
+  constexpr int out_rows = SWIGLU ? kTileRows / 2 : kTileRows;
 
   // balanced contiguous share of output rows for this CTA
   const int64_t R = p.n;
@@ -149,7 +213,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     fence_mbarrier_init();
   }
   __syncthreads();
-  pdl_launch_dependents();
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
@@ -160,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       const int nr = min(out_rows, r_end - r0);
       const int col0 = kc * p.kc;
       const int cols = min(p.kc, p.k - col0);
-      const uint32_t tx = (uint32_t)cols * (uint32_t)nr * (swiglu ? 2u : 1u);
+      const uint32_t tx = (uint32_t)cols * (uint32_t)nr * (SWIGLU ? 2u : 1u);
       if (lane == 0) mbar_arrive_expect_tx(&bars.full[s], tx);
       __syncwarp();
       uint8_t* dst = stages + (size_t)s * p.stage_bytes;
@@ -168,12 +231,12 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
         // whole rows: the block is one contiguous range (two for SwiGLU)
         if (lane == 0)
           bulk_g2s(dst, p.w + (int64_t)r0 * p.k, (uint32_t)(nr * p.k), &bars.full[s], policy);
-        if (swiglu && lane == 1)
+        if (SWIGLU && lane == 1)
           bulk_g2s(dst + (kTileRows / 2) * p.kc, p.w + (int64_t)(p.n + r0) * p.k,
                    (uint32_t)(nr * p.k), &bars.full[s], policy);
       } else {
-        const int i = swiglu ? (lane & 7) : lane;
-        const bool up = swiglu && lane >= 8;
+        const int i = SWIGLU ? (lane & 7) : lane;
+        const bool up = SWIGLU && lane >= 8;
         if (lane < kTileRows && i < nr) {
           const int64_t row = up ? (int64_t)p.n + r0 + i : (int64_t)r0 + i;
           bulk_g2s(dst + (size_t)lane * p.kc, p.w + row * p.k + col0, (uint32_t)cols,
@@ -185,12 +248,14 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     const int pre = min(S, total);
     for (int it = 0; it < pre; ++it) issue(it, it);
     pdl_wait();  // x is the previous kernel's output
-    if (lane == 0) mbar_arrive_expect_tx(&bars.x_full, (uint32_t)(p.m * p.k * xe));
-    __syncwarp();
-    if (lane < p.m)
-      bulk_g2s_nohint(xs + lane * p.x_pitch,
-                      static_cast<const uint8_t*>(p.x) + (int64_t)lane * p.ldx * xe,
-                      (uint32_t)(p.k * xe), &bars.x_full);
+    if (XMODE == kXBf16) {
+      if (lane == 0) mbar_arrive_expect_tx(&bars.x_full, (uint32_t)(p.m * p.k * 2));
+      __syncwarp();
+      if (lane < p.m)
+        bulk_g2s_nohint(xs + lane * p.x_pitch,
+                        static_cast<const uint8_t*>(p.x) + (int64_t)lane * p.ldx * 2,
+                        (uint32_t)(p.k * 2), &bars.x_full);
+    }
     for (int it = pre; it < total; ++it) {
       const int s = it % S;
       if (!mbar_wait(&bars.empty[s], ((it / S) - 1) & 1)) return;
@@ -201,32 +266,50 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
 
   const int g = lane >> 2;  // mma group id: A rows g, g+8; B column (token) g
   const int q = lane & 3;   // k-quad
-  const bool per_channel = p.groups == 1;
 
   if (warp == kEpilogueWarp) {
     // ------------------------------------------------------------ epilogue
     pdl_wait();  // y (or the residual it adds into) may be used by the previous kernel
+    pdl_launch_dependents();
+    const bool argmax = p.epilogue == kEpiArgmax;
+    float best_v[kMaxTokens];
+    int best_i[kMaxTokens];
+#pragma unroll
+    for (int t = 0; t < kMaxTokens; ++t) {
+      best_v[t] = -INFINITY;
+      best_i[t] = 0x7fffffff;
+    }
     for (int blk = 0; blk < n_blocks; ++blk) {
       const int b2 = blk & 1;
       if (!mbar_wait(&bars.epi_full[b2], (blk >> 1) & 1)) return;
       const int r0 = r_begin + blk * out_rows;
       const int nr = min(out_rows, r_end - r0);
       const float* rb = red + b2 * kRedFloats;
-      for (int idx = lane; idx < out_rows * kMaxTokens; idx += 32) {
+#pragma unroll
+      for (int tt = 0; tt < (out_rows * kMaxTokens) / 32; ++tt) {
+        const int idx = lane + 32 * tt;
         const int row = idx % out_rows, tok = idx / out_rows;
         if (row >= nr || tok >= p.m) continue;
         float v = 0.0f, u = 0.0f;
 #pragma unroll
         for (int w2 = 0; w2 < kConsumerWarps; ++w2) {
           v += rb[(w2 * kTileRows + row) * kMaxTokens + tok];
-          if (swiglu) u += rb[(w2 * kTileRows + row + 8) * kMaxTokens + tok];
+          if (SWIGLU) u += rb[(w2 * kTileRows + row + 8) * kMaxTokens + tok];
         }
         const int out_col = r0 + row;
         const int64_t o = (int64_t)tok * p.ldy + out_col;
-        if (swiglu) {
+        if (SWIGLU) {
           const float r = silu(bf16_round(v)) * bf16_round(u);
           if (p.y_f32) static_cast<float*>(p.y)[o] = r;
           else static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(r);
+        } else if (argmax) {
+          if (p.y) static_cast<float*>(p.y)[o] = v;
+#pragma unroll
+          for (int t = 0; t < kMaxTokens; ++t)
+            if (t == tok && (v > best_v[t] || (v == best_v[t] && out_col < best_i[t]))) {
+              best_v[t] = v;
+              best_i[t] = out_col;
+            }
         } else if (p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD) {
           float* yy = static_cast<float*>(p.y);
           yy[o] = yy[o] + bf16_round(v);
@@ -239,11 +322,108 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.epi_free[b2]);
     }
+    if (argmax) {
+      // per-CTA best of each row, then the last CTA to arrive picks the token
+#pragma unroll
+      for (int t = 0; t < kMaxTokens; ++t) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, best_v[t], o);
+          const int oi = __shfl_xor_sync(0xffffffffu, best_i[t], o);
+          if (ov > best_v[t] || (ov == best_v[t] && oi < best_i[t])) {
+            best_v[t] = ov;
+            best_i[t] = oi;
+          }
+        }
+      }
+      if (lane == 0) {
+        for (int t = 0; t < p.m; ++t) {
+          p.arg_val[blockIdx.x * kMaxTokens + t] = best_v[t];
+          p.arg_idx[blockIdx.x * kMaxTokens + t] = best_i[t];
+        }
+        __threadfence();
+        const uint32_t prev = atomicAdd(p.arg_count, 1u);
+        if (prev == gridDim.x - 1) {
+          __threadfence();
+          for (int t = 0; t < p.m; ++t) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int c = 0; c < (int)gridDim.x; ++c) {
+              const float v = __ldcg(p.arg_val + c * kMaxTokens + t);
+              const int i = __ldcg(p.arg_idx + c * kMaxTokens + t);
+              if (v > bv || (v == bv && i < bi)) {
+                bv = v;
+                bi = i;
+              }
+            }
+            p.arg_out[t] = bi == 0x7fffffff ? 0 : bi;
+            if (p.arg_advance) p.arg_advance[t] += 1;
+          }
+          *p.arg_count = 0u;
+        }
+      }
+    }
     return;
   }
 
   // -------------------------------------------------------------- consumers
-  if (!mbar_wait(&bars.x_full, 0)) return;
+  const int ctid = threadIdx.x;  // 0 .. 511
+  if (XMODE == kXBf16) {
+    if (!mbar_wait(&bars.x_full, 0)) return;
+  } else {
+    pdl_wait();  // x / h come from the previous kernel
+    const float* xf = static_cast<const float*>(p.x);
+    float inv[kMaxTokens];
+#pragma unroll
+    for (int t = 0; t < kMaxTokens; ++t) inv[t] = 1.0f;
+    if (XMODE == kXNorm) {
+      // sum of squares per token: threads stride over k, then warps, then CTA
+      float ss[kMaxTokens];
+#pragma unroll
+      for (int t = 0; t < kMaxTokens; ++t) {
+        float v = 0.0f;
+        if (t < p.m) {
+          const float* row = xf + (int64_t)t * p.ldx;
+          for (int c = ctid * 4; c < p.k; c += kConsumerWarps * 32 * 4) {
+            const float4 h = __ldg(reinterpret_cast<const float4*>(row + c));
+            v += h.x * h.x + h.y * h.y + h.z * h.z + h.w * h.w;
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        }
+        ss[t] = v;
+      }
+      if (lane == 0)
+#pragma unroll
+        for (int t = 0; t < kMaxTokens; ++t) bars.ss[warp][t] = ss[t];
+      if (!consumer_sync(&bars.grp[0], 0)) return;
+#pragma unroll
+      for (int t = 0; t < kMaxTokens; ++t) {
+        float tot = 0.0f;
+        for (int w2 = 0; w2 < kConsumerWarps; ++w2) tot += bars.ss[w2][t];
+        inv[t] = 1.0f / sqrtf(tot / (float)p.k + p.norm_eps);
+      }
+    }
+    for (int t = 0; t < p.m; ++t) {
+      const float* row = xf + (int64_t)t * p.ldx;
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(xs + t * p.x_pitch);
+      for (int c = ctid * 4; c < p.k; c += kConsumerWarps * 32 * 4) {
+        float4 h = __ldg(reinterpret_cast<const float4*>(row + c));
+        if (XMODE == kXNorm) {
+          const float4 nw = __ldg(reinterpret_cast<const float4*>(p.norm_w + c));
+          h.x = (h.x * inv[t]) * nw.x;
+          h.y = (h.y * inv[t]) * nw.y;
+          h.z = (h.z * inv[t]) * nw.z;
+          h.w = (h.w * inv[t]) * nw.w;
+        }
+        uint2 pk;
+        pk.x = pack_bf16x2(h.x, h.y);
+        pk.y = pack_bf16x2(h.z, h.w);
+        *reinterpret_cast<uint2*>(out + c) = pk;
+      }
+    }
+    if (!consumer_sync(&bars.grp[1], 0)) return;
+  }
   const bool has_tok = g < p.m;
   const uint8_t* xrow = xs + g * p.x_pitch;
 
@@ -252,9 +432,9 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     const int r0 = r_begin + blk * out_rows;
     const int nr = min(out_rows, r_end - r0);
     // weight rows of this lane's A fragment: tile rows g and g + 8
-    int ra, rb;
     bool va, vb;
-    if (swiglu) {
+    int ra, rb;
+    if (SWIGLU) {
       va = vb = g < nr;
       ra = r0 + g;
       rb = p.n + r0 + g;
@@ -266,59 +446,56 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     }
     const float* sa = p.scale + (int64_t)ra * p.groups;
     const float* sb = p.scale + (int64_t)rb * p.groups;
-    uint64_t s2a = 0, s2b = 0;
-    if (per_channel) {
-      const float x0 = va ? __ldg(sa) : 0.0f, x1 = vb ? __ldg(sb) : 0.0f;
-      s2a = f32x2(x0, x0);
-      s2b = f32x2(x1, x1);
+    RowScale rsa = row_scale(0.0f), rsb = row_scale(0.0f);
+    bool post = false;  // warp-uniform: some row's scale needs the power-of-two fixup
+    if (!GROUPED) {
+      rsa = row_scale(va ? __ldg(sa) : 0.0f);
+      rsb = row_scale(vb ? __ldg(sb) : 0.0f);
+      post = __any_sync(0xffffffffu, rsa.post != 1.0f || rsb.post != 1.0f);
     }
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float acc0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int kc = 0; kc < p.k_chunks; ++kc, ++it) {
       const int s = it % S;
       const int col0 = kc * p.kc;
       const int nbox = min(p.kc, p.k - col0) >> 6;
       if (!mbar_wait(&bars.full[s], (it / S) & 1)) return;
       const uint8_t* stage = stages + (size_t)s * p.stage_bytes;
-#pragma unroll 2
-      for (int box = warp; box < nbox; box += kConsumerWarps) {
-        const int lcol = box * 64 + 16 * q;  // stage-local column of this lane's 16 bytes
-        const int gcol = col0 + lcol;        // global K column
-        if (!per_channel) {
-          const int grp = gcol / p.group_size;
-          const float x0 = va ? __ldg(sa + grp) : 0.0f, x1 = vb ? __ldg(sb + grp) : 0.0f;
-          s2a = f32x2(x0, x0);
-          s2b = f32x2(x1, x1);
+      int box = warp;
+      // two independent boxes per iteration (separate accumulators)
+      for (; box + kConsumerWarps < nbox; box += 2 * kConsumerWarps) {
+        const int l0 = box * 64 + 16 * q, l1 = l0 + kConsumerWarps * 64;
+        RowScale a0 = rsa, b0 = rsb, a1 = rsa, b1 = rsb;
+        bool pst = post;
+        if (GROUPED) {
+          const int g0 = (col0 + l0) / p.group_size, g1 = (col0 + l1) / p.group_size;
+          a0 = row_scale(va ? __ldg(sa + g0) : 0.0f);
+          b0 = row_scale(vb ? __ldg(sb + g0) : 0.0f);
+          a1 = row_scale(va ? __ldg(sa + g1) : 0.0f);
+          b1 = row_scale(vb ? __ldg(sb + g1) : 0.0f);
+          pst = __any_sync(0xffffffffu, a0.post != 1.0f || b0.post != 1.0f ||
+                                            a1.post != 1.0f || b1.post != 1.0f);
         }
-        uint32_t bx[8];
-        if (has_tok) {
-          if (p.x_f32) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float4 v = *reinterpret_cast<const float4*>(xrow + (gcol + 4 * j) * 4);
-              bx[2 * j] = pack_bf16x2(v.x, v.y);
-              bx[2 * j + 1] = pack_bf16x2(v.z, v.w);
-            }
-          } else {
-            const uint4 v0 = *reinterpret_cast<const uint4*>(xrow + gcol * 2);
-            const uint4 v1 = *reinterpret_cast<const uint4*>(xrow + gcol * 2 + 16);
-            bx[0] = v0.x; bx[1] = v0.y; bx[2] = v0.z; bx[3] = v0.w;
-            bx[4] = v1.x; bx[5] = v1.y; bx[6] = v1.z; bx[7] = v1.w;
-          }
+        if (pst) {
+          box_mma<true>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, has_tok, g, a0, b0);
+          box_mma<true>(acc1, stage, p.kc, l1, xrow + (col0 + l1) * 2, has_tok, g, a1, b1);
         } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) bx[j] = 0u;
+          box_mma<false>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, has_tok, g, a0, b0);
+          box_mma<false>(acc1, stage, p.kc, l1, xrow + (col0 + l1) * 2, has_tok, g, a1, b1);
         }
-        const uint4 lo = *reinterpret_cast<const uint4*>(stage + g * p.kc + lcol);
-        const uint4 hi = *reinterpret_cast<const uint4*>(stage + (g + 8) * p.kc + lcol);
-        const uint32_t wl[4] = {lo.x, lo.y, lo.z, lo.w};
-        const uint32_t wh[4] = {hi.x, hi.y, hi.z, hi.w};
-#pragma unroll
-        for (int st = 0; st < 4; ++st) {
-          uint32_t a[4];
-          deq4(wl[st], s2a, a[0], a[2]);  // row g: k-low pair, k-high pair
-          deq4(wh[st], s2b, a[1], a[3]);  // row g+8
-          mma_bf16_16816(acc, a, bx[2 * st], bx[2 * st + 1]);
+      }
+      if (box < nbox) {
+        const int l0 = box * 64 + 16 * q;
+        RowScale a0 = rsa, b0 = rsb;
+        bool pst = post;
+        if (GROUPED) {
+          const int g0 = (col0 + l0) / p.group_size;
+          a0 = row_scale(va ? __ldg(sa + g0) : 0.0f);
+          b0 = row_scale(vb ? __ldg(sb + g0) : 0.0f);
+          pst = __any_sync(0xffffffffu, a0.post != 1.0f || b0.post != 1.0f);
         }
+        if (pst) box_mma<true>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, has_tok, g, a0, b0);
+        else box_mma<false>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, has_tok, g, a0, b0);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.empty[s]);
@@ -327,10 +504,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     const int b2 = blk & 1;
     if (blk >= 2 && !mbar_wait(&bars.epi_free[b2], ((blk >> 1) - 1) & 1)) return;
     float* mine = red + b2 * kRedFloats + warp * kTileRows * kMaxTokens;
-    mine[g * kMaxTokens + 2 * q] = acc[0];
-    mine[g * kMaxTokens + 2 * q + 1] = acc[1];
-    mine[(g + 8) * kMaxTokens + 2 * q] = acc[2];
-    mine[(g + 8) * kMaxTokens + 2 * q + 1] = acc[3];
+    mine[g * kMaxTokens + 2 * q] = acc0[0] + acc1[0];
+    mine[g * kMaxTokens + 2 * q + 1] = acc0[1] + acc1[1];
+    mine[(g + 8) * kMaxTokens + 2 * q] = acc0[2] + acc1[2];
+    mine[(g + 8) * kMaxTokens + 2 * q + 1] = acc0[3] + acc1[3];
     __syncwarp();
     if (lane == 0) mbar_arrive(&bars.epi_full[b2]);
   }
@@ -345,8 +522,8 @@ __global__ void w8_generic_kernel(const Params p) {
   const int lane = threadIdx.x & 31;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   const bool swiglu = p.epilogue == RXLA_B200_EPI_SWIGLU;
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
   const int64_t items = (int64_t)p.n * p.m;
   for (int64_t it = warp_global; it < items; it += nwarps) {
     const int col = (int)(it % p.n);
@@ -391,31 +568,55 @@ __global__ void w8_generic_kernel(const Params p) {
 
 // Shared-memory plan.  K is cut into k_chunks of kc columns so that one
 // stage (16 rows × kc) stays within 64 KB (80 KB if that avoids a split);
-// x (m tokens) is resident; the ring takes the rest, 2..8 stages.
+// x (m tokens, bf16) is resident; the ring takes the rest, 2..8 stages.
+static size_t env_size(const char* name, size_t dflt) {
+  const char* v = getenv(name);
+  return v ? (size_t)strtoull(v, nullptr, 10) : dflt;
+}
+
 static int32_t plan_skinny(Params& p, size_t& smem) {
-  const int xe = p.x_f32 ? 4 : 2;
-  int chunks = (int)(((int64_t)kTileRows * p.k + 80 * 1024 - 1) / (80 * 1024));
-  if (chunks > 1) chunks = (int)(((int64_t)kTileRows * p.k + 64 * 1024 - 1) / (64 * 1024));
+  // tuning knobs (bytes): largest stage, shared-memory budget of one CTA
+  static const size_t max_stage = env_size("RXLA_B200_GEMV_STAGE", 80 * 1024);
+  static const size_t budget = env_size("RXLA_B200_GEMV_SMEM", 227 * 1024);
+  int chunks = (int)(((int64_t)kTileRows * p.k + max_stage - 1) / max_stage);
   int kc = (int)((((int64_t)p.k + chunks - 1) / chunks + 63) / 64 * 64);
   p.kc = kc;
   p.k_chunks = (p.k + kc - 1) / kc;
   p.stage_bytes = kTileRows * kc;
-  p.x_pitch = p.k * xe + 16;
+  p.x_pitch = p.k * 2 + 16;
   const size_t fixed = kHeader + 2 * kRedFloats * 4 + (size_t)p.m * p.x_pitch;
-  const size_t budget = 227 * 1024;
   if (fixed + 2 * (size_t)p.stage_bytes > budget) return -1;
   p.stages = (int)std::min<size_t>(kMaxStages, (budget - fixed) / p.stage_bytes);
   smem = fixed + (size_t)p.stages * p.stage_bytes;
   return 0;
 }
 
-static cudaError_t launch_skinny(Params p, int grid, cudaStream_t stream) {
+template <bool SWIGLU, bool GROUPED, int XMODE>
+static cudaError_t launch_variant(const Params& p, int grid, size_t smem, cudaStream_t stream) {
+  auto k = w8_skinny_kernel<SWIGLU, GROUPED, XMODE>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(k, dim3(grid), dim3(kThreads), smem, stream, p);
+}
+
+template <bool SWIGLU, bool GROUPED>
+static cudaError_t launch_x(const Params& p, int xmode, int grid, size_t smem, cudaStream_t s) {
+  if (xmode == kXNorm) return launch_variant<SWIGLU, GROUPED, kXNorm>(p, grid, smem, s);
+  if (xmode == kXF32) return launch_variant<SWIGLU, GROUPED, kXF32>(p, grid, smem, s);
+  return launch_variant<SWIGLU, GROUPED, kXBf16>(p, grid, smem, s);
+}
+
+static cudaError_t launch_skinny(Params p, int xmode, int grid, cudaStream_t stream) {
   size_t smem = 0;
   if (plan_skinny(p, smem) != 0) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(w8_skinny_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  return launch_pdl(w8_skinny_kernel, dim3(grid), dim3(kThreads), smem, stream, p);
+  const bool swiglu = p.epilogue == RXLA_B200_EPI_SWIGLU;
+  const bool grouped = p.groups != 1;
+  if (swiglu) {
+    return grouped ? launch_x<true, true>(p, xmode, grid, smem, stream)
+                   : launch_x<true, false>(p, xmode, grid, smem, stream);
+  }
+  return grouped ? launch_x<false, true>(p, xmode, grid, smem, stream)
+                 : launch_x<false, false>(p, xmode, grid, smem, stream);
 }
 
 // Tokens per pass of the skinny kernel: up to 8, as long as the resident x
@@ -429,26 +630,69 @@ static int tokens_per_pass(Params p) {
   return 0;
 }
 
+static int grid_for(const Params& p) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int rows_min = 4;  // avoid CTAs with almost no rows on tiny layers
+  return (int)std::min<int64_t>(sm_count(dev), std::max<int64_t>(1, p.n / rows_min));
+}
+
 }  // namespace w8
 
 // Fast-path eligibility and launch of one pass of at most `pass_m` tokens.
-static int32_t w8_linear_pass(w8::Params p, bool fast, cudaStream_t stream) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int sms = sm_count(dev);
+static int32_t w8_linear_pass(w8::Params p, bool fast, int xmode, cudaStream_t stream) {
   cudaError_t e;
   if (fast) {
-    const int rows_min = 4;  // avoid CTAs with almost no rows on tiny layers
-    int grid = (int)std::min<int64_t>(sms, std::max<int64_t>(1, p.n / rows_min));
-    e = w8::launch_skinny(p, grid, stream);
+    e = w8::launch_skinny(p, xmode, w8::grid_for(p), stream);
   } else {
+    int dev = 0;
+    cudaGetDevice(&dev);
     const int64_t warps = (int64_t)p.n * p.m;
-    int blocks = (int)std::min<int64_t>((warps + 7) / 8, (int64_t)sms * 16);
+    int blocks = (int)std::min<int64_t>((warps + 7) / 8, (int64_t)sm_count(dev) * 16);
     e = launch_pdl(w8::w8_generic_kernel, dim3(std::max(blocks, 1)), dim3(256), 0, stream, p);
   }
   if (e != cudaSuccess) return cuda_fail(e, "w8a16 linear launch");
   return RXLA_B200_OK;
 }
+
+int32_t w8_norm_linear(const NormLinearArgs& a, cudaStream_t stream) {
+  RXLA_REQUIRE(a.k % 64 == 0 && (a.group == a.k || a.group % 64 == 0) &&
+                   reinterpret_cast<uintptr_t>(a.w) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(a.h) % 16 == 0,
+               "norm linear: shape is off the fused fast path");
+  w8::Params p{};
+  p.w = a.w;
+  p.scale = a.scale;
+  p.k = (int32_t)a.k;
+  p.n = (int32_t)a.n;
+  p.groups = (int32_t)(a.k / a.group);
+  p.group_size = (int32_t)a.group;
+  p.ldx = a.k;
+  p.ldy = a.n;
+  p.x_f32 = 1;
+  p.y_f32 = a.y_dtype == RXLA_B200_F32;
+  p.epilogue = a.epilogue;
+  p.norm_w = a.norm_w;
+  p.norm_eps = a.eps;
+  p.arg_val = a.arg_val;
+  p.arg_idx = a.arg_idx;
+  p.arg_count = a.arg_count;
+  const int per_pass = w8::tokens_per_pass(p);
+  RXLA_REQUIRE(per_pass > 0, "norm linear: k too large for the resident x");
+  const size_t ye = p.y_f32 ? 4 : 2;
+  for (int64_t m0 = 0; m0 < a.m; m0 += per_pass) {
+    p.m = (int32_t)std::min<int64_t>(per_pass, a.m - m0);
+    p.x = a.h + m0 * a.k;
+    p.y = a.y ? static_cast<uint8_t*>(a.y) + m0 * a.n * ye : nullptr;
+    p.arg_out = a.arg_out ? a.arg_out + m0 : nullptr;
+    p.arg_advance = a.arg_advance ? a.arg_advance + m0 : nullptr;
+    cudaError_t e = w8::launch_skinny(p, w8::kXNorm, w8::grid_for(p), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "norm linear launch");
+  }
+  return RXLA_B200_OK;
+}
+
+static_assert(kArgmaxEpilogue == w8::kEpiArgmax, "argmax epilogue code");
 
 }  // namespace rxla
 
@@ -489,12 +733,13 @@ extern "C" int32_t rxla_b200_w8a16_linear(const void* x, int32_t x_dtype, const 
   const int per_pass = w8::tokens_per_pass(p);
   const bool fast = aligned && (k % 64 == 0) && (p.groups == 1 || group_size % 64 == 0) &&
                     per_pass > 0;
+  const int xmode = p.x_f32 ? w8::kXF32 : w8::kXBf16;
   const int64_t step = fast ? per_pass : 32;
   for (int64_t m0 = 0; m0 < m; m0 += step) {
     p.m = (int32_t)std::min<int64_t>(step, m - m0);
     p.x = static_cast<const uint8_t*>(x) + m0 * k * xe;
     p.y = static_cast<uint8_t*>(y) + m0 * n * ye;
-    int32_t st = w8_linear_pass(p, fast, static_cast<cudaStream_t>(stream));
+    int32_t st = w8_linear_pass(p, fast, xmode, static_cast<cudaStream_t>(stream));
     if (st != RXLA_B200_OK) return st;
   }
   return RXLA_B200_OK;

@@ -76,6 +76,17 @@ def test_grouped_scales(cuda, group):
     _check(_run(x, w, s, group), x, w, s, group)
 
 
+@pytest.mark.parametrize("lo,hi", [(0.02, 0.2), (1e-30, 1e-20), (0.5, 40.0)])
+def test_scale_ranges(cuda, lo, hi):
+    """Scales at and beyond the kernel's fast dequant range (s >= 2^-5 takes the
+    power-of-two fixup path) and tiny scales stay bit-faithful to the reference."""
+    x, w, _ = _case(3, 256, 1024, 1024, seed=int(lo * 1000) + 5)
+    s = oracle.uniform(256 * 2, 8, lo, hi).reshape(256, 2)
+    _check(_run(x, w, s, 512), x, w, s, 512)
+    s1 = s[:, :1].copy()
+    _check(_run(x, w, s1, 1024), x, w, s1, 1024)
+
+
 @pytest.mark.parametrize("n,k,group", [(37, 48, 16), (5, 64, 32), (1, 64, 64), (3, 1000, 8)])
 def test_odd_shapes_generic_path(cuda, n, k, group):
     """Shapes off the fast path (K % 64 != 0, small groups) use the generic kernel."""

@@ -113,8 +113,10 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
     out = torch.empty(1, 8 * 64, dtype=torch.bfloat16, device=dev)
     one = torch.ones(64, device=dev)
     a = _args(c, cache, qkv, out, one, one, torch.ones(32, device=dev))
-    a.batch, a.max_context = 256, 1 << 20  # workspace far above the built-in scratch
+    a.batch = 16384  # split partials of 16384 sequences: far above the built-in scratch
     lib = _lib.load()
+    need = nn.paged_decode_workspace_size(16384, 8, 2, 64, a.max_context)
+    assert need > _lib.NOALLOC_SCRATCH_BYTES
     st = lib.rxla_b200_paged_decode_attention_noalloc(ctypes.byref(a), None)
     assert st == _lib.OUT_OF_RANGE
     assert b"scratch" in lib.rxla_b200_last_error_message()
