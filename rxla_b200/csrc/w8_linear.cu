@@ -104,43 +104,60 @@ static_assert(sizeof(Bars) <= kHeader, "header");
 
 // Row constants of the exact dequantization below: sbig = s·2^133 and
 // c = -128·s, both exact while s < 2^-5 (larger scales are pre-divided by a
-// power of two and the product multiplied back: `post`).
+// power of two and the product multiplied back: `post`).  Each constant is
+// held twice, as the f32x2 operand of the packed FMA.
 struct RowScale {
-  float sbig, c, post;
+  uint64_t sbig, c, post;
 };
 
+__device__ __forceinline__ uint64_t dup_f32(float v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
+  return r;
+}
+
 __device__ __forceinline__ RowScale row_scale(float s) {
-  RowScale r;
-  r.post = 1.0f;
+  float post = 1.0f;
   if (!(fabsf(s) < 0.03125f) && s == s && fabsf(s) < INFINITY) {
     const int e = ((__float_as_int(s) >> 23) & 0xff) - 127;  // s in [2^e, 2^(e+1))
     const int k = e + 6;                                     // s·2^-k < 2^-5
     s = s * __int_as_float((127 - k) << 23);
-    r.post = __int_as_float((127 + k) << 23);
+    post = __int_as_float((127 + k) << 23);
   }
-  r.c = -128.0f * s;
-  r.sbig = (s * 0x1p100f) * 0x1p33f;  // s·2^133 (exact: two power-of-two steps)
+  RowScale r;
+  r.c = dup_f32(-128.0f * s);
+  r.sbig = dup_f32((s * 0x1p100f) * 0x1p33f);  // s·2^133 (exact: two power-of-two steps)
+  r.post = dup_f32(post);
   return r;
+}
+
+__device__ __forceinline__ bool needs_post(const RowScale& r) {
+  return r.post != 0x3f8000003f800000ull;  // post != 1
 }
 
 // Four u8 weights of one row (value b, q = b - 128) -> two bf16x2 registers of
 // bf16(f32(q)·s), the reference's rounding: lo = (w0, w1), hi = (w2, w3).
-// PRMT places b in the mantissa of a denormal (b·2^-133, exact);
-// fma(b·2^-133, s·2^133, -128·s) rounds (b - 128)·s once, as f32(q)·s does.
+// PRMT places b in the mantissa of a denormal (b·2^-133, exact); the packed
+// fma(b·2^-133, s·2^133, -128·s) rounds (b - 128)·s once, as f32(q)·s does
+// (denormal operands are kept: no .ftz).
 template <bool POST>
 __device__ __forceinline__ void deq4(uint32_t w, const RowScale& r, uint32_t& lo, uint32_t& hi) {
-  float p0 = fmaf(__uint_as_float(__byte_perm(w, 0u, 0x4044u)), r.sbig, r.c);
-  float p1 = fmaf(__uint_as_float(__byte_perm(w, 0u, 0x4144u)), r.sbig, r.c);
-  float p2 = fmaf(__uint_as_float(__byte_perm(w, 0u, 0x4244u)), r.sbig, r.c);
-  float p3 = fmaf(__uint_as_float(__byte_perm(w, 0u, 0x4344u)), r.sbig, r.c);
+  uint64_t a01, a23, p01, p23;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a01) : "r"(__byte_perm(w, 0u, 0x4044u)),
+      "r"(__byte_perm(w, 0u, 0x4144u)));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a23) : "r"(__byte_perm(w, 0u, 0x4244u)),
+      "r"(__byte_perm(w, 0u, 0x4344u)));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p01) : "l"(a01), "l"(r.sbig), "l"(r.c));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p23) : "l"(a23), "l"(r.sbig), "l"(r.c));
   if (POST) {
-    p0 *= r.post;
-    p1 *= r.post;
-    p2 *= r.post;
-    p3 *= r.post;
+    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(p01) : "l"(r.post));
+    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(p23) : "l"(r.post));
   }
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(p1), "f"(p0));
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(p3), "f"(p2));
+  float f0, f1, f2, f3;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(f0), "=f"(f1) : "l"(p01));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(f2), "=f"(f3) : "l"(p23));
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(f1), "f"(f0));
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(f3), "f"(f2));
 }
 
 // Bounded barrier among the 16 consumer warps (one arrival per warp).
@@ -151,21 +168,15 @@ __device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t parity) {
 }
 
 // One 64-column box of a 16-row tile: 16 B of rows g and g+8 per lane, the
-// lane's 16 x values, four k-steps of m16n8k16.
+// lane's 16 x values, four k-steps of m16n8k16.  Lanes whose token column is
+// beyond the batch read a real token's x: those output columns are ignored.
 template <bool POST>
 __device__ __forceinline__ void box_mma(float (&acc)[4], const uint8_t* stage, int kc_stride,
-                                        int lcol, const uint8_t* xcol, bool has_tok, int g,
+                                        int lcol, const uint8_t* xcol, int g,
                                         const RowScale& ra, const RowScale& rb) {
-  uint32_t bx[8];
-  if (has_tok) {
-    const uint4 v0 = *reinterpret_cast<const uint4*>(xcol);
-    const uint4 v1 = *reinterpret_cast<const uint4*>(xcol + 16);
-    bx[0] = v0.x; bx[1] = v0.y; bx[2] = v0.z; bx[3] = v0.w;
-    bx[4] = v1.x; bx[5] = v1.y; bx[6] = v1.z; bx[7] = v1.w;
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) bx[j] = 0u;
-  }
+  const uint4 v0 = *reinterpret_cast<const uint4*>(xcol);
+  const uint4 v1 = *reinterpret_cast<const uint4*>(xcol + 16);
+  const uint32_t bx[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
   const uint4 lo = *reinterpret_cast<const uint4*>(stage + g * kc_stride + lcol);
   const uint4 hi = *reinterpret_cast<const uint4*>(stage + (g + 8) * kc_stride + lcol);
   const uint32_t wl[4] = {lo.x, lo.y, lo.z, lo.w};
@@ -424,16 +435,12 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     }
     if (!consumer_sync(&bars.grp[1], 0)) return;
   }
-  const bool has_tok = g < p.m;
-  const uint8_t* xrow = xs + g * p.x_pitch;
+  const uint8_t* xrow = xs + (g % p.m) * p.x_pitch;
 
-  int it = 0;
-  for (int blk = 0; blk < n_blocks; ++blk) {
+  // weight rows of this lane's A fragment in block blk: tile rows g and g + 8
+  auto block_rows = [&](int blk, bool& va, bool& vb, int& ra, int& rb) {
     const int r0 = r_begin + blk * out_rows;
     const int nr = min(out_rows, r_end - r0);
-    // weight rows of this lane's A fragment: tile rows g and g + 8
-    bool va, vb;
-    int ra, rb;
     if (SWIGLU) {
       va = vb = g < nr;
       ra = r0 + g;
@@ -444,14 +451,38 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       ra = r0 + g;
       rb = r0 + g + 8;
     }
+  };
+  // per-channel scales are loaded one block ahead, so their latency hides
+  // behind the current block's tiles
+  float next_sa = 0.0f, next_sb = 0.0f;
+  if (!GROUPED && n_blocks > 0) {
+    bool va, vb;
+    int ra, rb;
+    block_rows(0, va, vb, ra, rb);
+    next_sa = va ? __ldg(p.scale + ra) : 0.0f;
+    next_sb = vb ? __ldg(p.scale + rb) : 0.0f;
+  }
+
+  int it = 0;
+  for (int blk = 0; blk < n_blocks; ++blk) {
+    bool va, vb;
+    int ra, rb;
+    block_rows(blk, va, vb, ra, rb);
     const float* sa = p.scale + (int64_t)ra * p.groups;
     const float* sb = p.scale + (int64_t)rb * p.groups;
     RowScale rsa = row_scale(0.0f), rsb = row_scale(0.0f);
     bool post = false;  // warp-uniform: some row's scale needs the power-of-two fixup
     if (!GROUPED) {
-      rsa = row_scale(va ? __ldg(sa) : 0.0f);
-      rsb = row_scale(vb ? __ldg(sb) : 0.0f);
-      post = __any_sync(0xffffffffu, rsa.post != 1.0f || rsb.post != 1.0f);
+      rsa = row_scale(next_sa);
+      rsb = row_scale(next_sb);
+      post = __any_sync(0xffffffffu, needs_post(rsa) || needs_post(rsb));
+      if (blk + 1 < n_blocks) {
+        bool na, nb;
+        int rna, rnb;
+        block_rows(blk + 1, na, nb, rna, rnb);
+        next_sa = na ? __ldg(p.scale + rna) : 0.0f;
+        next_sb = nb ? __ldg(p.scale + rnb) : 0.0f;
+      }
     }
     float acc0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     float acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -473,15 +504,15 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
           b0 = row_scale(vb ? __ldg(sb + g0) : 0.0f);
           a1 = row_scale(va ? __ldg(sa + g1) : 0.0f);
           b1 = row_scale(vb ? __ldg(sb + g1) : 0.0f);
-          pst = __any_sync(0xffffffffu, a0.post != 1.0f || b0.post != 1.0f ||
-                                            a1.post != 1.0f || b1.post != 1.0f);
+          pst = __any_sync(0xffffffffu, needs_post(a0) || needs_post(b0) ||
+                                            needs_post(a1) || needs_post(b1));
         }
         if (pst) {
-          box_mma<true>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, has_tok, g, a0, b0);
-          box_mma<true>(acc1, stage, p.kc, l1, xrow + (col0 + l1) * 2, has_tok, g, a1, b1);
+          box_mma<true>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, g, a0, b0);
+          box_mma<true>(acc1, stage, p.kc, l1, xrow + (col0 + l1) * 2, g, a1, b1);
         } else {
-          box_mma<false>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, has_tok, g, a0, b0);
-          box_mma<false>(acc1, stage, p.kc, l1, xrow + (col0 + l1) * 2, has_tok, g, a1, b1);
+          box_mma<false>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, g, a0, b0);
+          box_mma<false>(acc1, stage, p.kc, l1, xrow + (col0 + l1) * 2, g, a1, b1);
         }
       }
       if (box < nbox) {
@@ -492,10 +523,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
           const int g0 = (col0 + l0) / p.group_size;
           a0 = row_scale(va ? __ldg(sa + g0) : 0.0f);
           b0 = row_scale(vb ? __ldg(sb + g0) : 0.0f);
-          pst = __any_sync(0xffffffffu, a0.post != 1.0f || b0.post != 1.0f);
+          pst = __any_sync(0xffffffffu, needs_post(a0) || needs_post(b0));
         }
-        if (pst) box_mma<true>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, has_tok, g, a0, b0);
-        else box_mma<false>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, has_tok, g, a0, b0);
+        if (pst) box_mma<true>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, g, a0, b0);
+        else box_mma<false>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, g, a0, b0);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.empty[s]);

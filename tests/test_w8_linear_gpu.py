@@ -87,6 +87,35 @@ def test_scale_ranges(cuda, lo, hi):
     _check(_run(x, w, s1, 1024), x, w, s1, 1024)
 
 
+@pytest.mark.parametrize("group", [1024, 64])
+def test_dequant_bit_exact(cuda, group):
+    """One-hot x rows read single dequantized weights through the unrounded f32
+    output: y[t, n] = bf16(f32(q - 128) · s) exactly, for every byte value and
+    scales from 1e-36 to 1e3, negative and zero (the kernel's packed
+    denormal-FMA dequantization against the reference's convert / subtract /
+    multiply / convert chain).  Zeros compare without their sign: a dot
+    product's sum of zero terms is +0."""
+    m, n, k = 8, 512, 1024
+    cols = np.array([0, 65, 130, 300, 511, 640, 900, 1023])
+    x = np.zeros((m, k), np.float32)
+    x[np.arange(m), cols] = 1.0
+    rows = np.arange(n)
+    w = np.zeros((n, k), np.uint8)
+    for t, c in enumerate(cols):
+        w[:, c] = (rows + 37 * t) % 256  # every byte value twice per column
+    groups = k // group
+    expo = oracle.uniform(n * groups, 31, -36.0, 3.0).reshape(n, groups)
+    s = (10.0 ** expo).astype(np.float32)
+    s[::7] *= -1.0
+    s[5::11] = 0.0
+    s[3::13] = 2.0 ** np.round(expo[3::13] * 3.3)  # exact powers of two
+    y = _run(x, w, s, group, out_dtype=torch.float32)
+    sg = np.repeat(s, group, axis=1)
+    wd = oracle.bf16_round(((w.astype(np.float32) - np.float32(128.0)) * sg).astype(np.float32))
+    expect = wd[:, cols].T.astype(np.float32) + np.float32(0.0)  # -0 -> +0
+    np.testing.assert_array_equal((y + np.float32(0.0)).view(np.uint32), expect.view(np.uint32))
+
+
 @pytest.mark.parametrize("n,k,group", [(37, 48, 16), (5, 64, 32), (1, 64, 64), (3, 1000, 8)])
 def test_odd_shapes_generic_path(cuda, n, k, group):
     """Shapes off the fast path (K % 64 != 0, small groups) use the generic kernel."""
