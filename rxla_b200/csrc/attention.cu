@@ -74,7 +74,8 @@ struct Params {
   int32_t batch;
   int32_t ctx_stable;    // ctx_lens is not written by the previous kernel: prefetch early
   int32_t stages;
-  int32_t stage_bytes;  // K + V of one page, all kv heads
+  int32_t stage_bytes;  // K + V of one page of one kv head
+  L2Prefetch next;      // the following kernel's first bytes
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
@@ -192,8 +193,13 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32)
   const int slot = pos < 0 ? 0 : (pos >= cap ? cap - 1 : pos);
   const bool owner = accept && split == (slot / kPage) / p.pps;
 
+  const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int ctas = gridDim.x * gridDim.y * gridDim.z;
   if (split >= n_splits) {  // nothing of this sequence in this split (exit = trigger)
-    if (threadIdx.x == 0) finish_cta(p);
+    if (threadIdx.x == 0) {
+      if (p.next.nseg > 0) l2_prefetch_share(p.next, cta, ctas);
+      finish_cta(p);
+    }
     return;
   }
 
@@ -225,6 +231,8 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32)
           tma_load_2d(kdst + kTile + j * kPage * 128, &vmap, 64 * j, row, &full[s]);
         }
       }
+      // pages are all requested: pull the next kernel's first bytes into L2
+      if (p.next.nseg > 0) l2_prefetch_share(p.next, cta, ctas);
     }
   } else {
     // ------------------------------------------------------- compute warps
@@ -632,7 +640,8 @@ namespace attn {
 // of ctx_lens and this one may still be running, so pages can be fetched
 // before griddepcontrol.wait (the decoder runner advances ctx_lens only at
 // the end of a step).
-int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx_stable) {
+int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx_stable,
+               const L2Prefetch* next) {
   RXLA_REQUIRE(a && a->struct_size >= sizeof(rxla_b200_paged_decode_args),
                "paged_decode: args struct missing or too small");
   const int D = a->head_dim;
@@ -709,6 +718,7 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   p.batch = a->batch;
   p.ctx_stable = ctx_stable ? 1 : 0;
   p.stages = attn::kStagesV2;
+  if (next) p.next = *next;
 
   CUtensorMap kmap, vmap;
   int32_t st = attn::make_page_map(&kmap, a->k_pages, a->num_pages, a->kv_heads, D);

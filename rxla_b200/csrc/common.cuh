@@ -164,6 +164,37 @@ __device__ __forceinline__ void bulk_g2s_nohint(void* dst, const void* src, uint
       : "memory");
 }
 
+// Bytes the NEXT kernel of a chain will read first (up to two contiguous
+// segments, e.g. the gate and up halves of a fused weight).  A kernel that is
+// done issuing its own loads pulls its share of them into L2, so the HBM
+// stays busy while it drains and the next kernel's first tiles hit in L2.
+struct L2Prefetch {
+  const void* seg[2];
+  int64_t bytes[2];
+  int32_t nseg;
+  int32_t per_cta;  // bytes per CTA over all segments
+};
+
+// CTA `cta` of `ctas` prefetches the start of its proportional share of each
+// segment (the next kernel partitions its rows the same way).  One thread.
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int cta, int ctas) {
+  for (int i = 0; i < pf.nseg && i < 2; ++i) {
+    const int64_t total = pf.bytes[i];
+    if (!pf.seg[i] || total <= 0) continue;
+    int64_t start = (total * cta) / ctas;
+    int64_t end = (total * (cta + 1)) / ctas;
+    end = min(end, start + (int64_t)(pf.per_cta / pf.nseg));
+    start &= ~(int64_t)15;
+    end &= ~(int64_t)15;
+    const uint8_t* base = static_cast<const uint8_t*>(pf.seg[i]);
+    for (int64_t off = start; off < end; off += 32768) {
+      const uint32_t len = (uint32_t)min((int64_t)32768, end - off);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"(len)
+                   : "memory");
+    }
+  }
+}
+
 // Programmatic dependent launch: wait for the previous grid's results, and
 // allow the next grid to start its prologue.  Every kernel of this library
 // triggers its dependents only after its own griddepcontrol.wait, so when a

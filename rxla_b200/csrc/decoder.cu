@@ -90,11 +90,39 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const uint8_t* 
   pdl_launch_dependents();
   int64_t t = tokens[blockIdx.x];
   t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+  float* out = h + blockIdx.x * hidden;
+  // 16 consecutive elements per thread, loaded before any is used (the row
+  // is a single round trip for hidden <= 16 * blockDim)
+  const bool vec = hidden % 16 == 0 && group % 16 == 0 &&
+                   (reinterpret_cast<uintptr_t>(w8 ? (const void*)w8 : (const void*)wb) % 16) == 0;
+  if (vec) {
+    for (int64_t j0 = threadIdx.x * 16; j0 < hidden; j0 += blockDim.x * 16) {
+      float v[16];
+      if (w8) {
+        const uint4 q = *reinterpret_cast<const uint4*>(w8 + t * hidden + j0);
+        const float sc = scale[t * groups + j0 / group];
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          v[i] = (float)((int)((qw[i >> 2] >> (8 * (i & 3))) & 0xffu) - 128) * sc;
+      } else {
+        const uint4 a = *reinterpret_cast<const uint4*>(wb + t * hidden + j0);
+        const uint4 b = *reinterpret_cast<const uint4*>(wb + t * hidden + j0 + 8);
+        const uint32_t bw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = (i & 1) ? bf16_hi(bw[i >> 1]) : bf16_lo(bw[i >> 1]);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; i += 4)
+        *reinterpret_cast<float4*>(out + j0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    }
+    return;
+  }
   for (int64_t j = threadIdx.x; j < hidden; j += blockDim.x) {
     float v;
     if (w8) v = (float)((int)w8[t * hidden + j] - 128) * scale[t * groups + j / group];
     else v = __bfloat162float(wb[t * hidden + j]);
-    h[blockIdx.x * hidden + j] = v;
+    out[j] = v;
   }
 }
 
@@ -197,8 +225,27 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
   if (e != cudaSuccess) return cuda_fail(e, "embed launch");
   const bool tp = c.tp_size > 1;
   const int64_t qd = (int64_t)d->hq * D, kd = (int64_t)d->hkv * D;
+  // each kernel pulls the start of the next weight matrix into L2 while it drains
+  auto pf = [](const void* w, int64_t bytes, int32_t per_cta) {
+    L2Prefetch f{};
+    f.seg[0] = w;
+    f.bytes[0] = bytes;
+    f.nseg = 1;
+    f.per_cta = per_cta;
+    return f;
+  };
+  constexpr int32_t kRingShare = 192 * 1024;
   for (int l = 0; l < c.layers; ++l) {
     const Layer& L = d->layers[l];
+    const L2Prefetch to_o = pf(L.wo, H * qd, 256 * 1024);
+    L2Prefetch to_gu = pf(L.wgu, d->inter * H, kRingShare);
+    to_gu.seg[1] = L.wgu + d->inter * H;
+    to_gu.bytes[1] = d->inter * H;
+    to_gu.nseg = 2;
+    const L2Prefetch to_down = pf(L.wd, H * d->inter, kRingShare);
+    const L2Prefetch to_next =
+        l + 1 < c.layers ? pf(d->layers[l + 1].wqkv, d->qkv_rows * H, kRingShare)
+                         : (d->emb_w8 ? pf(d->emb_w8, d->vocab * H, kRingShare) : L2Prefetch{});
     // qkv = W8(bf16(rms_norm(h) * input_layernorm)), the norm fused in the prologue
     NormLinearArgs na{};
     na.h = d->h;
@@ -213,6 +260,7 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
     na.y = d->qkv;
     na.y_dtype = RXLA_B200_BF16;
     na.epilogue = RXLA_B200_EPI_STORE;
+    na.next = to_o;
     int32_t st = w8_norm_linear(na, s);
     if (st) return st;
     rxla_b200_paged_decode_args a{};
@@ -247,11 +295,11 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
     a.workspace = d->ws;
     a.workspace_bytes = d->ws_bytes;
     a.max_context = c.max_context;
-    st = attn::launch(&a, s, true);
+    st = attn::launch(&a, s, true, &to_o);
     if (st) return st;
     if (!tp) {
-      st = rxla_b200_w8a16_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd,
-                                  d->h, RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s);
+      st = w8_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd, d->h,
+                     RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s, &to_gu);
       if (st) return st;
     } else {
       st = rxla_b200_w8a16_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd,
@@ -270,11 +318,12 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
     na.n = d->inter;
     na.y = d->act;
     na.epilogue = RXLA_B200_EPI_SWIGLU;
+    na.next = to_down;
     st = w8_norm_linear(na, s);
     if (st) return st;
     if (!tp) {
-      st = rxla_b200_w8a16_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H,
-                                  d->inter, d->h, RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s);
+      st = w8_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H, d->inter, d->h,
+                     RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s, &to_next);
       if (st) return st;
     } else {
       st = rxla_b200_w8a16_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H,
@@ -309,6 +358,12 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
     na.arg_count = d->arg_count;
     na.arg_out = d->tok_out;
     na.arg_advance = d->ctx;
+    if (c.layers > 0) {  // the next step starts with layer 0's qkv
+      na.next.seg[0] = d->layers[0].wqkv;
+      na.next.bytes[0] = d->qkv_rows * H;
+      na.next.nseg = 1;
+      na.next.per_cta = kRingShare;
+    }
     return w8_norm_linear(na, s);
   }
   int32_t st = rxla_b200_rms_norm_bf16(d->h, d->final_norm, batch, H, c.rms_eps, d->xn, s);

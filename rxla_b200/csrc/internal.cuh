@@ -24,15 +24,21 @@ struct NormLinearArgs {
   uint32_t* arg_count;
   int32_t* arg_out;
   int32_t* arg_advance;
+  L2Prefetch next;  // what the following kernel reads first (nseg = 0: none)
 };
 
 constexpr int kArgmaxEpilogue = 16;
 
 int32_t w8_norm_linear(const NormLinearArgs& a, cudaStream_t stream);
+// rxla_b200_w8a16_linear with an L2 prefetch of the next kernel's first bytes
+int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const float* scale,
+                  int64_t group_size, int64_t m, int64_t n, int64_t k, void* y, int32_t y_dtype,
+                  int32_t epilogue, cudaStream_t stream, const L2Prefetch* next);
 int32_t comm_allreduce_f32(rxla_b200_comm* comm, float* buf, int64_t count, cudaStream_t s);
 
 namespace attn {
-int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable);
+int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable,
+               const L2Prefetch* next = nullptr);
 }
 
 }  // namespace rxla

@@ -89,6 +89,7 @@ struct Params {
   int32_t stages;       // ring depth
   int32_t x_pitch;      // bytes of one resident bf16 token row of x
   int32_t stage_bytes;  // 16 rows × kc
+  L2Prefetch next;      // the following kernel's first bytes (last pass only)
 };
 
 struct Bars {
@@ -96,6 +97,7 @@ struct Bars {
   uint64_t empty[kMaxStages];
   uint64_t x_full;
   uint64_t grp[2];
+  uint64_t ss_free;  // norm: every warp has read a round's sums
   uint64_t epi_full[2];
   uint64_t epi_free[2];
   float ss[kConsumerWarps][kMaxTokens];  // norm: per-warp sums of squares
@@ -218,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     mbar_init(&bars.x_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars.grp[i], kConsumerWarps);
+      if (i == 0) mbar_init(&bars.ss_free, kConsumerWarps);
       mbar_init(&bars.epi_full[i], kConsumerWarps);
       mbar_init(&bars.epi_free[i], 1);
     }
@@ -272,6 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       if (!mbar_wait(&bars.empty[s], ((it / S) - 1) & 1)) return;
       issue(it, s);
     }
+    // own loads are all issued: pull the next kernel's first bytes into L2
+    if (lane == 0 && p.next.nseg > 0) l2_prefetch_share(p.next, blockIdx.x, gridDim.x);
     return;
   }
 
@@ -290,14 +295,26 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       best_v[t] = -INFINITY;
       best_i[t] = 0x7fffffff;
     }
+    constexpr int kPerLane = (out_rows * kMaxTokens) / 32;
     for (int blk = 0; blk < n_blocks; ++blk) {
       const int b2 = blk & 1;
-      if (!mbar_wait(&bars.epi_full[b2], (blk >> 1) & 1)) return;
       const int r0 = r_begin + blk * out_rows;
       const int nr = min(out_rows, r_end - r0);
+      // the residual this block adds into is read before its partials are
+      // waited for, so the load overlaps the consumers' tiles
+      float resid[kPerLane];
+#pragma unroll
+      for (int tt = 0; tt < kPerLane; ++tt) {
+        const int idx = lane + 32 * tt;
+        const int row = idx % out_rows, tok = idx / out_rows;
+        resid[tt] = (!SWIGLU && p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD && row < nr && tok < p.m)
+                        ? static_cast<const float*>(p.y)[(int64_t)tok * p.ldy + r0 + row]
+                        : 0.0f;
+      }
+      if (!mbar_wait(&bars.epi_full[b2], (blk >> 1) & 1)) return;
       const float* rb = red + b2 * kRedFloats;
 #pragma unroll
-      for (int tt = 0; tt < (out_rows * kMaxTokens) / 32; ++tt) {
+      for (int tt = 0; tt < kPerLane; ++tt) {
         const int idx = lane + 32 * tt;
         const int row = idx % out_rows, tok = idx / out_rows;
         if (row >= nr || tok >= p.m) continue;
@@ -322,8 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
               best_i[t] = out_col;
             }
         } else if (p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD) {
-          float* yy = static_cast<float*>(p.y);
-          yy[o] = yy[o] + bf16_round(v);
+          static_cast<float*>(p.y)[o] = resid[tt] + bf16_round(v);
         } else if (p.y_f32) {
           static_cast<float*>(p.y)[o] = v;
         } else {
@@ -353,25 +369,40 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
           p.arg_idx[blockIdx.x * kMaxTokens + t] = best_i[t];
         }
         __threadfence();
-        const uint32_t prev = atomicAdd(p.arg_count, 1u);
-        if (prev == gridDim.x - 1) {
-          __threadfence();
-          for (int t = 0; t < p.m; ++t) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-            for (int c = 0; c < (int)gridDim.x; ++c) {
-              const float v = __ldcg(p.arg_val + c * kMaxTokens + t);
-              const int i = __ldcg(p.arg_idx + c * kMaxTokens + t);
-              if (v > bv || (v == bv && i < bi)) {
-                bv = v;
-                bi = i;
-              }
+      }
+      uint32_t prev = 0;
+      if (lane == 0) prev = atomicAdd(p.arg_count, 1u);
+      prev = __shfl_sync(0xffffffffu, prev, 0);
+      if (prev == gridDim.x - 1) {
+        // the last CTA picks each row's token from all CTAs' partials: the
+        // lanes scan CTAs in parallel, then (value desc, index asc) reduce
+        __threadfence();
+        for (int t = 0; t < p.m; ++t) {
+          float bv = -INFINITY;
+          int bi = 0x7fffffff;
+          for (int c = lane; c < (int)gridDim.x; c += 32) {
+            const float v = __ldcg(p.arg_val + c * kMaxTokens + t);
+            const int i = __ldcg(p.arg_idx + c * kMaxTokens + t);
+            if (v > bv || (v == bv && i < bi)) {
+              bv = v;
+              bi = i;
             }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+              bv = ov;
+              bi = oi;
+            }
+          }
+          if (lane == 0) {
             p.arg_out[t] = bi == 0x7fffffff ? 0 : bi;
             if (p.arg_advance) p.arg_advance[t] += 1;
           }
-          *p.arg_count = 0u;
         }
+        if (lane == 0) *p.arg_count = 0u;
       }
     }
     return;
@@ -384,53 +415,106 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
   } else {
     pdl_wait();  // x / h come from the previous kernel
     const float* xf = static_cast<const float*>(p.x);
-    float inv[kMaxTokens];
+    // This runs between the previous kernel and the first tile, so every
+    // global load of a token is issued before any is used: one round trip per
+    // two tokens (each consumer thread holds kXV float4 of a row; larger k
+    // falls back to a strided loop).
+    constexpr int kXV = 4;
+    constexpr int kCT = kConsumerWarps * 32;
+    const bool regs = p.k <= kXV * 4 * kCT;
+    float4 nw[kXV];
 #pragma unroll
-    for (int t = 0; t < kMaxTokens; ++t) inv[t] = 1.0f;
-    if (XMODE == kXNorm) {
-      // sum of squares per token: threads stride over k, then warps, then CTA
-      float ss[kMaxTokens];
-#pragma unroll
-      for (int t = 0; t < kMaxTokens; ++t) {
-        float v = 0.0f;
-        if (t < p.m) {
-          const float* row = xf + (int64_t)t * p.ldx;
-          for (int c = ctid * 4; c < p.k; c += kConsumerWarps * 32 * 4) {
-            const float4 h = __ldg(reinterpret_cast<const float4*>(row + c));
-            v += h.x * h.x + h.y * h.y + h.z * h.z + h.w * h.w;
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        }
-        ss[t] = v;
-      }
-      if (lane == 0)
-#pragma unroll
-        for (int t = 0; t < kMaxTokens; ++t) bars.ss[warp][t] = ss[t];
-      if (!consumer_sync(&bars.grp[0], 0)) return;
-#pragma unroll
-      for (int t = 0; t < kMaxTokens; ++t) {
-        float tot = 0.0f;
-        for (int w2 = 0; w2 < kConsumerWarps; ++w2) tot += bars.ss[w2][t];
-        inv[t] = 1.0f / sqrtf(tot / (float)p.k + p.norm_eps);
-      }
+    for (int i = 0; i < kXV; ++i) {
+      const int c = (ctid + i * kCT) * 4;
+      nw[i] = (XMODE == kXNorm && regs && c < p.k)
+                  ? __ldg(reinterpret_cast<const float4*>(p.norm_w + c))
+                  : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
     }
-    for (int t = 0; t < p.m; ++t) {
-      const float* row = xf + (int64_t)t * p.ldx;
-      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(xs + t * p.x_pitch);
-      for (int c = ctid * 4; c < p.k; c += kConsumerWarps * 32 * 4) {
-        float4 h = __ldg(reinterpret_cast<const float4*>(row + c));
-        if (XMODE == kXNorm) {
-          const float4 nw = __ldg(reinterpret_cast<const float4*>(p.norm_w + c));
-          h.x = (h.x * inv[t]) * nw.x;
-          h.y = (h.y * inv[t]) * nw.y;
-          h.z = (h.z * inv[t]) * nw.z;
-          h.w = (h.w * inv[t]) * nw.w;
+    int round = 0;
+    for (int t0 = 0; t0 < p.m; t0 += 2, ++round) {
+      const int nt = min(2, p.m - t0);
+      float4 hv[2][kXV];
+      float ss[2] = {0.0f, 0.0f};
+      if (regs) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int i = 0; i < kXV; ++i) {
+            const int c = (ctid + i * kCT) * 4;
+            hv[u][i] = (u < nt && c < p.k)
+                           ? __ldg(reinterpret_cast<const float4*>(xf + (int64_t)(t0 + u) * p.ldx + c))
+                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            ss[u] += hv[u][i].x * hv[u][i].x + hv[u][i].y * hv[u][i].y +
+                     hv[u][i].z * hv[u][i].z + hv[u][i].w * hv[u][i].w;
+          }
+      } else if (XMODE == kXNorm) {
+        for (int u = 0; u < nt; ++u) {
+          const float* row = xf + (int64_t)(t0 + u) * p.ldx;
+          for (int c = ctid * 4; c < p.k; c += kCT * 4) {
+            const float4 h = __ldg(reinterpret_cast<const float4*>(row + c));
+            ss[u] += h.x * h.x + h.y * h.y + h.z * h.z + h.w * h.w;
+          }
         }
-        uint2 pk;
-        pk.x = pack_bf16x2(h.x, h.y);
-        pk.y = pack_bf16x2(h.z, h.w);
-        *reinterpret_cast<uint2*>(out + c) = pk;
+      }
+      float inv[2] = {1.0f, 1.0f};
+      if (XMODE == kXNorm) {
+        // sum of squares per token: threads, then warps, then the CTA
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
+        }
+        if (lane == 0) {
+          bars.ss[warp][0] = ss[0];
+          bars.ss[warp][1] = ss[1];
+        }
+        if (!consumer_sync(&bars.grp[0], round & 1)) return;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          float tot = 0.0f;
+          for (int w2 = 0; w2 < kConsumerWarps; ++w2) tot += bars.ss[w2][u];
+          inv[u] = 1.0f / sqrtf(tot / (float)p.k + p.norm_eps);
+        }
+        // every warp has read the sums before the next round overwrites them
+        if (t0 + 2 < p.m && !consumer_sync(&bars.ss_free, round & 1)) return;
+      }
+      for (int u = 0; u < nt; ++u) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(xs + (t0 + u) * p.x_pitch);
+        if (regs) {
+#pragma unroll
+          for (int i = 0; i < kXV; ++i) {
+            const int c = (ctid + i * kCT) * 4;
+            if (c < p.k) {
+              float4 h = hv[u][i];
+              if (XMODE == kXNorm) {
+                h.x = (h.x * inv[u]) * nw[i].x;
+                h.y = (h.y * inv[u]) * nw[i].y;
+                h.z = (h.z * inv[u]) * nw[i].z;
+                h.w = (h.w * inv[u]) * nw[i].w;
+              }
+              uint2 pk;
+              pk.x = pack_bf16x2(h.x, h.y);
+              pk.y = pack_bf16x2(h.z, h.w);
+              *reinterpret_cast<uint2*>(out + c) = pk;
+            }
+          }
+        } else {
+          const float* row = xf + (int64_t)(t0 + u) * p.ldx;
+          for (int c = ctid * 4; c < p.k; c += kCT * 4) {
+            float4 h = __ldg(reinterpret_cast<const float4*>(row + c));
+            if (XMODE == kXNorm) {
+              const float4 w = __ldg(reinterpret_cast<const float4*>(p.norm_w + c));
+              h.x = (h.x * inv[u]) * w.x;
+              h.y = (h.y * inv[u]) * w.y;
+              h.z = (h.z * inv[u]) * w.z;
+              h.w = (h.w * inv[u]) * w.w;
+            }
+            uint2 pk;
+            pk.x = pack_bf16x2(h.x, h.y);
+            pk.y = pack_bf16x2(h.z, h.w);
+            *reinterpret_cast<uint2*>(out + c) = pk;
+          }
+        }
       }
     }
     if (!consumer_sync(&bars.grp[1], 0)) return;
@@ -717,6 +801,7 @@ int32_t w8_norm_linear(const NormLinearArgs& a, cudaStream_t stream) {
     p.y = a.y ? static_cast<uint8_t*>(a.y) + m0 * a.n * ye : nullptr;
     p.arg_out = a.arg_out ? a.arg_out + m0 : nullptr;
     p.arg_advance = a.arg_advance ? a.arg_advance + m0 : nullptr;
+    p.next = m0 + per_pass >= a.m ? a.next : L2Prefetch{};
     cudaError_t e = w8::launch_skinny(p, w8::kXNorm, w8::grid_for(p), stream);
     if (e != cudaSuccess) return cuda_fail(e, "norm linear launch");
   }
@@ -727,11 +812,10 @@ static_assert(kArgmaxEpilogue == w8::kEpiArgmax, "argmax epilogue code");
 
 }  // namespace rxla
 
-extern "C" int32_t rxla_b200_w8a16_linear(const void* x, int32_t x_dtype, const uint8_t* weight,
-                                          const float* scale, int64_t group_size, int64_t m,
-                                          int64_t n, int64_t k, void* y, int32_t y_dtype,
-                                          int32_t epilogue, void* stream) {
-  using namespace rxla;
+namespace rxla {
+int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const float* scale,
+                  int64_t group_size, int64_t m, int64_t n, int64_t k, void* y, int32_t y_dtype,
+                  int32_t epilogue, cudaStream_t stream, const L2Prefetch* next) {
   RXLA_REQUIRE(m >= 0 && n >= 0 && k > 0, "w8a16_linear: m, n must be >= 0 and k > 0");
   RXLA_REQUIRE(group_size > 0 && k % group_size == 0,
                "w8a16_linear: group_size must be positive and divide k (layers.rs:266-275)");
@@ -770,8 +854,18 @@ extern "C" int32_t rxla_b200_w8a16_linear(const void* x, int32_t x_dtype, const 
     p.m = (int32_t)std::min<int64_t>(step, m - m0);
     p.x = static_cast<const uint8_t*>(x) + m0 * k * xe;
     p.y = static_cast<uint8_t*>(y) + m0 * n * ye;
-    int32_t st = w8_linear_pass(p, fast, xmode, static_cast<cudaStream_t>(stream));
+    p.next = (next && m0 + step >= m) ? *next : L2Prefetch{};
+    int32_t st = w8_linear_pass(p, fast, xmode, stream);
     if (st != RXLA_B200_OK) return st;
   }
   return RXLA_B200_OK;
+}
+}  // namespace rxla
+
+extern "C" int32_t rxla_b200_w8a16_linear(const void* x, int32_t x_dtype, const uint8_t* weight,
+                                          const float* scale, int64_t group_size, int64_t m,
+                                          int64_t n, int64_t k, void* y, int32_t y_dtype,
+                                          int32_t epilogue, void* stream) {
+  return rxla::w8_linear(x, x_dtype, weight, scale, group_size, m, n, k, y, y_dtype, epilogue,
+                         static_cast<cudaStream_t>(stream), nullptr);
 }
