@@ -234,7 +234,13 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
     f.per_cta = per_cta;
     return f;
   };
-  constexpr int32_t kRingShare = 192 * 1024;
+  // bytes of the next kernel's weights each CTA pulls into L2 (environment
+  // RXLA_B200_L2_AHEAD_KB overrides the default)
+  static const int32_t kRingShare = [] {
+    const char* v = getenv("RXLA_B200_L2_AHEAD_KB");
+    const long kb = v ? atol(v) : 192;
+    return (int32_t)std::min<long>(std::max<long>(kb, 0), 1 << 20) * 1024;
+  }();
   for (int l = 0; l < c.layers; ++l) {
     const Layer& L = d->layers[l];
     const L2Prefetch to_o = pf(L.wo, H * qd, 256 * 1024);

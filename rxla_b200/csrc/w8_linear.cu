@@ -173,14 +173,14 @@ __device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t parity) {
 // lane's 16 x values, four k-steps of m16n8k16.  Lanes whose token column is
 // beyond the batch read a real token's x: those output columns are ignored.
 template <bool POST>
-__device__ __forceinline__ void box_mma(float (&acc)[4], const uint8_t* stage, int kc_stride,
-                                        int lcol, const uint8_t* xcol, int g,
-                                        const RowScale& ra, const RowScale& rb) {
+__device__ __forceinline__ void box_mma(float (&acc)[4], const uint8_t* wg, int row8,
+                                        const uint8_t* xcol, const RowScale& ra,
+                                        const RowScale& rb) {
   const uint4 v0 = *reinterpret_cast<const uint4*>(xcol);
   const uint4 v1 = *reinterpret_cast<const uint4*>(xcol + 16);
   const uint32_t bx[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-  const uint4 lo = *reinterpret_cast<const uint4*>(stage + g * kc_stride + lcol);
-  const uint4 hi = *reinterpret_cast<const uint4*>(stage + (g + 8) * kc_stride + lcol);
+  const uint4 lo = *reinterpret_cast<const uint4*>(wg);
+  const uint4 hi = *reinterpret_cast<const uint4*>(wg + row8);
   const uint32_t wl[4] = {lo.x, lo.y, lo.z, lo.w};
   const uint32_t wh[4] = {hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
@@ -547,7 +547,14 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     next_sb = vb ? __ldg(p.scale + rb) : 0.0f;
   }
 
-  int it = 0;
+  // ring position, advanced incrementally (no division in the loop)
+  int s = 0;
+  uint32_t ph = 0;
+  // this lane's bytes in a stage: row g of the warp's first box; row g + 8 is
+  // row8 further, and the warp's boxes are kConsumerWarps * 64 bytes apart
+  const int lane_off = g * p.kc + warp * 64 + 16 * q;
+  const int row8 = 8 * p.kc;
+  constexpr int kBoxStep = kConsumerWarps * 64;
   for (int blk = 0; blk < n_blocks; ++blk) {
     bool va, vb;
     int ra, rb;
@@ -570,19 +577,20 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     }
     float acc0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     float acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int kc = 0; kc < p.k_chunks; ++kc, ++it) {
-      const int s = it % S;
+    for (int kc = 0; kc < p.k_chunks; ++kc) {
       const int col0 = kc * p.kc;
       const int nbox = min(p.kc, p.k - col0) >> 6;
-      if (!mbar_wait(&bars.full[s], (it / S) & 1)) return;
-      const uint8_t* stage = stages + (size_t)s * p.stage_bytes;
+      if (!mbar_wait(&bars.full[s], ph)) return;
+      const uint8_t* wg = stages + (size_t)s * p.stage_bytes + lane_off;
+      const uint8_t* xc = xrow + (col0 + warp * 64 + 16 * q) * 2;
       int box = warp;
       // two independent boxes per iteration (separate accumulators)
-      for (; box + kConsumerWarps < nbox; box += 2 * kConsumerWarps) {
-        const int l0 = box * 64 + 16 * q, l1 = l0 + kConsumerWarps * 64;
+      for (; box + kConsumerWarps < nbox;
+           box += 2 * kConsumerWarps, wg += 2 * kBoxStep, xc += 4 * kBoxStep) {
         RowScale a0 = rsa, b0 = rsb, a1 = rsa, b1 = rsb;
         bool pst = post;
         if (GROUPED) {
+          const int l0 = box * 64 + 16 * q, l1 = l0 + kBoxStep;
           const int g0 = (col0 + l0) / p.group_size, g1 = (col0 + l1) / p.group_size;
           a0 = row_scale(va ? __ldg(sa + g0) : 0.0f);
           b0 = row_scale(vb ? __ldg(sb + g0) : 0.0f);
@@ -592,28 +600,31 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
                                             needs_post(a1) || needs_post(b1));
         }
         if (pst) {
-          box_mma<true>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, g, a0, b0);
-          box_mma<true>(acc1, stage, p.kc, l1, xrow + (col0 + l1) * 2, g, a1, b1);
+          box_mma<true>(acc0, wg, row8, xc, a0, b0);
+          box_mma<true>(acc1, wg + kBoxStep, row8, xc + 2 * kBoxStep, a1, b1);
         } else {
-          box_mma<false>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, g, a0, b0);
-          box_mma<false>(acc1, stage, p.kc, l1, xrow + (col0 + l1) * 2, g, a1, b1);
+          box_mma<false>(acc0, wg, row8, xc, a0, b0);
+          box_mma<false>(acc1, wg + kBoxStep, row8, xc + 2 * kBoxStep, a1, b1);
         }
       }
       if (box < nbox) {
-        const int l0 = box * 64 + 16 * q;
         RowScale a0 = rsa, b0 = rsb;
         bool pst = post;
         if (GROUPED) {
-          const int g0 = (col0 + l0) / p.group_size;
+          const int g0 = (col0 + box * 64 + 16 * q) / p.group_size;
           a0 = row_scale(va ? __ldg(sa + g0) : 0.0f);
           b0 = row_scale(vb ? __ldg(sb + g0) : 0.0f);
           pst = __any_sync(0xffffffffu, needs_post(a0) || needs_post(b0));
         }
-        if (pst) box_mma<true>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, g, a0, b0);
-        else box_mma<false>(acc0, stage, p.kc, l0, xrow + (col0 + l0) * 2, g, a0, b0);
+        if (pst) box_mma<true>(acc0, wg, row8, xc, a0, b0);
+        else box_mma<false>(acc0, wg, row8, xc, a0, b0);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.empty[s]);
+      if (++s == S) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
     // hand the partial tile to the epilogue warp (double-buffered)
     const int b2 = blk & 1;
