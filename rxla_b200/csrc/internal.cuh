@@ -29,11 +29,30 @@ struct NormLinearArgs {
 
 constexpr int kArgmaxEpilogue = 16;
 
+// W8A16 GEMM on tcgen05 tensor cores (tokens > 8): y = x · W_deqᵀ with the
+// skinny kernel's epilogues.  x bf16 [m, ldx]; weight [n_rows, k] (n_rows =
+// 2n for SwiGLU); split-K over `splits` CTAs per tile needs `ws`.
+struct GemmArgs {
+  const void* x;
+  int64_t ldx;
+  const uint8_t* w;
+  const float* scale;
+  int64_t group, m, n, k;
+  void* y;
+  int64_t ldy;
+  int32_t y_dtype, epilogue;
+  int32_t splits;
+  void* ws;
+  size_t ws_bytes;
+};
+
 int32_t w8_norm_linear(const NormLinearArgs& a, cudaStream_t stream);
 // rxla_b200_w8a16_linear with an L2 prefetch of the next kernel's first bytes
 int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const float* scale,
                   int64_t group_size, int64_t m, int64_t n, int64_t k, void* y, int32_t y_dtype,
                   int32_t epilogue, cudaStream_t stream, const L2Prefetch* next);
+int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream);
+size_t w8_gemm_workspace_bytes(int64_t m, int64_t n_rows, int splits);
 int32_t comm_allreduce_f32(rxla_b200_comm* comm, float* buf, int64_t count, cudaStream_t s);
 
 namespace attn {

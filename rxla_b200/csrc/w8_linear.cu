@@ -859,6 +859,25 @@ int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const f
   const int per_pass = w8::tokens_per_pass(p);
   const bool fast = aligned && (k % 64 == 0) && (p.groups == 1 || group_size % 64 == 0) &&
                     per_pass > 0;
+  // more tokens than one skinny pass: the tcgen05 GEMM reads the weights once
+  if (m > w8::kMaxTokens && x_dtype == RXLA_B200_BF16 && aligned && k % 64 == 0 &&
+      group_size % 64 == 0) {
+    GemmArgs g{};
+    g.x = x;
+    g.ldx = k;
+    g.w = weight;
+    g.scale = scale;
+    g.group = group_size;
+    g.m = m;
+    g.n = n;
+    g.k = k;
+    g.y = y;
+    g.ldy = n;
+    g.y_dtype = y_dtype;
+    g.epilogue = epilogue;
+    g.splits = 1;
+    return w8_gemm(g, stream);
+  }
   const int xmode = p.x_f32 ? w8::kXF32 : w8::kXBf16;
   const int64_t step = fast ? per_pass : 32;
   for (int64_t m0 = 0; m0 < m; m0 += step) {

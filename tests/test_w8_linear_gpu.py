@@ -63,11 +63,52 @@ def test_sweep_shapes_small(cuda, m):
 
 
 @pytest.mark.parametrize("n,k", [(4096, 4096), (6144, 4096), (4096, 12288), (12288, 4096)])
-@pytest.mark.parametrize("m", [1, 8, 32])
+@pytest.mark.parametrize("m", [1, 8, 32, 128])
 def test_config2_shapes(cuda, n, k, m):
-    """(N,K) sweep, per-channel scales, M in {1,8,32}."""
+    """BASELINE config 2: (N,K) sweep, per-channel scales, M in {1,8,32,128}
+    (M > 8 runs on the tcgen05 GEMM)."""
     x, w, s = oracle.linear_sweep_case(m, n, k, seed=n + k + m)
     _check(_run(x, w, s, k), x, w, s, k)
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 4096, 4096), (2048, 4096, 4096), (512, 12288, 4096)])
+def test_config2_prefill_shapes(cuda, m, n, k):
+    """Config 2's tensor-bound rows (M = 512, 2048) on the tcgen05 GEMM."""
+    x, w, s = oracle.linear_sweep_case(m, n, k, seed=n + k + m)
+    _check(_run(x, w, s, k), x, w, s, k)
+
+
+@pytest.mark.parametrize("m,group", [(24, 1024), (130, 64), (9, 128)])
+def test_gemm_dequant_bit_exact(cuda, m, group):
+    """The tcgen05 GEMM's dequantization is the reference's, bit for bit: one-hot
+    x rows read single weights through the unrounded f32 output (partial tiles
+    in M and N, per-channel and grouped scales)."""
+    n, k = 300, 1024
+    rng = np.random.default_rng(m)
+    cols = rng.choice(k, size=m, replace=m > k)
+    x = np.zeros((m, k), np.float32)
+    x[np.arange(m), cols] = 1.0
+    w = ((np.arange(n)[:, None] * 7 + np.arange(k)[None, :] * 13) % 256).astype(np.uint8)
+    expo = oracle.uniform(n * (k // group), 77, -30.0, 2.0).reshape(n, k // group)
+    s = (10.0 ** expo).astype(np.float32)
+    s[::5] *= -1.0
+    y = _run(x, w, s, group, out_dtype=torch.float32)
+    sg = np.repeat(s, group, axis=1)
+    wd = oracle.bf16_round(((w.astype(np.float32) - np.float32(128.0)) * sg).astype(np.float32))
+    expect = wd[:, cols].T.astype(np.float32) + np.float32(0.0)
+    np.testing.assert_array_equal((y + np.float32(0.0)).view(np.uint32), expect.view(np.uint32))
+
+
+def test_gemm_residual_and_grouped(cuda):
+    """Residual epilogue and grouped scales on the GEMM path (M > 8)."""
+    x, w, s = _case(40, 384, 1024, 128, seed=41)
+    _check(_run(x, w, s, 128), x, w, s, 128)
+    h = oracle.normal(40 * 384, 42).reshape(40, 384)
+    ht = torch.from_numpy(h).cuda()
+    nn.quantized_linear(torch.from_numpy(x).cuda().bfloat16(), torch.from_numpy(w).cuda(),
+                        torch.from_numpy(s).cuda(), 128, epilogue=_lib.EPI_RESIDUAL_ADD, out=ht)
+    y = _run(x, w, s, 128)
+    np.testing.assert_array_equal(ht.cpu().numpy(), (h + y).astype(np.float32))
 
 
 @pytest.mark.parametrize("group", [64, 128, 512])
@@ -141,7 +182,8 @@ def test_residual_epilogue(cuda):
     np.testing.assert_array_equal(ht.cpu().numpy(), expect)
 
 
-@pytest.mark.parametrize("m,n,k,group", [(1, 1536, 512, 512), (8, 3000, 1024, 128), (20, 700, 2048, 2048)])
+@pytest.mark.parametrize("m,n,k,group", [(1, 1536, 512, 512), (8, 3000, 1024, 128), (20, 700, 2048, 2048),
+                                         (64, 1024, 1024, 1024)])
 def test_swiglu_epilogue(cuda, m, n, k, group):
     x, w, s = _case(m, 2 * n, k, group, seed=m + n)
     xt = torch.from_numpy(x).cuda().bfloat16()
