@@ -7,13 +7,16 @@
 // store, f32 residual add of the bf16 dot, SwiGLU of a fused [gate; up]).
 //
 // Tile: 128 tokens (MMA M) × 128 weight rows (MMA N), K staged 64 at a time.
-//  * warp 0 (producer): TMA loads of the x tile [128 × 64] bf16 (128-byte
-//    swizzle, the UMMA K-major SW128 layout) and the weight tile [128 × 64] u8
-//    (two 64-row boxes; for SwiGLU the gate rows and the matching up rows);
-//  * warps 2-5 (dequant, then epilogue): each thread turns one weight row of
-//    the stage into bf16 with the reference's rounding (packed denormal FMA,
-//    as in the skinny kernel) and stores it in the SW128 K-major layout the
-//    MMA reads, fences the generic->async proxy and arrives;
+//  * warp 0 (producer): TMA loads of the weight tile [128 × 64] u8 (two
+//    64-row boxes; for SwiGLU the gate rows and the matching up rows), which
+//    do not depend on the previous kernel; x tiles [128 × 64] bf16 use the
+//    128-byte swizzle, the UMMA K-major SW128 layout;
+//  * warp 2 (producer): the x tiles, in a ring of their own (they are L2
+//    hits with long latency, so it runs deeper than the weight ring);
+//  * warps 3-10 (dequant, then epilogue): two threads per weight row turn the
+//    stage's u8 tile into bf16 with the reference's rounding (packed denormal
+//    FMA, as in the skinny kernel), store it in the SW128 K-major layout the
+//    MMA reads, fence the generic->async proxy and arrive;
 //  * warp 1 (MMA): allocates 128 TMEM columns (fp32 accumulator 128 × 128),
 //    one elected thread issues four tcgen05.mma (K = 16 each) per stage and
 //    commits to the stage's "empty" barrier, finally to "acc_full";
@@ -34,14 +37,18 @@ using w8::needs_post;
 using w8::row_scale;
 using w8::RowScale;
 
-constexpr int kBM = 128, kBN = 128, kBK = 64;
-constexpr int kStages = 4;
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kHalfN = kBN / 2;         // rows per weight TMA box; SwiGLU outputs per tile
+constexpr int kWStages = 4;             // u8 weight tiles (TMA), 16 KB each
+constexpr int kXStages = 6;             // x tiles (TMA): deep, they are L2 hits with long latency
+constexpr int kBStages = 2;             // dequantized bf16 weight tiles, 32 KB each
 constexpr int kXTile = kBM * kBK * 2;   // 16 KB bf16, SW128
-constexpr int kBTile = kBN * kBK * 2;   // 16 KB bf16, SW128
-constexpr int kWTile = kBN * kBK;       // 8 KB u8
-constexpr int kStageBytes = kXTile + kBTile + kWTile;
-constexpr int kThreads = 6 * 32;
-constexpr int kTmemCols = 128;
+constexpr int kBTile = kBN * kBK * 2;   // 32 KB bf16, SW128
+constexpr int kWTile = kBN * kBK;       // 16 KB u8
+constexpr int kDeqWarps = 16;           // two threads per weight row
+constexpr int kThreads = (3 + kDeqWarps) * 32;
+constexpr int kTmemCols = kBN;          // fp32 accumulator 128 lanes × 256 columns
+constexpr int kChunk = 16;              // accumulator columns per tcgen05.ld in the epilogue
 
 struct Params {
   const float* scale;
@@ -52,18 +59,24 @@ struct Params {
   int64_t ldy;
   int32_t y_f32, epilogue;    // RXLA_B200_EPI_*
   int32_t k_per_split;        // multiple of kBK
-  float* ws;                  // [splits][m][n] fp32 partials (splits > 1)
+  float* ws;                  // [splits][m][n_rows] fp32 partials (splits > 1)
   uint32_t* counters;         // [tiles], zero between launches
 };
 
 struct Smem {
-  uint64_t full[kStages];
-  uint64_t bready[kStages];
-  uint64_t empty[kStages];
+  uint64_t w_full[kWStages];   // u8 weight tile landed (TMA)
+  uint64_t w_empty[kWStages];  // dequant warps are done with it
+  uint64_t x_full[kXStages];   // x tile landed (TMA)
+  uint64_t b_full[kBStages];   // bf16 weight tile written (dequant warps)
+  // MMAs of k-block it are complete (one commit per k-block, slot it % kXStages):
+  // frees x slot it % kXStages and bf16 slot it % kBStages
+  uint64_t mma_done[kXStages];
   uint64_t acc_full;
   uint32_t tmem_base;
   uint32_t last;
 };
+static_assert(sizeof(Smem) <= 1024, "barrier block");
+static_assert(kXStages >= kBStages, "one commit slot per x slot covers the bf16 ring");
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
@@ -117,20 +130,18 @@ __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t addr, float (&v)[32]) {
-  uint32_t r[32];
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[kChunk]) {
+  uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[14]), "=r"(r[15])
       : "r"(addr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Reference dequantization of 8 bytes (k order) into 4 bf16x2 words.
@@ -152,27 +163,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* base = smem_raw + pad;
   Smem& sm = *reinterpret_cast<Smem*>(base);
-  uint8_t* stages = base + 1024;  // stage s: x tile | bf16 weight tile | u8 weight tile
+  uint8_t* x_ring = base + 1024;                            // [kXStages][x tile]
+  uint8_t* b_ring = x_ring + (size_t)kXStages * kXTile;     // [kBStages][bf16 tile]
+  uint8_t* w_ring = b_ring + (size_t)kBStages * kBTile;     // [kWStages][u8 tile]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kBM;
   const int tile_n = blockIdx.y;
   const int split = blockIdx.z;
   const bool swiglu = p.epilogue == RXLA_B200_EPI_SWIGLU;
-  // weight rows of this tile: rows [wr0, wr0 + 64) and [wr1, wr1 + 64)
-  const int out0 = tile_n * (swiglu ? kBN / 2 : kBN);  // first output column
+  // weight rows of this tile: [wr0, wr0 + 128) and [wr1, wr1 + 128); for
+  // SwiGLU the gate rows of outputs out0 .. out0 + 127 and the matching up rows
+  const int out0 = tile_n * (swiglu ? kHalfN : kBN);  // first output column
   const int wr0 = out0;
-  const int wr1 = swiglu ? p.n + out0 : out0 + 64;
+  const int wr1 = swiglu ? p.n + out0 : out0 + kHalfN;
   const int k_begin = split * p.k_per_split;
   const int k_end = min(p.k, k_begin + p.k_per_split);
   const int n_k = (k_end - k_begin) / kBK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.bready[s], 4);
-      mbar_init(&sm.empty[s], 1);
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(&sm.w_full[s], 1);
+      mbar_init(&sm.w_empty[s], kDeqWarps);
     }
+    for (int s = 0; s < kXStages; ++s) {
+      mbar_init(&sm.x_full[s], 1);
+      mbar_init(&sm.mma_done[s], 1);
+    }
+    for (int s = 0; s < kBStages; ++s) mbar_init(&sm.b_full[s], kDeqWarps);
     mbar_init(&sm.acc_full, 1);
     fence_mbarrier_init();
   }
@@ -189,75 +207,105 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA
+    // ------------------------------------------------- weight producer (TMA)
+    // weights do not depend on the previous kernel: no wait before streaming
+    if (lane == 0) {
+      for (int it = 0; it < n_k; ++it) {
+        const int s = it % kWStages;
+        if (it >= kWStages && !mbar_wait(&sm.w_empty[s], ((it / kWStages) - 1) & 1)) break;
+        uint8_t* dst = w_ring + (size_t)s * kWTile;
+        const int k0 = k_begin + it * kBK;
+        mbar_arrive_expect_tx(&sm.w_full[s], (uint32_t)kWTile);
+        tma_load_2d(dst, &wmap, k0, wr0, &sm.w_full[s]);
+        tma_load_2d(dst + kHalfN * kBK, &wmap, k0, wr1, &sm.w_full[s]);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------ x producer (TMA)
     if (lane == 0) {
       pdl_wait();  // x (and the residual) come from the previous kernel
       for (int it = 0; it < n_k; ++it) {
-        const int s = it % kStages;
-        if (it >= kStages && !mbar_wait(&sm.empty[s], ((it / kStages) - 1) & 1)) break;
-        uint8_t* st = stages + (size_t)s * kStageBytes;
-        const int k0 = k_begin + it * kBK;
-        mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(kXTile + kWTile));
-        tma_load_2d(st, &xmap, k0, m0, &sm.full[s]);
-        tma_load_2d(st + kXTile + kBTile, &wmap, k0, wr0, &sm.full[s]);
-        tma_load_2d(st + kXTile + kBTile + 64 * kBK, &wmap, k0, wr1, &sm.full[s]);
+        const int s = it % kXStages;
+        // slot s was last read by the MMAs of k-block it - kXStages
+        if (it >= kXStages && !mbar_wait(&sm.mma_done[s], ((it / kXStages) - 1) & 1)) break;
+        mbar_arrive_expect_tx(&sm.x_full[s], (uint32_t)kXTile);
+        tma_load_2d(x_ring + (size_t)s * kXTile, &xmap, k_begin + it * kBK, m0, &sm.x_full[s]);
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
       for (int it = 0; it < n_k; ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait(&sm.full[s], ph) || !mbar_wait(&sm.bready[s], ph)) break;
+        const int xs = it % kXStages, bs = it % kBStages;
+        if (!mbar_wait(&sm.x_full[xs], (it / kXStages) & 1) ||
+            !mbar_wait(&sm.b_full[bs], (it / kBStages) & 1))
+          break;
         tc_fence_after();
-        uint8_t* st = stages + (size_t)s * kStageBytes;
-        const uint64_t ad = sw128_desc(st), bd = sw128_desc(st + kXTile);
+        const uint64_t ad = sw128_desc(x_ring + (size_t)xs * kXTile);
+        const uint64_t bd = sw128_desc(b_ring + (size_t)bs * kBTile);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes per K = 16 step
           mma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, it > 0 || kk > 0);
-        mma_commit(&sm.empty[s]);
+        mma_commit(&sm.mma_done[xs]);
       }
       mma_commit(&sm.acc_full);
     }
   } else {
     // ------------------------------------------- dequant, then epilogue
-    const int t = threadIdx.x - 64;  // 0 .. 127: weight row of the tile / token row
-    const int wrow = t < 64 ? wr0 + t : wr1 + (t - 64);
-    const bool wvalid = wrow < p.n_rows && (swiglu ? (t < 64 ? out0 + t : out0 + t - 64) < p.n : true);
+    // thread d (0 .. 511): weight row d / 2 of the tile, bytes 32·(d % 2) ..
+    const int d = threadIdx.x - 96;
+    const int t = d >> 1, half = d & 1;
+    const int wrow = t < kHalfN ? wr0 + t : wr1 + (t - kHalfN);
+    const bool wvalid =
+        wrow < p.n_rows && (swiglu ? (t < kHalfN ? out0 + t : out0 + t - kHalfN) < p.n : true);
     const float* srow = p.scale + (int64_t)(wvalid ? wrow : 0) * p.groups;
     RowScale rs = row_scale(wvalid ? __ldg(srow + k_begin / p.group_size) : 0.0f);
     int cur_group = k_begin / p.group_size;
     for (int it = 0; it < n_k; ++it) {
-      const int s = it % kStages;
-      if (!mbar_wait(&sm.full[s], (it / kStages) & 1)) break;
+      const int ws = it % kWStages, bs = it % kBStages;
+      if (!mbar_wait(&sm.w_full[ws], (it / kWStages) & 1)) break;
+      // bf16 slot bs was last read by the MMAs of k-block it - kBStages
+      if (it >= kBStages) {
+        const int j = it - kBStages;
+        if (!mbar_wait(&sm.mma_done[j % kXStages], (j / kXStages) & 1)) break;
+      }
       const int k0 = k_begin + it * kBK;
       if (p.groups > 1 && k0 / p.group_size != cur_group) {
         cur_group = k0 / p.group_size;
         rs = row_scale(wvalid ? __ldg(srow + cur_group) : 0.0f);
       }
       const bool post = __any_sync(0xffffffffu, needs_post(rs));
-      uint8_t* st = stages + (size_t)s * kStageBytes;
-      const uint8_t* wsrc = st + kXTile + kBTile + t * kBK;
-      uint8_t* bdst = st + kXTile + (t >> 3) * 1024 + (t & 7) * 128;
+      const uint8_t* wsrc = w_ring + (size_t)ws * kWTile + t * kBK + 32 * half;
+      uint8_t* bdst = b_ring + (size_t)bs * kBTile + (t >> 3) * 1024 + (t & 7) * 128;
+      uint4 wv[2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 16 bytes -> two 16-byte bf16 chunks
-        const uint4 w = *reinterpret_cast<const uint4*>(wsrc + 16 * c);
+      for (int c = 0; c < 2; ++c) wv[c] = *reinterpret_cast<const uint4*>(wsrc + 16 * c);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {  // 16 bytes -> two 16-byte bf16 chunks
         uint32_t o0[4], o1[4];
-        deq8(w.x, w.y, rs, post, o0);
-        deq8(w.z, w.w, rs, post, o1);
-        const int c0 = 2 * c, c1 = 2 * c + 1;
+        deq8(wv[c].x, wv[c].y, rs, post, o0);
+        deq8(wv[c].z, wv[c].w, rs, post, o1);
+        const int c0 = 4 * half + 2 * c, c1 = c0 + 1;
         *reinterpret_cast<uint4*>(bdst + ((c0 ^ (t & 7)) << 4)) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
         *reinterpret_cast<uint4*>(bdst + ((c1 ^ (t & 7)) << 4)) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
       }
+      // the u8 slot is released only after its values are consumed, and the
+      // proxy fence orders these generic-proxy accesses before the TMA's
+      // (async-proxy) rewrite of the slot and the MMA's read of the tile
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.bready[s]);
+      if (lane == 0) {
+        mbar_arrive(&sm.w_empty[ws]);
+        mbar_arrive(&sm.b_full[bs]);
+      }
     }
 
-    // epilogue: this warp reads TMEM lanes 32·(warp % 4) .. +31 = tokens, in
-    // chunks of 32 accumulator columns (SwiGLU: a gate chunk and its up chunk)
+    // epilogue: this warp reads TMEM lanes 32·(warp % 4) .. +31 = tokens; the
+    // four warps of a lane quarter split the columns: set cs takes columns
+    // [64·cs, 64·cs + 64) (SwiGLU: gate columns [32·cs, 32·cs + 32) and the
+    // matching up columns 128 further)
     const int q = warp & 3;
+    const int cs = (warp - 3) >> 2;
     const int tok = m0 + 32 * q + lane;
     const bool ok = mbar_wait(&sm.acc_full, 0);
     tc_fence_after();
@@ -265,52 +313,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
     const int ncols = p.n_rows;  // workspace row width
     // workspace column of accumulator column j
-    auto ws_col = [&](int j) { return swiglu ? (j < 64 ? out0 + j : p.n + out0 + j - 64) : out0 + j; };
-    // a 32-column chunk exists when its first output column does (split-K
-    // runs only for n % 64 == 0, so chunks are whole)
-    auto chunk_valid = [&](int c) { return (swiglu ? out0 + 32 * (c & 1) : out0 + 32 * c) < p.n; };
+    auto ws_col = [&](int j) {
+      return swiglu ? (j < kHalfN ? out0 + j : p.n + out0 + j - kHalfN) : out0 + j;
+    };
+    // accumulator column j holds a real output column (split-K runs only for
+    // n % 64 == 0, so 16-column chunks are whole)
+    auto col_valid = [&](int j) { return (swiglu ? out0 + (j % kHalfN) : out0 + j) < p.n; };
     bool finish = true;
     if (nsplit > 1) {
       // partial -> workspace; the last CTA of the tile sums all splits in order
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        float v[32];
-        tmem_ld32(lane_addr + 32 * c, v);
-        if (tok < p.m && chunk_valid(c)) {
-          float* dst = p.ws + ((int64_t)split * p.m + tok) * ncols + ws_col(32 * c);
+      for (int c = 0; c < 4; ++c) {
+        const int j0 = swiglu ? (c < 2 ? 32 * cs + 16 * c : kHalfN + 32 * cs + 16 * (c - 2))
+                              : 64 * cs + 16 * c;
+        float v[kChunk];
+        tmem_ld16(lane_addr + j0, v);
+        if (tok < p.m && col_valid(j0)) {
+          float* dst = p.ws + ((int64_t)split * p.m + tok) * ncols + ws_col(j0);
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
+          for (int i = 0; i < kChunk; i += 4)
             *reinterpret_cast<float4*>(dst + i) =
                 ok ? make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
       __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (t == 0) {
+      asm volatile("bar.sync 1, %0;" ::"r"(kDeqWarps * 32) : "memory");
+      if (d == 0) {
         const uint32_t prev = atomicAdd(&p.counters[blockIdx.y * gridDim.x + blockIdx.x], 1u);
         sm.last = prev == (uint32_t)(nsplit - 1) ? 1u : 0u;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(kDeqWarps * 32) : "memory");
       finish = sm.last != 0;
       if (finish) __threadfence();
     }
-    // accumulator chunk c (32 columns) of this token: from TMEM, or the sum of
-    // all splits' partials in split order
-    auto chunk = [&](int c, float (&v)[32]) {
+    // accumulator columns j0 .. j0 + 15 of this token: from TMEM, or the sum
+    // of all splits' partials in split order
+    auto chunk = [&](int j0, float (&v)[kChunk]) {
       if (nsplit == 1) {
-        tmem_ld32(lane_addr + 32 * c, v);
+        tmem_ld16(lane_addr + j0, v);
         if (!ok)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+          for (int i = 0; i < kChunk; ++i) v[i] = 0.0f;
         return;
       }
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-      if (tok >= p.m || !chunk_valid(c)) return;
+      for (int i = 0; i < kChunk; ++i) v[i] = 0.0f;
+      if (tok >= p.m || !col_valid(j0)) return;
       for (int sp = 0; sp < nsplit; ++sp) {
-        const float* src = p.ws + ((int64_t)sp * p.m + tok) * ncols + ws_col(32 * c);
+        const float* src = p.ws + ((int64_t)sp * p.m + tok) * ncols + ws_col(j0);
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
+        for (int i = 0; i < kChunk; i += 4) {
           const float4 x4 = __ldcg(reinterpret_cast<const float4*>(src + i));
           v[i] += x4.x;
           v[i + 1] += x4.y;
@@ -323,16 +375,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (swiglu) {
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
-          float g[32], u[32];
-          chunk(c, g);
-          chunk(c + 2, u);
-          const int j0 = out0 + 32 * c;
+          const int j0 = 32 * cs + 16 * c;  // gate columns; up columns j0 + 128
+          float g[kChunk], u[kChunk];
+          chunk(j0, g);
+          chunk(kHalfN + j0, u);
           if (tok < p.m) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              if (j0 + i < p.n) {
+            for (int i = 0; i < kChunk; ++i) {
+              if (out0 + j0 + i < p.n) {
                 const float r = silu(bf16_round(g[i])) * bf16_round(u[i]);
-                const int64_t o = (int64_t)tok * p.ldy + j0 + i;
+                const int64_t o = (int64_t)tok * p.ldy + out0 + j0 + i;
                 if (p.y_f32) static_cast<float*>(p.y)[o] = r;
                 else static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(r);
               }
@@ -341,28 +393,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
-          float v[32];
-          chunk(c, v);
-          const int j0 = out0 + 32 * c;
-          if (tok >= p.m || j0 >= p.n) continue;
-          const int nv = min(32, p.n - j0);
-          const int64_t o = (int64_t)tok * p.ldy + j0;
+        for (int c = 0; c < 4; ++c) {
+          const int j0 = 64 * cs + 16 * c;
+          float v[kChunk];
+          chunk(j0, v);
+          const int col = out0 + j0;
+          if (tok >= p.m || col >= p.n) continue;
+          const int nv = min(kChunk, p.n - col);
+          const int64_t o = (int64_t)tok * p.ldy + col;
           if (p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD) {
             float* yy = static_cast<float*>(p.y) + o;
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
+            for (int i = 0; i < kChunk; ++i)
               if (i < nv) yy[i] = yy[i] + bf16_round(v[i]);
           } else if (p.y_f32) {
             float* yy = static_cast<float*>(p.y) + o;
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
+            for (int i = 0; i < kChunk; ++i)
               if (i < nv) yy[i] = v[i];
           } else {
             __nv_bfloat16* yy = static_cast<__nv_bfloat16*>(p.y) + o;
-            if (nv == 32 && (reinterpret_cast<uintptr_t>(yy) & 15) == 0) {
+            if (nv == kChunk && (reinterpret_cast<uintptr_t>(yy) & 15) == 0) {
 #pragma unroll
-              for (int i = 0; i < 32; i += 8) {
+              for (int i = 0; i < kChunk; i += 8) {
                 uint4 pk;
                 pk.x = pack_bf16x2(v[i], v[i + 1]);
                 pk.y = pack_bf16x2(v[i + 2], v[i + 3]);
@@ -372,18 +425,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
+              for (int i = 0; i < kChunk; ++i)
                 if (i < nv) yy[i] = __float2bfloat16_rn(v[i]);
             }
           }
         }
       }
-      if (nsplit > 1 && t == 0) p.counters[blockIdx.y * gridDim.x + blockIdx.x] = 0u;
+      if (nsplit > 1 && d == 0) p.counters[blockIdx.y * gridDim.x + blockIdx.x] = 0u;
     }
     tc_fence_before();
   }
-  // dependents wait for this grid's completion before reading its output
-  if (threadIdx.x == 0) pdl_launch_dependents();
+  // dependents wait for this grid's completion before reading its output; the
+  // trigger comes from the thread that waited for the previous grid
+  if (threadIdx.x == 64) pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -427,7 +481,7 @@ int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream) {
   const bool swiglu = a.epilogue == RXLA_B200_EPI_SWIGLU;
   const int64_t n_rows = swiglu ? 2 * a.n : a.n;
   const int64_t tiles_m = (a.m + kBM - 1) / kBM;
-  const int64_t tiles_n = swiglu ? (a.n + 63) / 64 : (a.n + kBN - 1) / kBN;
+  const int64_t tiles_n = swiglu ? (a.n + kHalfN - 1) / kHalfN : (a.n + kBN - 1) / kBN;
   RXLA_REQUIRE(tiles_m <= 65535 && tiles_n <= 65535, "w8 gemm: too many tiles");
   int splits = std::max(1, a.splits);
   const int64_t kb = a.k / kBK;
@@ -456,7 +510,7 @@ int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream) {
   {
     const cuuint64_t dims[2] = {(cuuint64_t)a.k, (cuuint64_t)n_rows};
     const cuuint64_t strides[1] = {(cuuint64_t)a.k};
-    const cuuint32_t box[2] = {kBK, 64};
+    const cuuint32_t box[2] = {kBK, kHalfN};
     const cuuint32_t estr[2] = {1, 1};
     if (fn(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.w), dims, strides, box,
            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -482,7 +536,8 @@ int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream) {
     p.counters = static_cast<uint32_t*>(a.ws);
     p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(a.ws) + counters);
   }
-  const size_t smem = 1024 /*align*/ + 1024 /*barriers*/ + (size_t)kStages * kStageBytes;
+  const size_t smem = 1024 /*align*/ + 1024 /*barriers*/ + (size_t)kXStages * kXTile +
+                      (size_t)kBStages * kBTile + (size_t)kWStages * kWTile;
   cudaError_t e = cudaFuncSetAttribute(w8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e == cudaSuccess)
