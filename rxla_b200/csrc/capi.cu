@@ -53,24 +53,57 @@ __global__ void rms_norm_bf16_kernel(const float* __restrict__ x, const float* _
   pdl_wait();
   pdl_launch_dependents();
   const float* xr = x + blockIdx.x * width;
+  __nv_bfloat16* yr = y + blockIdx.x * width;
+  // rows of up to 8 float4 per thread are held in registers, all loads issued
+  // before any is used (one round trip); wider or unaligned rows use a loop
+  constexpr int kV = 8;
+  const bool regs = width % 4 == 0 && width <= (int64_t)kV * 4 * blockDim.x &&
+                    (reinterpret_cast<uintptr_t>(xr) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(yr) & 7) == 0;
+  float4 v[kV];
   float ss = 0.0f;
-  for (int64_t c = threadIdx.x; c < width; c += blockDim.x) ss += xr[c] * xr[c];
+  if (regs) {
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int64_t c = ((int64_t)threadIdx.x + (int64_t)i * blockDim.x) * 4;
+      v[i] = c < width ? *reinterpret_cast<const float4*>(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < kV; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  } else {
+    for (int64_t c = threadIdx.x; c < width; c += blockDim.x) ss += xr[c] * xr[c];
+  }
   __shared__ float red[32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (threadIdx.x == 0) red[0] = v;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
   }
   __syncthreads();
   const float mean = red[0] / (float)width;
   const float rs = 1.0f / sqrtf(mean + eps);
-  for (int64_t c = threadIdx.x; c < width; c += blockDim.x)
-    y[blockIdx.x * width + c] = __float2bfloat16_rn((xr[c] * rs) * w[c]);
+  if (regs) {
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int64_t c = ((int64_t)threadIdx.x + (int64_t)i * blockDim.x) * 4;
+      if (c < width) {
+        const float4 ww = *reinterpret_cast<const float4*>(w + c);
+        uint2 pk;
+        pk.x = pack_bf16x2((v[i].x * rs) * ww.x, (v[i].y * rs) * ww.y);
+        pk.y = pack_bf16x2((v[i].z * rs) * ww.z, (v[i].w * rs) * ww.w);
+        *reinterpret_cast<uint2*>(yr + c) = pk;
+      }
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < width; c += blockDim.x)
+      yr[c] = __float2bfloat16_rn((xr[c] * rs) * w[c]);
+  }
 }
 
 // ------------------------------------------------------------------- argmax
@@ -84,12 +117,40 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int64_t vocab,
   const float* r = logits + blockIdx.x * vocab;
   float best = -INFINITY;
   int32_t idx = 0x7fffffff;
-  for (int64_t c = threadIdx.x; c < vocab; c += blockDim.x) {
-    float v = r[c];
-    if (v > best || (v == best && (int32_t)c < idx)) {
+  auto take = [&](float v, int32_t c) {
+    if (v > best || (v == best && c < idx)) {
       best = v;
-      idx = (int32_t)c;
+      idx = c;
     }
+  };
+  if (vocab % 4 == 0 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+    // float4 loads, four per thread in flight before they are compared
+    const int64_t nq = vocab / 4;
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+    int64_t q = threadIdx.x;
+    for (; q + 3 * (int64_t)blockDim.x < nq; q += 4 * (int64_t)blockDim.x) {
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = r4[q + j * (int64_t)blockDim.x];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int32_t c = (int32_t)(4 * (q + j * (int64_t)blockDim.x));
+        take(v[j].x, c);
+        take(v[j].y, c + 1);
+        take(v[j].z, c + 2);
+        take(v[j].w, c + 3);
+      }
+    }
+    for (; q < nq; q += blockDim.x) {
+      const float4 v = r4[q];
+      const int32_t c = (int32_t)(4 * q);
+      take(v.x, c);
+      take(v.y, c + 1);
+      take(v.z, c + 2);
+      take(v.w, c + 3);
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < vocab; c += blockDim.x) take(r[c], (int32_t)c);
   }
   __shared__ float sb[32];
   __shared__ int32_t si[32];

@@ -197,6 +197,9 @@ struct rxla_b200_decoder {
   float* inv_freq = nullptr;
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  // split-K workspace of the tcgen05 GEMM path (batch > 8)
+  void* gws = nullptr;
+  size_t gws_bytes = 0;
   // fused LM-head argmax: per-CTA partials and the arrival counter
   float* arg_val = nullptr;
   int32_t* arg_idx = nullptr;
@@ -208,9 +211,125 @@ struct rxla_b200_decoder {
 namespace rxla {
 namespace dec {
 
+// Batches above one skinny-GEMV pass run their linears on the tcgen05 GEMM.
+constexpr int kSkinnyTokens = 8;
+
+// Split-K depth for a GEMM of m tokens × n outputs × k: enough CTAs to cover
+// the SMs, at least two 64-wide k-blocks per split, at most 16 splits.
+static int gemm_splits(int64_t m, int64_t n, int64_t k, bool swiglu) {
+  if (n % 64 != 0) return 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t tiles = ((m + 127) / 128) * (swiglu ? (n + 127) / 128 : (n + 255) / 256);
+  const int64_t want = (sm_count(dev) + tiles - 1) / tiles;
+  return (int)std::max<int64_t>(1, std::min<int64_t>({want, 16, k / 128}));
+}
+
 static int32_t alloc_dev(void** p, size_t bytes) {
   cudaError_t e = cudaMalloc(p, bytes);
   if (e != cudaSuccess) return cuda_fail(e, "decoder allocation");
+  return RXLA_B200_OK;
+}
+
+// Paged decode attention arguments of one layer of the runner.
+static rxla_b200_paged_decode_args attention_args(const rxla_b200_decoder* d, const Layer& L,
+                                                  int batch) {
+  const auto& c = d->cfg;
+  const int64_t D = c.head_dim;
+  const int64_t qd = (int64_t)d->hq * D, kd = (int64_t)d->hkv * D;
+  rxla_b200_paged_decode_args a{};
+  a.struct_size = sizeof(a);
+  a.batch = batch;
+  a.q_heads = d->hq;
+  a.kv_heads = d->hkv;
+  a.head_dim = (int32_t)D;
+  a.q = d->qkv;
+  a.k_new = d->qkv + qd;
+  a.v_new = d->qkv + qd + kd;
+  a.q_row_stride = d->qkv_rows;
+  a.kv_row_stride = d->qkv_rows;
+  a.q_norm_weight = L.qn;
+  a.k_norm_weight = L.kn;
+  a.norm_eps = c.rms_eps;
+  a.inv_freq = d->inv_freq;
+  a.rotary_dim = (int32_t)D;
+  a.scale = 0.0f;
+  a.k_pages = L.kc;
+  a.v_pages = L.vc;
+  a.num_pages = (int64_t)c.max_batch * d->max_pages;
+  a.page_size = 16;
+  a.max_pages_per_seq = d->max_pages;
+  a.page_table = d->page_table;
+  a.pages_per_seq = nullptr;
+  a.ctx_lens = d->ctx;
+  a.kv_update = RXLA_B200_KV_CLAMP;
+  a.advance_ctx = 0;
+  a.accepted = nullptr;
+  a.out = d->att;
+  a.workspace = d->ws;
+  a.workspace_bytes = d->ws_bytes;
+  a.max_context = c.max_context;
+  return a;
+}
+
+// Linears of a step with more tokens than one skinny pass: bf16 x from a
+// separate RMSNorm kernel, the tcgen05 GEMM (split-K over the runner's
+// workspace), the same epilogues; the LM head writes f32 logits and a
+// per-row argmax kernel picks the token and advances the position.
+static int32_t enqueue_gemm_layers(rxla_b200_decoder* d, int batch, cudaStream_t s) {
+  const auto& c = d->cfg;
+  const int64_t H = c.hidden, D = c.head_dim;
+  const int64_t qd = (int64_t)d->hq * D;
+  auto gemm = [&](const void* x, int64_t k, const uint8_t* w, const float* sc, int64_t group,
+                  int64_t n, void* y, int32_t y_dtype, int32_t epi) {
+    GemmArgs g{};
+    g.x = x;
+    g.ldx = k;
+    g.w = w;
+    g.scale = sc;
+    g.group = group;
+    g.m = batch;
+    g.n = n;
+    g.k = k;
+    g.y = y;
+    g.ldy = n;
+    g.y_dtype = y_dtype;
+    g.epilogue = epi;
+    g.splits = gemm_splits(batch, n, k, epi == RXLA_B200_EPI_SWIGLU);
+    g.ws = d->gws;
+    g.ws_bytes = d->gws_bytes;
+    return w8_gemm(g, s);
+  };
+  for (int l = 0; l < c.layers; ++l) {
+    const Layer& L = d->layers[l];
+    int32_t st = rxla_b200_rms_norm_bf16(d->h, L.ln1, batch, H, c.rms_eps, d->xn, s);
+    if (!st) st = gemm(d->xn, H, L.wqkv, L.sqkv, d->group_h, d->qkv_rows, d->qkv, RXLA_B200_BF16,
+                       RXLA_B200_EPI_STORE);
+    if (st) return st;
+    rxla_b200_paged_decode_args a = attention_args(d, L, batch);
+    st = attn::launch(&a, s, true);
+    if (!st) st = gemm(d->att, qd, L.wo, L.so, d->group_o, H, d->h, RXLA_B200_F32,
+                       RXLA_B200_EPI_RESIDUAL_ADD);
+    if (!st) st = rxla_b200_rms_norm_bf16(d->h, L.ln2, batch, H, c.rms_eps, d->xn, s);
+    if (!st) st = gemm(d->xn, H, L.wgu, L.sgu, d->group_h, d->inter, d->act, RXLA_B200_BF16,
+                       RXLA_B200_EPI_SWIGLU);
+    if (!st) st = gemm(d->act, d->inter, L.wd, L.sd, d->group_i, H, d->h, RXLA_B200_F32,
+                       RXLA_B200_EPI_RESIDUAL_ADD);
+    if (st) return st;
+  }
+  int32_t st = rxla_b200_rms_norm_bf16(d->h, d->final_norm, batch, H, c.rms_eps, d->xn, s);
+  if (st) return st;
+  if (d->emb_w8) {
+    st = gemm(d->xn, H, d->emb_w8, d->emb_scale, d->group_h, d->vocab, d->logits, RXLA_B200_F32,
+              RXLA_B200_EPI_STORE);
+  } else {
+    st = rxla_b200_bf16_linear(d->xn, RXLA_B200_BF16, d->emb_bf16, batch, d->vocab, H, d->logits,
+                               RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
+  }
+  if (st) return st;
+  cudaError_t e = launch_pdl(argmax_kernel, dim3(batch), dim3(1024), 0, s, (const float*)d->logits,
+                             (int64_t)d->vocab, d->tok_out, d->ctx);
+  if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
   return RXLA_B200_OK;
 }
 
@@ -224,6 +343,9 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
                              (int64_t)d->groups_h, (int64_t)d->group_h, d->h);
   if (e != cudaSuccess) return cuda_fail(e, "embed launch");
   const bool tp = c.tp_size > 1;
+  if (batch > kSkinnyTokens && !tp && d->gws_bytes > 0 && d->group_h % 64 == 0 &&
+      d->group_o % 64 == 0 && d->group_i % 64 == 0)
+    return enqueue_gemm_layers(d, batch, s);
   const int64_t qd = (int64_t)d->hq * D, kd = (int64_t)d->hkv * D;
   // each kernel pulls the start of the next weight matrix into L2 while it drains
   auto pf = [](const void* w, int64_t bytes, int32_t per_cta) {
@@ -269,38 +391,7 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
     na.next = to_o;
     int32_t st = w8_norm_linear(na, s);
     if (st) return st;
-    rxla_b200_paged_decode_args a{};
-    a.struct_size = sizeof(a);
-    a.batch = batch;
-    a.q_heads = d->hq;
-    a.kv_heads = d->hkv;
-    a.head_dim = (int32_t)D;
-    a.q = d->qkv;
-    a.k_new = d->qkv + qd;
-    a.v_new = d->qkv + qd + kd;
-    a.q_row_stride = d->qkv_rows;
-    a.kv_row_stride = d->qkv_rows;
-    a.q_norm_weight = L.qn;
-    a.k_norm_weight = L.kn;
-    a.norm_eps = c.rms_eps;
-    a.inv_freq = d->inv_freq;
-    a.rotary_dim = (int32_t)D;
-    a.scale = 0.0f;
-    a.k_pages = L.kc;
-    a.v_pages = L.vc;
-    a.num_pages = (int64_t)c.max_batch * d->max_pages;
-    a.page_size = 16;
-    a.max_pages_per_seq = d->max_pages;
-    a.page_table = d->page_table;
-    a.pages_per_seq = nullptr;
-    a.ctx_lens = d->ctx;
-    a.kv_update = RXLA_B200_KV_CLAMP;
-    a.advance_ctx = 0;
-    a.accepted = nullptr;
-    a.out = d->att;
-    a.workspace = d->ws;
-    a.workspace_bytes = d->ws_bytes;
-    a.max_context = c.max_context;
+    rxla_b200_paged_decode_args a = attention_args(d, L, batch);
     st = attn::launch(&a, s, true, &to_o);
     if (st) return st;
     if (!tp) {
@@ -525,6 +616,15 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
   rxla_b200_paged_decode_workspace_size(c.max_batch, d->hq, d->hkv, (int32_t)D, c.max_context,
                                         &need_ws);
   d->ws_bytes = need_ws;
+  if (B > dec::kSkinnyTokens) {
+    size_t g = 0;
+    const int64_t shapes[][3] = {{d->qkv_rows, H, 0}, {H, (int64_t)d->hq * D, 0},
+                                 {(int64_t)I, H, 1}, {H, (int64_t)I, 0}, {(int64_t)d->vocab, H, 0}};
+    for (auto& sh : shapes)
+      g = std::max(g, w8_gemm_workspace_bytes(B, sh[2] ? 2 * sh[0] : sh[0],
+                                              dec::gemm_splits(B, sh[0], sh[1], sh[2] != 0)));
+    d->gws_bytes = g;
+  }
   struct A {
     void** p;
     size_t bytes;
@@ -542,6 +642,7 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
       {(void**)&d->tok_out, (size_t)B * 4},
       {(void**)&d->inv_freq, (size_t)D * 2},
       {&d->ws, need_ws},
+      {&d->gws, d->gws_bytes},
       {(void**)&d->arg_val, (size_t)1024 * 8 * 4},
       {(void**)&d->arg_idx, (size_t)1024 * 8 * 4},
       {(void**)&d->arg_count, 256},
@@ -592,7 +693,7 @@ extern "C" int32_t rxla_b200_decoder_destroy(rxla_b200_decoder* d) {
   }
   void* ptrs[] = {d->arena, d->page_table, d->ctx, d->h, d->xn, d->qkv, d->att, d->act,
                   d->part, d->logits, d->tok_in, d->tok_out, d->inv_freq, d->ws,
-                  d->arg_val, d->arg_idx, d->arg_count};
+                  d->gws, d->arg_val, d->arg_idx, d->arg_count};
   for (void* p : ptrs) cudaFree(p);
   if (d->host_pinned) cudaFreeHost(d->host_pinned);
   delete d;

@@ -343,33 +343,78 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm.last = prev == (uint32_t)(nsplit - 1) ? 1u : 0u;
       }
       asm volatile("bar.sync 1, %0;" ::"r"(kDeqWarps * 32) : "memory");
-      finish = sm.last != 0;
-      if (finish) __threadfence();
-    }
-    // accumulator columns j0 .. j0 + 15 of this token: from TMEM, or the sum
-    // of all splits' partials in split order
-    auto chunk = [&](int j0, float (&v)[kChunk]) {
-      if (nsplit == 1) {
-        tmem_ld16(lane_addr + j0, v);
-        if (!ok)
+      finish = false;  // the split partials are reduced below, not from TMEM
+      if (sm.last != 0) {
+        // the last CTA of the tile: all epilogue threads sum the splits of
+        // 4 consecutive output columns of one token each, in split order, with
+        // up to 4 splits' loads in flight, and apply the epilogue
+        __threadfence();
+        const int ntok = min(kBM, p.m - m0);
+        const int nout = swiglu ? min(kHalfN, p.n - out0) : min(kBN, p.n - out0);
+        const int nq = nout / 4;  // split-K runs only for n % 64 == 0
+        const bool vec_y = (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && p.ldy % 4 == 0;
+        for (int e = d; e < ntok * nq; e += kDeqWarps * 32) {
+          const int tt = m0 + e / nq, c4 = (e % nq) * 4;
+          float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+          for (int sp0 = 0; sp0 < nsplit; sp0 += 4) {
+            float4 gv[4], uv[4];
 #pragma unroll
-          for (int i = 0; i < kChunk; ++i) v[i] = 0.0f;
-        return;
-      }
+            for (int j = 0; j < 4; ++j) {
+              if (sp0 + j < nsplit) {
+                const float* row = p.ws + ((int64_t)(sp0 + j) * p.m + tt) * ncols;
+                gv[j] = __ldcg(reinterpret_cast<const float4*>(row + out0 + c4));
+                if (swiglu) uv[j] = __ldcg(reinterpret_cast<const float4*>(row + p.n + out0 + c4));
+              }
+            }
 #pragma unroll
-      for (int i = 0; i < kChunk; ++i) v[i] = 0.0f;
-      if (tok >= p.m || !col_valid(j0)) return;
-      for (int sp = 0; sp < nsplit; ++sp) {
-        const float* src = p.ws + ((int64_t)sp * p.m + tok) * ncols + ws_col(j0);
+            for (int j = 0; j < 4; ++j) {
+              if (sp0 + j < nsplit) {
+                g.x += gv[j].x; g.y += gv[j].y; g.z += gv[j].z; g.w += gv[j].w;
+                if (swiglu) { u.x += uv[j].x; u.y += uv[j].y; u.z += uv[j].z; u.w += uv[j].w; }
+              }
+            }
+          }
+          const float gg[4] = {g.x, g.y, g.z, g.w}, uu[4] = {u.x, u.y, u.z, u.w};
+          const int64_t off = (int64_t)tt * p.ldy + out0 + c4;
+          if (swiglu) {
+            float r4[4];
 #pragma unroll
-        for (int i = 0; i < kChunk; i += 4) {
-          const float4 x4 = __ldcg(reinterpret_cast<const float4*>(src + i));
-          v[i] += x4.x;
-          v[i + 1] += x4.y;
-          v[i + 2] += x4.z;
-          v[i + 3] += x4.w;
+            for (int i = 0; i < 4; ++i) r4[i] = silu(bf16_round(gg[i])) * bf16_round(uu[i]);
+            if (p.y_f32) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) static_cast<float*>(p.y)[off + i] = r4[i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) static_cast<__nv_bfloat16*>(p.y)[off + i] = __float2bfloat16_rn(r4[i]);
+            }
+          } else if (p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD) {
+            float* yy = static_cast<float*>(p.y) + off;
+            if (vec_y) {
+              float4 h4 = *reinterpret_cast<float4*>(yy);
+              h4.x += bf16_round(gg[0]); h4.y += bf16_round(gg[1]);
+              h4.z += bf16_round(gg[2]); h4.w += bf16_round(gg[3]);
+              *reinterpret_cast<float4*>(yy) = h4;
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) yy[i] = yy[i] + bf16_round(gg[i]);
+            }
+          } else if (p.y_f32) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) static_cast<float*>(p.y)[off + i] = gg[i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) static_cast<__nv_bfloat16*>(p.y)[off + i] = __float2bfloat16_rn(gg[i]);
+          }
         }
+        if (d == 0) p.counters[blockIdx.y * gridDim.x + blockIdx.x] = 0u;
       }
+    }
+    // accumulator columns j0 .. j0 + 15 of this token (no split-K)
+    auto chunk = [&](int j0, float (&v)[kChunk]) {
+      tmem_ld16(lane_addr + j0, v);
+      if (!ok)
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) v[i] = 0.0f;
     };
     if (finish) {
       if (swiglu) {
@@ -431,7 +476,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (nsplit > 1 && d == 0) p.counters[blockIdx.y * gridDim.x + blockIdx.x] = 0u;
     }
     tc_fence_before();
   }
