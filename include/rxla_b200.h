@@ -252,7 +252,16 @@ typedef struct rxla_b200_decoder_config {
   int32_t embedding_dtype; /* RXLA_B200_U8 (W8 tied head) or RXLA_B200_BF16 */
   int32_t group_size;      /* 0 = per-output-channel */
   int32_t max_batch, max_context;
-  int32_t tp_rank, tp_size; /* tensor parallel shard of this process */
+  /* Tensor-parallel shard of this process (tp_size 1: the whole model).
+   * Rank r holds q heads [r·Hq/tp, ...), kv heads [r·Hkv/tp, ...), the
+   * matching q/k/v rows of the fused qkv, columns of o_proj, intermediate
+   * slice [r·I/tp, ...) of gate/up rows and down_proj columns, and vocab
+   * slice [r·V/tp, ...) of the tied head; embeddings and norms are whole.
+   * o_proj / down_proj partial sums are all-reduced (f32) over `comm` before
+   * the bf16 rounding and residual add; the greedy token is the argmax over
+   * all ranks' slices (all-gathered candidates).  kv_heads, intermediate and
+   * vocab must divide by tp_size. */
+  int32_t tp_rank, tp_size;
 } rxla_b200_decoder_config;
 
 typedef struct rxla_b200_decoder rxla_b200_decoder;
@@ -279,8 +288,9 @@ int32_t rxla_b200_decoder_init_synthetic(rxla_b200_decoder* decoder, uint64_t se
 int32_t rxla_b200_decoder_reset(rxla_b200_decoder* decoder, void* stream);
 /* One decode step of `batch` sequences: tokens (device int32 [batch]) at the
  * next position of each sequence.  Writes the greedy next token (device
- * int32 [batch]) and, if logits is non-NULL, the f32 logits [batch, vocab]
- * of this shard.  Stream-ordered; replays a captured CUDA graph. */
+ * int32 [batch]) and, if logits is non-NULL, the f32 logits [batch, vocab/tp]
+ * of this shard's vocab slice.  Stream-ordered; replays a captured CUDA graph.
+ * With tp_size > 1 every rank calls this for the same step (collectives). */
 int32_t rxla_b200_decoder_step(rxla_b200_decoder* decoder, const int32_t* tokens,
                                int32_t batch, int32_t* next_tokens, float* logits,
                                void* stream);
@@ -289,7 +299,7 @@ int32_t rxla_b200_decoder_step(rxla_b200_decoder* decoder, const int32_t* tokens
 int32_t rxla_b200_decoder_step_host(rxla_b200_decoder* decoder, const int32_t* tokens_host,
                                     int32_t batch, int32_t* next_tokens_host, void* stream);
 /* Device buffers the step reads and writes: tokens in (int32 [max_batch]),
- * next tokens out (int32 [max_batch]) and logits (f32 [max_batch, vocab]).
+ * next tokens out (int32 [max_batch]) and logits (f32 [max_batch, vocab/tp]).
  * Passing tokens_in / tokens_out to rxla_b200_decoder_step skips its copies. */
 int32_t rxla_b200_decoder_io(rxla_b200_decoder* decoder, int32_t** tokens_in,
                              int32_t** tokens_out, float** logits);

@@ -26,6 +26,7 @@ F32, BF16, U8, I32 = 0, 1, 2, 3
 EPI_STORE, EPI_RESIDUAL_ADD, EPI_SWIGLU = 0, 1, 2
 KV_CLAMP, KV_CHECKED = 0, 1
 NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024  # RXLA_B200_NOALLOC_SCRATCH_BYTES
+COMM_ID_BYTES = 128  # RXLA_B200_COMM_ID_BYTES
 
 _STATUS_NAMES = {v: k for k, v in list(globals().items()) if k.isupper() and isinstance(v, int)
                  and v <= 0 and k not in ("F32",)}

@@ -28,6 +28,8 @@ struct Nccl {
   ncclResult_t (*destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   bool ok = false;
 };
@@ -43,8 +45,10 @@ static Nccl& nccl() {
     n.init_rank = reinterpret_cast<decltype(n.init_rank)>(dlsym(h, "ncclCommInitRank"));
     n.destroy = reinterpret_cast<decltype(n.destroy)>(dlsym(h, "ncclCommDestroy"));
     n.all_reduce = reinterpret_cast<decltype(n.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    n.all_gather = reinterpret_cast<decltype(n.all_gather)>(dlsym(h, "ncclAllGather"));
     n.error_string = reinterpret_cast<decltype(n.error_string)>(dlsym(h, "ncclGetErrorString"));
-    n.ok = n.get_unique_id && n.init_rank && n.destroy && n.all_reduce && n.error_string;
+    n.ok = n.get_unique_id && n.init_rank && n.destroy && n.all_reduce && n.all_gather &&
+           n.error_string;
   });
   return n;
 }
@@ -59,6 +63,17 @@ static int32_t nccl_fail(ncclResult_t r, const char* what) {
 int32_t comm_allreduce_f32(rxla_b200_comm* c, float* buf, int64_t count, cudaStream_t s) {
   return rxla_b200_allreduce(c, buf, count, RXLA_B200_F32, s);
 }
+
+int32_t comm_allgather_bytes(rxla_b200_comm* c, const void* in, void* out, int64_t bytes,
+                             cudaStream_t s) {
+  RXLA_REQUIRE(c && c->nccl && in && out && bytes >= 0, "allgather: bad arguments");
+  if (bytes == 0) return RXLA_B200_OK;
+  ncclResult_t r = comm::nccl().all_gather(in, out, (size_t)bytes, ncclUint8, c->nccl, s);
+  if (r != ncclSuccess) return comm::nccl_fail(r, "ncclAllGather");
+  return RXLA_B200_OK;
+}
+
+int32_t comm_world(const rxla_b200_comm* c) { return c ? c->world : 1; }
 
 }  // namespace rxla
 

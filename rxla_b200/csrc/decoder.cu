@@ -56,12 +56,33 @@ __device__ __forceinline__ float normal_at(uint64_t seed, uint64_t i) {
 
 // Synthetic W8 weights: N(0, 0.02) quantized symmetrically per row with the
 // clip at 4.5σ (scale = 0.02·4.5/127): q = clamp(round(z·127/4.5)).
+// Where the rows and columns of a rank's shard sit in the full (tp = 1)
+// matrix: up to three row segments, then a column offset.  Synthetic weights
+// are a function of the element's index in the full matrix, so every tensor-
+// parallel degree holds slices of one and the same model.
+struct Shard {
+  int64_t k_full;                 // columns of the full matrix
+  int64_t col_off;                // first full column of the shard
+  int32_t nseg;
+  int64_t seg_rows[3], seg_full_row[3];
+};
+
+__device__ __forceinline__ int64_t full_index(const Shard& sh, int64_t row, int64_t col) {
+  int64_t r = row;
+  for (int i = 0; i < sh.nseg; ++i) {
+    if (r < sh.seg_rows[i]) return (sh.seg_full_row[i] + r) * sh.k_full + sh.col_off + col;
+    r -= sh.seg_rows[i];
+  }
+  return 0;
+}
+
 __global__ void fill_w8_kernel(uint8_t* w, float* scale, int64_t rows, int64_t k, int64_t groups,
-                               uint64_t seed) {
+                               uint64_t seed, Shard sh) {
   const int64_t n = rows * k;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    float q = rintf(normal_at(seed, (uint64_t)i) * (127.0f / 4.5f));
+    const uint64_t g = (uint64_t)full_index(sh, i / k, i % k);
+    float q = rintf(normal_at(seed, g) * (127.0f / 4.5f));
     q = fminf(127.0f, fmaxf(-127.0f, q));
     w[i] = (uint8_t)((int)q + 128);
     if (i < rows * groups) scale[i] = 0.02f * 4.5f / 127.0f;
@@ -137,6 +158,74 @@ __global__ void residual_add_kernel(const float* __restrict__ part, float* __res
     h[i] = h[i] + bf16_round(part[i]);
 }
 
+// Tensor-parallel greedy head: each rank's best logit of its vocab slice
+// (value, global index), then the best over all ranks' candidates with the
+// same tie rule as a full argmax (highest value, then lowest index).
+struct Cand {
+  float v;
+  int32_t i;
+};
+
+__global__ void argmax_candidates_kernel(const float* __restrict__ logits, int64_t vocab_local,
+                                         int32_t index_offset, Cand* __restrict__ cand) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const float* r = logits + blockIdx.x * vocab_local;
+  float best = -INFINITY;
+  int32_t idx = 0x7fffffff;
+  for (int64_t c = threadIdx.x; c < vocab_local; c += blockDim.x) {
+    const float v = r[c];
+    if (v > best || (v == best && (int32_t)c < idx)) {
+      best = v;
+      idx = (int32_t)c;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int32_t si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ob > best || (ob == best && oi < idx)) {
+      best = ob;
+      idx = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sb[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sb[w] > best || (sb[w] == best && si[w] < idx)) {
+        best = sb[w];
+        idx = si[w];
+      }
+    cand[blockIdx.x].v = best;
+    cand[blockIdx.x].i = idx == 0x7fffffff ? 0x7fffffff : idx + index_offset;
+  }
+}
+
+__global__ void argmax_merge_kernel(const Cand* __restrict__ all, int32_t ranks, int32_t batch,
+                                    int32_t* __restrict__ out, int32_t* __restrict__ advance) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  float best = -INFINITY;
+  int32_t idx = 0x7fffffff;
+  for (int r = 0; r < ranks; ++r) {
+    const Cand c = all[(int64_t)r * batch + b];
+    if (c.v > best || (c.v == best && c.i < idx)) {
+      best = c.v;
+      idx = c.i;
+    }
+  }
+  out[b] = idx == 0x7fffffff ? 0 : idx;
+  if (advance) advance[b] += 1;
+}
+
 struct Param {
   std::string name;
   void* ptr;
@@ -197,6 +286,10 @@ struct rxla_b200_decoder {
   float* inv_freq = nullptr;
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  // tensor-parallel head: this rank's vocab slice and the argmax candidates
+  int64_t vocab_local = 0;
+  rxla::dec::Cand* cand = nullptr;      // [max_batch]
+  rxla::dec::Cand* cand_all = nullptr;  // [tp][max_batch]
   // split-K workspace of the tcgen05 GEMM path (batch > 8)
   void* gws = nullptr;
   size_t gws_bytes = 0;
@@ -272,12 +365,40 @@ static rxla_b200_paged_decode_args attention_args(const rxla_b200_decoder* d, co
   return a;
 }
 
+// Tensor-parallel LM head: this rank's logits slice [batch, vocab_local] is in
+// d->logits; pick its best per row, gather every rank's candidates, merge.
+static int32_t tp_head_tail(rxla_b200_decoder* d, int batch, cudaStream_t s) {
+  const int tp = d->cfg.tp_size;
+  cudaError_t e = launch_pdl(argmax_candidates_kernel, dim3(batch), dim3(1024), 0, s,
+                             (const float*)d->logits, d->vocab_local,
+                             (int32_t)(d->cfg.tp_rank * d->vocab_local), d->cand);
+  if (e != cudaSuccess) return cuda_fail(e, "argmax candidates launch");
+  int32_t st = comm_allgather_bytes(d->comm, d->cand, d->cand_all, (int64_t)batch * sizeof(Cand), s);
+  if (st) return st;
+  e = launch_pdl(argmax_merge_kernel, dim3((batch + 127) / 128), dim3(128), 0, s,
+                 (const Cand*)d->cand_all, (int32_t)tp, (int32_t)batch, d->tok_out, d->ctx);
+  if (e != cudaSuccess) return cuda_fail(e, "argmax merge launch");
+  return RXLA_B200_OK;
+}
+
+// h += bf16(part): the all-reduced row-parallel partial sums of o_proj / down.
+static int32_t tp_residual(rxla_b200_decoder* d, int batch, cudaStream_t s) {
+  const int64_t H = d->cfg.hidden;
+  int32_t st = comm_allreduce_f32(d->comm, d->part, batch * H, s);
+  if (st) return st;
+  cudaError_t e = launch_pdl(residual_add_kernel, dim3(std::max(1, (int)((batch * H + 1023) / 1024))),
+                             dim3(1024), 0, s, (const float*)d->part, d->h, (int64_t)batch * H);
+  if (e != cudaSuccess) return cuda_fail(e, "residual add launch");
+  return RXLA_B200_OK;
+}
+
 // Linears of a step with more tokens than one skinny pass: bf16 x from a
 // separate RMSNorm kernel, the tcgen05 GEMM (split-K over the runner's
 // workspace), the same epilogues; the LM head writes f32 logits and a
 // per-row argmax kernel picks the token and advances the position.
 static int32_t enqueue_gemm_layers(rxla_b200_decoder* d, int batch, cudaStream_t s) {
   const auto& c = d->cfg;
+  const bool tp = c.tp_size > 1;
   const int64_t H = c.hidden, D = c.head_dim;
   const int64_t qd = (int64_t)d->hq * D;
   auto gemm = [&](const void* x, int64_t k, const uint8_t* w, const float* sc, int64_t group,
@@ -308,25 +429,36 @@ static int32_t enqueue_gemm_layers(rxla_b200_decoder* d, int batch, cudaStream_t
     if (st) return st;
     rxla_b200_paged_decode_args a = attention_args(d, L, batch);
     st = attn::launch(&a, s, true);
-    if (!st) st = gemm(d->att, qd, L.wo, L.so, d->group_o, H, d->h, RXLA_B200_F32,
-                       RXLA_B200_EPI_RESIDUAL_ADD);
+    // row-parallel linears: the full residual add, or (tensor parallel) an
+    // unrounded partial that is all-reduced first
+    if (!st) st = tp ? gemm(d->att, qd, L.wo, L.so, d->group_o, H, d->part, RXLA_B200_F32,
+                            RXLA_B200_EPI_STORE)
+                     : gemm(d->att, qd, L.wo, L.so, d->group_o, H, d->h, RXLA_B200_F32,
+                            RXLA_B200_EPI_RESIDUAL_ADD);
+    if (!st && tp) st = tp_residual(d, batch, s);
     if (!st) st = rxla_b200_rms_norm_bf16(d->h, L.ln2, batch, H, c.rms_eps, d->xn, s);
     if (!st) st = gemm(d->xn, H, L.wgu, L.sgu, d->group_h, d->inter, d->act, RXLA_B200_BF16,
                        RXLA_B200_EPI_SWIGLU);
-    if (!st) st = gemm(d->act, d->inter, L.wd, L.sd, d->group_i, H, d->h, RXLA_B200_F32,
-                       RXLA_B200_EPI_RESIDUAL_ADD);
+    if (!st) st = tp ? gemm(d->act, d->inter, L.wd, L.sd, d->group_i, H, d->part, RXLA_B200_F32,
+                            RXLA_B200_EPI_STORE)
+                     : gemm(d->act, d->inter, L.wd, L.sd, d->group_i, H, d->h, RXLA_B200_F32,
+                            RXLA_B200_EPI_RESIDUAL_ADD);
+    if (!st && tp) st = tp_residual(d, batch, s);
     if (st) return st;
   }
   int32_t st = rxla_b200_rms_norm_bf16(d->h, d->final_norm, batch, H, c.rms_eps, d->xn, s);
   if (st) return st;
+  // the head over this rank's vocab slice (all of it without tensor parallelism)
+  const int64_t v0 = (int64_t)c.tp_rank * d->vocab_local;
   if (d->emb_w8) {
-    st = gemm(d->xn, H, d->emb_w8, d->emb_scale, d->group_h, d->vocab, d->logits, RXLA_B200_F32,
-              RXLA_B200_EPI_STORE);
+    st = gemm(d->xn, H, d->emb_w8 + v0 * H, d->emb_scale + v0 * d->groups_h, d->group_h,
+              d->vocab_local, d->logits, RXLA_B200_F32, RXLA_B200_EPI_STORE);
   } else {
-    st = rxla_b200_bf16_linear(d->xn, RXLA_B200_BF16, d->emb_bf16, batch, d->vocab, H, d->logits,
-                               RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
+    st = rxla_b200_bf16_linear(d->xn, RXLA_B200_BF16, d->emb_bf16 + v0 * H, batch, d->vocab_local,
+                               H, d->logits, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
   }
   if (st) return st;
+  if (tp) return tp_head_tail(d, batch, s);
   cudaError_t e = launch_pdl(argmax_kernel, dim3(batch), dim3(1024), 0, s, (const float*)d->logits,
                              (int64_t)d->vocab, d->tok_out, d->ctx);
   if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
@@ -343,7 +475,7 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
                              (int64_t)d->groups_h, (int64_t)d->group_h, d->h);
   if (e != cudaSuccess) return cuda_fail(e, "embed launch");
   const bool tp = c.tp_size > 1;
-  if (batch > kSkinnyTokens && !tp && d->gws_bytes > 0 && d->group_h % 64 == 0 &&
+  if (batch > kSkinnyTokens && d->gws_bytes > 0 && d->group_h % 64 == 0 &&
       d->group_o % 64 == 0 && d->group_i % 64 == 0)
     return enqueue_gemm_layers(d, batch, s);
   const int64_t qd = (int64_t)d->hq * D, kd = (int64_t)d->hkv * D;
@@ -402,11 +534,8 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
       st = rxla_b200_w8a16_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd,
                                   d->part, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
       if (st) return st;
-      st = comm_allreduce_f32(d->comm, d->part, batch * H, s);
+      st = tp_residual(d, batch, s);
       if (st) return st;
-      e = launch_pdl(residual_add_kernel, dim3(std::max(1, (int)((batch * H + 1023) / 1024))),
-                     dim3(1024), 0, s, (const float*)d->part, d->h, (int64_t)batch * H);
-      if (e != cudaSuccess) return cuda_fail(e, "residual add launch");
     }
     // act = silu(gate) * up of bf16(rms_norm(h) * post_attention_layernorm)
     na.norm_w = L.ln2;
@@ -426,14 +555,40 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
       st = rxla_b200_w8a16_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H,
                                   d->inter, d->part, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
       if (st) return st;
-      st = comm_allreduce_f32(d->comm, d->part, batch * H, s);
+      st = tp_residual(d, batch, s);
       if (st) return st;
-      e = launch_pdl(residual_add_kernel, dim3(std::max(1, (int)((batch * H + 1023) / 1024))),
-                     dim3(1024), 0, s, (const float*)d->part, d->h, (int64_t)batch * H);
-      if (e != cudaSuccess) return cuda_fail(e, "residual add launch");
     }
   }
-  if (tp) return fail(RXLA_B200_UNIMPLEMENTED, "tensor-parallel LM head argmax");
+  if (tp) {
+    // this rank's vocab slice of the tied head into d->logits, then the
+    // cross-rank argmax
+    const int64_t v0 = (int64_t)c.tp_rank * d->vocab_local;
+    int32_t st;
+    if (d->emb_w8) {
+      NormLinearArgs na{};
+      na.h = d->h;
+      na.norm_w = d->final_norm;
+      na.eps = c.rms_eps;
+      na.w = d->emb_w8 + v0 * H;
+      na.scale = d->emb_scale + v0 * d->groups_h;
+      na.group = d->group_h;
+      na.m = batch;
+      na.n = d->vocab_local;
+      na.k = H;
+      na.y = d->logits;
+      na.y_dtype = RXLA_B200_F32;
+      na.epilogue = RXLA_B200_EPI_STORE;
+      st = w8_norm_linear(na, s);
+    } else {
+      st = rxla_b200_rms_norm_bf16(d->h, d->final_norm, batch, H, c.rms_eps, d->xn, s);
+      if (!st)
+        st = rxla_b200_bf16_linear(d->xn, RXLA_B200_BF16, d->emb_bf16 + v0 * H, batch,
+                                   d->vocab_local, H, d->logits, RXLA_B200_F32,
+                                   RXLA_B200_EPI_STORE, s);
+    }
+    if (st) return st;
+    return tp_head_tail(d, batch, s);
+  }
   if (d->emb_w8) {
     // tied W8 head: logits = bf16(rms_norm(h) * norm) · Eᵀ (f32), greedy token
     // and the position advance in the same kernel
@@ -498,7 +653,7 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
   RXLA_REQUIRE(c.kv_heads % tp == 0 && c.intermediate % tp == 0,
                "decoder_create: kv_heads and intermediate must divide by tp_size");
   RXLA_REQUIRE(tp == 1 || comm, "decoder_create: tensor parallel needs a comm");
-  RXLA_REQUIRE(tp == 1, "decoder_create: tensor-parallel decoding is not available in this build");
+  RXLA_REQUIRE(c.vocab % tp == 0, "decoder_create: vocab must divide by tp_size (sharded head)");
   const int gsz = c.group_size;
   auto groups_for = [&](int64_t k) -> int64_t { return gsz > 0 ? k / gsz : 1; };
   RXLA_REQUIRE(gsz <= 0 || (c.hidden % gsz == 0 && (c.q_heads * c.head_dim / tp) % gsz == 0 &&
@@ -519,6 +674,7 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
   d->hkv = c.kv_heads / tp;
   d->inter = c.intermediate / tp;
   d->vocab = c.vocab;
+  d->vocab_local = c.vocab / tp;
   const int64_t H = c.hidden, D = c.head_dim, I = d->inter;
   d->qkv_rows = (int64_t)(d->hq + 2 * d->hkv) * D;
   d->groups_h = (int)groups_for(H);
@@ -619,7 +775,7 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
   if (B > dec::kSkinnyTokens) {
     size_t g = 0;
     const int64_t shapes[][3] = {{d->qkv_rows, H, 0}, {H, (int64_t)d->hq * D, 0},
-                                 {(int64_t)I, H, 1}, {H, (int64_t)I, 0}, {(int64_t)d->vocab, H, 0}};
+                                 {(int64_t)I, H, 1}, {H, (int64_t)I, 0}, {d->vocab_local, H, 0}};
     for (auto& sh : shapes)
       g = std::max(g, w8_gemm_workspace_bytes(B, sh[2] ? 2 * sh[0] : sh[0],
                                               dec::gemm_splits(B, sh[0], sh[1], sh[2] != 0)));
@@ -637,7 +793,9 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
       {(void**)&d->att, (size_t)B * d->hq * D * 2},
       {(void**)&d->act, (size_t)B * I * 2},
       {(void**)&d->part, (size_t)B * H * 4},
-      {(void**)&d->logits, (size_t)B * c.vocab * 4},
+      {(void**)&d->logits, (size_t)B * d->vocab_local * 4},
+      {(void**)&d->cand, (size_t)B * sizeof(dec::Cand)},
+      {(void**)&d->cand_all, (size_t)tp * B * sizeof(dec::Cand)},
       {(void**)&d->tok_in, (size_t)B * 4},
       {(void**)&d->tok_out, (size_t)B * 4},
       {(void**)&d->inv_freq, (size_t)D * 2},
@@ -693,7 +851,7 @@ extern "C" int32_t rxla_b200_decoder_destroy(rxla_b200_decoder* d) {
   }
   void* ptrs[] = {d->arena, d->page_table, d->ctx, d->h, d->xn, d->qkv, d->att, d->act,
                   d->part, d->logits, d->tok_in, d->tok_out, d->inv_freq, d->ws,
-                  d->gws, d->arg_val, d->arg_idx, d->arg_count};
+                  d->gws, d->arg_val, d->arg_idx, d->arg_count, d->cand, d->cand_all};
   for (void* p : ptrs) cudaFree(p);
   if (d->host_pinned) cudaFreeHost(d->host_pinned);
   delete d;
@@ -776,8 +934,38 @@ extern "C" int32_t rxla_b200_decoder_init_synthetic(rxla_b200_decoder* d, uint64
                                                                            : d->cfg.hidden);
       const int64_t rows = p.bytes / k;
       const int64_t groups = sc.bytes / 4 / rows;
+      // this rank's slice of the full matrix
+      const int r = d->cfg.tp_rank, tp = d->cfg.tp_size;
+      const int64_t H = d->cfg.hidden, D = d->cfg.head_dim;
+      const int64_t hq = d->hq, hkv = d->hkv, I = d->inter;
+      dec::Shard sh{};
+      sh.k_full = k;
+      sh.nseg = 1;
+      sh.seg_rows[0] = rows;
+      if (p.name.find("self_attn.qkv") != std::string::npos) {  // [q; k; v] of local heads
+        sh.nseg = 3;
+        sh.seg_rows[0] = hq * D;
+        sh.seg_full_row[0] = r * hq * D;
+        sh.seg_rows[1] = hkv * D;
+        sh.seg_full_row[1] = tp * hq * D + r * hkv * D;
+        sh.seg_rows[2] = hkv * D;
+        sh.seg_full_row[2] = tp * (hq + hkv) * D + r * hkv * D;
+      } else if (p.name.find("o_proj") != std::string::npos) {  // columns of local heads
+        sh.k_full = tp * hq * D;
+        sh.col_off = r * hq * D;
+      } else if (p.name.find("gate_up") != std::string::npos) {  // [gate; up] of local slice
+        sh.nseg = 2;
+        sh.seg_rows[0] = I;
+        sh.seg_full_row[0] = r * I;
+        sh.seg_rows[1] = I;
+        sh.seg_full_row[1] = tp * I + r * I;
+      } else if (p.name.find("down_proj") != std::string::npos) {  // columns of local slice
+        sh.k_full = tp * I;
+        sh.col_off = r * I;
+      }
+      (void)H;
       dec::fill_w8_kernel<<<grid, 256>>>(static_cast<uint8_t*>(p.ptr), static_cast<float*>(sc.ptr),
-                                         rows, k, groups, s);
+                                         rows, k, groups, s, sh);
     } else if (p.dtype == RXLA_B200_BF16) {
       dec::fill_bf16_kernel<<<grid, 256>>>(static_cast<__nv_bfloat16*>(p.ptr), p.bytes / 2, s);
     } else if (p.name.find(".scale") == std::string::npos) {
@@ -850,7 +1038,7 @@ extern "C" int32_t rxla_b200_decoder_step(rxla_b200_decoder* d, const int32_t* t
     RXLA_CUDA_CHECK(cudaMemcpyAsync(next_tokens, d->tok_out, (size_t)batch * 4,
                                     cudaMemcpyDeviceToDevice, s));
   if (logits)
-    RXLA_CUDA_CHECK(cudaMemcpyAsync(logits, d->logits, (size_t)batch * d->vocab * 4,
+    RXLA_CUDA_CHECK(cudaMemcpyAsync(logits, d->logits, (size_t)batch * d->vocab_local * 4,
                                     cudaMemcpyDeviceToDevice, s));
   return RXLA_B200_OK;
 }

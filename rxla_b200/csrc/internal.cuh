@@ -54,6 +54,10 @@ int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const f
 int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream);
 size_t w8_gemm_workspace_bytes(int64_t m, int64_t n_rows, int splits);
 int32_t comm_allreduce_f32(rxla_b200_comm* comm, float* buf, int64_t count, cudaStream_t s);
+// every rank's `bytes` from `in`, concatenated in rank order into `out`
+int32_t comm_allgather_bytes(rxla_b200_comm* comm, const void* in, void* out, int64_t bytes,
+                             cudaStream_t s);
+int32_t comm_world(const rxla_b200_comm* comm);
 
 namespace attn {
 int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable,

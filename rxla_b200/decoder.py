@@ -98,3 +98,69 @@ class Decoder:
         _lib.call("rxla_b200_decoder_step_host", self._h, tokens.ctypes.data_as(ctypes.c_void_p),
                   b, self._out_host.ctypes.data_as(ctypes.c_void_p), stream)
         return self._out_host[:b].copy()
+
+
+# ------------------------------------------------------------ tensor parallel
+
+class Comm:
+    """NCCL communicator of one tensor-parallel rank (rxla_b200_comm_*).
+
+    Rank 0 creates the unique id; the 128 bytes reach the other ranks through
+    any host channel — ``share`` is a callable that broadcasts them from rank 0
+    (for example via ``torch.distributed.broadcast_object_list``), in the way
+    rxla's KeyValueStore rendezvous moves its client id
+    (crates/rxla-pjrt/src/distributed.rs:40-120)."""
+
+    def __init__(self, rank: int, world: int, device: int, share):
+        uid = (ctypes.c_uint8 * _lib.COMM_ID_BYTES)()
+        if rank == 0:
+            _lib.call("rxla_b200_comm_unique_id", uid)
+        data = share(bytes(uid) if rank == 0 else None)
+        uid = (ctypes.c_uint8 * _lib.COMM_ID_BYTES).from_buffer_copy(data)
+        h = ctypes.c_void_p()
+        _lib.call("rxla_b200_comm_init", uid, rank, world, device, ctypes.byref(h))
+        self._h = h
+        self.rank, self.world = rank, world
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if self._h:
+            _lib.load().rxla_b200_comm_destroy(self._h)
+            self._h = None
+
+
+def shard_parameter(name: str, full: np.ndarray, rank: int, tp: int, *, q_heads: int,
+                    kv_heads: int, head_dim: int, intermediate: int, hidden: int,
+                    vocab: int, group_size: int = 0) -> np.ndarray:
+    """The slice of a full (tp = 1) parameter that rank `rank` of `tp` holds.
+
+    Column-parallel (split output rows): q_proj / k_proj / v_proj by heads,
+    gate_proj / up_proj by the intermediate slice.  Row-parallel (split input
+    columns): o_proj / down_proj weights; their per-output-channel scales are
+    whole, grouped scales are split with the columns.  Embeddings and norms
+    are whole (the tied head reads its vocab slice of the whole embedding)."""
+    if tp == 1:
+        return full
+    D = head_dim
+    if name.endswith(("q_proj.weight", "q_proj.scale")):
+        n = q_heads // tp * D
+        return full[rank * n:(rank + 1) * n]
+    if name.endswith(("k_proj.weight", "k_proj.scale", "v_proj.weight", "v_proj.scale")):
+        n = kv_heads // tp * D
+        return full[rank * n:(rank + 1) * n]
+    if name.endswith(("gate_proj.weight", "gate_proj.scale", "up_proj.weight", "up_proj.scale")):
+        n = intermediate // tp
+        return full[rank * n:(rank + 1) * n]
+    if name.endswith(("o_proj.weight", "down_proj.weight")):
+        k_full = full.shape[1]
+        n = k_full // tp
+        return full[:, rank * n:(rank + 1) * n]
+    if name.endswith(("o_proj.scale", "down_proj.scale")):
+        if full.shape[1] == 1:  # per output channel: the same scale on every rank
+            return full
+        n = full.shape[1] // tp
+        return full[:, rank * n:(rank + 1) * n]
+    return full

@@ -1,0 +1,130 @@
+"""Tensor-parallel decoding on two GPUs against the single-process oracle.
+
+Two ranks (one process per GPU) run the tiny W8 decoder at tp_size 2 over an
+NCCL communicator: each holds its heads, its intermediate slice and its vocab
+slice of the tied head, with the parameters sliced from the oracle's full
+model by ``shard_parameter``.  Each rank's logits slice and the greedy tokens
+(argmax over both slices) are compared with the oracle's full model.
+Skipped with fewer than two GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(layers=2, hidden=512, q_heads=8, kv_heads=2, head_dim=64, intermediate=1536,
+            vocab=4096)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, batch, q):
+    import ctypes
+    import torch.distributed as dist
+
+    import oracle
+    from rxla_b200 import _lib
+    from rxla_b200.decoder import Comm, Decoder, shard_parameter
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+
+        def share(data):
+            obj = [data]
+            dist.broadcast_object_list(obj, src=0)
+            return obj[0]
+
+        comm = Comm(rank, world, rank, share)
+        ref = oracle.Decoder(**TINY, embedding_bf16=False, group_size=0, max_batch=batch,
+                             max_context=64)
+        ref.init_synthetic(9)
+        gpu = Decoder(**TINY, embedding_dtype="u8", max_batch=batch, max_context=64, device=rank,
+                      comm=comm.handle, tp_rank=rank, tp_size=world)
+        H, D, I = TINY["hidden"], TINY["head_dim"], TINY["intermediate"]
+        rows = {"q_proj": TINY["q_heads"] * D, "k_proj": TINY["kv_heads"] * D,
+                "v_proj": TINY["kv_heads"] * D, "o_proj": H, "gate_proj": I, "up_proj": I,
+                "down_proj": H}
+        names = ["embed_tokens.weight", "embed_tokens.scale", "norm.weight"]
+        for i in range(TINY["layers"]):
+            p = f"layers.{i}."
+            names += [p + "input_layernorm.weight", p + "post_attention_layernorm.weight",
+                      p + "self_attn.q_norm.weight", p + "self_attn.k_norm.weight"]
+            names += [f"{p}self_attn.{pr}.{k}" for pr in ("q_proj", "k_proj", "v_proj", "o_proj")
+                      for k in ("weight", "scale")]
+            names += [f"{p}mlp.{pr}.{k}" for pr in ("gate_proj", "up_proj", "down_proj")
+                      for k in ("weight", "scale")]
+        kw = dict(q_heads=TINY["q_heads"], kv_heads=TINY["kv_heads"], head_dim=D, intermediate=I,
+                  hidden=H, vocab=TINY["vocab"])
+        for n in names:
+            a = np.array(ref.parameter(n))
+            for pr, r in rows.items():
+                if f".{pr}." in n:
+                    a = a.reshape(r, -1)
+            gpu.set_parameter(n, shard_parameter(n, a, rank, world, **kw))
+
+        V, vl = TINY["vocab"], TINY["vocab"] // world
+        prompt = oracle.randint(batch * 12, 21, 0, V).reshape(batch, 12)
+        lg = torch.empty(batch, vl, dtype=torch.float32, device="cuda")
+        tok_in = torch.empty(batch, dtype=torch.int32, device="cuda")
+        tok_out = torch.empty(batch, dtype=torch.int32, device="cuda")
+        s = torch.cuda.current_stream().cuda_stream
+        cur = prompt[:, 0].copy()
+        emax, flips, gaps, steps = 0.0, 0, [], 8
+        for t in range(prompt.shape[1] + steps):
+            l_ref, n_ref = ref.step(cur)
+            tok_in.copy_(torch.from_numpy(cur))
+            _lib.call("rxla_b200_decoder_step", gpu.handle, ctypes.c_void_p(tok_in.data_ptr()),
+                      batch, ctypes.c_void_p(tok_out.data_ptr()), ctypes.c_void_p(lg.data_ptr()),
+                      ctypes.c_void_p(s))
+            torch.cuda.synchronize()
+            err = float(np.abs(lg.cpu().numpy() - l_ref[:, rank * vl:(rank + 1) * vl]).max())
+            emax = max(emax, err)
+            if t + 1 >= prompt.shape[1]:
+                got = tok_out.cpu().numpy()
+                top2 = np.sort(l_ref, axis=1)[:, -2:]
+                for b in range(batch):
+                    if got[b] != n_ref[b]:
+                        flips += 1
+                        gaps.append(float(top2[b, 1] - top2[b, 0]))
+                cur = n_ref
+            else:
+                cur = prompt[:, t + 1].copy()
+        gpu.close()  # releases the captured graphs (they hold NCCL calls) before the comm
+        comm.close()
+        ref.close()
+        dist.destroy_process_group()
+        q.put((rank, emax, flips, gaps, None))
+    except Exception as e:
+        q.put((rank, None, None, None, repr(e)))
+
+
+@pytest.mark.parametrize("batch", [2, 12])
+def test_tp2_decoder_matches_oracle(batch):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor-parallel test needs two GPUs")
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, batch, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, emax, flips, gaps, err in results:
+        assert err is None, f"rank {rank}: {err}"
+        print(f"rank {rank}: logits max-abs {emax:.4g}, greedy flips {flips} (oracle gaps {gaps})")
+        assert emax <= 2e-2
+        assert all(g <= 2 * emax for g in gaps), "a greedy flip away from a near-tie"
