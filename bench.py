@@ -8,9 +8,10 @@ per-channel weights, synthetic seeded values), a 2048-token random prompt fed
 through the decoder, then greedy decode steps.  A "step" is one decode step
 at batch 1 (the headline `value`); the same is measured at batch 64.
 
-N > 1 (torchrun, one process per GPU): N independent replicas of the batch-1
-workload (no data-path collective); value = tokens of all ranks / max-over-
-ranks time ("scaling": "weak").
+N > 1 (torchrun, one process per GPU): the same 8B model sharded tensor-
+parallel over the N GPUs (heads, intermediate and vocab split; NCCL all-
+reduce after o_proj and down_proj over NVLink); value = tokens/s of the
+batch-1 sequence (and of batch 64), max-over-ranks time ("scaling": "strong").
 
 `--impl reference`: the reference path's CPU restatement (oracle/, the
 reference's Rust/XLA stack cannot run here) timed on all host cores, rank 0.
@@ -153,7 +154,7 @@ def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
     from rxla_b200 import _lib
-    from rxla_b200.decoder import Decoder
+    from rxla_b200.decoder import Comm, Decoder
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -162,9 +163,19 @@ def run_ours(args, rank, world, local_rank):
     lib = _lib.load()
     cfg = dict(CONFIG4)
     max_ctx = PROMPT + args.warmup + args.steps + 32
-    b64 = 64 if (world == 1 and not args.no_batch64) else 1
+    b64 = 1 if args.no_batch64 else 64
+    # N > 1: one 8B model sharded tensor-parallel over the N GPUs (NCCL over
+    # NVLink), the same synthetic model at every N
+    comm = None
+    if world > 1:
+        def share(data):
+            obj = [data]
+            torch.distributed.broadcast_object_list(obj, src=0)
+            return obj[0]
+        comm = Comm(rank, world, local_rank, share)
     dec = Decoder(**cfg, embedding_dtype="u8", max_batch=b64, max_context=max_ctx,
-                  device=local_rank)
+                  device=local_rank, comm=comm.handle if comm else None, tp_rank=rank,
+                  tp_size=world)
     dec.init_synthetic(1234)
 
     tin = ctypes.c_void_p(dec.tokens_in_ptr)
@@ -234,25 +245,28 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- roofline of the dominant kernel: the W8 linear, all launches of one
     # batch-1 step (qkv, o, gate/up, down per layer + tied head) replayed in a graph
-    roof = gemv_roofline(dec, cfg, dev, stream, lib)
-    status = lib.rxla_b200_device_status(0)
-    dec.close()
+    roof = gemv_roofline(dec, cfg, dev, stream, lib, world)
+    status = lib.rxla_b200_device_status(local_rank)
+    dec.close()  # releases the captured graphs (they hold NCCL calls) before the comm
+    if comm:
+        comm.close()
 
     weights, kv1 = step_bytes(cfg, 1, ctx_b1)
-    tok_s = world * args.steps / (ms1 / 1e3)
+    tok_s = args.steps / (ms1 / 1e3)  # one sequence, decoded by all N GPUs together
     out = {
         "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms1 / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u8 weights, bf16 activations, fp32 accumulate",
+        "scaling": "strong", "vs_baseline": None, "dtype": "u8 weights, bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded random W8 weights, random 2048-token prompt)",
         "config": {"workload": "config4: 8B-shaped W8 decoder, batch 1 decode after a 2048-token prompt",
                    "model": "qwen3-style-8B-shape", "layers": 36, "hidden": 4096, "vocab": 151936,
-                   "global_batch": world, "seq_len": PROMPT, "parallelism": f"replicas x{world}",
+                   "global_batch": 1, "seq_len": PROMPT,
+                   "parallelism": f"tp{world} (NCCL all-reduce after o_proj and down_proj)" if world > 1 else "single GPU",
                    "l2": "inputs > L2 (7.6 GB of weights per step)"},
         "step_gbs": (weights + kv1) / (ms1 / args.steps * 1e-3) / 1e9,
-        "step_frac_of_hbm": (weights + kv1) / (ms1 / args.steps * 1e-3) / 1e9 / measured_peaks()[0],
+        "step_frac_of_hbm": (weights + kv1) / (ms1 / args.steps * 1e-3) / 1e9 / (world * measured_peaks()[0]),
         "batch64": res64,
-        "e2e": {"value": world * args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 4,
+        "e2e": {"value": args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},
         "roofline": roof,
         "clocks": clocks,
@@ -262,15 +276,17 @@ def run_ours(args, rank, world, local_rank):
     return out
 
 
-def gemv_roofline(dec, cfg, dev, stream, lib):
-    """Time every W8 linear of one batch-1 step, replayed as one CUDA graph.
+def gemv_roofline(dec, cfg, dev, stream, lib, tp=1):
+    """Time every W8 linear of one batch-1 step of this rank's shard, replayed as
+    one CUDA graph.
 
     Algorithmic bytes per launch = N·K weights + 4·N scales + 2·K (x) + output;
     achieved = Σ bytes / Σ time of the launches (bytes-weighted mean)."""
     import torch
-    H, D, I, V = cfg["hidden"], cfg["head_dim"], cfg["intermediate"], cfg["vocab"]
-    qkv_rows = (cfg["q_heads"] + 2 * cfg["kv_heads"]) * D
-    x = torch.zeros(1, max(H, I, cfg["q_heads"] * D), dtype=torch.bfloat16, device=dev)
+    H, D = cfg["hidden"], cfg["head_dim"]
+    I, V, hq = cfg["intermediate"] // tp, cfg["vocab"] // tp, cfg["q_heads"] // tp
+    qkv_rows = (hq + 2 * cfg["kv_heads"] // tp) * D
+    x = torch.zeros(1, max(H, I, hq * D), dtype=torch.bfloat16, device=dev)
     ybf = torch.empty(1, max(qkv_rows, I), dtype=torch.bfloat16, device=dev)
     yf = torch.zeros(1, max(H, V), dtype=torch.float32, device=dev)
     s = ctypes.c_void_p(stream.cuda_stream)
@@ -278,15 +294,18 @@ def gemv_roofline(dec, cfg, dev, stream, lib):
     for l in range(cfg["layers"]):
         p = f"layers.{l}."
         launches.append((p + "self_attn.qkv", qkv_rows, H, ybf, 1, 0))
-        launches.append((p + "self_attn.o_proj", H, cfg["q_heads"] * D, yf, 0, 1))
+        launches.append((p + "self_attn.o_proj", H, hq * D, yf, 0, 1))
         launches.append((p + "mlp.gate_up", I, H, ybf, 1, 2))
         launches.append((p + "mlp.down_proj", H, I, yf, 0, 1))
     launches.append(("embed_tokens", V, H, yf, 0, 0))
     total_bytes = 0
     calls = []
+    rank = int(os.environ.get("RANK", "0"))
     for name, n, k, y, ybf16, epi in launches:
         w, _, _ = dec.parameter(name + ".weight")
         sc, _, _ = dec.parameter(name + ".scale")
+        if name == "embed_tokens":  # the rank's vocab slice of the tied head
+            w, sc = w + rank * V * k, sc + rank * V * 4
         rows = 2 * n if epi == 2 else n
         total_bytes += rows * k + 4 * rows + 2 * k + (2 if ybf16 else 4) * n * (2 if epi == 1 else 1)
         calls.append((x.data_ptr(), w, sc, k, n, k, y.data_ptr(), 1 if ybf16 else 0, epi))
