@@ -333,25 +333,42 @@ def gemv_roofline(dec, cfg, dev, stream, lib, tp=1):
     sec = e0.elapsed_time(e1) / 1e3 / reps
     peak, kind = measured_peaks()
     achieved = total_bytes / sec / 1e9
+    # DRAM bytes per launch: the algorithmic bytes scaled by the LM-head ncu
+    # capture's measured ratio (dram read + write 626.74 MB / algorithmic
+    # 623.25 MB, profiles/w8_gemv_lm_head_config4.md)
+    traffic = total_bytes / len(calls) * (626.74 / 623.25)
     return {"bound": "hbm", "kernel": "w8_skinny_kernel (all W8 linears of one batch-1 step)",
             "achieved": achieved, "peak": peak, "peak_kind": kind, "unit": "GB/s",
-            "frac": achieved / peak, "traffic": None, "launches": len(calls),
-            "avg_launch_us": sec / len(calls) * 1e6, "bytes_per_step": total_bytes}
+            "frac": achieved / peak, "traffic": traffic,
+            "traffic_note": "per launch, scaled from the LM-head ncu capture",
+            "launches": len(calls), "avg_launch_us": sec / len(calls) * 1e6,
+            "bytes_per_step": total_bytes}
 
 
 def profile_case(what: str):
     """Small, self-contained cases for ncu captures (no JSON line).
 
     gemv:      one W8 linear, N=32768 K=4096 M=1 (134 MB of weights > L2), 3 launches
+    head:      the tied LM head of config 4, N=151936 K=4096 M=1 (622 MB), 3 launches
+    gemm:      config-2 tensor-bound row, M=2048 N=4096 K=4096 on the tcgen05 GEMM, 3 launches
     step:      the config-4 decoder after a 256-token prompt, 2 decode steps inside
                the NVTX range "profile"
-    attention: config-3 shaped paged decode attention (batch 8, ctx ~U[512, 8192])
+    attention: config-3 paged decode attention (batch 64, 32 q / 8 kv heads, d 128,
+               ctx ~U[512, 8192]), 3 launches
     """
     import numpy as np
     import torch
     from rxla_b200 import _lib, nn
     dev = torch.device("cuda:0")
-    if what == "gemv":
+    if what in ("head", "gemm"):
+        m, n, k = (1, 151936, 4096) if what == "head" else (2048, 4096, 4096)
+        w = torch.randint(0, 256, (n, k), dtype=torch.uint8, device=dev)
+        sc = torch.rand(n, 1, device=dev) * 1e-2
+        x = torch.randn(m, k, device=dev).bfloat16()
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            nn.quantized_linear(x, w, sc, k, out=y)
+    elif what == "gemv":
         n, k = 32768, 4096
         w = torch.randint(0, 256, (n, k), dtype=torch.uint8, device=dev)
         sc = torch.rand(n, 1, device=dev) * 1e-2
@@ -375,7 +392,7 @@ def profile_case(what: str):
         torch.cuda.nvtx.range_pop()
         dec.close()
     elif what == "attention":
-        batch, hq, hkv, d, max_ctx = 8, 32, 8, 128, 8192
+        batch, hq, hkv, d, max_ctx = 64, 32, 8, 128, 8192
         cache = nn.PagedKvCache(batch=batch, kv_heads=hkv, head_dim=d, max_context=max_ctx)
         cache.k.normal_()
         cache.v.normal_()
@@ -402,7 +419,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-batch64", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["gemv", "step", "attention"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "step", "attention"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.profile:

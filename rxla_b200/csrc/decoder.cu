@@ -1010,6 +1010,23 @@ extern "C" int32_t rxla_b200_decoder_step(rxla_b200_decoder* d, const int32_t* t
   if (tokens != d->tok_in)
     RXLA_CUDA_CHECK(cudaMemcpyAsync(d->tok_in, tokens, (size_t)batch * 4,
                                     cudaMemcpyDeviceToDevice, s));
+  // RXLA_B200_NO_GRAPH=1: launch the step's kernels directly on `stream`
+  // (for profilers that attribute work per kernel launch)
+  static const bool no_graph = [] {
+    const char* v = getenv("RXLA_B200_NO_GRAPH");
+    return v && v[0] == '1';
+  }();
+  if (no_graph) {
+    int32_t st = dec::enqueue_step(d, batch, s);
+    if (st) return st;
+    if (next_tokens != d->tok_out)
+      RXLA_CUDA_CHECK(cudaMemcpyAsync(next_tokens, d->tok_out, (size_t)batch * 4,
+                                      cudaMemcpyDeviceToDevice, s));
+    if (logits)
+      RXLA_CUDA_CHECK(cudaMemcpyAsync(logits, d->logits, (size_t)batch * d->vocab_local * 4,
+                                      cudaMemcpyDeviceToDevice, s));
+    return RXLA_B200_OK;
+  }
   auto it = d->graphs.find(batch);
   if (it == d->graphs.end()) {
     // first use of this batch size: one eager step (sets kernel attributes and
