@@ -149,12 +149,20 @@ __device__ __forceinline__ void rope_q(float (&qv)[KS][4], const float2* cs, int
 }
 
 constexpr int kComputeWarps = 4;
-constexpr int kStagesV2 = 8;
+// Ring depth and occupancy: small batches (few CTAs, latency-bound) use a
+// deep ring; large batches fit three CTAs per SM with a shallower ring.  The
+// page iterations of a split go round-robin to the compute warps, so a stage
+// is always consumed by the same warp only if the depth is a multiple of the
+// warp count — otherwise a warp could wait on a stage barrier two phases
+// ahead, where the parity test aliases.
+constexpr int kStagesSmall = 8, kStagesLarge = 4;
+constexpr int kMergeBatch = 16;  // split partials in flight per thread in the final merge
 
-template <int D>
-__global__ void __launch_bounds__((kComputeWarps + 1) * 32)
+template <int D, int kStagesV2, int kMinBlocks>
+__global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const Params p) {
+  static_assert(kStagesV2 % kComputeWarps == 0, "ring depth must be a multiple of the warps");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   constexpr int DL = D / 32;     // dims per lane for the new k / v and the merges
   constexpr int KS = D / 16;     // k-steps of q·kᵀ
@@ -541,15 +549,15 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32)
           for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, wts[sp * 8 + j]);
           float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           float l = 0.0f;
-          for (int sp0 = 0; sp0 < n_splits; sp0 += 8) {
-            float4 x[8];
+          for (int sp0 = 0; sp0 < n_splits; sp0 += kMergeBatch) {
+            float4 x[kMergeBatch];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < kMergeBatch; ++u)
               if (sp0 + u < n_splits)
                 x[u] = __ldcg(reinterpret_cast<const float4*>(
                     p.ws_o + (base + (int64_t)(sp0 + u) * G + j) * D + d));
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < kMergeBatch; ++u) {
               if (sp0 + u < n_splits) {
                 const float mw = wts[(sp0 + u) * 8 + j];
                 const float wgt = mw == -INFINITY ? 0.0f : expf(mw - m);
@@ -717,7 +725,8 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   p.stage_bytes = 2 * attn::kPage * D * 2;
   p.batch = a->batch;
   p.ctx_stable = ctx_stable ? 1 : 0;
-  p.stages = attn::kStagesV2;
+  const bool large = a->batch >= 16;  // enough CTAs to fill the SMs several times
+  p.stages = large ? attn::kStagesLarge : attn::kStagesSmall;
   if (next) p.next = *next;
 
   CUtensorMap kmap, vmap;
@@ -732,18 +741,20 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   const dim3 grid(p.max_splits, a->kv_heads, a->batch);
   const dim3 block((attn::kComputeWarps + 1) * 32);
   cudaStream_t s = s_in;
+  auto go = [&](auto kernel) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e == cudaSuccess) e = launch_pdl(kernel, grid, block, smem, s, kmap, vmap, p);
+    return e;
+  };
+  using namespace attn;
   cudaError_t e;
-  if (D == 128) {
-    e = cudaFuncSetAttribute(attn::paged_decode_kernel<128>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess)
-      e = launch_pdl(attn::paged_decode_kernel<128>, grid, block, smem, s, kmap, vmap, p);
-  } else {
-    e = cudaFuncSetAttribute(attn::paged_decode_kernel<64>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess)
-      e = launch_pdl(attn::paged_decode_kernel<64>, grid, block, smem, s, kmap, vmap, p);
-  }
+  if (D == 128)
+    e = large ? go(paged_decode_kernel<128, kStagesLarge, 3>)
+              : go(paged_decode_kernel<128, kStagesSmall, 1>);
+  else
+    e = large ? go(paged_decode_kernel<64, kStagesLarge, 3>)
+              : go(paged_decode_kernel<64, kStagesSmall, 1>);
   if (e != cudaSuccess) return cuda_fail(e, "paged decode attention launch");
   return RXLA_B200_OK;
 }
