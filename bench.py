@@ -261,7 +261,9 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": "config4: 8B-shaped W8 decoder, batch 1 decode after a 2048-token prompt",
                    "model": "qwen3-style-8B-shape", "layers": 36, "hidden": 4096, "vocab": 151936,
                    "global_batch": 1, "seq_len": PROMPT,
-                   "parallelism": f"tp{world} (NCCL all-reduce after o_proj and down_proj)" if world > 1 else "single GPU",
+                   "parallelism": (f"tp{world} (" + ("NCCL" if os.environ.get("RXLA_B200_P2P") == "0"
+                                                      else "one-shot NVLink peer")
+                                   + " all-reduce after o_proj and down_proj)") if world > 1 else "single GPU",
                    "l2": "inputs > L2 (7.6 GB of weights per step)"},
         "step_gbs": (weights + kv1) / (ms1 / args.steps * 1e-3) / 1e9,
         "step_frac_of_hbm": (weights + kv1) / (ms1 / args.steps * 1e-3) / 1e9 / (world * measured_peaks()[0]),

@@ -325,6 +325,18 @@ int32_t rxla_b200_comm_destroy(rxla_b200_comm* comm);
 /* In-place bf16 or f32 sum all-reduce of `count` elements on `stream`. */
 int32_t rxla_b200_allreduce(rxla_b200_comm* comm, void* buffer, int64_t count,
                             int32_t dtype, void* stream);
+/* Collective: reserve IPC-shared peer buffers for one-shot all-reduces of up
+ * to `max_count` f32 (handles exchanged through the comm itself).  The
+ * decoder runner enables it for its row-parallel linears. */
+int32_t rxla_b200_comm_p2p_enable(rxla_b200_comm* comm, int64_t max_count);
+/* One-shot f32 sum all-reduce over NVLink peer memory: every rank pushes its
+ * `partial` [count] into every rank's buffer, waits (bounded, ~4 s, then
+ * RXLA_B200_DEADLINE_EXCEEDED in the device status word) for all pushes, and
+ * sums in rank order, so every rank gets the same bits.  residual == NULL:
+ * partial = sum; else residual += bf16(sum) (the row-parallel epilogue of
+ * o_proj / down_proj, crates/rxla-nn/src/layers.rs:293-298 rounding). */
+int32_t rxla_b200_p2p_allreduce_f32(rxla_b200_comm* comm, float* partial, float* residual,
+                                    int64_t count, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -115,6 +115,8 @@ SIGNATURES = {
     "rxla_b200_comm_init": (_i32, [_vp, _i32, _i32, _i32, ctypes.POINTER(_vp)]),
     "rxla_b200_comm_destroy": (_i32, [_vp]),
     "rxla_b200_allreduce": (_i32, [_vp, _vp, _i64, _i32, _vp]),
+    "rxla_b200_comm_p2p_enable": (_i32, [_vp, _i64]),
+    "rxla_b200_p2p_allreduce_f32": (_i32, [_vp, _vp, _vp, _i64, _vp]),
 }
 
 _lib = None

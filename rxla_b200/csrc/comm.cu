@@ -11,12 +11,46 @@
 
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "internal.cuh"
+
+namespace rxla {
+namespace p2p {
+constexpr int kMaxRanks = 8;
+constexpr int kChunk = 2048;  // floats of the all-reduce per CTA
+constexpr int kThreads = 256;
+
+// One rank's IPC-shared all-reduce buffer: two slots of [world][cap] f32
+// partials (alternating per call, so a rank may start the next all-reduce
+// while a slower peer still reads the last one), then [world][max_ctas]
+// arrival flags (monotonic epochs).
+struct Layout {
+  int64_t cap = 0;  // floats per (slot, rank)
+  int max_ctas = 0;
+  size_t data_bytes() const { return (size_t)2 * kMaxRanks * cap * 4; }
+  size_t bytes() const { return data_bytes() + (size_t)kMaxRanks * max_ctas * 8; }
+};
+
+struct Args {
+  const float* partial;  // this rank's partial sums [count]
+  float* out;            // sum (STORE) or the f32 residual (RESIDUAL_BF16)
+  int64_t count, cap;
+  int32_t rank, world, max_ctas, residual;
+  uint8_t* peer[kMaxRanks];  // every rank's buffer, mapped here (own one included)
+  uint64_t* epoch;           // [max_ctas] per-CTA call counter of this rank
+};
+}  // namespace p2p
+}  // namespace rxla
 
 struct rxla_b200_comm {
   ncclComm_t nccl = nullptr;
   int rank = 0, world = 1, device = 0;
+  // one-shot peer all-reduce (rxla_b200_comm_p2p_enable)
+  rxla::p2p::Layout p2p;
+  uint8_t* p2p_local = nullptr;
+  uint8_t* p2p_peer[rxla::p2p::kMaxRanks] = {};
+  uint64_t* p2p_epoch = nullptr;
 };
 
 namespace rxla {
@@ -59,6 +93,137 @@ static int32_t nccl_fail(ncclResult_t r, const char* what) {
 }
 
 }  // namespace comm
+
+namespace p2p {
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// CTA c owns floats [c·kChunk, (c+1)·kChunk): it pushes this rank's partial of
+// that range into slot (e & 1), row `rank`, of every rank's buffer (NVLink
+// stores), publishes epoch e in each rank's flag [rank][c], waits (bounded)
+// until every rank's flag [q][c] reached e in its own buffer, then sums the
+// rows in rank order 0..world-1 (the same order on every rank, so the result
+// is bit-identical everywhere) and stores the sum, or adds bf16(sum) to the
+// f32 residual (the row-parallel epilogue of o_proj / down_proj).
+__global__ void __launch_bounds__(kThreads) allreduce_kernel(const Args a) {
+  pdl_wait();  // the partials come from the previous kernel
+  pdl_launch_dependents();
+  const int c = blockIdx.x;
+  const uint64_t e = a.epoch[c] + 1;
+  const int slot = (int)(e & 1);
+  const int64_t lo = (int64_t)c * kChunk;
+  const int64_t n = min((int64_t)kChunk, a.count - lo);
+  const size_t data_bytes = (size_t)2 * kMaxRanks * a.cap * 4;
+  const bool vec = (a.count % 4) == 0;
+  // push
+  for (int q = 0; q < a.world; ++q) {
+    float* dst = reinterpret_cast<float*>(a.peer[q]) + ((int64_t)slot * kMaxRanks + a.rank) * a.cap + lo;
+    if (vec) {
+      for (int64_t i = threadIdx.x * 4; i < n; i += kThreads * 4)
+        *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(a.partial + lo + i);
+    } else {
+      for (int64_t i = threadIdx.x; i < n; i += kThreads) dst[i] = a.partial[lo + i];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // cumulative over the CTA's pushes (ordered by the barrier)
+    for (int q = 0; q < a.world; ++q)
+      st_relaxed_sys(reinterpret_cast<uint64_t*>(a.peer[q] + data_bytes) +
+                         (int64_t)a.rank * a.max_ctas + c,
+                     e);
+  }
+  // wait for every rank's push of this range
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < a.world) {
+    const uint64_t* flag = reinterpret_cast<const uint64_t*>(a.peer[a.rank] + data_bytes) +
+                           (int64_t)threadIdx.x * a.max_ctas + c;
+    if (ld_acquire_sys(flag) < e) {
+      const uint64_t t0 = globaltimer();
+      while (ld_acquire_sys(flag) < e) {
+        if (globaltimer() - t0 > kWaitTimeoutNs) {
+          record_device_error(RXLA_B200_DEADLINE_EXCEEDED);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok) return;
+  const float* rows = reinterpret_cast<const float*>(a.peer[a.rank]) + (int64_t)slot * kMaxRanks * a.cap + lo;
+  if (vec) {
+    for (int64_t i = threadIdx.x * 4; i < n; i += kThreads * 4) {
+      float4 acc = __ldcv(reinterpret_cast<const float4*>(rows + i));
+      for (int q = 1; q < a.world; ++q) {
+        const float4 v = __ldcv(reinterpret_cast<const float4*>(rows + (int64_t)q * a.cap + i));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      float4* o = reinterpret_cast<float4*>(a.out + lo + i);
+      if (a.residual) {
+        float4 h = *o;
+        h.x += bf16_round(acc.x);
+        h.y += bf16_round(acc.y);
+        h.z += bf16_round(acc.z);
+        h.w += bf16_round(acc.w);
+        *o = h;
+      } else {
+        *o = acc;
+      }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+      float acc = __ldcv(rows + i);
+      for (int q = 1; q < a.world; ++q) acc += __ldcv(rows + (int64_t)q * a.cap + i);
+      if (a.residual) a.out[lo + i] += bf16_round(acc);
+      else a.out[lo + i] = acc;
+    }
+  }
+  if (threadIdx.x == 0) a.epoch[c] = e;
+}
+
+}  // namespace p2p
+
+// The peer all-reduce of the decoder's row-parallel linears: out = Σ partial
+// (residual false) or out += bf16(Σ partial) (residual true).  Falls back to
+// NCCL + a residual kernel when the comm has no peer buffers.
+bool comm_has_p2p(const rxla_b200_comm* c) { return c && c->p2p_local != nullptr; }
+
+int32_t comm_p2p_allreduce(rxla_b200_comm* c, const float* partial, float* out, int64_t count,
+                           bool residual, cudaStream_t s) {
+  RXLA_REQUIRE(c && c->p2p_local, "p2p allreduce: not enabled on this comm");
+  RXLA_REQUIRE(count >= 0 && count <= c->p2p.cap, "p2p allreduce: count above the reserved capacity");
+  RXLA_REQUIRE(partial && out, "p2p allreduce: null buffer");
+  if (count == 0) return RXLA_B200_OK;
+  p2p::Args a{};
+  a.partial = partial;
+  a.out = out;
+  a.count = count;
+  a.cap = c->p2p.cap;
+  a.rank = c->rank;
+  a.world = c->world;
+  a.max_ctas = c->p2p.max_ctas;
+  a.residual = residual ? 1 : 0;
+  for (int q = 0; q < c->world; ++q) a.peer[q] = c->p2p_peer[q];
+  a.epoch = c->p2p_epoch;
+  const int grid = (int)((count + p2p::kChunk - 1) / p2p::kChunk);
+  cudaError_t e = launch_pdl(p2p::allreduce_kernel, dim3(grid), dim3(p2p::kThreads), 0, s, a);
+  if (e != cudaSuccess) return cuda_fail(e, "p2p allreduce launch");
+  return RXLA_B200_OK;
+}
 
 int32_t comm_allreduce_f32(rxla_b200_comm* c, float* buf, int64_t count, cudaStream_t s) {
   return rxla_b200_allreduce(c, buf, count, RXLA_B200_F32, s);
@@ -116,8 +281,102 @@ extern "C" int32_t rxla_b200_comm_init(const uint8_t id[RXLA_B200_COMM_ID_BYTES]
   return RXLA_B200_OK;
 }
 
+extern "C" int32_t rxla_b200_comm_p2p_enable(rxla_b200_comm* c, int64_t max_count) {
+  RXLA_REQUIRE(c && c->nccl, "comm_p2p_enable: comm not initialised");
+  RXLA_REQUIRE(max_count > 0, "comm_p2p_enable: max_count must be positive");
+  RXLA_REQUIRE(c->world <= p2p::kMaxRanks, "comm_p2p_enable: at most 8 ranks");
+  if (c->p2p_local) {
+    RXLA_REQUIRE(max_count <= c->p2p.cap, "comm_p2p_enable: already enabled with a smaller capacity");
+    return RXLA_B200_OK;
+  }
+  RXLA_CUDA_CHECK(cudaSetDevice(c->device));
+  p2p::Layout L;
+  L.cap = (max_count + 3) / 4 * 4;
+  L.max_ctas = (int)((L.cap + p2p::kChunk - 1) / p2p::kChunk);
+  uint8_t* local = nullptr;
+  uint64_t* epoch = nullptr;
+  uint8_t* xfer = nullptr;
+  cudaError_t e = cudaMalloc(&local, L.bytes());
+  if (e == cudaSuccess) e = cudaMemset(local, 0, L.bytes());
+  if (e == cudaSuccess) e = cudaMalloc(&epoch, (size_t)L.max_ctas * 8);
+  if (e == cudaSuccess) e = cudaMemset(epoch, 0, (size_t)L.max_ctas * 8);
+  if (e == cudaSuccess) e = cudaMalloc(&xfer, (size_t)p2p::kMaxRanks * sizeof(cudaIpcMemHandle_t));
+  cudaIpcMemHandle_t mine{};
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine, local);
+  // every rank's handle, through the comm itself (no host store needed)
+  std::vector<cudaIpcMemHandle_t> all(c->world);
+  if (e == cudaSuccess) e = cudaMemcpy(xfer + c->rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
+  int32_t st = RXLA_B200_OK;
+  if (e == cudaSuccess) {
+    ncclResult_t r = comm::nccl().all_gather(xfer + c->rank * sizeof(mine), xfer, sizeof(mine),
+                                             ncclUint8, c->nccl, nullptr);
+    if (r != ncclSuccess) st = comm::nccl_fail(r, "comm_p2p_enable: handle exchange");
+  }
+  if (e == cudaSuccess && !st) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess && !st) e = cudaMemcpy(all.data(), xfer, c->world * sizeof(mine), cudaMemcpyDeviceToHost);
+  uint8_t* peer[p2p::kMaxRanks] = {};
+  for (int q = 0; q < c->world && e == cudaSuccess && !st; ++q) {
+    if (q == c->rank) {
+      peer[q] = local;
+      continue;
+    }
+    void* ptr = nullptr;
+    e = cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess);
+    peer[q] = static_cast<uint8_t*>(ptr);
+  }
+  // every rank must take the same path: agree on success (min over ranks)
+  if (!st) {
+    const int32_t mine_ok = e == cudaSuccess ? 1 : 0;
+    cudaGetLastError();
+    int32_t* flag = reinterpret_cast<int32_t*>(xfer);
+    cudaError_t e2 = cudaMemcpy(flag, &mine_ok, 4, cudaMemcpyHostToDevice);
+    ncclResult_t r = e2 == cudaSuccess ? comm::nccl().all_reduce(flag, flag, 1, ncclInt32, ncclMin,
+                                                                 c->nccl, nullptr)
+                                       : ncclInternalError;
+    int32_t all_ok = 0;
+    if (r == ncclSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+        cudaMemcpy(&all_ok, flag, 4, cudaMemcpyDeviceToHost) == cudaSuccess && !all_ok &&
+        e == cudaSuccess)
+      e = cudaErrorPeerAccessUnsupported;  // a peer failed: nobody uses the buffers
+    if (r != ncclSuccess) st = comm::nccl_fail(r, "comm_p2p_enable: agreement");
+  }
+  if (xfer) cudaFree(xfer);
+  if (e != cudaSuccess || st) {
+    for (int q = 0; q < c->world; ++q)
+      if (q != c->rank && peer[q]) cudaIpcCloseMemHandle(peer[q]);
+    if (local) cudaFree(local);
+    if (epoch) cudaFree(epoch);
+    return st ? st : cuda_fail(e, "comm_p2p_enable");
+  }
+  c->p2p = L;
+  c->p2p_local = local;
+  c->p2p_epoch = epoch;
+  for (int q = 0; q < c->world; ++q) c->p2p_peer[q] = peer[q];
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_p2p_allreduce_f32(rxla_b200_comm* c, float* partial, float* residual,
+                                               int64_t count, void* stream) {
+  return comm_p2p_allreduce(c, partial, residual ? residual : partial, count, residual != nullptr,
+                            static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int32_t rxla_b200_comm_destroy(rxla_b200_comm* c) {
   if (!c) return RXLA_B200_OK;
+  if (c->p2p_local) {
+    cudaSetDevice(c->device);
+    cudaDeviceSynchronize();
+    for (int q = 0; q < c->world; ++q)
+      if (q != c->rank && c->p2p_peer[q]) cudaIpcCloseMemHandle(c->p2p_peer[q]);
+    // every rank has unmapped the peers' buffers before any rank frees its own
+    // (collective, like the rest of the comm's life cycle)
+    if (c->nccl &&
+        comm::nccl().all_reduce(c->p2p_epoch, c->p2p_epoch, 1, ncclUint64, ncclSum, c->nccl,
+                                nullptr) == ncclSuccess)
+      cudaDeviceSynchronize();
+    cudaFree(c->p2p_local);
+    cudaFree(c->p2p_epoch);
+  }
   if (c->nccl) comm::nccl().destroy(c->nccl);
   delete c;
   return RXLA_B200_OK;

@@ -401,6 +401,8 @@ static int32_t tp_head_tail(rxla_b200_decoder* d, int batch, cudaStream_t s) {
 // h += bf16(part): the all-reduced row-parallel partial sums of o_proj / down.
 static int32_t tp_residual(rxla_b200_decoder* d, int batch, cudaStream_t s) {
   const int64_t H = d->cfg.hidden;
+  // one-shot peer all-reduce fused with the residual add, else NCCL + a kernel
+  if (comm_has_p2p(d->comm)) return comm_p2p_allreduce(d->comm, d->part, d->h, batch * H, true, s);
   int32_t st = comm_allreduce_f32(d->comm, d->part, batch * H, s);
   if (st) return st;
   cudaError_t e = launch_pdl(residual_add_kernel, dim3(std::max(1, (int)((batch * H + 1023) / 1024))),
@@ -1021,6 +1023,14 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
     cudaMemset(L.vc, 0, cache_bytes);
   }
   RXLA_CUDA_CHECK(cudaDeviceSynchronize());
+  if (tp > 1) {
+    // row-parallel all-reduces over NVLink peer memory (collective; every rank
+    // ends up on the same path).  RXLA_B200_P2P=0 keeps NCCL.
+    const char* pv = getenv("RXLA_B200_P2P");
+    if (!(pv && pv[0] == '0') &&
+        rxla_b200_comm_p2p_enable(comm, (int64_t)c.max_batch * H) != RXLA_B200_OK)
+      cudaGetLastError();  // NCCL path
+  }
   *out = d;
   return RXLA_B200_OK;
 }

@@ -104,6 +104,10 @@ int32_t comm_allreduce_f32(rxla_b200_comm* comm, float* buf, int64_t count, cuda
 int32_t comm_allgather_bytes(rxla_b200_comm* comm, const void* in, void* out, int64_t bytes,
                              cudaStream_t s);
 int32_t comm_world(const rxla_b200_comm* comm);
+bool comm_has_p2p(const rxla_b200_comm* comm);
+// out = Σ partial over ranks (residual false) or out += bf16(Σ partial)
+int32_t comm_p2p_allreduce(rxla_b200_comm* comm, const float* partial, float* out, int64_t count,
+                           bool residual, cudaStream_t s);
 
 namespace attn {
 int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable,

@@ -1,4 +1,5 @@
-"""Tensor-parallel decoding on two GPUs against the single-process oracle.
+"""Tensor-parallel decoding on two GPUs against the single-process oracle,
+and the one-shot peer all-reduce against the rank-order sum.
 
 Two ranks (one process per GPU) run the tiny W8 decoder at tp_size 2 over an
 NCCL communicator: each holds its heads, its intermediate slice and its vocab
@@ -128,3 +129,77 @@ def test_tp2_decoder_matches_oracle(batch):
         print(f"rank {rank}: logits max-abs {emax:.4g}, greedy flips {flips} (oracle gaps {gaps})")
         assert emax <= 2e-2
         assert all(g <= 2 * emax for g in gaps), "a greedy flip away from a near-tie"
+
+
+def _p2p_main(rank, world, port, q):
+    import ctypes
+    import torch.distributed as dist
+
+    from rxla_b200 import _lib
+    from rxla_b200.decoder import Comm
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+
+        def share(data):
+            obj = [data]
+            dist.broadcast_object_list(obj, src=0)
+            return obj[0]
+
+        comm = Comm(rank, world, rank, share)
+        cap = 64 * 4096
+        _lib.call("rxla_b200_comm_p2p_enable", comm.handle, cap)
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        worst = 0.0
+        # counts: one row, a ragged (non-float4) count, several CTAs, the capacity
+        for it, count in enumerate([4096, 5, 2048 * 3 + 4, cap, 4096, 1]):
+            for residual in (False, True):
+                parts = [np.random.default_rng(100 * it + r).standard_normal(count).astype(np.float32)
+                         for r in range(world)]
+                total = parts[0].copy()
+                for r in range(1, world):
+                    total = total + parts[r]  # rank order, f32
+                h0 = np.random.default_rng(7 + it).standard_normal(count).astype(np.float32)
+                part = torch.from_numpy(parts[rank]).cuda()
+                h = torch.from_numpy(h0).cuda()
+                _lib.call("rxla_b200_p2p_allreduce_f32", comm.handle,
+                          ctypes.c_void_p(part.data_ptr()),
+                          ctypes.c_void_p(h.data_ptr()) if residual else None, count, s)
+                torch.cuda.synchronize()
+                if residual:  # h += bf16(sum), round to nearest even
+                    want = h0 + torch.from_numpy(total).bfloat16().float().numpy()
+                    got = h.cpu().numpy()
+                else:
+                    want, got = total, part.cpu().numpy()
+                worst = max(worst, float(np.abs(got - want).max()))
+        status = _lib.load().rxla_b200_device_status(1)
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, worst, status, None))
+    except Exception as e:
+        q.put((rank, None, None, repr(e)))
+
+
+def test_p2p_allreduce_matches_rank_order_sum():
+    """One-shot NVLink all-reduce (IPC-mapped peer buffers, bounded flag
+    waits): store mode equals the f32 rank-order sum bit for bit; residual
+    mode adds its bf16 rounding to the residual; several calls in a row
+    exercise the alternating slots and the per-CTA epochs."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("peer all-reduce test needs two GPUs")
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_p2p_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, worst, status, err in results:
+        assert err is None, f"rank {rank}: {err}"
+        assert status == 0, f"rank {rank}: device status {status}"
+        assert worst == 0.0, f"rank {rank}: max deviation {worst}"
