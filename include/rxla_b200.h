@@ -310,6 +310,12 @@ int32_t rxla_b200_decoder_kv_cache(rxla_b200_decoder* decoder, int32_t layer, vo
                                    void** v_pages, int64_t* bytes);
 /* Current context length of each sequence (device int32 [max_batch]). */
 int32_t rxla_b200_decoder_context_lengths(rxla_b200_decoder* decoder, const int32_t** lens);
+/* Set the context length of sequences 0..count-1 (host int32, each below
+ * max_context) after their K/V pages were written by another engine, e.g. a
+ * prefill: the next step appends at that position.  Synchronises `stream`. */
+int32_t rxla_b200_decoder_set_context_lengths(rxla_b200_decoder* decoder,
+                                              const int32_t* lens_host, int32_t count,
+                                              void* stream);
 
 /* ---------------------------------------------------- tensor-parallel comm
  *

@@ -109,6 +109,7 @@ SIGNATURES = {
     "rxla_b200_decoder_step": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
     "rxla_b200_decoder_step_host": (_i32, [_vp, _vp, _i32, _vp, _vp]),
     "rxla_b200_decoder_context_lengths": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "rxla_b200_decoder_set_context_lengths": (_i32, [_vp, _vp, _i32, _vp]),
     "rxla_b200_decoder_kv_cache": (_i32, [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                           ctypes.POINTER(_i64)]),
     "rxla_b200_comm_unique_id": (_i32, [_vp]),

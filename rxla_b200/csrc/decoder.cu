@@ -1197,6 +1197,27 @@ extern "C" int32_t rxla_b200_decoder_context_lengths(rxla_b200_decoder* d, const
   return RXLA_B200_OK;
 }
 
+extern "C" int32_t rxla_b200_decoder_set_context_lengths(rxla_b200_decoder* d,
+                                                         const int32_t* lens_host, int32_t count,
+                                                         void* stream) {
+  RXLA_REQUIRE(d && lens_host, "decoder_set_context_lengths: null argument");
+  RXLA_REQUIRE(count >= 0 && count <= d->cfg.max_batch,
+               "decoder_set_context_lengths: count out of range");
+  for (int32_t b = 0; b < count; ++b)
+    RXLA_REQUIRE(lens_host[b] >= 0 && lens_host[b] < d->cfg.max_context,
+                 "decoder_set_context_lengths: length must leave room for the next token");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  RXLA_CUDA_CHECK(cudaSetDevice(d->device));
+  if (count == 0) return RXLA_B200_OK;
+  // staged through the pinned buffer so the copy is stream-ordered
+  RXLA_CUDA_CHECK(cudaStreamSynchronize(s));
+  std::memcpy(d->host_pinned, lens_host, (size_t)count * 4);
+  RXLA_CUDA_CHECK(cudaMemcpyAsync(d->ctx, d->host_pinned, (size_t)count * 4,
+                                  cudaMemcpyHostToDevice, s));
+  RXLA_CUDA_CHECK(cudaStreamSynchronize(s));
+  return RXLA_B200_OK;
+}
+
 extern "C" int32_t rxla_b200_decoder_step(rxla_b200_decoder* d, const int32_t* tokens,
                                           int32_t batch, int32_t* next_tokens, float* logits,
                                           void* stream) {

@@ -86,6 +86,13 @@ class Decoder:
     def reset(self, stream=None):
         _lib.call("rxla_b200_decoder_reset", self._h, stream)
 
+    def set_context_lengths(self, lens, stream=None):
+        """Context length of sequences 0..len(lens)-1, after their K/V pages
+        were written by another engine (rxla_b200_decoder_set_context_lengths)."""
+        a = np.ascontiguousarray(np.asarray(lens, dtype=np.int32))
+        _lib.call("rxla_b200_decoder_set_context_lengths", self._h,
+                  a.ctypes.data_as(ctypes.c_void_p), len(a), stream)
+
     def step_device(self, batch: int, stream=None, logits_ptr=None):
         """One step on tokens already in the runner's device input buffer."""
         _lib.call("rxla_b200_decoder_step", self._h, self.tokens_in_ptr, batch,
