@@ -409,6 +409,8 @@ def profile_case(what: str):
     gemm:      config-2 tensor-bound row, M=2048 N=4096 K=4096 on the tcgen05 GEMM, 3 launches
     step:      the config-4 decoder after a 256-token prompt, 2 decode steps inside
                the NVTX range "profile"
+    step64:    config 4 at batch 64 (2048 context), 1 step inside "profile"
+    step5:     config 5 (32B shape) at batch 32 (4096 context), 1 step inside "profile"
     attention: config-3 paged decode attention (batch 64, 32 q / 8 kv heads, d 128,
                ctx ~U[512, 8192]), 3 launches
     """
@@ -447,6 +449,24 @@ def profile_case(what: str):
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
         dec.close()
+    elif what in ("step64", "step5"):
+        # batch 64 of config 4 at a 2048 context / batch 32 of config 5 at 4096:
+        # 2 warm-up steps, then 1 step inside the NVTX range "profile"
+        from rxla_b200.decoder import Decoder
+        cfg, batch, ctx = (CONFIG4, 64, PROMPT) if what == "step64" else (CONFIG5, BATCH5, PROMPT5)
+        dec = Decoder(**cfg, embedding_dtype="u8", max_batch=batch, max_context=ctx + 16)
+        dec.init_synthetic(1)
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        dec.set_context_lengths([ctx] * batch, s)
+        tout = ctypes.c_void_p(dec.tokens_out_ptr)
+        for _ in range(2):
+            _lib.call("rxla_b200_decoder_step", dec.handle, tout, batch, tout, None, s)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("profile")
+        _lib.call("rxla_b200_decoder_step", dec.handle, tout, batch, tout, None, s)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        dec.close()
     elif what == "attention":
         batch, hq, hkv, d, max_ctx = 64, 32, 8, 128, 8192
         cache = nn.PagedKvCache(batch=batch, kv_heads=hkv, head_dim=d, max_context=max_ctx)
@@ -476,7 +496,7 @@ def main():
     ap.add_argument("--no-batch64", action="store_true")
     ap.add_argument("--no-config5", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "step", "attention"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "step", "step64", "step5", "attention"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.profile:

@@ -324,15 +324,40 @@ namespace dec {
 // Batches above one skinny-GEMV pass run their linears on the tcgen05 GEMM.
 constexpr int kSkinnyTokens = 8;
 
-// Split-K depth for a GEMM of m tokens × n outputs × k: enough CTAs to cover
-// the SMs, at least two 64-wide k-blocks per split, at most 16 splits.
+// Split-K depth for a GEMM of m tokens × n outputs × k (one CTA per SM): the
+// depth that minimises the grid's critical path, counted in 16 KB weight
+// k-blocks: waves × (k-blocks per split + the split's partial tile write) +
+// the last CTA's ordered reduction of all partials; at least two 64-wide
+// k-blocks per split, at most 16 splits.  Against ceil(SMs / tiles) (which
+// put a few CTAs in a second, nearly empty wave): config 4 batch 64 5.7k ->
+// 6.4k tok/s, config 5 batch 32 1.25k -> 1.52k.  RXLA_B200_SPLIT_POLICY=0
+// restores the old rule, 1 drops the partial-traffic terms.
 static int gemm_splits(int64_t m, int64_t n, int64_t k, bool swiglu) {
   if (n % 64 != 0) return 1;
   int dev = 0;
   cudaGetDevice(&dev);
+  const int64_t sms = sm_count(dev);
   const int64_t tiles = ((m + 127) / 128) * (swiglu ? (n + 127) / 128 : (n + 255) / 256);
-  const int64_t want = (sm_count(dev) + tiles - 1) / tiles;
-  return (int)std::max<int64_t>(1, std::min<int64_t>({want, 16, k / 128}));
+  const int64_t kb = (k + 63) / 64;
+  const int64_t smax = std::max<int64_t>(1, std::min<int64_t>(16, kb / 2));
+  const char* pv = getenv("RXLA_B200_SPLIT_POLICY");
+  const int policy = pv ? atoi(pv) : 2;
+  if (policy == 0)
+    return (int)std::max<int64_t>(1, std::min<int64_t>({(sms + tiles - 1) / tiles, 16, k / 128}));
+  // partial tile (m rows × 256 f32) in units of one k-block of weights (16 KB)
+  const double pu = policy == 2 ? (double)std::min<int64_t>(m, 128) / 16.0 : 0.0;
+  int64_t best = 1;
+  double best_cost = 1e300;
+  for (int64_t sp = 1; sp <= smax; ++sp) {
+    const double waves = (double)((tiles * sp + sms - 1) / sms);
+    const double cost = waves * ((double)((kb + sp - 1) / sp) + (sp > 1 ? pu : 0.0)) +
+                        (sp > 1 ? (double)sp * pu : 0.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return (int)best;
 }
 
 static int32_t alloc_dev(void** p, size_t bytes) {
