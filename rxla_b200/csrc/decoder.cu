@@ -324,40 +324,10 @@ namespace dec {
 // Batches above one skinny-GEMV pass run their linears on the tcgen05 GEMM.
 constexpr int kSkinnyTokens = 8;
 
-// Split-K depth for a GEMM of m tokens × n outputs × k (one CTA per SM): the
-// depth that minimises the grid's critical path, counted in 16 KB weight
-// k-blocks: waves × (k-blocks per split + the split's partial tile write) +
-// the last CTA's ordered reduction of all partials; at least two 64-wide
-// k-blocks per split, at most 16 splits.  Against ceil(SMs / tiles) (which
-// put a few CTAs in a second, nearly empty wave): config 4 batch 64 5.7k ->
-// 6.4k tok/s, config 5 batch 32 1.25k -> 1.52k.  RXLA_B200_SPLIT_POLICY=0
-// restores the old rule, 1 drops the partial-traffic terms.
-static int gemm_splits(int64_t m, int64_t n, int64_t k, bool swiglu) {
-  if (n % 64 != 0) return 1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int64_t sms = sm_count(dev);
-  const int64_t tiles = ((m + 127) / 128) * (swiglu ? (n + 127) / 128 : (n + 255) / 256);
-  const int64_t kb = (k + 63) / 64;
-  const int64_t smax = std::max<int64_t>(1, std::min<int64_t>(16, kb / 2));
-  const char* pv = getenv("RXLA_B200_SPLIT_POLICY");
-  const int policy = pv ? atoi(pv) : 2;
-  if (policy == 0)
-    return (int)std::max<int64_t>(1, std::min<int64_t>({(sms + tiles - 1) / tiles, 16, k / 128}));
-  // partial tile (m rows × 256 f32) in units of one k-block of weights (16 KB)
-  const double pu = policy == 2 ? (double)std::min<int64_t>(m, 128) / 16.0 : 0.0;
-  int64_t best = 1;
-  double best_cost = 1e300;
-  for (int64_t sp = 1; sp <= smax; ++sp) {
-    const double waves = (double)((tiles * sp + sms - 1) / sms);
-    const double cost = waves * ((double)((kb + sp - 1) / sp) + (sp > 1 ? pu : 0.0)) +
-                        (sp > 1 ? (double)sp * pu : 0.0);
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = sp;
-    }
-  }
-  return (int)best;
+// Split-K depth of the decoder's GEMMs (w8_gemm_splits); the group size is
+// the runner's for that input width.
+static int gemm_splits(int64_t m, int64_t n, int64_t k, int64_t group, bool swiglu) {
+  return w8_gemm_splits(m, n, k, group, swiglu);
 }
 
 static int32_t alloc_dev(void** p, size_t bytes) {
@@ -460,7 +430,7 @@ static int32_t enqueue_gemm_layers(rxla_b200_decoder* d, int batch, cudaStream_t
     g.ldy = n;
     g.y_dtype = y_dtype;
     g.epilogue = epi;
-    g.splits = gemm_splits(batch, n, k, epi == RXLA_B200_EPI_SWIGLU);
+    g.splits = gemm_splits(batch, n, k, group, epi == RXLA_B200_EPI_SWIGLU);
     g.ws = d->gws;
     g.ws_bytes = d->gws_bytes;
     return w8_gemm(g, s);
@@ -984,11 +954,14 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
   d->ws_bytes = need_ws;
   if (B > dec::kSkinnyTokens) {
     size_t g = 0;
-    const int64_t shapes[][3] = {{d->qkv_rows, H, 0}, {H, (int64_t)d->hq * D, 0},
-                                 {(int64_t)I, H, 1}, {H, (int64_t)I, 0}, {d->vocab_local, H, 0}};
+    const int64_t shapes[][4] = {{d->qkv_rows, H, 0, d->group_h},
+                                 {H, (int64_t)d->hq * D, 0, d->group_o},
+                                 {(int64_t)I, H, 1, d->group_h},
+                                 {H, (int64_t)I, 0, d->group_i},
+                                 {d->vocab_local, H, 0, d->group_h}};
     for (auto& sh : shapes)
       g = std::max(g, w8_gemm_workspace_bytes(B, sh[2] ? 2 * sh[0] : sh[0],
-                                              dec::gemm_splits(B, sh[0], sh[1], sh[2] != 0)));
+                                              dec::gemm_splits(B, sh[0], sh[1], sh[3], sh[2] != 0)));
     d->gws_bytes = g;
   }
   struct A {

@@ -507,16 +507,31 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace gemm
 
+// Decode batches run w8_gemm_dec unless RXLA_B200_GEMM_DEC=0.
+bool gemm_dec_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("RXLA_B200_GEMM_DEC");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// enough counters for either GEMM's tiles (128-token × 256-row or 128-row)
+int64_t w8_gemm_counter_slots(int64_t m, int64_t n_rows) {
+  return ((m + 31) / 32) * ((n_rows + 127) / 128);
+}
+
 size_t w8_gemm_workspace_bytes(int64_t m, int64_t n_rows, int splits) {
   if (splits <= 1) return 0;
-  const int64_t tiles = ((m + gemm::kBM - 1) / gemm::kBM) * ((n_rows + gemm::kBN - 1) / gemm::kBN);
-  const size_t counters = ((size_t)tiles * 4 + 255) / 256 * 256;
+  const size_t counters = ((size_t)w8_gemm_counter_slots(m, n_rows) * 4 + 255) / 256 * 256;
   return counters + (size_t)splits * m * n_rows * 4;
 }
 
 int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream) {
   using namespace gemm;
   RXLA_REQUIRE(a.m > 0 && a.n > 0 && a.k > 0, "w8 gemm: empty shape");
+  // decode batches: weights on the MMA's M side, dequantized into tensor memory
+  if (w8_gemm_dec_applies(a.m, a.k, a.group)) return w8_gemm_dec(a, stream);
   RXLA_REQUIRE(a.k % kBK == 0, "w8 gemm: K must be a multiple of 64");
   RXLA_REQUIRE(a.group % kBK == 0 && a.k % a.group == 0, "w8 gemm: group must be a multiple of 64");
   RXLA_REQUIRE(reinterpret_cast<uintptr_t>(a.x) % 16 == 0 && reinterpret_cast<uintptr_t>(a.w) % 16 == 0,
@@ -575,8 +590,7 @@ int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.epilogue = a.epilogue;
   p.k_per_split = (int32_t)(kb_per * kBK);
   if (splits > 1) {
-    const int64_t tiles = tiles_m * tiles_n;
-    const size_t counters = ((size_t)tiles * 4 + 255) / 256 * 256;
+    const size_t counters = ((size_t)w8_gemm_counter_slots(a.m, n_rows) * 4 + 255) / 256 * 256;
     p.counters = static_cast<uint32_t*>(a.ws);
     p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(a.ws) + counters);
   }
