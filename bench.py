@@ -411,6 +411,8 @@ def profile_case(what: str):
                the NVTX range "profile"
     step64:    config 4 at batch 64 (2048 context), 1 step inside "profile"
     step5:     config 5 (32B shape) at batch 32 (4096 context), 1 step inside "profile"
+    gemmdec:   a 2-layer config-4-shaped decoder at batch 64, 1 step (the decode-batch
+               GEMM launches: qkv, o, gate/up, down per layer, then the head)
     attention: config-3 paged decode attention (batch 64, 32 q / 8 kv heads, d 128,
                ctx ~U[512, 8192]), 3 launches
     """
@@ -448,6 +450,19 @@ def profile_case(what: str):
             _lib.call("rxla_b200_decoder_step", dec.handle, tout, 1, tout, None, s)
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
+        dec.close()
+    elif what == "gemmdec":
+        # the decode-batch GEMMs of a 2-layer config-4-shaped decoder at batch 64
+        # (2048 context): 1 step, kernels launched directly (RXLA_B200_NO_GRAPH=1)
+        from rxla_b200.decoder import Decoder
+        cfg = dict(CONFIG4, layers=2)
+        dec = Decoder(**cfg, embedding_dtype="u8", max_batch=64, max_context=PROMPT + 16)
+        dec.init_synthetic(1)
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        dec.set_context_lengths([PROMPT] * 64, s)
+        tout = ctypes.c_void_p(dec.tokens_out_ptr)
+        _lib.call("rxla_b200_decoder_step", dec.handle, tout, 64, tout, None, s)
+        torch.cuda.synchronize()
         dec.close()
     elif what in ("step64", "step5"):
         # batch 64 of config 4 at a 2048 context / batch 32 of config 5 at 4096:
@@ -496,7 +511,7 @@ def main():
     ap.add_argument("--no-batch64", action="store_true")
     ap.add_argument("--no-config5", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "step", "step64", "step5", "attention"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "gemmdec", "step", "step64", "step5", "attention"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.profile:
