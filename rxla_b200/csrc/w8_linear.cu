@@ -192,7 +192,29 @@ __device__ __forceinline__ void box_mma(float (&acc)[4], const uint8_t* wg, int 
   }
 }
 
-template <bool SWIGLU, bool GROUPED, int XMODE>
+// The same box with the lane's x fragments held in registers (loaded once per
+// launch when the whole row is one stage: the x shared-memory loads per box
+// were half of the loop's shared traffic).
+template <bool POST>
+__device__ __forceinline__ void box_mma_xr(float (&acc)[4], const uint8_t* wg, int row8,
+                                           const uint32_t (&bx)[8], const RowScale& ra,
+                                           const RowScale& rb) {
+  const uint4 lo = *reinterpret_cast<const uint4*>(wg);
+  const uint4 hi = *reinterpret_cast<const uint4*>(wg + row8);
+  const uint32_t wl[4] = {lo.x, lo.y, lo.z, lo.w};
+  const uint32_t wh[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+  for (int st = 0; st < 4; ++st) {
+    uint32_t a[4];
+    deq4<POST>(wl[st], ra, a[0], a[2]);
+    deq4<POST>(wh[st], rb, a[1], a[3]);
+    mma_bf16_16816(acc, a, bx[2 * st], bx[2 * st + 1]);
+  }
+}
+
+constexpr int kXRegBoxes = 4;  // x of up to 4 boxes per warp (k <= 4096) in registers
+
+template <bool SWIGLU, bool GROUPED, int XMODE, bool XREG = false>
 __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Bars& bars = *reinterpret_cast<Bars*>(smem_raw);
@@ -520,6 +542,22 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     if (!consumer_sync(&bars.grp[1], 0)) return;
   }
   const uint8_t* xrow = xs + (g % p.m) * p.x_pitch;
+  // XREG (one stage holds whole rows, k <= 4096): this warp's boxes of the
+  // row are column blocks warp + 16 i; their x fragments stay in registers
+  uint32_t xr[XREG ? kXRegBoxes : 1][8];
+  const int nbx = XREG ? p.k / (kConsumerWarps * 64) : 0;
+  if (XREG) {
+#pragma unroll
+    for (int i = 0; i < (XREG ? kXRegBoxes : 1); ++i) {
+      if (i < nbx) {
+        const uint8_t* xc = xrow + ((warp + kConsumerWarps * i) * 64 + 16 * q) * 2;
+        const uint4 v0 = *reinterpret_cast<const uint4*>(xc);
+        const uint4 v1 = *reinterpret_cast<const uint4*>(xc + 16);
+        xr[i][0] = v0.x; xr[i][1] = v0.y; xr[i][2] = v0.z; xr[i][3] = v0.w;
+        xr[i][4] = v1.x; xr[i][5] = v1.y; xr[i][6] = v1.z; xr[i][7] = v1.w;
+      }
+    }
+  }
 
   // weight rows of this lane's A fragment in block blk: tile rows g and g + 8
   auto block_rows = [&](int blk, bool& va, bool& vb, int& ra, int& rb) {
@@ -577,7 +615,31 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     }
     float acc0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     float acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int kc = 0; kc < p.k_chunks; ++kc) {
+    if (XREG) {
+      // one stage per block; boxes i and i + 1 go to the two accumulators,
+      // as in the loop below (the same sums)
+      if (!mbar_wait(&bars.full[s], ph)) return;
+      const uint8_t* wg = stages + (size_t)s * p.stage_bytes + lane_off;
+#pragma unroll
+      for (int i = 0; i < (XREG ? kXRegBoxes : 1); i += 2) {
+        if (i >= nbx) break;
+        const bool two = i + 1 < nbx;
+        if (post) {
+          box_mma_xr<true>(acc0, wg + i * kBoxStep, row8, xr[i], rsa, rsb);
+          if (two) box_mma_xr<true>(acc1, wg + (i + 1) * kBoxStep, row8, xr[i + 1], rsa, rsb);
+        } else {
+          box_mma_xr<false>(acc0, wg + i * kBoxStep, row8, xr[i], rsa, rsb);
+          if (two) box_mma_xr<false>(acc1, wg + (i + 1) * kBoxStep, row8, xr[i + 1], rsa, rsb);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.empty[s]);
+      if (++s == S) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+    for (int kc = 0; kc < (XREG ? 0 : p.k_chunks); ++kc) {
       const int col0 = kc * p.kc;
       const int nbox = min(p.kc, p.k - col0) >> 6;
       if (!mbar_wait(&bars.full[s], ph)) return;
@@ -700,6 +762,15 @@ static size_t env_size(const char* name, size_t dflt) {
   return v ? (size_t)strtoull(v, nullptr, 10) : dflt;
 }
 
+// x fragments in registers for rows of at most 4096 (RXLA_B200_GEMV_XREG=0: off)
+static bool xreg_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("RXLA_B200_GEMV_XREG");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 static int32_t plan_skinny(Params& p, size_t& smem) {
   // tuning knobs (bytes): largest stage, shared-memory budget of one CTA
   static const size_t max_stage = env_size("RXLA_B200_GEMV_STAGE", 80 * 1024);
@@ -719,7 +790,10 @@ static int32_t plan_skinny(Params& p, size_t& smem) {
 
 template <bool SWIGLU, bool GROUPED, int XMODE>
 static cudaError_t launch_variant(const Params& p, int grid, size_t smem, cudaStream_t stream) {
-  auto k = w8_skinny_kernel<SWIGLU, GROUPED, XMODE>;
+  auto k = w8_skinny_kernel<SWIGLU, GROUPED, XMODE, false>;
+  if (!GROUPED && p.k_chunks == 1 && p.k % (kConsumerWarps * 64) == 0 &&
+      p.k <= kXRegBoxes * kConsumerWarps * 64 && xreg_enabled())
+    k = w8_skinny_kernel<SWIGLU, GROUPED, XMODE, !GROUPED>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(k, dim3(grid), dim3(kThreads), smem, stream, p);
