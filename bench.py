@@ -99,11 +99,16 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def launches_per_step(cfg):
-    """Our kernels in one decode step: embedding, per layer qkv (norm fused),
-    attention, o_proj, gate/up (norm fused), down, and the LM head with the
-    norm and the greedy argmax fused."""
-    return 1 + cfg["layers"] * 5 + 1
+def launches_per_step(cfg, tp=1):
+    """Our kernels in one batch-1 decode step: embedding, per layer qkv (norm
+    fused), attention, o_proj, gate/up (norm fused), down, and the LM head with
+    the norm and the greedy argmax fused.  Tensor parallel adds per layer the
+    two peer all-reduce kernels (fused with the residual add) and, after the
+    head, the argmax candidate and merge kernels (the head's own argmax is
+    not fused then); NCCL's all-gather of the candidates is not ours."""
+    if tp == 1:
+        return 1 + cfg["layers"] * 5 + 1
+    return 1 + cfg["layers"] * 7 + 1 + 2
 
 
 def measured_peaks():
@@ -280,7 +285,7 @@ def run_ours(args, rank, world, local_rank):
                 "d2h_bytes_per_step": 4},
         "roofline": roof,
         "clocks": clocks,
-        "gpu_launches": args.steps * launches_per_step(cfg),
+        "gpu_launches": args.steps * launches_per_step(cfg, world),
         "device_status": status,
     }
     return out
