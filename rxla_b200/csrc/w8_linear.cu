@@ -283,15 +283,9 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     // weights do not depend on the previous kernel: fill the ring first
     const int pre = min(S, total);
     for (int it = 0; it < pre; ++it) issue(it, it);
-    pdl_wait();  // x is the previous kernel's output
-    if (XMODE == kXBf16) {
-      if (lane == 0) mbar_arrive_expect_tx(&bars.x_full, (uint32_t)(p.m * p.k * 2));
-      __syncwarp();
-      if (lane < p.m)
-        bulk_g2s_nohint(xs + lane * p.x_pitch,
-                        static_cast<const uint8_t*>(p.x) + (int64_t)lane * p.ldx * 2,
-                        (uint32_t)(p.k * 2), &bars.x_full);
-    }
+    // bf16 x is copied by the consumers after griddepcontrol.wait: a bulk
+    // copy issued here would queue behind the ring's weight copies in this
+    // SM's TMA engine (down_proj's 48 row copies delayed x by ~1.7 µs)
     for (int it = pre; it < total; ++it) {
       const int s = it % S;
       if (!mbar_wait(&bars.empty[s], ((it / S) - 1) & 1)) return;
@@ -433,7 +427,15 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
   // -------------------------------------------------------------- consumers
   const int ctid = threadIdx.x;  // 0 .. 511
   if (XMODE == kXBf16) {
-    if (!mbar_wait(&bars.x_full, 0)) return;
+    pdl_wait();  // x is the previous kernel's output
+    const int chunks = p.k / 8;  // 16-byte chunks of a token row (k % 64 == 0)
+    for (int t = 0; t < p.m; ++t) {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) +
+                                                        (int64_t)t * p.ldx * 2);
+      uint4* dst = reinterpret_cast<uint4*>(xs + t * p.x_pitch);
+      for (int c = ctid; c < chunks; c += kConsumerWarps * 32) dst[c] = __ldcg(src + c);
+    }
+    if (!consumer_sync(&bars.grp[1], 0)) return;
   } else {
     pdl_wait();  // x / h come from the previous kernel
     const float* xf = static_cast<const float*>(p.x);
