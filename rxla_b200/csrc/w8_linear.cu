@@ -426,6 +426,33 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
 
   // -------------------------------------------------------------- consumers
   const int ctid = threadIdx.x;  // 0 .. 511
+  // weight rows of this lane's A fragment in block blk: tile rows g and g + 8
+  // (the first block's scales are constants: loaded before the wait below)
+  auto block_rows = [&](int blk, bool& va, bool& vb, int& ra, int& rb) {
+    const int r0 = r_begin + blk * out_rows;
+    const int nr = min(out_rows, r_end - r0);
+    if (SWIGLU) {
+      va = vb = g < nr;
+      ra = r0 + g;
+      rb = p.n + r0 + g;
+    } else {
+      va = g < nr;
+      vb = g + 8 < nr;
+      ra = r0 + g;
+      rb = r0 + g + 8;
+    }
+  };
+  // per-channel scales are loaded one block ahead, so their latency hides
+  // behind the current block's tiles
+  float next_sa = 0.0f, next_sb = 0.0f;
+  if (!GROUPED && n_blocks > 0) {
+    bool va, vb;
+    int ra, rb;
+    block_rows(0, va, vb, ra, rb);
+    next_sa = va ? __ldg(p.scale + ra) : 0.0f;
+    next_sb = vb ? __ldg(p.scale + rb) : 0.0f;
+  }
+
   if (XMODE == kXBf16) {
     pdl_wait();  // x is the previous kernel's output
     const int chunks = p.k / 8;  // 16-byte chunks of a token row (k % 64 == 0)
@@ -437,7 +464,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     }
     if (!consumer_sync(&bars.grp[1], 0)) return;
   } else {
-    pdl_wait();  // x / h come from the previous kernel
     const float* xf = static_cast<const float*>(p.x);
     // This runs between the previous kernel and the first tile, so every
     // global load of a token is issued before any is used: one round trip per
@@ -446,6 +472,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     constexpr int kXV = 4;
     constexpr int kCT = kConsumerWarps * 32;
     const bool regs = p.k <= kXV * 4 * kCT;
+    // the norm weights are constants: fetched before the wait, so their
+    // latency overlaps the previous kernel's tail
     float4 nw[kXV];
 #pragma unroll
     for (int i = 0; i < kXV; ++i) {
@@ -454,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
                   ? __ldg(reinterpret_cast<const float4*>(p.norm_w + c))
                   : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
     }
+    pdl_wait();  // x / h come from the previous kernel
     int round = 0;
     for (int t0 = 0; t0 < p.m; t0 += 2, ++round) {
       const int nt = min(2, p.m - t0);
@@ -559,32 +588,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
         xr[i][4] = v1.x; xr[i][5] = v1.y; xr[i][6] = v1.z; xr[i][7] = v1.w;
       }
     }
-  }
-
-  // weight rows of this lane's A fragment in block blk: tile rows g and g + 8
-  auto block_rows = [&](int blk, bool& va, bool& vb, int& ra, int& rb) {
-    const int r0 = r_begin + blk * out_rows;
-    const int nr = min(out_rows, r_end - r0);
-    if (SWIGLU) {
-      va = vb = g < nr;
-      ra = r0 + g;
-      rb = p.n + r0 + g;
-    } else {
-      va = g < nr;
-      vb = g + 8 < nr;
-      ra = r0 + g;
-      rb = r0 + g + 8;
-    }
-  };
-  // per-channel scales are loaded one block ahead, so their latency hides
-  // behind the current block's tiles
-  float next_sa = 0.0f, next_sb = 0.0f;
-  if (!GROUPED && n_blocks > 0) {
-    bool va, vb;
-    int ra, rb;
-    block_rows(0, va, vb, ra, rb);
-    next_sa = va ? __ldg(p.scale + ra) : 0.0f;
-    next_sb = vb ? __ldg(p.scale + rb) : 0.0f;
   }
 
   // ring position, advanced incrementally (no division in the loop)
