@@ -617,16 +617,23 @@ static int32_t make_page_map(CUtensorMap* map, void* base, int64_t num_pages, in
 // SM when every sequence is at max_context, with at most 32 pages per split
 // for balance, but never more than 32 splits (the merge depth).
 // Pages per split: enough CTAs for ~4 per SM over all (sequence, kv head)
-// pairs, at least ceil(pages / 32) pages, at most 48 (RXLA_B200_ATTN_PPS_CAP):
-// longer splits cost a fuller last wave but fewer merges (batch 64 at 2048
-// context: 111.4 µs with 32, 105.8 with 48, 109.7 with 64).
+// pairs, at least ceil(pages / 16) pages (RXLA_B200_ATTN_MAX_SPLITS: at most
+// 16 splits per sequence and head; batch 1 at 2048 context: 9.8 µs with 16,
+// 11.2 with 32, 16.9 with 48 — the last CTA merges every split), at most 48
+// (RXLA_B200_ATTN_PPS_CAP: longer splits cost a fuller last wave but fewer
+// merges; batch 64 at 2048 context: 111.4 µs with 32, 105.8 with 48, 109.7
+// with 64).
 static int pages_per_split(int batch, int kv_heads, int max_pages) {
   static const int64_t cap = [] {
     const char* v = getenv("RXLA_B200_ATTN_PPS_CAP");
     return v ? (int64_t)std::max(1, atoi(v)) : (int64_t)48;
   }();
+  static const int64_t most = [] {  // splits per (sequence, kv head) at most
+    const char* v = getenv("RXLA_B200_ATTN_MAX_SPLITS");
+    return v ? (int64_t)std::max(1, atoi(v)) : (int64_t)16;
+  }();
   const int64_t want = ((int64_t)batch * kv_heads * max_pages + 4 * 148 - 1) / (4 * 148);
-  const int64_t depth = ((int64_t)max_pages + 31) / 32;
+  const int64_t depth = ((int64_t)max_pages + most - 1) / most;
   return (int)std::max<int64_t>(1, std::max(depth, std::min<int64_t>(cap, want)));
 }
 
