@@ -112,10 +112,11 @@ def test_w8_embedding_grouped_batch3(cuda):
     ref.close()
 
 
-@pytest.mark.parametrize("batch,emb_bf16,group", [(12, True, 0), (20, False, 128)])
+@pytest.mark.parametrize("batch,emb_bf16,group", [(12, True, 0), (20, False, 128), (64, False, 0)])
 def test_gemm_path_batches(cuda, batch, emb_bf16, group):
     """Batches above one skinny pass (8 tokens) run every linear on the tcgen05
-    GEMM with split-K; same tokens and logits bar as the batch-1 path."""
+    decode GEMM (32 or 64 token columns) with split-K; same tokens and logits
+    bar as the batch-1 path."""
     prompt = oracle.randint(batch * 16, 11 + batch, 0, 4096).reshape(batch, 16)
     ref, gpu = _pair(batch=batch, max_context=64, embedding_bf16=emb_bf16, group_size=group,
                      seed=batch)
