@@ -105,3 +105,15 @@ def test_decoder_config_validation_without_cuda():
     assert lib.rxla_b200_decoder_create(ctypes.byref(cfg), 0, None, ctypes.byref(h)) == \
         _lib.INVALID_ARGUMENT
     assert lib.rxla_b200_decoder_destroy(None) == _lib.OK
+
+
+def test_context_lengths_and_peer_allreduce_validation_without_cuda():
+    """The entry points added for external prefill and the one-shot peer
+    all-reduce reject bad arguments before any CUDA call."""
+    lib = _lib.load()
+    lens = (ctypes.c_int32 * 2)(5, 7)
+    assert lib.rxla_b200_decoder_set_context_lengths(None, lens, 2, None) == _lib.INVALID_ARGUMENT
+    assert lib.rxla_b200_comm_p2p_enable(None, 1024) == _lib.INVALID_ARGUMENT
+    assert lib.rxla_b200_p2p_allreduce_f32(None, None, None, 16, None) == _lib.INVALID_ARGUMENT
+    msg = lib.rxla_b200_last_error_message().decode()
+    assert "p2p allreduce" in msg
