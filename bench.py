@@ -406,6 +406,84 @@ def gemv_roofline(dec, cfg, dev, stream, lib, tp=1):
             "bytes_per_step": total_bytes}
 
 
+def prefill_flops(cfg, tokens):
+    """Algorithmic FLOPs of a prompt through the decoder: 2 per weight per row
+    for every layer's linears, the causal attention (q·k and p·v, 4·Hq·D per
+    key, row t seeing t + 1 keys), and the head for the last row only."""
+    h, d, hq, hkv, i = cfg["hidden"], cfg["head_dim"], cfg["q_heads"], cfg["kv_heads"], cfg["intermediate"]
+    per_layer = h * (hq + 2 * hkv) * d + hq * d * h + 2 * i * h + i * h
+    lin = 2.0 * per_layer * cfg["layers"] * tokens
+    att = 4.0 * hq * d * tokens * (tokens + 1) / 2 * cfg["layers"]
+    return lin + att + 2.0 * cfg["vocab"] * h
+
+
+def run_prefill(args):
+    """Config 4 prefill: a PROMPT-token prompt of one sequence through
+    rxla_b200_decoder_prefill (chunks of rows on the tcgen05 GEMM, causal
+    paged attention), from position 0 each step.  Tensor-bound: the roofline
+    is the measured bf16 GEMM peak.  Prints one JSON line."""
+    import numpy as np
+    import torch
+    from rxla_b200.decoder import Decoder
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dec = Decoder(**CONFIG4, embedding_dtype="u8", max_batch=1, max_context=PROMPT + 16)
+    dec.init_synthetic(1)
+    stream = torch.cuda.current_stream()
+    s = ctypes.c_void_p(stream.cuda_stream)
+    prompt = torch.from_numpy(np.random.default_rng(5).integers(0, CONFIG4["vocab"], PROMPT)
+                              .astype(np.int32)).to(dev)
+    host_prompt = prompt.cpu().pin_memory()
+    for _ in range(args.warmup):
+        dec.reset(s)
+        dec.prefill(0, prompt, stream=s)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    sampler = ClockSampler(0)
+    sampler.start()
+    t0 = time.perf_counter()
+    ev[0].record(stream)
+    for _ in range(args.steps):
+        dec.reset(s)
+        dec.prefill(0, prompt, stream=s)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) / args.steps
+    ms = ev[0].elapsed_time(ev[1]) / args.steps
+    # end to end: the prompt from pinned host memory, the token back to the host
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        dec.reset(s)
+        prompt.copy_(host_prompt, non_blocking=True)
+        tok = dec.prefill(0, prompt, stream=s)
+        tok.cpu()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    clocks = sampler.stop()
+    flops = prefill_flops(CONFIG4, PROMPT)
+    try:
+        with open(ROOT / "MEASURED_PEAKS.json") as f:
+            peak, how = float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        peak, how = 1590.0, "fallback"
+    achieved = flops / (ms * 1e-3) / 1e12
+    line = {"metric": "W8 prefill tokens/sec", "value": PROMPT / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "wall_ms_per_step": wall * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8 weights, bf16 operands, f32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": f"config4: 8B-shaped W8 decoder, {PROMPT}-token prompt, "
+                                   "one sequence, prefill from position 0",
+                       "l2": "weights 6.95 GB per pass, larger than L2"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": how,
+                         "flops_per_step": flops, "traffic": None},
+            "e2e": {"value": PROMPT / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 4,
+                    "d2h_bytes_per_step": 4},
+            "clocks": clocks}
+    dec.close()
+    print(json.dumps(line), flush=True)
+
+
 def profile_case(what: str):
     """Small, self-contained cases for ncu captures (no JSON line).
 
@@ -516,6 +594,8 @@ def main():
     ap.add_argument("--no-batch64", action="store_true")
     ap.add_argument("--no-config5", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill", action="store_true",
+                    help="measure the config-4 prompt prefill instead of decode (one JSON line)")
     ap.add_argument("--profile", choices=["gemv", "head", "gemm", "gemmdec", "step", "step64", "step5", "attention"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
@@ -523,6 +603,9 @@ def main():
         profile_case(args.profile)
         return
     args.warmup = max(args.warmup, 3)
+    if args.prefill:
+        run_prefill(args)
+        return
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -294,6 +294,22 @@ int32_t rxla_b200_decoder_reset(rxla_b200_decoder* decoder, void* stream);
 int32_t rxla_b200_decoder_step(rxla_b200_decoder* decoder, const int32_t* tokens,
                                int32_t batch, int32_t* next_tokens, float* logits,
                                void* stream);
+/* Prefill: run `count` prompt tokens (device int32 [count]) of sequence `seq`
+ * through every layer at positions ctx[seq] .. ctx[seq] + count - 1, append
+ * their K/V to the sequence's pages and advance ctx[seq] by count.  The
+ * linears run over a whole chunk of prompt rows (tcgen05 GEMM) and each row
+ * attends causally over the cache up to its own position.  Writes the greedy
+ * token after the prompt to next_tokens[seq] of rxla_b200_decoder_io (and to
+ * next_token, device int32 [1], if non-NULL) and, if logits is non-NULL, the
+ * last row's f32 logits [vocab/tp].  Replaces the full-sequence forward of
+ * crates/rxla-models/src/qwen3_5/mod.rs:199-260 (qwen3_5() over a [1, T]
+ * prompt with the causal mask of mod.rs:229) for the full-attention layers,
+ * one sequence of the paged state at a time.  Synchronises `stream`
+ * once to read the position; ctx[seq] + count must not exceed max_context.
+ * With tp_size > 1 every rank calls this with the same arguments. */
+int32_t rxla_b200_decoder_prefill(rxla_b200_decoder* decoder, int32_t seq, const int32_t* tokens,
+                                  int32_t count, int32_t* next_token, float* logits,
+                                  void* stream);
 /* Host-buffer convenience for one step: copies tokens in and next tokens out
  * through pinned staging on `stream` and synchronises it. */
 int32_t rxla_b200_decoder_step_host(rxla_b200_decoder* decoder, const int32_t* tokens_host,

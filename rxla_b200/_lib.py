@@ -108,6 +108,7 @@ SIGNATURES = {
     "rxla_b200_decoder_reset": (_i32, [_vp, _vp]),
     "rxla_b200_decoder_step": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
     "rxla_b200_decoder_step_host": (_i32, [_vp, _vp, _i32, _vp, _vp]),
+    "rxla_b200_decoder_prefill": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _vp]),
     "rxla_b200_decoder_context_lengths": (_i32, [_vp, ctypes.POINTER(_vp)]),
     "rxla_b200_decoder_set_context_lengths": (_i32, [_vp, _vp, _i32, _vp]),
     "rxla_b200_decoder_kv_cache": (_i32, [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp),

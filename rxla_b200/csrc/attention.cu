@@ -73,6 +73,7 @@ struct Params {
   uint32_t* ws_counter;  // [batch * hkv] split arrivals, then [1] CTA exits
   int32_t batch;
   int32_t ctx_stable;    // ctx_lens is not written by the previous kernel: prefetch early
+  int32_t append_only;   // write the new K/V rows only (the decoder's prefill, first pass)
   int32_t stages;
   int32_t stage_bytes;  // K + V of one page of one kv head
   L2Prefetch next;      // the following kernel's first bytes
@@ -203,7 +204,8 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
 
   const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   const int ctas = gridDim.x * gridDim.y * gridDim.z;
-  if (split >= n_splits) {  // nothing of this sequence in this split (exit = trigger)
+  if (split >= n_splits || (p.append_only && !owner)) {
+    // nothing of this sequence in this split, or nothing to append (exit = trigger)
     if (threadIdx.x == 0) {
       if (p.next.nseg > 0) l2_prefetch_share(p.next, cta, ctas);
       finish_cta(p);
@@ -225,6 +227,9 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
     // Pages hold rows appended by earlier kernels only (the new row is patched
     // in from registers); with a stable ctx_lens they are fetched before
     // griddepcontrol.wait.
+    // append-only: every warp leaves before the closing barrier (the compute
+    // warps right after the append), so the CTA's exit needs no barrier
+    if (p.append_only) return;
     if (lane == 0) {
       for (int it = 0; it < n_it; ++it) {
         const int s = it % kStagesV2;
@@ -334,6 +339,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
         p.v_pages[base + i] = __float2bfloat16_rn(vn[i]);
       }
     }
+    if (p.append_only) return;  // no page loop, no output (the producer has left)
 
     // q of the G heads of this kv head in B-fragment layout, normed, rotated
     // and split into bf16 hi + lo
@@ -664,7 +670,7 @@ namespace attn {
 // before griddepcontrol.wait (the decoder runner advances ctx_lens only at
 // the end of a step).
 int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx_stable,
-               const L2Prefetch* next) {
+               const L2Prefetch* next, bool append_only) {
   RXLA_REQUIRE(a && a->struct_size >= sizeof(rxla_b200_paged_decode_args),
                "paged_decode: args struct missing or too small");
   const int D = a->head_dim;
@@ -740,6 +746,7 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   p.stage_bytes = 2 * attn::kPage * D * 2;
   p.batch = a->batch;
   p.ctx_stable = ctx_stable ? 1 : 0;
+  p.append_only = append_only ? 1 : 0;
   const bool large = a->batch >= 16;  // enough CTAs to fill the SMs several times
   p.stages = large ? attn::kStagesLarge : attn::kStagesSmall;
   if (next) p.next = *next;

@@ -161,6 +161,25 @@ __global__ void residual_add_kernel(const float* __restrict__ part, float* __res
     h[i] = h[i] + bf16_round(part[i]);
 }
 
+// Rows of a prefill chunk: row t gets a copy of the sequence's page-table row
+// and the position pos0 + t.
+__global__ void prefill_rows_kernel(const int32_t* __restrict__ page_table, int32_t max_pages,
+                                    int32_t seq, int32_t pos0, int32_t* __restrict__ pt_out,
+                                    int32_t* __restrict__ ctx_out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t t = blockIdx.x;
+  for (int i = threadIdx.x; i < max_pages; i += blockDim.x)
+    pt_out[t * max_pages + i] = page_table[(int64_t)seq * max_pages + i];
+  if (threadIdx.x == 0) ctx_out[t] = pos0 + (int32_t)t;
+}
+
+__global__ void set_position_kernel(int32_t* __restrict__ ctx, int32_t seq, int32_t pos) {
+  pdl_wait();
+  pdl_launch_dependents();
+  ctx[seq] = pos;
+}
+
 // Tensor-parallel greedy head: each rank's best logit of its vocab slice
 // (value, global index), then the best over all ranks' candidates with the
 // same tie rule as a full argmax (highest value, then lowest index).
@@ -316,6 +335,22 @@ struct rxla_b200_decoder {
   bool packed_valid = false;
   int32_t* host_pinned = nullptr;
   std::map<int, cudaGraphExec_t> graphs;
+  // multi-token prefill: chunk buffers (rows = tokens of one prompt chunk),
+  // allocated by the first rxla_b200_decoder_prefill
+  int pf_chunk = 0;
+  uint8_t* pf_mem = nullptr;
+  float* pf_h = nullptr;
+  uint16_t* pf_xn = nullptr;
+  uint16_t* pf_qkv = nullptr;
+  uint16_t* pf_att = nullptr;
+  uint16_t* pf_act = nullptr;
+  float* pf_part = nullptr;
+  int32_t* pf_pt = nullptr;
+  int32_t* pf_ctx = nullptr;
+  void* pf_ws = nullptr;
+  size_t pf_ws_bytes = 0;
+  void* pf_gws = nullptr;
+  size_t pf_gws_bytes = 0;
 };
 
 namespace rxla {
@@ -334,6 +369,32 @@ static int32_t alloc_dev(void** p, size_t bytes) {
   cudaError_t e = cudaMalloc(p, bytes);
   if (e != cudaSuccess) return cuda_fail(e, "decoder allocation");
   return RXLA_B200_OK;
+}
+
+// Row buffers of a batched pass through the layers: the decode step's
+// (one row per sequence) or a prefill chunk's (one row per prompt token of a
+// single sequence, each with its own copy of that sequence's page-table row
+// and its own position).
+struct Rows {
+  int n;
+  float* h;
+  uint16_t* xn;
+  uint16_t* qkv;
+  uint16_t* att;
+  uint16_t* act;
+  float* part;
+  void* gws;
+  size_t gws_bytes;
+  int32_t* page_table;
+  int32_t* ctx;
+  void* ws;
+  size_t ws_bytes;
+  bool prefill;
+};
+
+static Rows step_rows(rxla_b200_decoder* d, int batch) {
+  return Rows{batch,     d->h,  d->xn,  d->qkv,      d->att, d->act,      d->part,
+              d->gws,    d->gws_bytes,  d->page_table, d->ctx, d->ws, d->ws_bytes, false};
 }
 
 // Paged decode attention arguments of one layer of the runner.
@@ -377,9 +438,25 @@ static rxla_b200_paged_decode_args attention_args(const rxla_b200_decoder* d, co
   return a;
 }
 
+static rxla_b200_paged_decode_args attention_args(const rxla_b200_decoder* d, const Layer& L,
+                                                  const Rows& r) {
+  rxla_b200_paged_decode_args a = attention_args(d, L, r.n);
+  const int64_t qd = (int64_t)d->hq * d->cfg.head_dim, kd = (int64_t)d->hkv * d->cfg.head_dim;
+  a.q = r.qkv;
+  a.k_new = r.qkv + qd;
+  a.v_new = r.qkv + qd + kd;
+  a.page_table = r.page_table;
+  a.ctx_lens = r.ctx;
+  a.out = r.att;
+  a.workspace = r.ws;
+  a.workspace_bytes = r.ws_bytes;
+  return a;
+}
+
 // Tensor-parallel LM head: this rank's logits slice [batch, vocab_local] is in
 // d->logits; pick its best per row, gather every rank's candidates, merge.
-static int32_t tp_head_tail(rxla_b200_decoder* d, int batch, cudaStream_t s) {
+static int32_t tp_head_tail(rxla_b200_decoder* d, int batch, cudaStream_t s, int32_t* out,
+                            int32_t* advance) {
   const int tp = d->cfg.tp_size;
   cudaError_t e = launch_pdl(argmax_candidates_kernel, dim3(batch), dim3(1024), 0, s,
                              (const float*)d->logits, d->vocab_local,
@@ -388,33 +465,102 @@ static int32_t tp_head_tail(rxla_b200_decoder* d, int batch, cudaStream_t s) {
   int32_t st = comm_allgather_bytes(d->comm, d->cand, d->cand_all, (int64_t)batch * sizeof(Cand), s);
   if (st) return st;
   e = launch_pdl(argmax_merge_kernel, dim3((batch + 127) / 128), dim3(128), 0, s,
-                 (const Cand*)d->cand_all, (int32_t)tp, (int32_t)batch, d->tok_out, d->ctx);
+                 (const Cand*)d->cand_all, (int32_t)tp, (int32_t)batch, out, advance);
   if (e != cudaSuccess) return cuda_fail(e, "argmax merge launch");
   return RXLA_B200_OK;
 }
 
 // h += bf16(part): the all-reduced row-parallel partial sums of o_proj / down.
-static int32_t tp_residual(rxla_b200_decoder* d, int batch, cudaStream_t s) {
+static int32_t tp_residual(rxla_b200_decoder* d, int batch, cudaStream_t s, float* part,
+                           float* h, bool p2p) {
   const int64_t H = d->cfg.hidden;
-  // one-shot peer all-reduce fused with the residual add, else NCCL + a kernel
-  if (comm_has_p2p(d->comm)) return comm_p2p_allreduce(d->comm, d->part, d->h, batch * H, true, s);
-  int32_t st = comm_allreduce_f32(d->comm, d->part, batch * H, s);
+  // one-shot peer all-reduce fused with the residual add (its buffers hold
+  // max_batch rows), else NCCL + a kernel
+  if (p2p && comm_has_p2p(d->comm)) return comm_p2p_allreduce(d->comm, part, h, batch * H, true, s);
+  int32_t st = comm_allreduce_f32(d->comm, part, batch * H, s);
   if (st) return st;
   cudaError_t e = launch_pdl(residual_add_kernel, dim3(std::max(1, (int)((batch * H + 1023) / 1024))),
-                             dim3(1024), 0, s, (const float*)d->part, d->h, (int64_t)batch * H);
+                             dim3(1024), 0, s, (const float*)part, h, (int64_t)batch * H);
   if (e != cudaSuccess) return cuda_fail(e, "residual add launch");
   return RXLA_B200_OK;
 }
 
-// Linears of a step with more tokens than one skinny pass: bf16 x from a
-// separate RMSNorm kernel, the tcgen05 GEMM (split-K over the runner's
-// workspace), the same epilogues; the LM head writes f32 logits and a
-// per-row argmax kernel picks the token and advances the position.
-static int32_t enqueue_gemm_layers(rxla_b200_decoder* d, int batch, cudaStream_t s) {
+// The layers over a batch of rows: bf16 x from a separate RMSNorm kernel,
+// the W8 linears (the tcgen05 GEMM with split-K over the rows' workspace;
+// skinny passes for a prefill chunk of at most kSkinnyTokens rows), the same
+// epilogues.  A prefill chunk's attention runs twice: an append-only pass
+// writes every row's K/V to its slot, then the full pass lets row t attend
+// over the sequence's cache up to its own slot (the causal mask of the
+// prompt), re-writing identical K/V bytes.
+static int32_t enqueue_rows_layers(rxla_b200_decoder* d, const Rows& r, cudaStream_t s) {
   const auto& c = d->cfg;
   const bool tp = c.tp_size > 1;
   const int64_t H = c.hidden, D = c.head_dim;
   const int64_t qd = (int64_t)d->hq * D;
+  auto gemm = [&](const void* x, int64_t k, const uint8_t* w, const float* sc, int64_t group,
+                  int64_t n, void* y, int32_t y_dtype, int32_t epi) {
+    if (r.n <= kSkinnyTokens)
+      return w8_linear(x, RXLA_B200_BF16, w, sc, group, r.n, n, k, y, y_dtype, epi, s, nullptr);
+    GemmArgs g{};
+    g.x = x;
+    g.ldx = k;
+    g.w = w;
+    g.scale = sc;
+    g.group = group;
+    g.m = r.n;
+    g.n = n;
+    g.k = k;
+    g.y = y;
+    g.ldy = n;
+    g.y_dtype = y_dtype;
+    g.epilogue = epi;
+    g.splits = gemm_splits(r.n, n, k, group, epi == RXLA_B200_EPI_SWIGLU);
+    g.ws = r.gws;
+    g.ws_bytes = r.gws_bytes;
+    return w8_gemm(g, s);
+  };
+  for (int l = 0; l < c.layers; ++l) {
+    const Layer& L = d->layers[l];
+    int32_t st = rxla_b200_rms_norm_bf16(r.h, L.ln1, r.n, H, c.rms_eps, r.xn, s);
+    if (!st) st = gemm(r.xn, H, L.wqkv, L.sqkv, d->group_h, d->qkv_rows, r.qkv, RXLA_B200_BF16,
+                       RXLA_B200_EPI_STORE);
+    if (st) return st;
+    rxla_b200_paged_decode_args a = attention_args(d, L, r);
+    if (r.prefill) {
+      // positions were written before the layers; the full pass must not
+      // fetch pages before the append pass has finished
+      st = attn::launch(&a, s, true, nullptr, true);
+      if (!st) st = attn::launch(&a, s, false);
+    } else {
+      st = attn::launch(&a, s, true);
+    }
+    // row-parallel linears: the full residual add, or (tensor parallel) an
+    // unrounded partial that is all-reduced first
+    if (!st) st = tp ? gemm(r.att, qd, L.wo, L.so, d->group_o, H, r.part, RXLA_B200_F32,
+                            RXLA_B200_EPI_STORE)
+                     : gemm(r.att, qd, L.wo, L.so, d->group_o, H, r.h, RXLA_B200_F32,
+                            RXLA_B200_EPI_RESIDUAL_ADD);
+    if (!st && tp) st = tp_residual(d, r.n, s, r.part, r.h, !r.prefill);
+    if (!st) st = rxla_b200_rms_norm_bf16(r.h, L.ln2, r.n, H, c.rms_eps, r.xn, s);
+    if (!st) st = gemm(r.xn, H, L.wgu, L.sgu, d->group_h, d->inter, r.act, RXLA_B200_BF16,
+                       RXLA_B200_EPI_SWIGLU);
+    if (!st) st = tp ? gemm(r.act, d->inter, L.wd, L.sd, d->group_i, H, r.part, RXLA_B200_F32,
+                            RXLA_B200_EPI_STORE)
+                     : gemm(r.act, d->inter, L.wd, L.sd, d->group_i, H, r.h, RXLA_B200_F32,
+                            RXLA_B200_EPI_RESIDUAL_ADD);
+    if (!st && tp) st = tp_residual(d, r.n, s, r.part, r.h, !r.prefill);
+    if (st) return st;
+  }
+  return RXLA_B200_OK;
+}
+
+// Linears of a step with more tokens than one skinny pass: the layers over
+// the step's rows; the LM head writes f32 logits and a per-row argmax kernel
+// picks the token and advances the position.
+static int32_t enqueue_gemm_layers(rxla_b200_decoder* d, int batch, cudaStream_t s) {
+  const auto& c = d->cfg;
+  const bool tp = c.tp_size > 1;
+  const int64_t H = c.hidden;
   auto gemm = [&](const void* x, int64_t k, const uint8_t* w, const float* sc, int64_t group,
                   int64_t n, void* y, int32_t y_dtype, int32_t epi) {
     GemmArgs g{};
@@ -435,29 +581,8 @@ static int32_t enqueue_gemm_layers(rxla_b200_decoder* d, int batch, cudaStream_t
     g.ws_bytes = d->gws_bytes;
     return w8_gemm(g, s);
   };
-  for (int l = 0; l < c.layers; ++l) {
-    const Layer& L = d->layers[l];
-    int32_t st = rxla_b200_rms_norm_bf16(d->h, L.ln1, batch, H, c.rms_eps, d->xn, s);
-    if (!st) st = gemm(d->xn, H, L.wqkv, L.sqkv, d->group_h, d->qkv_rows, d->qkv, RXLA_B200_BF16,
-                       RXLA_B200_EPI_STORE);
-    if (st) return st;
-    rxla_b200_paged_decode_args a = attention_args(d, L, batch);
-    st = attn::launch(&a, s, true);
-    // row-parallel linears: the full residual add, or (tensor parallel) an
-    // unrounded partial that is all-reduced first
-    if (!st) st = tp ? gemm(d->att, qd, L.wo, L.so, d->group_o, H, d->part, RXLA_B200_F32,
-                            RXLA_B200_EPI_STORE)
-                     : gemm(d->att, qd, L.wo, L.so, d->group_o, H, d->h, RXLA_B200_F32,
-                            RXLA_B200_EPI_RESIDUAL_ADD);
-    if (!st && tp) st = tp_residual(d, batch, s);
-    if (!st) st = rxla_b200_rms_norm_bf16(d->h, L.ln2, batch, H, c.rms_eps, d->xn, s);
-    if (!st) st = gemm(d->xn, H, L.wgu, L.sgu, d->group_h, d->inter, d->act, RXLA_B200_BF16,
-                       RXLA_B200_EPI_SWIGLU);
-    if (!st) st = tp ? gemm(d->act, d->inter, L.wd, L.sd, d->group_i, H, d->part, RXLA_B200_F32,
-                            RXLA_B200_EPI_STORE)
-                     : gemm(d->act, d->inter, L.wd, L.sd, d->group_i, H, d->h, RXLA_B200_F32,
-                            RXLA_B200_EPI_RESIDUAL_ADD);
-    if (!st && tp) st = tp_residual(d, batch, s);
+  {
+    int32_t st = enqueue_rows_layers(d, step_rows(d, batch), s);
     if (st) return st;
   }
   int32_t st = rxla_b200_rms_norm_bf16(d->h, d->final_norm, batch, H, c.rms_eps, d->xn, s);
@@ -472,7 +597,7 @@ static int32_t enqueue_gemm_layers(rxla_b200_decoder* d, int batch, cudaStream_t
                                H, d->logits, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
   }
   if (st) return st;
-  if (tp) return tp_head_tail(d, batch, s);
+  if (tp) return tp_head_tail(d, batch, s, d->tok_out, d->ctx);
   cudaError_t e = launch_pdl(argmax_kernel, dim3(batch), dim3(1024), 0, s, (const float*)d->logits,
                              (int64_t)d->vocab, d->tok_out, d->ctx);
   if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
@@ -715,7 +840,7 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
       st = rxla_b200_w8a16_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd,
                                   d->part, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
       if (st) return st;
-      st = tp_residual(d, batch, s);
+      st = tp_residual(d, batch, s, d->part, d->h, true);
       if (st) return st;
     }
     // act = silu(gate) * up of bf16(rms_norm(h) * post_attention_layernorm)
@@ -736,7 +861,7 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
       st = rxla_b200_w8a16_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H,
                                   d->inter, d->part, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
       if (st) return st;
-      st = tp_residual(d, batch, s);
+      st = tp_residual(d, batch, s, d->part, d->h, true);
       if (st) return st;
     }
   }
@@ -768,7 +893,7 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
                                    RXLA_B200_EPI_STORE, s);
     }
     if (st) return st;
-    return tp_head_tail(d, batch, s);
+    return tp_head_tail(d, batch, s, d->tok_out, d->ctx);
   }
   if (d->emb_w8) {
     // tied W8 head: logits = bf16(rms_norm(h) * norm) · Eᵀ (f32), greedy token
@@ -1045,7 +1170,7 @@ extern "C" int32_t rxla_b200_decoder_destroy(rxla_b200_decoder* d) {
   void* ptrs[] = {d->arena, d->page_table, d->ctx, d->h, d->xn, d->qkv, d->att, d->act,
                   d->part, d->logits, d->tok_in, d->tok_out, d->inv_freq, d->ws,
                   d->gws, d->arg_val, d->arg_idx, d->arg_count, d->cand, d->cand_all,
-                  d->chain_bar, d->packed};
+                  d->chain_bar, d->packed, d->pf_mem};
   for (void* p : ptrs) cudaFree(p);
   if (d->host_pinned) cudaFreeHost(d->host_pinned);
   delete d;
@@ -1279,6 +1404,151 @@ extern "C" int32_t rxla_b200_decoder_step(rxla_b200_decoder* d, const int32_t* t
                                     cudaMemcpyDeviceToDevice, s));
   if (logits)
     RXLA_CUDA_CHECK(cudaMemcpyAsync(logits, d->logits, (size_t)batch * d->vocab_local * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+  return RXLA_B200_OK;
+}
+
+namespace rxla {
+namespace dec {
+
+// Prefill chunk rows (RXLA_B200_PREFILL_CHUNK, default 1024, at most
+// max_context): buffers for that many rows are allocated once.
+static int32_t prefill_alloc(rxla_b200_decoder* d) {
+  if (d->pf_mem) return RXLA_B200_OK;
+  const auto& c = d->cfg;
+  const char* v = getenv("RXLA_B200_PREFILL_CHUNK");
+  int C = v ? atoi(v) : 1024;
+  C = std::max(1, std::min(C, c.max_context));
+  const int64_t H = c.hidden, D = c.head_dim, I = d->inter;
+  // workspaces: the largest any chunk of 1..C rows plans
+  size_t ws = 0, gws = 0;
+  const int64_t shapes[][4] = {{d->qkv_rows, H, 0, d->group_h},
+                               {H, (int64_t)d->hq * D, 0, d->group_o},
+                               {I, H, 1, d->group_h},
+                               {H, I, 0, d->group_i}};
+  for (int n = 1; n <= C; ++n) {
+    size_t w = 0;
+    rxla_b200_paged_decode_workspace_size(n, d->hq, d->hkv, (int32_t)D, c.max_context, &w);
+    ws = std::max(ws, w);
+    if (n <= kSkinnyTokens) continue;
+    for (auto& sh : shapes)
+      gws = std::max(gws, w8_gemm_workspace_bytes(n, sh[2] ? 2 * sh[0] : sh[0],
+                                                  gemm_splits(n, sh[0], sh[1], sh[3], sh[2] != 0)));
+  }
+  const size_t sizes[] = {(size_t)C * H * 4,           (size_t)C * H * 2,
+                          (size_t)C * d->qkv_rows * 2, (size_t)C * d->hq * D * 2,
+                          (size_t)C * I * 2,           (size_t)C * H * 4,
+                          (size_t)C * d->max_pages * 4, (size_t)C * 4,
+                          ws,                          gws};
+  size_t off[10], total = 0;
+  for (int i = 0; i < 10; ++i) {
+    off[i] = total;
+    total += (std::max<size_t>(sizes[i], 1) + 255) / 256 * 256;
+  }
+  int32_t st = alloc_dev(reinterpret_cast<void**>(&d->pf_mem), total);
+  if (st) return st;
+  RXLA_CUDA_CHECK(cudaMemset(d->pf_mem, 0, total));
+  uint8_t* b = d->pf_mem;
+  d->pf_h = reinterpret_cast<float*>(b + off[0]);
+  d->pf_xn = reinterpret_cast<uint16_t*>(b + off[1]);
+  d->pf_qkv = reinterpret_cast<uint16_t*>(b + off[2]);
+  d->pf_att = reinterpret_cast<uint16_t*>(b + off[3]);
+  d->pf_act = reinterpret_cast<uint16_t*>(b + off[4]);
+  d->pf_part = reinterpret_cast<float*>(b + off[5]);
+  d->pf_pt = reinterpret_cast<int32_t*>(b + off[6]);
+  d->pf_ctx = reinterpret_cast<int32_t*>(b + off[7]);
+  d->pf_ws = b + off[8];
+  d->pf_ws_bytes = ws;
+  d->pf_gws = gws ? b + off[9] : nullptr;
+  d->pf_gws_bytes = gws;
+  d->pf_chunk = C;
+  return RXLA_B200_OK;
+}
+
+}  // namespace dec
+}  // namespace rxla
+
+extern "C" int32_t rxla_b200_decoder_prefill(rxla_b200_decoder* d, int32_t seq,
+                                             const int32_t* tokens, int32_t count,
+                                             int32_t* next_token, float* logits, void* stream) {
+  RXLA_REQUIRE(d && tokens, "decoder_prefill: null argument");
+  RXLA_REQUIRE(seq >= 0 && seq < d->cfg.max_batch, "decoder_prefill: sequence out of range");
+  RXLA_REQUIRE(count > 0, "decoder_prefill: count must be positive");
+  const auto& c = d->cfg;
+  const int64_t H = c.hidden;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  RXLA_CUDA_CHECK(cudaSetDevice(d->device));
+  int32_t st = dec::prefill_alloc(d);
+  if (st) return st;
+  // the sequence's position: one synchronous read
+  RXLA_CUDA_CHECK(cudaMemcpyAsync(d->host_pinned, d->ctx + seq, 4, cudaMemcpyDeviceToHost, s));
+  RXLA_CUDA_CHECK(cudaStreamSynchronize(s));
+  const int32_t pos0 = d->host_pinned[0];
+  RXLA_REQUIRE(pos0 >= 0 && (int64_t)pos0 + count <= c.max_context,
+               "decoder_prefill: the prompt does not fit the sequence's remaining context");
+  int32_t n = 0;
+  for (int32_t c0 = 0; c0 < count; c0 += n) {
+    n = std::min(count - c0, d->pf_chunk);
+    cudaError_t e = launch_pdl(dec::prefill_rows_kernel, dim3(n), dim3(128), 0, s,
+                               (const int32_t*)d->page_table, (int32_t)d->max_pages, seq,
+                               pos0 + c0, d->pf_pt, d->pf_ctx);
+    if (e == cudaSuccess)
+      e = launch_pdl(dec::embed_kernel, dim3(n), dim3(256), 0, s, tokens + c0,
+                     (const uint8_t*)d->emb_w8, (const float*)d->emb_scale,
+                     (const __nv_bfloat16*)d->emb_bf16, (int64_t)c.vocab, H,
+                     (int64_t)d->groups_h, (int64_t)d->group_h, d->pf_h, (uint32_t*)nullptr, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill rows launch");
+    const dec::Rows r{n,         d->pf_h,         d->pf_xn, d->pf_qkv, d->pf_att,
+                      d->pf_act, d->pf_part,      d->pf_gws, d->pf_gws_bytes, d->pf_pt,
+                      d->pf_ctx, d->pf_ws,        d->pf_ws_bytes, true};
+    st = dec::enqueue_rows_layers(d, r, s);
+    if (st) return st;
+  }
+  // greedy head on the prompt's last row; the token goes to the sequence's
+  // slot of the step output
+  const float* hl = d->pf_h + (int64_t)(n - 1) * H;
+  int32_t* out = d->tok_out + seq;
+  const int64_t v0 = (int64_t)c.tp_rank * d->vocab_local;
+  if (d->emb_w8) {
+    NormLinearArgs na{};
+    na.h = hl;
+    na.norm_w = d->final_norm;
+    na.eps = c.rms_eps;
+    na.w = d->emb_w8 + v0 * H;
+    na.scale = d->emb_scale + v0 * d->groups_h;
+    na.group = d->group_h;
+    na.m = 1;
+    na.n = d->vocab_local;
+    na.k = H;
+    na.y = d->logits;
+    na.y_dtype = RXLA_B200_F32;
+    na.epilogue = c.tp_size > 1 ? RXLA_B200_EPI_STORE : kArgmaxEpilogue;
+    na.arg_val = d->arg_val;
+    na.arg_idx = d->arg_idx;
+    na.arg_count = d->arg_count;
+    na.arg_out = out;
+    na.arg_advance = nullptr;
+    st = w8_norm_linear(na, s);
+  } else {
+    st = rxla_b200_rms_norm_bf16(hl, d->final_norm, 1, H, c.rms_eps, d->xn, s);
+    if (!st)
+      st = rxla_b200_bf16_linear(d->xn, RXLA_B200_BF16, d->emb_bf16 + v0 * H, 1, d->vocab_local,
+                                 H, d->logits, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
+    if (!st && c.tp_size == 1) {
+      cudaError_t e = launch_pdl(argmax_kernel, dim3(1), dim3(1024), 0, s,
+                                 (const float*)d->logits, (int64_t)d->vocab, out, (int32_t*)nullptr);
+      if (e != cudaSuccess) st = cuda_fail(e, "argmax launch");
+    }
+  }
+  if (!st && c.tp_size > 1) st = dec::tp_head_tail(d, 1, s, out, nullptr);
+  if (st) return st;
+  cudaError_t e = launch_pdl(dec::set_position_kernel, dim3(1), dim3(1), 0, s, d->ctx, seq,
+                             pos0 + count);
+  if (e != cudaSuccess) return cuda_fail(e, "prefill position launch");
+  if (next_token && next_token != out)
+    RXLA_CUDA_CHECK(cudaMemcpyAsync(next_token, out, 4, cudaMemcpyDeviceToDevice, s));
+  if (logits)
+    RXLA_CUDA_CHECK(cudaMemcpyAsync(logits, d->logits, (size_t)d->vocab_local * 4,
                                     cudaMemcpyDeviceToDevice, s));
   return RXLA_B200_OK;
 }

@@ -121,8 +121,10 @@ int32_t comm_p2p_allreduce(rxla_b200_comm* comm, const float* partial, float* ou
                            bool residual, cudaStream_t s);
 
 namespace attn {
+// append_only: write the new K/V rows and nothing else (no page loop, no
+// output, no context advance)
 int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable,
-               const L2Prefetch* next = nullptr);
+               const L2Prefetch* next = nullptr, bool append_only = false);
 }
 
 }  // namespace rxla

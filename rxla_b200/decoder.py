@@ -33,6 +33,7 @@ class Decoder:
         self.cfg = cfg
         self.vocab = vocab
         self.max_batch = max_batch
+        self._device = device
         h = ctypes.c_void_p()
         _lib.call("rxla_b200_decoder_create", ctypes.byref(cfg), device, comm, ctypes.byref(h))
         self._h = h
@@ -97,6 +98,18 @@ class Decoder:
         """One step on tokens already in the runner's device input buffer."""
         _lib.call("rxla_b200_decoder_step", self._h, self.tokens_in_ptr, batch,
                   self.tokens_out_ptr, logits_ptr, stream)
+
+    def prefill(self, seq: int, tokens, stream=None, logits_ptr=None):
+        """Run a prompt (device int32 tensor or any int sequence) through the
+        layers for sequence ``seq`` (rxla_b200_decoder_prefill); returns the
+        device int32 tensor [1] holding the greedy token after the prompt."""
+        import torch
+        dev = torch.device("cuda", self._device)
+        t = torch.as_tensor(tokens, dtype=torch.int32).to(dev).contiguous()
+        out = torch.empty(1, dtype=torch.int32, device=dev)
+        _lib.call("rxla_b200_decoder_prefill", self._h, seq, t.data_ptr(), t.numel(),
+                  out.data_ptr(), logits_ptr, stream)
+        return out
 
     def step_host(self, tokens, stream=None) -> np.ndarray:
         """One step from host tokens to host next tokens (copies + sync inside)."""

@@ -117,3 +117,11 @@ def test_context_lengths_and_peer_allreduce_validation_without_cuda():
     assert lib.rxla_b200_p2p_allreduce_f32(None, None, None, 16, None) == _lib.INVALID_ARGUMENT
     msg = lib.rxla_b200_last_error_message().decode()
     assert "p2p allreduce" in msg
+
+
+def test_prefill_validation_without_cuda():
+    """The prefill entry rejects a missing decoder or prompt before any CUDA call."""
+    lib = _lib.load()
+    toks = (ctypes.c_int32 * 4)(1, 2, 3, 4)
+    assert lib.rxla_b200_decoder_prefill(None, 0, toks, 4, None, None, None) == _lib.INVALID_ARGUMENT
+    assert "decoder_prefill" in lib.rxla_b200_last_error_message().decode()
