@@ -496,6 +496,8 @@ def profile_case(what: str):
     step5:     config 5 (32B shape) at batch 32 (4096 context), 1 step inside "profile"
     gemmdec:   a 2-layer config-4-shaped decoder at batch 64, 1 step (the decode-batch
                GEMM launches: qkv, o, gate/up, down per layer, then the head)
+    prefill:   a 2-layer config-4-shaped decoder, one 2048-token prompt (two
+               1024-row chunks) after one warm-up prompt
     attention: config-3 paged decode attention (batch 64, 32 q / 8 kv heads, d 128,
                ctx ~U[512, 8192]), 3 launches
     """
@@ -547,6 +549,18 @@ def profile_case(what: str):
         _lib.call("rxla_b200_decoder_step", dec.handle, tout, 64, tout, None, s)
         torch.cuda.synchronize()
         dec.close()
+    elif what == "prefill":
+        from rxla_b200.decoder import Decoder
+        cfg = dict(CONFIG4, layers=2)
+        dec = Decoder(**cfg, embedding_dtype="u8", max_batch=1, max_context=PROMPT + 16)
+        dec.init_synthetic(1)
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        prompt = torch.randint(0, cfg["vocab"], (PROMPT,), dtype=torch.int32, device=dev)
+        for _ in range(2):
+            dec.reset(s)
+            dec.prefill(0, prompt, stream=s)
+        torch.cuda.synchronize()
+        dec.close()
     elif what in ("step64", "step5"):
         # batch 64 of config 4 at a 2048 context / batch 32 of config 5 at 4096:
         # 2 warm-up steps, then 1 step inside the NVTX range "profile"
@@ -596,7 +610,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill", action="store_true",
                     help="measure the config-4 prompt prefill instead of decode (one JSON line)")
-    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "gemmdec", "step", "step64", "step5", "attention"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "gemmdec", "step", "step64", "step5", "prefill", "attention"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.profile:

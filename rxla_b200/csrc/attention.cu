@@ -590,6 +590,299 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
   if (threadIdx.x == 0) finish_cta(p);
 }
 
+// ------------------------------------------------ prefill (causal) attention
+//
+// The rows of a prompt chunk of one sequence after their K/V were appended
+// (the append-only pass of paged_decode_kernel): row t holds the query at
+// position pos[t] and attends over keys 0 .. pos[t] of the sequence's pages —
+// the causal mask of the reference's full-sequence forward
+// (crates/rxla-models/src/qwen3_5/mod.rs:229 with the SDPA of
+// crates/rxla-core/src/attention.rs:83-252).  Same numerics as the decode
+// kernel: q normed, rotated and split into bf16 hi + lo, the softmax weights
+// split likewise, f32 accumulation.
+//
+// CTA = (block of kPfRows / G queries, kv head).  Its kPfRows (query, head)
+// rows are the MMA M side — eight warps of 16 rows, row r is query r / G and
+// head r % G — with q held as A fragments in registers.  A producer warp
+// streams the key pages 0 .. (the block's last position) through a ring (TMA,
+// the decode kernel's [64 dims × 16 rows] swizzled boxes) and every warp
+// consumes every page: S = Q·Kᵀ (two 8-key n-blocks, K by ldmatrix), an
+// online softmax per row, O += P·V with P taken from the S accumulators (the
+// m16n8 C fragment is the next MMA's A fragment) and V by ldmatrix.trans.
+// Pages above a warp's last position are skipped; the heaviest query blocks
+// are scheduled first.
+constexpr int kPfWarps = 8;
+constexpr int kPfRows = kPfWarps * 16;
+constexpr int kPfStages = 8;
+
+struct PrefillParams {
+  const __nv_bfloat16* q;
+  int64_t q_stride;
+  const float* q_norm_w;
+  float eps;
+  const float* inv_freq;
+  int32_t rot;
+  float scale;
+  const int32_t* page_table;  // the sequence's pages
+  const int32_t* pos;         // [n] position of each row (increasing)
+  int32_t n, hq, hkv, group, bq;
+  __nv_bfloat16* out;         // [n, hq, D]
+};
+
+// RoPE of one q row in the A-fragment layout at position pos: the angles are
+// f32(pos) · inv_freq as paged_decode_kernel forms its table.
+template <int KS, int HS>
+__device__ __forceinline__ void rope_q_at(float (&qv)[KS][4], int pos, const float* inv_freq,
+                                          int q4) {
+#pragma unroll
+  for (int ks = 0; ks < HS; ++ks)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int d = ks * 16 + 2 * q4 + (i & 1) + (i >> 1) * 8;
+      const float ang = (float)pos * inv_freq[d];
+      const float c = cosf(ang), sn = sinf(ang);
+      const float x0 = qv[ks][i], x1 = qv[ks + HS][i];
+      qv[ks][i] = x0 * c - x1 * sn;
+      qv[ks + HS][i] = x1 * c + x0 * sn;
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__((kPfWarps + 1) * 32, 1)
+    prefill_attention_kernel(const __grid_constant__ CUtensorMap kmap,
+                             const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  constexpr int KS = D / 16;
+  constexpr int kTile = kPage * D * 2;
+  constexpr int kStage = 2 * kTile;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty = full + kPfStages;
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* ring = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u) + 1024;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blk = gridDim.x - 1 - blockIdx.x, h = blockIdx.y;
+  const int G = p.group;
+  const int t_begin = blk * p.bq;
+  const int t_last = min(p.n, t_begin + p.bq) - 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kPfWarps);
+    }
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  // the pages were written by the append pass, q by the qkv linear
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  const int n_keys = p.pos[t_last] + 1;
+  const int n_pages = (n_keys + kPage - 1) / kPage;
+
+  if (warp == kPfWarps) {
+    // producer; no CTA-wide barrier follows, so the warp may leave
+    if (lane == 0) {
+      for (int it = 0; it < n_pages; ++it) {
+        const int s = it % kPfStages;
+        if (it >= kPfStages && !mbar_wait(&empty[s], ((it / kPfStages) - 1) & 1)) break;
+        const int row = (p.page_table[it] * p.hkv + h) * kPage;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)kStage);
+        uint8_t* kdst = ring + (size_t)s * kStage;
+#pragma unroll
+        for (int j = 0; j < D / 64; ++j) {
+          tma_load_2d(kdst + j * kPage * 128, &kmap, 64 * j, row, &full[s]);
+          tma_load_2d(kdst + kTile + j * kPage * 128, &vmap, 64 * j, row, &full[s]);
+        }
+      }
+    }
+    return;
+  }
+
+  const int g = lane >> 2, q4 = lane & 3;
+  // this thread's rows g and g + 8 of the warp: (query, head), position, q
+  int pos_r[2];
+  float qv[2][KS][4];
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int r = warp * 16 + g + 8 * rr;
+    const int qi = r / G, j = r % G, t = t_begin + qi;
+    const bool valid = qi < p.bq && t <= t_last;
+    pos_r[rr] = valid ? p.pos[t] : -1;  // -1: every key masked, nothing stored
+    const __nv_bfloat16* qr =
+        p.q + (int64_t)(valid ? t : t_begin) * p.q_stride + (int64_t)(h * G + j) * D;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const int d0 = ks * 16 + 2 * q4;
+      const __nv_bfloat162 x0 = *reinterpret_cast<const __nv_bfloat162*>(qr + d0);
+      const __nv_bfloat162 x1 = *reinterpret_cast<const __nv_bfloat162*>(qr + d0 + 8);
+      qv[rr][ks][0] = __low2float(x0);
+      qv[rr][ks][1] = __high2float(x0);
+      qv[rr][ks][2] = __low2float(x1);
+      qv[rr][ks][3] = __high2float(x1);
+    }
+    if (p.q_norm_w) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ss += qv[rr][ks][i] * qv[rr][ks][i];
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      const float rs = 1.0f / sqrtf(ss / (float)D + p.eps);
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int d = ks * 16 + 2 * q4 + (i & 1) + (i >> 1) * 8;
+          qv[rr][ks][i] = (qv[rr][ks][i] * rs) * __ldg(p.q_norm_w + d);
+        }
+    }
+    switch (p.rot / 32) {
+      case 1: rope_q_at<KS, 1>(qv[rr], pos_r[rr], p.inv_freq, q4); break;
+      case 2: rope_q_at<KS, 2>(qv[rr], pos_r[rr], p.inv_freq, q4); break;
+      case 3: if constexpr (KS >= 6) rope_q_at<KS, 3>(qv[rr], pos_r[rr], p.inv_freq, q4); break;
+      case 4: if constexpr (KS >= 8) rope_q_at<KS, 4>(qv[rr], pos_r[rr], p.inv_freq, q4); break;
+      default: break;
+    }
+  }
+  // A fragments: {row g dims 2q4..+1, row g+8 dims 2q4..+1, row g dims +8..9, row g+8 dims +8..9}
+  uint32_t qhi[KS][4], qlo[KS][4];
+#pragma unroll
+  for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const float x0 = qv[rr][ks][2 * half], x1 = qv[rr][ks][2 * half + 1];
+        const float h0 = bf16_round(x0), h1 = bf16_round(x1);
+        qhi[ks][rr + 2 * half] = pack_bf16x2(h0, h1);
+        qlo[ks][rr + 2 * half] = pack_bf16x2(x0 - h0, x1 - h1);
+      }
+  int wmax = max(pos_r[0], pos_r[1]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+  const float scale = p.scale;
+
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_part[2] = {0.0f, 0.0f};
+  float o[D / 8][4];
+#pragma unroll
+  for (int nd = 0; nd < D / 8; ++nd)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[nd][i] = 0.0f;
+
+  const int mi = lane >> 3, r8 = lane & 7;
+  for (int it = 0; it < n_pages; ++it) {
+    const int s = it % kPfStages;
+    if (!mbar_wait(&full[s], (it / kPfStages) & 1)) break;
+    const int kb = it * kPage;
+    if (kb <= wmax) {
+      const uint32_t kbase = smem_u32(ring + (size_t)s * kStage);
+      const uint32_t vbase = kbase + kTile;
+      // ---- S (16 rows × 16 keys) = Q · Kᵀ, hi and lo in separate chains
+      float sc[2][4], sl[2][4];
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[nb][i] = sl[nb][i] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        // matrices: (keys 0-7, d 0-7), (keys 0-7, d 8-15), (keys 8-15, d 0-7), (keys 8-15, d 8-15)
+        uint32_t b[4];
+        ldsm_x4(b, kbase + swz(r8 + ((mi >> 1) << 3), ks * 16 + ((mi & 1) << 3), kPage));
+        mma_bf16_16816(sc[0], qhi[ks], b[0], b[1]);
+        mma_bf16_16816(sl[0], qlo[ks], b[0], b[1]);
+        mma_bf16_16816(sc[1], qhi[ks], b[2], b[3]);
+        mma_bf16_16816(sl[1], qlo[ks], b[2], b[3]);
+      }
+      // sc[nb][2*rr + e]: row g + 8*rr, key kb + nb*8 + 2*q4 + e
+      float pv[2][4], alpha[2];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        float sv[4];
+        float mt = -INFINITY;
+#pragma unroll
+        for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = kb + nb * 8 + 2 * q4 + e;
+            const float v = sc[nb][2 * rr + e] + sl[nb][2 * rr + e];
+            sv[2 * nb + e] = key <= pos_r[rr] ? v * scale : -INFINITY;
+            mt = fmaxf(mt, sv[2 * nb + e]);
+          }
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+        const float mn = fmaxf(m_run[rr], mt);
+        float sum = 0.0f;
+        if (mn == -INFINITY) {
+          alpha[rr] = 1.0f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) pv[rr][i] = 0.0f;
+        } else {
+          alpha[rr] = expf(m_run[rr] - mn);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            pv[rr][i] = expf(sv[i] - mn);
+            sum += pv[rr][i];
+          }
+        }
+        m_run[rr] = mn;
+        l_part[rr] = l_part[rr] * alpha[rr] + sum;
+      }
+#pragma unroll
+      for (int nd = 0; nd < D / 8; ++nd) {
+        o[nd][0] *= alpha[0];
+        o[nd][1] *= alpha[0];
+        o[nd][2] *= alpha[1];
+        o[nd][3] *= alpha[1];
+      }
+      // P as A fragments {row g keys 2q4..+1, row g+8 keys 2q4..+1, row g keys 8+2q4..,
+      // row g+8 keys 8+2q4..}, split into bf16 hi + lo
+      uint32_t ph[4], pl[4];
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const float x0 = pv[rr][2 * nb], x1 = pv[rr][2 * nb + 1];
+          const float h0 = bf16_round(x0), h1 = bf16_round(x1);
+          ph[2 * nb + rr] = pack_bf16x2(h0, h1);
+          pl[2 * nb + rr] = pack_bf16x2(x0 - h0, x1 - h1);
+        }
+      // ---- O += P · V: V (keys × dims) by ldmatrix.trans
+#pragma unroll
+      for (int n2 = 0; n2 < D / 16; ++n2) {
+        // matrices: (keys 0-7, d 0-7), (keys 8-15, d 0-7), (keys 0-7, d 8-15), (keys 8-15, d 8-15)
+        uint32_t b[4];
+        ldsm_x4_t(b, vbase + swz(r8 + ((mi & 1) << 3), n2 * 16 + ((mi >> 1) << 3), kPage));
+        mma_bf16_16816(o[2 * n2], ph, b[0], b[1]);
+        mma_bf16_16816(o[2 * n2], pl, b[0], b[1]);
+        mma_bf16_16816(o[2 * n2 + 1], ph, b[2], b[3]);
+        mma_bf16_16816(o[2 * n2 + 1], pl, b[2], b[3]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---- normalise and store: o[nd][2*rr + e] = O[row g + 8*rr][nd*8 + 2*q4 + e]
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    float l = l_part[rr];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (pos_r[rr] < 0) continue;
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    const int r = warp * 16 + g + 8 * rr;
+    const int t = t_begin + r / G, j = r % G;
+    __nv_bfloat16* orow = p.out + (int64_t)t * p.hq * D + (int64_t)(h * G + j) * D + 2 * q4;
+#pragma unroll
+    for (int nd = 0; nd < D / 8; ++nd)
+      *reinterpret_cast<uint32_t*>(orow + nd * 8) =
+          pack_bf16x2(o[nd][2 * rr] * inv, o[nd][2 * rr + 1] * inv);
+  }
+}
+
 // ---------------------------------------------------------- host helpers
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -778,6 +1071,66 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
     e = large ? go(paged_decode_kernel<64, kStagesLarge, 3>)
               : go(paged_decode_kernel<64, kStagesSmall, 1>);
   if (e != cudaSuccess) return cuda_fail(e, "paged decode attention launch");
+  return RXLA_B200_OK;
+}
+
+// Causal attention of a prompt chunk's rows (the decoder's prefill) after the
+// append-only pass wrote their K/V: a->batch rows of one sequence, row t at
+// position a->ctx_lens[t] (increasing), the sequence's pages in
+// a->page_table's first row.  Output [rows, q_heads, D] bf16.
+int32_t prefill_launch(const rxla_b200_paged_decode_args* a, cudaStream_t s) {
+  RXLA_REQUIRE(a && a->struct_size >= sizeof(rxla_b200_paged_decode_args),
+               "prefill_attention: args struct missing or too small");
+  const int D = a->head_dim;
+  RXLA_REQUIRE(a->batch >= 0 && a->kv_heads > 0 && a->q_heads > 0 &&
+                   a->q_heads % a->kv_heads == 0 && a->q_heads / a->kv_heads <= 8,
+               "prefill_attention: 1 to 8 query heads per kv head");
+  RXLA_REQUIRE(D == 64 || D == 128, "prefill_attention: head_dim must be 64 or 128");
+  RXLA_REQUIRE(a->page_size == attn::kPage && a->kv_heads <= 65535,
+               "prefill_attention: page_size must be 16");
+  RXLA_REQUIRE(a->rotary_dim == 0 || a->inv_freq == nullptr ||
+                   (a->rotary_dim % 32 == 0 && a->rotary_dim <= D),
+               "prefill_attention: rotary_dim must be a multiple of 32 and <= head_dim");
+  RXLA_REQUIRE(a->scale == 0.0f || std::isfinite(a->scale), "prefill_attention: scale must be finite");
+  RXLA_REQUIRE(a->q_row_stride % 2 == 0 && reinterpret_cast<uintptr_t>(a->q) % 4 == 0 &&
+                   reinterpret_cast<uintptr_t>(a->out) % 4 == 0,
+               "prefill_attention: q rows and out must be 4-byte aligned");
+  if (a->batch == 0) return RXLA_B200_OK;
+  RXLA_REQUIRE(a->q && a->k_pages && a->v_pages && a->page_table && a->ctx_lens && a->out,
+               "prefill_attention: null pointer");
+  attn::PrefillParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(a->q);
+  p.q_stride = a->q_row_stride;
+  p.q_norm_w = a->q_norm_weight;
+  p.eps = a->norm_eps;
+  p.inv_freq = a->inv_freq;
+  p.rot = a->inv_freq ? a->rotary_dim : 0;
+  p.scale = a->scale == 0.0f ? 1.0f / std::sqrt((float)D) : a->scale;
+  p.page_table = a->page_table;
+  p.pos = a->ctx_lens;
+  p.n = a->batch;
+  p.hq = a->q_heads;
+  p.hkv = a->kv_heads;
+  p.group = a->q_heads / a->kv_heads;
+  p.bq = attn::kPfRows / p.group;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
+  CUtensorMap kmap, vmap;
+  int32_t st = attn::make_page_map(&kmap, a->k_pages, a->num_pages, a->kv_heads, D);
+  if (st != RXLA_B200_OK) return st;
+  st = attn::make_page_map(&vmap, a->v_pages, a->num_pages, a->kv_heads, D);
+  if (st != RXLA_B200_OK) return st;
+  const size_t smem = 2048 + (size_t)attn::kPfStages * 2 * attn::kPage * D * 2;
+  const dim3 grid((unsigned)((p.n + p.bq - 1) / p.bq), (unsigned)a->kv_heads);
+  const dim3 block((attn::kPfWarps + 1) * 32);
+  auto go = [&](auto kernel) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e == cudaSuccess) e = launch_pdl(kernel, grid, block, smem, s, kmap, vmap, p);
+    return e;
+  };
+  cudaError_t e = D == 128 ? go(attn::prefill_attention_kernel<128>)
+                           : go(attn::prefill_attention_kernel<64>);
+  if (e != cudaSuccess) return cuda_fail(e, "prefill attention launch");
   return RXLA_B200_OK;
 }
 }  // namespace attn

@@ -527,10 +527,10 @@ static int32_t enqueue_rows_layers(rxla_b200_decoder* d, const Rows& r, cudaStre
     if (st) return st;
     rxla_b200_paged_decode_args a = attention_args(d, L, r);
     if (r.prefill) {
-      // positions were written before the layers; the full pass must not
-      // fetch pages before the append pass has finished
+      // positions were written before the layers; the causal pass reads the
+      // pages only after the append pass has finished
       st = attn::launch(&a, s, true, nullptr, true);
-      if (!st) st = attn::launch(&a, s, false);
+      if (!st) st = attn::prefill_launch(&a, s);
     } else {
       st = attn::launch(&a, s, true);
     }

@@ -125,6 +125,8 @@ namespace attn {
 // output, no context advance)
 int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s, bool ctx_stable,
                const L2Prefetch* next = nullptr, bool append_only = false);
+// causal attention of a prompt chunk's rows after an append-only launch
+int32_t prefill_launch(const rxla_b200_paged_decode_args* a, cudaStream_t s);
 }
 
 }  // namespace rxla
