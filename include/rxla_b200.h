@@ -72,7 +72,8 @@ typedef enum rxla_b200_dtype {
   RXLA_B200_F32 = 0,
   RXLA_B200_BF16 = 1,
   RXLA_B200_U8 = 2,
-  RXLA_B200_I32 = 3
+  RXLA_B200_I32 = 3,
+  RXLA_B200_F16 = 4
 } rxla_b200_dtype;
 
 /* Linear epilogues. */
@@ -310,6 +311,48 @@ int32_t rxla_b200_decoder_step(rxla_b200_decoder* decoder, const int32_t* tokens
 int32_t rxla_b200_decoder_prefill(rxla_b200_decoder* decoder, int32_t seq, const int32_t* tokens,
                                   int32_t count, int32_t* next_token, float* logits,
                                   void* stream);
+/* ---------------------------------------------------------------------------
+ * Checkpoints: safetensors reader and the decoder's W8 checkpoint loader
+ * (crates/rxla-safetensors/src/lib.rs).  Host code; no GPU needed for the
+ * reader.
+ * ------------------------------------------------------------------------- */
+typedef struct rxla_b200_safetensors rxla_b200_safetensors;
+/* Open and validate a .safetensors file (SafeTensors::new, lib.rs:147-177):
+ * header of at most 100 MB, tensors tiling the payload exactly, byte ranges
+ * matching shape × dtype size, payload length matching the file. */
+int32_t rxla_b200_safetensors_open(const char* path, rxla_b200_safetensors** out);
+int32_t rxla_b200_safetensors_close(rxla_b200_safetensors* reader);
+int32_t rxla_b200_safetensors_count(const rxla_b200_safetensors* reader, int32_t* count);
+/* Tensor `index` (header order): name (valid while open), dtype (RXLA_B200_*,
+ * -1 for a type without a code here, e.g. F64), rank, shape [<= 8], bytes. */
+int32_t rxla_b200_safetensors_info(const rxla_b200_safetensors* reader, int32_t index,
+                                   const char** name, int32_t* dtype, int32_t* ndim,
+                                   int64_t* shape, int64_t* bytes);
+/* Index of a tensor by name (SafeTensors::info); RXLA_B200_NOT_FOUND if absent. */
+int32_t rxla_b200_safetensors_find(const rxla_b200_safetensors* reader, const char* name,
+                                   int32_t* index);
+/* A "__metadata__" string (SafeTensors::metadata); RXLA_B200_NOT_FOUND if absent. */
+int32_t rxla_b200_safetensors_metadata(const rxla_b200_safetensors* reader, const char* key,
+                                       const char** value);
+/* Exact payload bytes (read_u8 / read_f32 without conversion, lib.rs:299-386)
+ * of the block [row0, row0 + rows) × [col0, col0 + cols) of the tensor seen
+ * as a matrix (rank 0/1: one row; rank >= 2: first dimension × the rest).
+ * dst_bytes must equal rows × cols × element size. */
+int32_t rxla_b200_safetensors_read(const rxla_b200_safetensors* reader, int32_t index,
+                                   int64_t row0, int64_t rows, int64_t col0, int64_t cols,
+                                   void* dst, int64_t dst_bytes);
+/* Load a checkpoint into the decoder's parameters: every tensor whose name
+ * starts with `prefix` (e.g. "model.language_model." of the rxla-qwen3.5-w8-v1
+ * format, benchmarks/quantize_qwen3_5_w8.py) is matched, prefix removed,
+ * against rxla_b200_decoder_parameter names (q/k/v_proj and gate/up_proj
+ * land in the fused matrices); U8 weights and F32 scales are uploaded as
+ * stored (upload_u8, lib.rs:664-700).  With tp_size > 1 each rank takes its
+ * slice of the full tensors.  Fails if a tensor's dtype or size does not
+ * match, if metadata "group_size" differs from the decoder's, or if any
+ * decoder parameter is left unfilled.  Synchronous. */
+int32_t rxla_b200_decoder_load_safetensors(rxla_b200_decoder* decoder, const char* path,
+                                           const char* prefix, int32_t* loaded,
+                                           int32_t* skipped);
 /* Host-buffer convenience for one step: copies tokens in and next tokens out
  * through pinned staging on `stream` and synchronises it. */
 int32_t rxla_b200_decoder_step_host(rxla_b200_decoder* decoder, const int32_t* tokens_host,

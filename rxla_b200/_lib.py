@@ -22,7 +22,7 @@ UNIMPLEMENTED = -12
 INTERNAL = -13
 UNAVAILABLE = -14
 
-F32, BF16, U8, I32 = 0, 1, 2, 3
+F32, BF16, U8, I32, F16 = 0, 1, 2, 3, 4
 EPI_STORE, EPI_RESIDUAL_ADD, EPI_SWIGLU = 0, 1, 2
 KV_CLAMP, KV_CHECKED = 0, 1
 NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024  # RXLA_B200_NOALLOC_SCRATCH_BYTES
@@ -109,6 +109,18 @@ SIGNATURES = {
     "rxla_b200_decoder_step": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
     "rxla_b200_decoder_step_host": (_i32, [_vp, _vp, _i32, _vp, _vp]),
     "rxla_b200_decoder_prefill": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _vp]),
+    "rxla_b200_safetensors_open": (_i32, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "rxla_b200_safetensors_close": (_i32, [_vp]),
+    "rxla_b200_safetensors_count": (_i32, [_vp, ctypes.POINTER(_i32)]),
+    "rxla_b200_safetensors_info": (_i32, [_vp, _i32, ctypes.POINTER(ctypes.c_char_p),
+                                          ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                                          ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
+    "rxla_b200_safetensors_find": (_i32, [_vp, ctypes.c_char_p, ctypes.POINTER(_i32)]),
+    "rxla_b200_safetensors_metadata": (_i32, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p)]),
+    "rxla_b200_safetensors_read": (_i32, [_vp, _i32, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                          ctypes.c_int64, _vp, ctypes.c_int64]),
+    "rxla_b200_decoder_load_safetensors": (_i32, [_vp, ctypes.c_char_p, ctypes.c_char_p,
+                                                  ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "rxla_b200_decoder_context_lengths": (_i32, [_vp, ctypes.POINTER(_vp)]),
     "rxla_b200_decoder_set_context_lengths": (_i32, [_vp, _vp, _i32, _vp]),
     "rxla_b200_decoder_kv_cache": (_i32, [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp),

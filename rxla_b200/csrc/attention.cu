@@ -73,7 +73,6 @@ struct Params {
   uint32_t* ws_counter;  // [batch * hkv] split arrivals, then [1] CTA exits
   int32_t batch;
   int32_t ctx_stable;    // ctx_lens is not written by the previous kernel: prefetch early
-  int32_t append_only;   // write the new K/V rows only (the decoder's prefill, first pass)
   int32_t stages;
   int32_t stage_bytes;  // K + V of one page of one kv head
   L2Prefetch next;      // the following kernel's first bytes
@@ -149,6 +148,48 @@ __device__ __forceinline__ void rope_q(float (&qv)[KS][4], const float2* cs, int
     }
 }
 
+// The new k / v row of one kv head (lane holds dims DL·lane ..): k RMSNorm
+// over the head (kw null: none), SplitHalf RoPE from the position table cs
+// (the partner of dim d < rot/2 is d + rot/2, held by lane + rot/(2·DL)),
+// both rounded to bf16 — the values the cache stores.
+template <int DL>
+__device__ __forceinline__ void prep_new_kv(float (&kn)[DL], float (&vn)[DL], int lane,
+                                            const float* kw, const float2* cs, int rot,
+                                            float eps) {
+  constexpr int D = DL * 32;
+  if (kw) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DL; ++i) ss += kn[i] * kn[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rs = 1.0f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < DL; ++i) kn[i] = (kn[i] * rs) * kw[DL * lane + i];
+  }
+  if (rot > 0) {
+    const int half = rot / 2, off = half / DL;
+#pragma unroll
+    for (int i = 0; i < DL; ++i) {
+      const int d = DL * lane + i;
+      const float up = __shfl_sync(0xffffffffu, kn[i], (lane + off) & 31);
+      const float dn = __shfl_sync(0xffffffffu, kn[i], (lane - off) & 31);
+      if (d < half) {
+        const float2 t = cs[d];
+        kn[i] = kn[i] * t.x - up * t.y;
+      } else if (d < rot) {
+        const float2 t = cs[d - half];
+        kn[i] = kn[i] * t.x + dn * t.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < DL; ++i) {
+    kn[i] = bf16_round(kn[i]);
+    vn[i] = bf16_round(vn[i]);
+  }
+}
+
 constexpr int kComputeWarps = 4;
 // Ring depth and occupancy: small batches (few CTAs, latency-bound) use a
 // deep ring; large batches fit three CTAs per SM with a shallower ring.  The
@@ -204,8 +245,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
 
   const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   const int ctas = gridDim.x * gridDim.y * gridDim.z;
-  if (split >= n_splits || (p.append_only && !owner)) {
-    // nothing of this sequence in this split, or nothing to append (exit = trigger)
+  if (split >= n_splits) {  // nothing of this sequence in this split (exit = trigger)
     if (threadIdx.x == 0) {
       if (p.next.nseg > 0) l2_prefetch_share(p.next, cta, ctas);
       finish_cta(p);
@@ -227,9 +267,6 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
     // Pages hold rows appended by earlier kernels only (the new row is patched
     // in from registers); with a stable ctx_lens they are fetched before
     // griddepcontrol.wait.
-    // append-only: every warp leaves before the closing barrier (the compute
-    // warps right after the append), so the CTA's exit needs no barrier
-    if (p.append_only) return;
     if (lane == 0) {
       for (int it = 0; it < n_it; ++it) {
         const int s = it % kStagesV2;
@@ -299,38 +336,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
     if (appender) {
       // k: RMSNorm over the head, RoPE, bf16; appended at the slot and patched
       // into this warp's tile of the slot's page below
-      if (p.k_norm_w) {
-        float ss = 0.0f;
-#pragma unroll
-        for (int i = 0; i < DL; ++i) ss += kn[i] * kn[i];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float rs = 1.0f / sqrtf(ss / (float)D + p.eps);
-#pragma unroll
-        for (int i = 0; i < DL; ++i) kn[i] = (kn[i] * rs) * kw[DL * lane + i];
-      }
-      if (p.rot > 0) {
-        // partner of dim d < rot/2 is d + rot/2, held by lane + rot/(2·DL)
-        const int half = p.rot / 2, off = half / DL;
-#pragma unroll
-        for (int i = 0; i < DL; ++i) {
-          const int d = DL * lane + i;
-          const float up = __shfl_sync(0xffffffffu, kn[i], (lane + off) & 31);
-          const float dn = __shfl_sync(0xffffffffu, kn[i], (lane - off) & 31);
-          if (d < half) {
-            const float2 t = cs[d];
-            kn[i] = kn[i] * t.x - up * t.y;
-          } else if (d < p.rot) {
-            const float2 t = cs[d - half];
-            kn[i] = kn[i] * t.x + dn * t.y;
-          }
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < DL; ++i) {
-        kn[i] = bf16_round(kn[i]);
-        vn[i] = bf16_round(vn[i]);
-      }
+      prep_new_kv<DL>(kn, vn, lane, p.k_norm_w ? kw : nullptr, cs, p.rot, p.eps);
       const int page = p.page_table[(int64_t)b * p.max_pages + slot_pg];
       const int64_t base = (((int64_t)page * hkv + h) * kPage + slot % kPage) * D + DL * lane;
 #pragma unroll
@@ -339,7 +345,6 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
         p.v_pages[base + i] = __float2bfloat16_rn(vn[i]);
       }
     }
-    if (p.append_only) return;  // no page loop, no output (the producer has left)
 
     // q of the G heads of this kv head in B-fragment layout, normed, rotated
     // and split into bf16 hi + lo
@@ -588,6 +593,49 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
   }
   __syncthreads();
   if (threadIdx.x == 0) finish_cta(p);
+}
+
+// The new K/V rows of a batch without the attention (the decoder's prefill
+// appends all rows of a prompt chunk before any row attends): block = row,
+// warp = kv head; positions, slots, normalisation, rotation and rounding as
+// paged_decode_kernel's append.
+template <int D>
+__global__ void __launch_bounds__(256) append_rows_kernel(const Params p) {
+  constexpr int DL = D / 32;
+  __shared__ float2 cs[64];
+  __shared__ float kw[128];
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  pdl_wait();  // k_new / v_new come from the previous kernel
+  if (tid == 0) pdl_launch_dependents();
+  const int pos = p.ctx_lens[b];
+  const int cap = (p.pages_per_seq ? p.pages_per_seq[b] : p.max_pages) * kPage;
+  const bool accept = cap > 0 && ((pos >= 0 && pos < cap) || p.kv_update == RXLA_B200_KV_CLAMP);
+  const int slot = pos < 0 ? 0 : (pos >= cap ? cap - 1 : pos);
+  if (p.rot > 0 && tid < p.rot / 2) {
+    const float ang = (float)pos * p.inv_freq[tid];
+    cs[tid] = make_float2(cosf(ang), sinf(ang));
+  }
+  if (p.k_norm_w && tid < D) kw[tid] = p.k_norm_w[tid];
+  __syncthreads();
+  if (!accept) return;
+  for (int h = tid >> 5; h < p.hkv; h += blockDim.x >> 5) {
+    const __nv_bfloat16* kr = p.k_new + (int64_t)b * p.kv_stride + (int64_t)h * D;
+    const __nv_bfloat16* vr = p.v_new + (int64_t)b * p.kv_stride + (int64_t)h * D;
+    float kn[DL], vn[DL];
+#pragma unroll
+    for (int i = 0; i < DL; ++i) {
+      kn[i] = __bfloat162float(kr[DL * lane + i]);
+      vn[i] = __bfloat162float(vr[DL * lane + i]);
+    }
+    prep_new_kv<DL>(kn, vn, lane, p.k_norm_w ? kw : nullptr, cs, p.rot, p.eps);
+    const int page = p.page_table[(int64_t)b * p.max_pages + slot / kPage];
+    const int64_t base = (((int64_t)page * p.hkv + h) * kPage + slot % kPage) * D + DL * lane;
+#pragma unroll
+    for (int i = 0; i < DL; ++i) {
+      p.k_pages[base + i] = __float2bfloat16_rn(kn[i]);
+      p.v_pages[base + i] = __float2bfloat16_rn(vn[i]);
+    }
+  }
 }
 
 // ------------------------------------------------ prefill (causal) attention
@@ -961,7 +1009,8 @@ namespace attn {
 // Validate, plan and launch.  `ctx_stable`: no kernel between the last write
 // of ctx_lens and this one may still be running, so pages can be fetched
 // before griddepcontrol.wait (the decoder runner advances ctx_lens only at
-// the end of a step).
+// the end of a step).  `append_only`: write the new K/V rows and nothing else
+// (append_rows_kernel).
 int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx_stable,
                const L2Prefetch* next, bool append_only) {
   RXLA_REQUIRE(a && a->struct_size >= sizeof(rxla_b200_paged_decode_args),
@@ -1039,7 +1088,15 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   p.stage_bytes = 2 * attn::kPage * D * 2;
   p.batch = a->batch;
   p.ctx_stable = ctx_stable ? 1 : 0;
-  p.append_only = append_only ? 1 : 0;
+  if (append_only) {
+    const int warps = std::max(4, std::min(a->kv_heads, 8));
+    cudaError_t e = D == 128 ? launch_pdl(attn::append_rows_kernel<128>, dim3(a->batch),
+                                          dim3(warps * 32), 0, s_in, p)
+                             : launch_pdl(attn::append_rows_kernel<64>, dim3(a->batch),
+                                          dim3(warps * 32), 0, s_in, p);
+    if (e != cudaSuccess) return cuda_fail(e, "kv append launch");
+    return RXLA_B200_OK;
+  }
   const bool large = a->batch >= 16;  // enough CTAs to fill the SMs several times
   p.stages = large ? attn::kStagesLarge : attn::kStagesSmall;
   if (next) p.next = *next;

@@ -1411,13 +1411,13 @@ extern "C" int32_t rxla_b200_decoder_step(rxla_b200_decoder* d, const int32_t* t
 namespace rxla {
 namespace dec {
 
-// Prefill chunk rows (RXLA_B200_PREFILL_CHUNK, default 1024, at most
+// Prefill chunk rows (RXLA_B200_PREFILL_CHUNK, default 2048, at most
 // max_context): buffers for that many rows are allocated once.
 static int32_t prefill_alloc(rxla_b200_decoder* d) {
   if (d->pf_mem) return RXLA_B200_OK;
   const auto& c = d->cfg;
   const char* v = getenv("RXLA_B200_PREFILL_CHUNK");
-  int C = v ? atoi(v) : 1024;
+  int C = v ? atoi(v) : 2048;
   C = std::max(1, std::min(C, c.max_context));
   const int64_t H = c.hidden, D = c.head_dim, I = d->inter;
   // workspaces: the largest any chunk of 1..C rows plans

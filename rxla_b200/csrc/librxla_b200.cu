@@ -10,5 +10,6 @@
 #include "dense_linear.cu"
 #include "attention.cu"
 #include "decoder.cu"
+#include "loader.cu"
 #include "comm.cu"
 #include "noalloc.cu"

@@ -111,6 +111,15 @@ class Decoder:
                   out.data_ptr(), logits_ptr, stream)
         return out
 
+    def load_safetensors(self, path, prefix: str = "model.language_model."):
+        """Fill every parameter from a safetensors checkpoint
+        (rxla_b200_decoder_load_safetensors); returns (loaded, skipped) tensor
+        counts."""
+        loaded, skipped = ctypes.c_int32(), ctypes.c_int32()
+        _lib.call("rxla_b200_decoder_load_safetensors", self._h, str(path).encode(),
+                  prefix.encode(), ctypes.byref(loaded), ctypes.byref(skipped))
+        return loaded.value, skipped.value
+
     def step_host(self, tokens, stream=None) -> np.ndarray:
         """One step from host tokens to host next tokens (copies + sync inside)."""
         tokens = np.ascontiguousarray(tokens, np.int32)

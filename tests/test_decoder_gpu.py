@@ -256,3 +256,45 @@ def test_prefill_matches_token_by_token_oracle(cuda, emb_bf16, group, monkeypatc
     gpu.close()
     for r in refs:
         r.close()
+
+
+@pytest.mark.parametrize("emb_bf16,group", [(True, 0), (False, 128)])
+def test_load_safetensors_matches_set_parameter(cuda, tmp_path, emb_bf16, group):
+    """A W8 checkpoint in the rxla-qwen3.5-w8-v1 layout (U8 weights, F32
+    scales, "model.language_model." names, format / group_size metadata) loaded
+    with rxla_b200_decoder_load_safetensors gives the same parameters as
+    set_parameter: identical logits and tokens over a prompt and decode."""
+    from rxla_b200.checkpoint import save_file
+    ref, gpu_a = _pair(batch=2, max_context=64, embedding_bf16=emb_bf16, group_size=group, seed=9)
+    names = [n for n in PARAMS if not (emb_bf16 and n == "embed_tokens.scale")]
+    if not emb_bf16:
+        names.append("embed_tokens.scale")
+    tensors = {"model.language_model." + n: ref.parameter(n) for n in names}
+    tensors["model.visual.unused"] = np.zeros(4, np.float32)  # skipped: other prefix
+    path = tmp_path / "w8.safetensors"
+    bf16 = {"model.language_model.embed_tokens.weight"} if emb_bf16 else None
+    save_file(path, tensors, metadata={"format": "rxla-qwen3.5-w8-v1",
+                                       "group_size": group or TINY["hidden"]}, bf16=bf16)
+    gpu_b = Decoder(**TINY, embedding_dtype="bf16" if emb_bf16 else "u8", group_size=group,
+                    max_batch=2, max_context=64)
+    loaded, skipped = gpu_b.load_safetensors(path)
+    assert (loaded, skipped) == (len(names), 1)
+    prompt = oracle.randint(2 * 12, 90, 0, 4096).reshape(2, 12)
+    outs = []
+    for gpu in (gpu_a, gpu_b):
+        lg = []
+        cur = prompt[:, 0].copy()
+        for t in range(20):
+            nxt = gpu.step_host(cur)
+            lg.append(nxt)
+            cur = prompt[:, t + 1].copy() if t + 1 < 12 else nxt
+        outs.append(np.stack(lg))
+    np.testing.assert_array_equal(outs[0], outs[1])
+    # a checkpoint missing a tensor does not fill the decoder
+    del tensors["model.language_model.layers.1.mlp.down_proj.weight"]
+    save_file(path, tensors, bf16=bf16)
+    with pytest.raises(Exception, match="down_proj"):
+        gpu_b.load_safetensors(path)
+    gpu_a.close()
+    gpu_b.close()
+    ref.close()
