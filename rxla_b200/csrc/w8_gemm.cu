@@ -425,13 +425,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           chunk(j0, g);
           chunk(kHalfN + j0, u);
           if (tok < p.m) {
+            const int64_t o0 = (int64_t)tok * p.ldy + out0 + j0;
+            __nv_bfloat16* yb = static_cast<__nv_bfloat16*>(p.y) + o0;
+            if (!p.y_f32 && out0 + j0 + kChunk <= p.n &&
+                (reinterpret_cast<uintptr_t>(yb) & 15) == 0) {
+              // a whole chunk: two 16-byte stores instead of 16 scattered ones
+              uint32_t pk[kChunk / 2];
 #pragma unroll
-            for (int i = 0; i < kChunk; ++i) {
-              if (out0 + j0 + i < p.n) {
-                const float r = silu(bf16_round(g[i])) * bf16_round(u[i]);
-                const int64_t o = (int64_t)tok * p.ldy + out0 + j0 + i;
-                if (p.y_f32) static_cast<float*>(p.y)[o] = r;
-                else static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(r);
+              for (int i = 0; i < kChunk; i += 2)
+                pk[i / 2] = pack_bf16x2(silu(bf16_round(g[i])) * bf16_round(u[i]),
+                                        silu(bf16_round(g[i + 1])) * bf16_round(u[i + 1]));
+              reinterpret_cast<uint4*>(yb)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              reinterpret_cast<uint4*>(yb)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < kChunk; ++i) {
+                if (out0 + j0 + i < p.n) {
+                  const float r = silu(bf16_round(g[i])) * bf16_round(u[i]);
+                  if (p.y_f32) static_cast<float*>(p.y)[o0 + i] = r;
+                  else yb[i] = __float2bfloat16_rn(r);
+                }
               }
             }
           }
@@ -448,14 +461,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t o = (int64_t)tok * p.ldy + col;
           if (p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD) {
             float* yy = static_cast<float*>(p.y) + o;
+            if (nv == kChunk && (reinterpret_cast<uintptr_t>(yy) & 15) == 0) {
+              // all four 16-byte loads in flight, then the stores
+              float4 r[kChunk / 4];
 #pragma unroll
-            for (int i = 0; i < kChunk; ++i)
-              if (i < nv) yy[i] = yy[i] + bf16_round(v[i]);
+              for (int i = 0; i < kChunk / 4; ++i) r[i] = reinterpret_cast<const float4*>(yy)[i];
+#pragma unroll
+              for (int i = 0; i < kChunk / 4; ++i) {
+                r[i].x += bf16_round(v[4 * i]);
+                r[i].y += bf16_round(v[4 * i + 1]);
+                r[i].z += bf16_round(v[4 * i + 2]);
+                r[i].w += bf16_round(v[4 * i + 3]);
+                reinterpret_cast<float4*>(yy)[i] = r[i];
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < kChunk; ++i)
+                if (i < nv) yy[i] = yy[i] + bf16_round(v[i]);
+            }
           } else if (p.y_f32) {
             float* yy = static_cast<float*>(p.y) + o;
+            if (nv == kChunk && (reinterpret_cast<uintptr_t>(yy) & 15) == 0) {
 #pragma unroll
-            for (int i = 0; i < kChunk; ++i)
-              if (i < nv) yy[i] = v[i];
+              for (int i = 0; i < kChunk / 4; ++i)
+                reinterpret_cast<float4*>(yy)[i] =
+                    make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < kChunk; ++i)
+                if (i < nv) yy[i] = v[i];
+            }
           } else {
             __nv_bfloat16* yy = static_cast<__nv_bfloat16*>(p.y) + o;
             if (nv == kChunk && (reinterpret_cast<uintptr_t>(yy) & 15) == 0) {
