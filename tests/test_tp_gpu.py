@@ -203,3 +203,115 @@ def test_p2p_allreduce_matches_rank_order_sum():
         assert err is None, f"rank {rank}: {err}"
         assert status == 0, f"rank {rank}: device status {status}"
         assert worst == 0.0, f"rank {rank}: max deviation {worst}"
+
+
+def _rank_prefill_main(rank, world, port, path, q):
+    import ctypes
+    import torch.distributed as dist
+
+    import oracle
+    from rxla_b200 import _lib
+    from rxla_b200.decoder import Comm, Decoder
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+
+        def share(data):
+            obj = [data]
+            dist.broadcast_object_list(obj, src=0)
+            return obj[0]
+
+        comm = Comm(rank, world, rank, share)
+        ref = oracle.Decoder(**TINY, embedding_bf16=False, group_size=0, max_batch=1,
+                             max_context=64)
+        ref.init_synthetic(9)
+        gpu = Decoder(**TINY, embedding_dtype="u8", max_batch=1, max_context=64, device=rank,
+                      comm=comm.handle, tp_rank=rank, tp_size=world)
+        loaded, skipped = gpu.load_safetensors(path)
+        V, vl = TINY["vocab"], TINY["vocab"] // world
+        prompt = oracle.randint(40, 31, 0, V)
+        lg = torch.empty(vl, dtype=torch.float32, device="cuda")
+        tok = gpu.prefill(0, prompt, logits_ptr=ctypes.c_void_p(lg.data_ptr()))
+        torch.cuda.synchronize()
+        for t in prompt:
+            l_ref, n_ref = ref.step(np.array([t], np.int32))
+        errs = [float(np.abs(lg.cpu().numpy() - l_ref[0, rank * vl:(rank + 1) * vl]).max())]
+        top2 = np.sort(l_ref[0])[-2:]
+        flip_ok = int(tok.item()) == int(n_ref[0]) or top2[1] - top2[0] <= 2 * max(errs)
+        # decode from the prefilled cache (teacher forcing)
+        lgb = torch.empty(1, vl, dtype=torch.float32, device="cuda")
+        tin = torch.empty(1, dtype=torch.int32, device="cuda")
+        tout = torch.empty(1, dtype=torch.int32, device="cuda")
+        s = torch.cuda.current_stream().cuda_stream
+        cur = n_ref.astype(np.int32)
+        for _ in range(6):
+            l_ref, n_ref = ref.step(cur)
+            tin.copy_(torch.from_numpy(cur))
+            _lib.call("rxla_b200_decoder_step", gpu.handle, ctypes.c_void_p(tin.data_ptr()), 1,
+                      ctypes.c_void_p(tout.data_ptr()), ctypes.c_void_p(lgb.data_ptr()),
+                      ctypes.c_void_p(s))
+            torch.cuda.synchronize()
+            errs.append(float(np.abs(lgb.cpu().numpy() - l_ref[:, rank * vl:(rank + 1) * vl]).max()))
+            cur = n_ref.astype(np.int32)
+        gpu.close()
+        comm.close()
+        ref.close()
+        dist.destroy_process_group()
+        q.put((rank, (loaded, skipped), errs, flip_ok, None))
+    except Exception as e:
+        q.put((rank, None, None, None, repr(e)))
+
+
+def test_tp2_checkpoint_load_and_prefill(tmp_path):
+    """Two ranks load their slices of one full W8 checkpoint
+    (rxla_b200_decoder_load_safetensors), prefill a 40-token prompt (the
+    row-parallel partial sums all-reduced over NCCL) and decode from the
+    prefilled cache; each rank's logits slice against the oracle."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor-parallel test needs two GPUs")
+    import oracle
+    from rxla_b200.checkpoint import save_file
+    ref = oracle.Decoder(**TINY, embedding_bf16=False, group_size=0, max_batch=1, max_context=64)
+    ref.init_synthetic(9)
+    H, D, I = TINY["hidden"], TINY["head_dim"], TINY["intermediate"]
+    rows = {"q_proj": TINY["q_heads"] * D, "k_proj": TINY["kv_heads"] * D,
+            "v_proj": TINY["kv_heads"] * D, "o_proj": H, "gate_proj": I, "up_proj": I,
+            "down_proj": H, "embed_tokens": TINY["vocab"]}
+    names = ["embed_tokens.weight", "embed_tokens.scale", "norm.weight"]
+    for i in range(TINY["layers"]):
+        p = f"layers.{i}."
+        names += [p + "input_layernorm.weight", p + "post_attention_layernorm.weight",
+                  p + "self_attn.q_norm.weight", p + "self_attn.k_norm.weight"]
+        names += [f"{p}self_attn.{pr}.{k}" for pr in ("q_proj", "k_proj", "v_proj", "o_proj")
+                  for k in ("weight", "scale")]
+        names += [f"{p}mlp.{pr}.{k}" for pr in ("gate_proj", "up_proj", "down_proj")
+                  for k in ("weight", "scale")]
+    tensors = {}
+    for n in names:
+        a = np.array(ref.parameter(n))
+        for pr, r in rows.items():
+            if n.startswith(pr) or f".{pr}." in n:
+                a = a.reshape(r, -1)
+        tensors["model.language_model." + n] = a
+    ref.close()
+    path = str(tmp_path / "tp.safetensors")
+    save_file(path, tensors, metadata={"format": "rxla-qwen3.5-w8-v1"})
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_prefill_main, args=(r, world, port, path, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, counts, errs, flip_ok, err in results:
+        assert err is None, f"rank {rank}: {err}"
+        print(f"rank {rank}: loaded/skipped {counts}, logits max-abs per step {errs}")
+        assert counts == (len(names), 0)
+        assert max(errs) <= 2e-2
+        assert flip_ok
