@@ -783,7 +783,7 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
     return enqueue_gemm_layers(d, batch, s);
   if (batch <= kChainMaxTokens && chain_kc(d) > 0 && d->packed_valid)
     return enqueue_chain_layers(d, batch, s);
-  const int64_t qd = (int64_t)d->hq * D, kd = (int64_t)d->hkv * D;
+  const int64_t qd = (int64_t)d->hq * D;
   // each kernel pulls the start of the next weight matrix into L2 while it drains
   auto pf = [](const void* w, int64_t bytes, int32_t per_cta) {
     L2Prefetch f{};
