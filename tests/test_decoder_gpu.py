@@ -298,3 +298,65 @@ def test_load_safetensors_matches_set_parameter(cuda, tmp_path, emb_bf16, group)
     gpu_a.close()
     gpu_b.close()
     ref.close()
+
+
+@pytest.mark.parametrize("q_heads,kv_heads,head_dim", [(8, 1, 128), (6, 2, 64)])
+def test_prefill_head_groupings(cuda, q_heads, kv_heads, head_dim):
+    """The causal prefill attention with 8 query heads per kv head and
+    head_dim 128 (16 queries per CTA block), and with 3 per kv head (42
+    queries, the last two rows of each block empty), against the oracle
+    stepping the same 70-token prompt: last-row logits within the prefill bar,
+    then decode from the prefilled cache, whose logits error must stay within
+    the decode bar or within that of the same decoder fed the prompt token by
+    token (these head shapes have their own noise floor against the oracle)."""
+    import ctypes
+    from rxla_b200 import _lib
+    cfg = dict(TINY, q_heads=q_heads, kv_heads=kv_heads, head_dim=head_dim)
+    ref = oracle.Decoder(**cfg, embedding_bf16=True, group_size=0, max_batch=1, max_context=128)
+    ref.init_synthetic(13)
+    gpu = Decoder(**cfg, embedding_dtype="bf16", group_size=0, max_batch=1, max_context=128)
+    for n in PARAMS:
+        if n != "embed_tokens.scale":
+            gpu.set_parameter(n, ref.parameter(n))
+    prompt = oracle.randint(70, 44, 0, 4096)
+    lg = torch.empty(gpu.vocab, dtype=torch.float32, device="cuda")
+    gpu.prefill(0, prompt, logits_ptr=ctypes.c_void_p(lg.data_ptr()))
+    torch.cuda.synchronize()
+    l_ref, n_ref = _ref_prompt(ref, prompt)
+    d = np.abs(lg.cpu().numpy() - l_ref)
+    print(f"G={q_heads // kv_heads} D={head_dim}: prefill max-abs {d.max():.4g} mean-abs {d.mean():.4g}")
+    assert d.max() <= 2e-2 and d.mean() <= 3e-3
+    lgb = torch.empty(1, gpu.vocab, dtype=torch.float32, device="cuda")
+    tin = torch.empty(1, dtype=torch.int32, device="cuda")
+    tout = torch.empty(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    # the same model decoded token by token from an empty cache
+    tok = Decoder(**cfg, embedding_dtype="bf16", group_size=0, max_batch=1, max_context=128)
+    for n in PARAMS:
+        if n != "embed_tokens.scale":
+            tok.set_parameter(n, ref.parameter(n))
+    for t in prompt:
+        tok.step_host(np.array([t], np.int32))
+
+    def step(dec, cur):
+        tin.copy_(torch.from_numpy(cur))
+        _lib.call("rxla_b200_decoder_step", dec.handle, ctypes.c_void_p(tin.data_ptr()), 1,
+                  ctypes.c_void_p(tout.data_ptr()), ctypes.c_void_p(lgb.data_ptr()),
+                  ctypes.c_void_p(s))
+        torch.cuda.synchronize()
+        return lgb.cpu().numpy()
+
+    cur, errs, errs_tok = np.array([n_ref], np.int32), [], []
+    for _ in range(8):
+        l2, n2 = ref.step(cur)
+        errs.append(np.abs(step(gpu, cur) - l2))
+        errs_tok.append(np.abs(step(tok, cur) - l2))
+        cur = n2.astype(np.int32)
+    e, et = np.stack(errs), np.stack(errs_tok)
+    print(f"decode after prefill: max-abs {e.max():.4g} mean-abs {e.mean():.4g}; "
+          f"token-by-token decoder: max-abs {et.max():.4g} mean-abs {et.mean():.4g}")
+    assert e.max() <= 2e-2
+    assert e.mean() <= max(2e-3, 1.25 * et.mean())
+    tok.close()
+    gpu.close()
+    ref.close()
