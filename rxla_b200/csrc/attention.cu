@@ -651,14 +651,16 @@ __global__ void __launch_bounds__(256) append_rows_kernel(const Params p) {
 //
 // CTA = (block of kPfRows / G queries, kv head).  Its kPfRows (query, head)
 // rows are the MMA M side — eight warps of 16 rows, row r is query r / G and
-// head r % G — with q held as A fragments in registers.  A producer warp
-// streams the key pages 0 .. (the block's last position) through a ring (TMA,
-// the decode kernel's [64 dims × 16 rows] swizzled boxes) and every warp
-// consumes every page: S = Q·Kᵀ (two 8-key n-blocks, K by ldmatrix), an
-// online softmax per row, O += P·V with P taken from the S accumulators (the
-// m16n8 C fragment is the next MMA's A fragment) and V by ldmatrix.trans.
-// Pages above a warp's last position are skipped; the heaviest query blocks
-// are scheduled first.
+// head r % G — with q held as A fragments in registers.  The key pages
+// 0 .. (the block's last position) stream through a ring (TMA, the decode
+// kernel's [64 dims × 16 rows] swizzled boxes) that lane 0 of warp 0 keeps
+// filled — no separate producer warp, so with 8 warps per CTA a thread may
+// hold up to 255 registers — and every warp consumes every page, two per
+// iteration: S = Q·Kᵀ (four 8-key n-blocks, K by ldmatrix), an online
+// softmax per row, O += P·V with P taken from the S accumulators (the m16n8
+// C fragment is the next MMA's A fragment) and V by ldmatrix.trans.  Pages
+// above a warp's last position are skipped; the heaviest query blocks are
+// scheduled first.
 constexpr int kPfWarps = 8;
 constexpr int kPfRows = kPfWarps * 16;
 constexpr int kPfStages = 8;
@@ -696,7 +698,7 @@ __device__ __forceinline__ void rope_q_at(float (&qv)[KS][4], int pos, const flo
 }
 
 template <int D>
-__global__ void __launch_bounds__((kPfWarps + 1) * 32, 1)
+__global__ void __launch_bounds__(kPfWarps * 32, 1)
     prefill_attention_kernel(const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -728,24 +730,23 @@ __global__ void __launch_bounds__((kPfWarps + 1) * 32, 1)
   const int n_keys = p.pos[t_last] + 1;
   const int n_pages = (n_keys + kPage - 1) / kPage;
 
-  if (warp == kPfWarps) {
-    // producer; no CTA-wide barrier follows, so the warp may leave
-    if (lane == 0) {
-      for (int it = 0; it < n_pages; ++it) {
-        const int s = it % kPfStages;
-        if (it >= kPfStages && !mbar_wait(&empty[s], ((it / kPfStages) - 1) & 1)) break;
-        const int row = (p.page_table[it] * p.hkv + h) * kPage;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)kStage);
-        uint8_t* kdst = ring + (size_t)s * kStage;
+  // page pg -> ring stage pg % kPfStages (K then V); issued by lane 0 of
+  // warp 0: the first kPfStages pages now, page pg + kPfStages once every
+  // warp has released page pg
+  auto issue = [&](int pg) {
+    const int s = pg % kPfStages;
+    const int row = (p.page_table[pg] * p.hkv + h) * kPage;
+    mbar_arrive_expect_tx(&full[s], (uint32_t)kStage);
+    uint8_t* kdst = ring + (size_t)s * kStage;
 #pragma unroll
-        for (int j = 0; j < D / 64; ++j) {
-          tma_load_2d(kdst + j * kPage * 128, &kmap, 64 * j, row, &full[s]);
-          tma_load_2d(kdst + kTile + j * kPage * 128, &vmap, 64 * j, row, &full[s]);
-        }
-      }
+    for (int j = 0; j < D / 64; ++j) {
+      tma_load_2d(kdst + j * kPage * 128, &kmap, 64 * j, row, &full[s]);
+      tma_load_2d(kdst + kTile + j * kPage * 128, &vmap, 64 * j, row, &full[s]);
     }
-    return;
-  }
+  };
+  if (threadIdx.x == 0)
+    for (int pg = 0; pg < min(n_pages, kPfStages); ++pg) issue(pg);
+  bool ring_ok = true;  // lane 0 of warp 0: a refill wait has not timed out
 
   const int g = lane >> 2, q4 = lane & 3;
   // this thread's rows g and g + 8 of the warp: (query, head), position, q
@@ -821,37 +822,58 @@ __global__ void __launch_bounds__((kPfWarps + 1) * 32, 1)
     for (int i = 0; i < 4; ++i) o[nd][i] = 0.0f;
 
   const int mi = lane >> 3, r8 = lane & 7;
-  for (int it = 0; it < n_pages; ++it) {
-    const int s = it % kPfStages;
-    if (!mbar_wait(&full[s], (it / kPfStages) & 1)) break;
+  // two pages (32 keys) per iteration: twice the independent MMA chains in
+  // S = Q·Kᵀ and one softmax rescale per 32 keys
+  for (int it = 0; it < n_pages; it += 2) {
+    if (threadIdx.x == 0 && it > 0 && ring_ok) {
+      // refill the stages of the previous iteration's pages
+      for (int pg = it - 2; pg < it; ++pg) {
+        if (pg + kPfStages >= n_pages) break;
+        if (!mbar_wait(&empty[pg % kPfStages], (pg / kPfStages) & 1)) {
+          ring_ok = false;
+          break;
+        }
+        issue(pg + kPfStages);
+      }
+    }
+    __syncwarp();
+    const int s0 = it % kPfStages, s1 = (it + 1) % kPfStages;
+    const bool two = it + 1 < n_pages;
+    if (!mbar_wait(&full[s0], (it / kPfStages) & 1)) break;
+    if (two && !mbar_wait(&full[s1], ((it + 1) / kPfStages) & 1)) break;
     const int kb = it * kPage;
     if (kb <= wmax) {
-      const uint32_t kbase = smem_u32(ring + (size_t)s * kStage);
-      const uint32_t vbase = kbase + kTile;
-      // ---- S (16 rows × 16 keys) = Q · Kᵀ, hi and lo in separate chains
-      float sc[2][4], sl[2][4];
+      const uint32_t kbase[2] = {smem_u32(ring + (size_t)s0 * kStage),
+                                 smem_u32(ring + (size_t)s1 * kStage)};
+      // ---- S (16 rows × 32 keys) = Q · Kᵀ, hi and lo in separate chains
+      float sc[4][4], sl[4][4];
 #pragma unroll
-      for (int nb = 0; nb < 2; ++nb)
+      for (int nb = 0; nb < 4; ++nb)
 #pragma unroll
         for (int i = 0; i < 4; ++i) sc[nb][i] = sl[nb][i] = 0.0f;
 #pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        // matrices: (keys 0-7, d 0-7), (keys 0-7, d 8-15), (keys 8-15, d 0-7), (keys 8-15, d 8-15)
-        uint32_t b[4];
-        ldsm_x4(b, kbase + swz(r8 + ((mi >> 1) << 3), ks * 16 + ((mi & 1) << 3), kPage));
-        mma_bf16_16816(sc[0], qhi[ks], b[0], b[1]);
-        mma_bf16_16816(sl[0], qlo[ks], b[0], b[1]);
-        mma_bf16_16816(sc[1], qhi[ks], b[2], b[3]);
-        mma_bf16_16816(sl[1], qlo[ks], b[2], b[3]);
+      for (int pg = 0; pg < 2; ++pg) {
+        if (pg == 1 && !two) break;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          // matrices: (keys 0-7, d 0-7), (keys 0-7, d 8-15), (keys 8-15, d 0-7), (keys 8-15, d 8-15)
+          uint32_t b[4];
+          ldsm_x4(b, kbase[pg] + swz(r8 + ((mi >> 1) << 3), ks * 16 + ((mi & 1) << 3), kPage));
+          mma_bf16_16816(sc[2 * pg], qhi[ks], b[0], b[1]);
+          mma_bf16_16816(sl[2 * pg], qlo[ks], b[0], b[1]);
+          mma_bf16_16816(sc[2 * pg + 1], qhi[ks], b[2], b[3]);
+          mma_bf16_16816(sl[2 * pg + 1], qlo[ks], b[2], b[3]);
+        }
       }
-      // sc[nb][2*rr + e]: row g + 8*rr, key kb + nb*8 + 2*q4 + e
-      float pv[2][4], alpha[2];
+      // sc[nb][2*rr + e]: row g + 8*rr, key kb + nb*8 + 2*q4 + e (keys of an
+      // absent second page lie past every row's position)
+      float pv[2][8], alpha[2];
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
-        float sv[4];
+        float sv[8];
         float mt = -INFINITY;
 #pragma unroll
-        for (int nb = 0; nb < 2; ++nb)
+        for (int nb = 0; nb < 4; ++nb)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int key = kb + nb * 8 + 2 * q4 + e;
@@ -866,11 +888,11 @@ __global__ void __launch_bounds__((kPfWarps + 1) * 32, 1)
         if (mn == -INFINITY) {
           alpha[rr] = 1.0f;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) pv[rr][i] = 0.0f;
+          for (int i = 0; i < 8; ++i) pv[rr][i] = 0.0f;
         } else {
           alpha[rr] = expf(m_run[rr] - mn);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < 8; ++i) {
             pv[rr][i] = expf(sv[i] - mn);
             sum += pv[rr][i];
           }
@@ -885,32 +907,42 @@ __global__ void __launch_bounds__((kPfWarps + 1) * 32, 1)
         o[nd][2] *= alpha[1];
         o[nd][3] *= alpha[1];
       }
-      // P as A fragments {row g keys 2q4..+1, row g+8 keys 2q4..+1, row g keys 8+2q4..,
-      // row g+8 keys 8+2q4..}, split into bf16 hi + lo
-      uint32_t ph[4], pl[4];
+      // P as A fragments per page: {row g keys 2q4..+1, row g+8 keys 2q4..+1,
+      // row g keys 8+2q4.., row g+8 keys 8+2q4..}, split into bf16 hi + lo
+      uint32_t ph[2][4], pl[2][4];
 #pragma unroll
-      for (int nb = 0; nb < 2; ++nb)
+      for (int pg = 0; pg < 2; ++pg)
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const float x0 = pv[rr][2 * nb], x1 = pv[rr][2 * nb + 1];
-          const float h0 = bf16_round(x0), h1 = bf16_round(x1);
-          ph[2 * nb + rr] = pack_bf16x2(h0, h1);
-          pl[2 * nb + rr] = pack_bf16x2(x0 - h0, x1 - h1);
-        }
+        for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const float x0 = pv[rr][4 * pg + 2 * nb], x1 = pv[rr][4 * pg + 2 * nb + 1];
+            const float h0 = bf16_round(x0), h1 = bf16_round(x1);
+            ph[pg][2 * nb + rr] = pack_bf16x2(h0, h1);
+            pl[pg][2 * nb + rr] = pack_bf16x2(x0 - h0, x1 - h1);
+          }
       // ---- O += P · V: V (keys × dims) by ldmatrix.trans
 #pragma unroll
-      for (int n2 = 0; n2 < D / 16; ++n2) {
-        // matrices: (keys 0-7, d 0-7), (keys 8-15, d 0-7), (keys 0-7, d 8-15), (keys 8-15, d 8-15)
-        uint32_t b[4];
-        ldsm_x4_t(b, vbase + swz(r8 + ((mi & 1) << 3), n2 * 16 + ((mi >> 1) << 3), kPage));
-        mma_bf16_16816(o[2 * n2], ph, b[0], b[1]);
-        mma_bf16_16816(o[2 * n2], pl, b[0], b[1]);
-        mma_bf16_16816(o[2 * n2 + 1], ph, b[2], b[3]);
-        mma_bf16_16816(o[2 * n2 + 1], pl, b[2], b[3]);
+      for (int pg = 0; pg < 2; ++pg) {
+        if (pg == 1 && !two) break;
+        const uint32_t vbase = kbase[pg] + kTile;
+#pragma unroll
+        for (int n2 = 0; n2 < D / 16; ++n2) {
+          // matrices: (keys 0-7, d 0-7), (keys 8-15, d 0-7), (keys 0-7, d 8-15), (keys 8-15, d 8-15)
+          uint32_t b[4];
+          ldsm_x4_t(b, vbase + swz(r8 + ((mi & 1) << 3), n2 * 16 + ((mi >> 1) << 3), kPage));
+          mma_bf16_16816(o[2 * n2], ph[pg], b[0], b[1]);
+          mma_bf16_16816(o[2 * n2], pl[pg], b[0], b[1]);
+          mma_bf16_16816(o[2 * n2 + 1], ph[pg], b[2], b[3]);
+          mma_bf16_16816(o[2 * n2 + 1], pl[pg], b[2], b[3]);
+        }
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (lane == 0) {
+      mbar_arrive(&empty[s0]);
+      if (two) mbar_arrive(&empty[s1]);
+    }
   }
 
   // ---- normalise and store: o[nd][2*rr + e] = O[row g + 8*rr][nd*8 + 2*q4 + e]
@@ -1178,7 +1210,7 @@ int32_t prefill_launch(const rxla_b200_paged_decode_args* a, cudaStream_t s) {
   if (st != RXLA_B200_OK) return st;
   const size_t smem = 2048 + (size_t)attn::kPfStages * 2 * attn::kPage * D * 2;
   const dim3 grid((unsigned)((p.n + p.bq - 1) / p.bq), (unsigned)a->kv_heads);
-  const dim3 block((attn::kPfWarps + 1) * 32);
+  const dim3 block(attn::kPfWarps * 32);
   auto go = [&](auto kernel) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
