@@ -1478,6 +1478,15 @@ extern "C" int32_t rxla_b200_decoder_prefill(rxla_b200_decoder* d, int32_t seq,
   const int64_t H = c.hidden;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   RXLA_CUDA_CHECK(cudaSetDevice(d->device));
+  {
+    // the embedding kernel reads the prompt directly: ordinary (unregistered)
+    // host memory would be an illegal address there, so refuse it here
+    cudaPointerAttributes pa{};
+    const cudaError_t e = cudaPointerGetAttributes(&pa, tokens);
+    if (e != cudaSuccess) cudaGetLastError();
+    RXLA_REQUIRE(e == cudaSuccess && pa.type != cudaMemoryTypeUnregistered,
+                 "decoder_prefill: tokens must be device, managed or pinned host memory");
+  }
   int32_t st = dec::prefill_alloc(d);
   if (st) return st;
   // the sequence's position: one synchronous read

@@ -360,3 +360,21 @@ def test_prefill_head_groupings(cuda, q_heads, kv_heads, head_dim):
     tok.close()
     gpu.close()
     ref.close()
+
+
+def test_prefill_refuses_unregistered_host_tokens(cuda):
+    """The prefill's embedding kernel reads the prompt in place, so a prompt in
+    ordinary host memory is refused with INVALID_ARGUMENT (no kernel runs)."""
+    import ctypes
+    from rxla_b200 import _lib
+    _, gpu = _pair(batch=1, max_context=64)
+    host = np.arange(8, dtype=np.int32)
+    rc = _lib.load().rxla_b200_decoder_prefill(gpu.handle, 0, host.ctypes.data_as(ctypes.c_void_p),
+                                               8, None, None, None)
+    assert rc == _lib.INVALID_ARGUMENT
+    assert "device, managed or pinned" in _lib.load().rxla_b200_last_error_message().decode()
+    # the decoder is untouched: a device prompt still prefills
+    tok = gpu.prefill(0, host)
+    torch.cuda.synchronize()
+    assert 0 <= int(tok.item()) < gpu.vocab
+    gpu.close()
