@@ -295,7 +295,8 @@ int32_t rxla_b200_decoder_reset(rxla_b200_decoder* decoder, void* stream);
 int32_t rxla_b200_decoder_step(rxla_b200_decoder* decoder, const int32_t* tokens,
                                int32_t batch, int32_t* next_tokens, float* logits,
                                void* stream);
-/* Prefill: run `count` prompt tokens (device int32 [count]) of sequence `seq`
+/* Prefill: run `count` prompt tokens (int32 [count] in device, managed or
+ * pinned host memory; ordinary host memory is refused) of sequence `seq`
  * through every layer at positions ctx[seq] .. ctx[seq] + count - 1, append
  * their K/V to the sequence's pages and advance ctx[seq] by count.  The
  * linears run over a whole chunk of prompt rows (tcgen05 GEMM) and each row
