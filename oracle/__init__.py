@@ -82,6 +82,7 @@ def lib() -> ctypes.CDLL:
         "oracle_decoder_init_synthetic": (None, [_vp, ctypes.c_uint64]),
         "oracle_decoder_reset": (None, [_vp]),
         "oracle_decoder_step": (None, [_vp, _i32p, _i32, _f32p, _i32p]),
+        "oracle_decoder_forward": (None, [_vp, _i32p, _i32, _f32p, _i32p]),
         "oracle_decoder_context": (_i32, [_vp, _i32]),
         "oracle_decoder_kv": (None, [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
         "oracle_num_threads": (_i32, []),
@@ -341,6 +342,16 @@ class Decoder:
 
     def reset(self):
         lib().oracle_decoder_reset(self._h)
+
+    def forward(self, prompt):
+        """Full-sequence causal forward of one prompt from position 0 (the
+        reference's prompt path, qwen3_5/mod.rs:199-260): the last row's
+        logits [vocab] and greedy token.  The decoder's state is untouched."""
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        logits = np.empty(self.vocab, np.float32)
+        nxt = np.empty(1, np.int32)
+        lib().oracle_decoder_forward(self._h, prompt, prompt.shape[0], logits, nxt)
+        return logits, int(nxt[0])
 
     def step(self, tokens):
         tokens = np.ascontiguousarray(tokens, np.int32)

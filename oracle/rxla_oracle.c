@@ -745,6 +745,140 @@ void oracle_decoder_step(oracle_decoder* dec, const int32_t* tokens, int32_t bat
   free(up);
 }
 
+/* Full-sequence forward of one prompt (positions 0 .. T-1) with the causal
+ * mask, the way the reference runs a prompt (crates/rxla-models/src/qwen3_5/
+ * mod.rs:199-260: causal_attention_mask at :229, SDPA of
+ * crates/rxla-core/src/attention.rs:83-252): every linear over all T rows,
+ * attention of the whole [T, T] score matrix under the additive mask.  K and V
+ * are rounded to bf16 as the paged cache stores them.  Writes the last row's
+ * logits [V] and its greedy token; the decoder's state is not touched. */
+void oracle_decoder_forward(oracle_decoder* dec, const int32_t* tokens, int32_t T, float* logits,
+                            int32_t* next_token) {
+  const oracle_decoder_config* c = &dec->cfg;
+  int64_t H = c->hidden, D = c->head_dim, I = c->intermediate, V = c->vocab;
+  int64_t HQ = c->q_heads, HKV = c->kv_heads;
+  int64_t M = T;
+  float* h = (float*)calloc((size_t)(M * H), 4);
+  float* xn = (float*)calloc((size_t)(M * H), 4);
+  float* q = (float*)calloc((size_t)(M * HQ * D), 4);
+  float* kk = (float*)calloc((size_t)(M * HKV * D), 4);
+  float* vv = (float*)calloc((size_t)(M * HKV * D), 4);
+  float* qh = (float*)calloc((size_t)(M * HQ * D), 4);  /* [HQ, T, D] */
+  float* kh = (float*)calloc((size_t)(M * HKV * D), 4); /* [HKV, T, D] */
+  float* vh = (float*)calloc((size_t)(M * HKV * D), 4);
+  float* oh = (float*)calloc((size_t)(M * HQ * D), 4);
+  float* att = (float*)calloc((size_t)(M * HQ * D), 4);
+  float* o = (float*)calloc((size_t)(M * H), 4);
+  float* gate = (float*)calloc((size_t)(M * I), 4);
+  float* up = (float*)calloc((size_t)(M * I), 4);
+  float* mask = (float*)calloc((size_t)(M * M), 4);
+  int32_t* pos = (int32_t*)calloc((size_t)M, 4);
+  char pre[96];
+  for (int64_t t = 0; t < M; ++t) pos[t] = (int32_t)t;
+  oracle_causal_mask(pos, M, pos, M, mask);
+
+  oracle_param* emb = find_param(dec, "embed_tokens.weight");
+  oracle_param* embs = find_param(dec, "embed_tokens.scale");
+  for (int64_t b = 0; b < M; ++b) {
+    int64_t t = tokens[b];
+    for (int64_t j = 0; j < H; ++j) {
+      if (c->embedding_bf16) {
+        h[b * H + j] = oracle_bf16_to_f32(((uint16_t*)emb->data)[t * H + j]);
+      } else {
+        int64_t groups = embs->elems / V;
+        int64_t grp = c->group_size > 0 ? j / c->group_size : 0;
+        h[b * H + j] = (float)((int32_t)((uint8_t*)emb->data)[t * H + j] - 128) *
+                       ((float*)embs->data)[t * groups + grp];
+      }
+    }
+  }
+  for (int32_t l = 0; l < c->layers; ++l) {
+    snprintf(pre, sizeof(pre), "layers.%d.input_layernorm.weight", l);
+    oracle_rms_norm(h, M, H, (float*)find_param(dec, pre)->data, c->rms_eps, xn);
+    snprintf(pre, sizeof(pre), "layers.%d.self_attn.q_proj", l);
+    dec_w8(dec, pre, xn, M, H, HQ * D, q);
+    snprintf(pre, sizeof(pre), "layers.%d.self_attn.k_proj", l);
+    dec_w8(dec, pre, xn, M, H, HKV * D, kk);
+    snprintf(pre, sizeof(pre), "layers.%d.self_attn.v_proj", l);
+    dec_w8(dec, pre, xn, M, H, HKV * D, vv);
+    snprintf(pre, sizeof(pre), "layers.%d.self_attn.q_norm.weight", l);
+    float* qn = (float*)find_param(dec, pre)->data;
+    snprintf(pre, sizeof(pre), "layers.%d.self_attn.k_norm.weight", l);
+    float* kn = (float*)find_param(dec, pre)->data;
+    for (int64_t t = 0; t < M; ++t) {
+      for (int64_t hh = 0; hh < HQ; ++hh) {
+        float* v = q + t * HQ * D + hh * D;
+        head_rms_norm(v, (int32_t)D, qn, c->rms_eps);
+        oracle_rope_split_half(v, 1, D, (int32_t)D, &pos[t], dec->inv_freq);
+        memcpy(qh + (hh * M + t) * D, v, (size_t)D * 4);
+      }
+      for (int64_t hh = 0; hh < HKV; ++hh) {
+        float* v = kk + t * HKV * D + hh * D;
+        head_rms_norm(v, (int32_t)D, kn, c->rms_eps);
+        oracle_rope_split_half(v, 1, D, (int32_t)D, &pos[t], dec->inv_freq);
+        for (int64_t i = 0; i < D; ++i) {
+          kh[(hh * M + t) * D + i] = oracle_bf16_round(v[i]);
+          vh[(hh * M + t) * D + i] = oracle_bf16_round(vv[t * HKV * D + hh * D + i]);
+        }
+      }
+    }
+    oracle_gqa_attention(qh, kh, vh, mask, 0, 0, 1, HQ, HKV, M, M, D, D,
+                         1.0f / sqrtf((float)D), oh);
+    for (int64_t t = 0; t < M; ++t)
+      for (int64_t hh = 0; hh < HQ; ++hh)
+        memcpy(att + t * HQ * D + hh * D, oh + (hh * M + t) * D, (size_t)D * 4);
+    snprintf(pre, sizeof(pre), "layers.%d.self_attn.o_proj", l);
+    dec_w8(dec, pre, att, M, HQ * D, H, o);
+    for (int64_t i = 0; i < M * H; ++i) h[i] = h[i] + o[i];
+    snprintf(pre, sizeof(pre), "layers.%d.post_attention_layernorm.weight", l);
+    oracle_rms_norm(h, M, H, (float*)find_param(dec, pre)->data, c->rms_eps, xn);
+    snprintf(pre, sizeof(pre), "layers.%d.mlp.gate_proj", l);
+    dec_w8(dec, pre, xn, M, H, I, gate);
+    snprintf(pre, sizeof(pre), "layers.%d.mlp.up_proj", l);
+    dec_w8(dec, pre, xn, M, H, I, up);
+    for (int64_t i = 0; i < M * I; ++i) gate[i] = silu_f32(gate[i]) * up[i];
+    snprintf(pre, sizeof(pre), "layers.%d.mlp.down_proj", l);
+    dec_w8(dec, pre, gate, M, I, H, o);
+    for (int64_t i = 0; i < M * H; ++i) h[i] = h[i] + o[i];
+  }
+  /* the head on the last row */
+  const float* hl = h + (M - 1) * H;
+  oracle_rms_norm(hl, 1, H, (float*)find_param(dec, "norm.weight")->data, c->rms_eps, xn);
+  if (c->embedding_bf16) {
+    uint16_t* e = (uint16_t*)emb->data;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < V; ++r) {
+      double acc = 0.0;
+      for (int64_t j = 0; j < H; ++j)
+        acc += (double)oracle_bf16_round(xn[j]) * (double)oracle_bf16_to_f32(e[r * H + j]);
+      logits[r] = (float)acc;
+    }
+  } else {
+    int64_t group = c->group_size > 0 ? c->group_size : H;
+    oracle_w8_linear(xn, 1, H, (const uint8_t*)emb->data, (const float*)embs->data, V, group, 2,
+                     logits);
+  }
+  int32_t best = 0;
+  for (int64_t r = 1; r < V; ++r)
+    if (logits[r] > logits[best]) best = (int32_t)r;
+  *next_token = best;
+  free(h);
+  free(xn);
+  free(q);
+  free(kk);
+  free(vv);
+  free(qh);
+  free(kh);
+  free(vh);
+  free(oh);
+  free(att);
+  free(o);
+  free(gate);
+  free(up);
+  free(mask);
+  free(pos);
+}
+
 int32_t oracle_num_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

@@ -138,6 +138,9 @@ int64_t oracle_decoder_parameter(oracle_decoder* dec, const char* name, void** p
 void oracle_decoder_init_synthetic(oracle_decoder* dec, uint64_t seed);
 void oracle_decoder_reset(oracle_decoder* dec);
 /* One step: tokens [batch] -> logits [batch, vocab] (f32), next tokens [batch]. */
+/* full-sequence forward of one prompt with the causal mask (state untouched) */
+void oracle_decoder_forward(oracle_decoder* dec, const int32_t* tokens, int32_t T, float* logits,
+                            int32_t* next_token);
 void oracle_decoder_step(oracle_decoder* dec, const int32_t* tokens, int32_t batch,
                          float* logits, int32_t* next_tokens);
 int32_t oracle_decoder_context(oracle_decoder* dec, int32_t b);

@@ -309,3 +309,24 @@ def test_tiny_decoder_runs_and_is_deterministic():
     np.testing.assert_array_equal(outs[0][0], outs[1][0])
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
     assert np.isfinite(outs[0][1]).all()
+
+
+@pytest.mark.parametrize("emb_bf16,group", [(True, 0), (False, 128)])
+def test_stepped_decoder_equals_full_sequence_causal_forward(emb_bf16, group):
+    """The oracle decoder stepped one token at a time (what the GPU prefill and
+    decode tests compare against) gives the same last-row logits and token as
+    the full-sequence forward under the causal mask — the reference's prompt
+    path (qwen3_5/mod.rs:199-260 with the mask of :229).  Both read K/V
+    rounded to bf16 and sum in the same order, so they agree exactly."""
+    cfg = dict(layers=2, hidden=512, q_heads=8, kv_heads=2, head_dim=64, intermediate=1536,
+               vocab=4096)
+    dec = oracle.Decoder(**cfg, embedding_bf16=emb_bf16, group_size=group, max_batch=1,
+                         max_context=64)
+    dec.init_synthetic(17)
+    prompt = oracle.randint(24, 3, 0, cfg["vocab"])
+    full_logits, full_tok = dec.forward(prompt)
+    for t in prompt:
+        step_logits, step_tok = dec.step(np.array([t], np.int32))
+    np.testing.assert_array_equal(full_logits, step_logits[0])
+    assert full_tok == int(step_tok[0])
+    dec.close()
