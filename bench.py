@@ -156,6 +156,37 @@ def cpu_decode_sample(threads_note=True):
                       f"(step {t_step:.3f}s, head {t_head:.3f}s), extrapolated to 36 layers"}
 
 
+def cpu_prefill_sample():
+    """Time the CPU oracle's full-sequence causal forward on a bounded sample
+    of the config-4 prefill: 1 of the 36 layers over a 64-token prompt plus
+    the tied head on the last row, extrapolated to 36 layers (the linears,
+    nearly all of the work, scale with the prompt length)."""
+    import numpy as np
+    import oracle
+    cfg = dict(CONFIG4, layers=1)
+    dec = oracle.Decoder(**cfg, max_batch=1, max_context=80)
+    dec.init_synthetic(0)
+    n = 64
+    prompt = np.arange(1, n + 1, dtype=np.int32)
+    t0 = time.perf_counter()
+    dec.forward(prompt)
+    t_fwd = time.perf_counter() - t0
+    emb_w = dec.parameter("embed_tokens.weight").reshape(CONFIG4["vocab"], CONFIG4["hidden"])
+    emb_s = dec.parameter("embed_tokens.scale").reshape(CONFIG4["vocab"], 1)
+    x = np.ones((1, CONFIG4["hidden"]), np.float32)
+    t0 = time.perf_counter()
+    oracle.w8_linear(x, emb_w, emb_s, CONFIG4["hidden"], mode=2)
+    t_head = time.perf_counter() - t0
+    dec.close()
+    t_layer = max(t_fwd - t_head, 1e-9)
+    t_prompt = CONFIG4["layers"] * t_layer + t_head
+    return {"value": n / t_prompt, "unit": "tokens/s", "cores": oracle.num_threads(),
+            "kind": "port",
+            "sample": f"oracle C restatement, full-sequence causal forward, 1 of 36 layers over "
+                      f"a {n}-token prompt ({t_fwd:.2f}s incl. head {t_head:.2f}s), "
+                      f"extrapolated to 36 layers"}
+
+
 # --------------------------------------------------------------- our path
 
 def run_ours(args, rank, world, local_rank):
@@ -481,6 +512,8 @@ def run_prefill(args):
                     "d2h_bytes_per_step": 4},
             "clocks": clocks}
     dec.close()
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_prefill_sample()
     print(json.dumps(line), flush=True)
 
 
