@@ -125,3 +125,11 @@ def test_prefill_validation_without_cuda():
     toks = (ctypes.c_int32 * 4)(1, 2, 3, 4)
     assert lib.rxla_b200_decoder_prefill(None, 0, toks, 4, None, None, None) == _lib.INVALID_ARGUMENT
     assert "decoder_prefill" in lib.rxla_b200_last_error_message().decode()
+
+
+def test_python_constants_match_header_enums():
+    """The dtype and status codes the Python binding uses are the header's."""
+    text = (ROOT / "include" / "rxla_b200.h").read_text()
+    enums = {m.group(1): int(m.group(2)) for m in re.finditer(r"RXLA_B200_(\w+)\s*=\s*(-?\d+)", text)}
+    for name in ("F32", "BF16", "U8", "I32", "F16", "OK", "INVALID_ARGUMENT", "NOT_FOUND"):
+        assert getattr(_lib, name) == enums[name], name
