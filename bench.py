@@ -4,14 +4,27 @@
 
 Workload (one GPU): the 8B-shaped Qwen3-style W8 decoder (36 layers, hidden
 4096, 32 q / 8 kv heads, head_dim 128, SwiGLU 12288, vocab 151936, int8
-per-channel weights, synthetic seeded values), a 2048-token random prompt fed
-through the decoder, then greedy decode steps.  A "step" is one decode step
-at batch 1 (the headline `value`); the same is measured at batch 64.
+per-channel weights, synthetic seeded values), a 2048-token random prompt run
+through the prefill, then greedy decode steps.  A "step" is one decode step at
+batch 1 (the headline `value`); the same is measured at batch 64, and config
+5 (the 32B shape, batch 32 at a 4096-token context).
+
+Before any timing, every rank checks tensor-parallel parity: a small W8
+decoder with 8 kv heads (so TP-8 divides it) runs 16 prompt and 32 greedy
+decode steps at TP-N against the CPU oracle holding the same full model; the
+line's `parity` key carries the logits errors and the token comparison, and
+the run exits non-zero when it fails.
+
+At N = 1 the line also carries the kernel-level BASELINE configs, each timed
+with CUDA events on inputs larger than L2: config 2 (the W8A16 linear sweep,
+24 (N, K, M) points), config 3 (paged GQA decode attention, batch 64) and the
+config-4 prefill of the 2048-token prompt.
 
 N > 1 (torchrun, one process per GPU): the same 8B model sharded tensor-
-parallel over the N GPUs (heads, intermediate and vocab split; NCCL all-
-reduce after o_proj and down_proj over NVLink); value = tokens/s of the
-batch-1 sequence (and of batch 64), max-over-ranks time ("scaling": "strong").
+parallel over the N GPUs (heads, intermediate and vocab split; the
+row-parallel partial sums all-reduced over NVLink peer memory after o_proj
+and down_proj); value = tokens/s of the batch-1 sequence, max-over-ranks time
+("scaling": "strong").
 
 `--impl reference`: the reference path's CPU restatement (oracle/, the
 reference's Rust/XLA stack cannot run here) timed on all host cores, rank 0.
@@ -40,6 +53,13 @@ PROMPT = 2048
 PROMPT5, BATCH5 = 4096, 32
 METRIC = "W8 decode tokens/sec"
 UNIT = "tokens/s"
+# tensor-parallel parity model: 8 kv heads (TP-8 divides heads, intermediate
+# and vocab); weights and prompt seeds whose 33 oracle tokens all beat their
+# runner-up by at least the 2e-2 logits tolerance (chosen by running the oracle)
+PARITY_CFG = dict(layers=2, hidden=1024, q_heads=16, kv_heads=8, head_dim=64, intermediate=2048,
+                  vocab=8192, rms_eps=1e-6, rope_theta=1e6)
+PARITY_SEED, PARITY_PROMPT_SEED, PARITY_PROMPT, PARITY_STEPS = 6, 106, 16, 32
+PARITY_MAX_ABS, PARITY_MEAN_ABS = 2e-2, 2e-3
 
 
 def step_bytes(cfg, batch, ctx):
@@ -51,6 +71,23 @@ def step_bytes(cfg, batch, ctx):
     weights = cfg["layers"] * per_layer + V * H
     kv = cfg["layers"] * batch * (ctx + 1) * hkv * D * 2 * 2
     return weights, kv
+
+
+def workload_config(world):
+    """The `config` of the JSON line: the same dict for both arms."""
+    return {"workload": "config4: 8B-shaped W8 decoder, batch 1 decode after a 2048-token prompt",
+            "model": "qwen3-style-8B-shape", "layers": 36, "hidden": 4096, "vocab": 151936,
+            "global_batch": 1, "seq_len": PROMPT,
+            "parallelism": f"tp{world} (one-shot NVLink peer all-reduce after o_proj and down_proj)"
+                           if world > 1 else "single GPU",
+            "l2": "inputs > L2 (7.6 GB of weights per step)"}
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 class ClockSampler:
@@ -112,31 +149,36 @@ def launches_per_step(cfg, tp=1):
 
 
 def measured_peaks():
+    """(HBM GB/s, bf16 TF/s burst, bf16 TF/s sustained, source)."""
     try:
         with open(ROOT / "MEASURED_PEAKS.json") as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return (float(p["hbm_gbs"]), float(p["bf16_tflops"]),
+                float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured")
     except Exception:
-        return 6650.0, "fallback"
+        return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 # ------------------------------------------------------------------ CPU legs
 
-def cpu_decode_sample(threads_note=True):
-    """Time the CPU oracle on a bounded sample of the config-4 decoder.
+def cpu_decode_sample():
+    """Time the CPU oracle on a bounded sample of the config-4 decode step.
 
-    Sample: the decoder with 2 of the 36 layers (full 151936-token tied head),
-    4 decode steps after 4 prompt tokens; the per-layer time is
-    (step - head) / 2 and a full token costs 36 layers + head.
-    """
+    Sample: the decoder with 2 of the 36 layers and the full 151936-token
+    tied head, sequence context set to the GPU arm's 2048 tokens, 3 timed
+    decode steps; per layer (step - head) / 2, a token = 36 layers + head.
+    All host cores (OpenMP threads set explicitly, whatever OMP_NUM_THREADS
+    the launcher exported)."""
     import numpy as np
     import oracle
+    cores = host_cores()
+    oracle.set_num_threads(cores)
     cfg = dict(CONFIG4, layers=2)
-    dec = oracle.Decoder(**cfg, max_batch=1, max_context=32)
+    dec = oracle.Decoder(**cfg, max_batch=1, max_context=PROMPT + 16)
     dec.init_synthetic(0)
+    dec.set_context(0, PROMPT)
     tok = np.array([1], np.int32)
-    for _ in range(4):
-        _, tok = dec.step(tok)
+    _, tok = dec.step(tok)
     t0 = time.perf_counter()
     n = 3
     for _ in range(n):
@@ -152,8 +194,10 @@ def cpu_decode_sample(threads_note=True):
     t_layer = max(t_step - t_head, 1e-9) / 2
     t_token = CONFIG4["layers"] * t_layer + t_head
     return {"value": 1.0 / t_token, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"oracle C restatement, 2 of 36 layers + full head, {n} timed decode steps "
-                      f"(step {t_step:.3f}s, head {t_head:.3f}s), extrapolated to 36 layers"}
+            "sample": f"oracle C restatement on {oracle.num_threads()} host threads: 2 of 36 "
+                      f"layers + the full tied head at a {PROMPT}-token context, {n} timed "
+                      f"decode steps (step {t_step:.3f}s, head {t_head:.3f}s), extrapolated "
+                      f"linearly to 36 layers"}
 
 
 def cpu_prefill_sample():
@@ -163,6 +207,7 @@ def cpu_prefill_sample():
     nearly all of the work, scale with the prompt length)."""
     import numpy as np
     import oracle
+    oracle.set_num_threads(host_cores())
     cfg = dict(CONFIG4, layers=1)
     dec = oracle.Decoder(**cfg, max_batch=1, max_context=80)
     dec.init_synthetic(0)
@@ -187,6 +232,103 @@ def cpu_prefill_sample():
                       f"extrapolated to 36 layers"}
 
 
+# --------------------------------------------------------------- parity
+
+def tp_parity(rank, world, local_rank, comm):
+    """Tensor-parallel parity at this N against the CPU oracle (every rank).
+
+    PARITY_CFG's W8 decoder (tied W8 head, per-channel scales) is built by the
+    oracle from PARITY_SEED on every rank (deterministic, so every rank holds
+    the same full model) and sliced to this rank's shard with
+    shard_parameter.  16 prompt tokens and 32 greedy decode steps, teacher
+    forced; each rank compares its vocab slice of the logits, the slices'
+    errors are combined over the ranks (max, and the sum for the mean), and
+    the greedy tokens (the cross-rank argmax) are compared with the oracle's.
+    Pattern of the reference's stateful decode test
+    (crates/rxla-core/tests/masked_decode.rs:54-142)."""
+    import numpy as np
+    import torch
+    import oracle
+    from rxla_b200 import _lib
+    from rxla_b200.decoder import Decoder, shard_parameter
+    cfg = PARITY_CFG
+    oracle.set_num_threads(max(1, host_cores() // world))
+    ref = oracle.Decoder(**cfg, embedding_bf16=False, group_size=0, max_batch=1, max_context=64)
+    ref.init_synthetic(PARITY_SEED)
+    gpu = Decoder(**cfg, embedding_dtype="u8", max_batch=1, max_context=64, device=local_rank,
+                  comm=comm.handle if comm else None, tp_rank=rank, tp_size=world)
+    H, D, I, V = cfg["hidden"], cfg["head_dim"], cfg["intermediate"], cfg["vocab"]
+    rows = {"q_proj": cfg["q_heads"] * D, "k_proj": cfg["kv_heads"] * D,
+            "v_proj": cfg["kv_heads"] * D, "o_proj": H, "gate_proj": I, "up_proj": I,
+            "down_proj": H}
+    names = ["embed_tokens.weight", "embed_tokens.scale", "norm.weight"]
+    for l in range(cfg["layers"]):
+        p = f"layers.{l}."
+        names += [p + "input_layernorm.weight", p + "post_attention_layernorm.weight",
+                  p + "self_attn.q_norm.weight", p + "self_attn.k_norm.weight"]
+        names += [f"{p}self_attn.{pr}.{k}" for pr in ("q_proj", "k_proj", "v_proj", "o_proj")
+                  for k in ("weight", "scale")]
+        names += [f"{p}mlp.{pr}.{k}" for pr in ("gate_proj", "up_proj", "down_proj")
+                  for k in ("weight", "scale")]
+    kw = dict(q_heads=cfg["q_heads"], kv_heads=cfg["kv_heads"], head_dim=D, intermediate=I,
+              hidden=H, vocab=V)
+    for n in names:
+        a = np.array(ref.parameter(n))
+        for pr, r in rows.items():
+            if f".{pr}." in n:
+                a = a.reshape(r, -1)
+        gpu.set_parameter(n, shard_parameter(n, a, rank, world, **kw))
+    vl = V // world
+    dev = torch.device("cuda", local_rank)
+    lg = torch.empty(1, vl, dtype=torch.float32, device=dev)
+    tin = torch.empty(1, dtype=torch.int32, device=dev)
+    tout = torch.empty(1, dtype=torch.int32, device=dev)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    prompt = oracle.randint(PARITY_PROMPT, PARITY_PROMPT_SEED, 0, V)
+    errs_max, errs_sum, tok_ref, tok_gpu, gaps = [], [], [], [], []
+    cur = prompt[:1].copy()
+    for t in range(PARITY_PROMPT + PARITY_STEPS):
+        l_ref, n_ref = ref.step(cur)
+        tin.copy_(torch.from_numpy(cur))
+        _lib.call("rxla_b200_decoder_step", gpu.handle, ctypes.c_void_p(tin.data_ptr()), 1,
+                  ctypes.c_void_p(tout.data_ptr()), ctypes.c_void_p(lg.data_ptr()), s)
+        torch.cuda.synchronize()
+        if t + 1 >= PARITY_PROMPT:  # last prompt row + the decode steps
+            d = np.abs(lg.cpu().numpy()[0] - l_ref[0, rank * vl:(rank + 1) * vl])
+            errs_max.append(float(d.max()))
+            errs_sum.append(float(d.sum()))
+            top2 = np.sort(l_ref[0])[-2:]
+            gaps.append(float(top2[1] - top2[0]))
+            tok_ref.append(int(n_ref[0]))
+            tok_gpu.append(int(tout.cpu().item()))
+            cur = n_ref.astype(np.int32)
+        else:
+            cur = prompt[t + 1:t + 2].copy()
+    status = _lib.load().rxla_b200_device_status(0)
+    gpu.close()
+    ref.close()
+    mx, sm = max(errs_max), sum(errs_sum)
+    if world > 1:
+        t = torch.tensor([mx, sm, float(status != 0), float(tok_gpu != tok_ref)], device=dev,
+                         dtype=torch.float64)
+        u = t.clone()
+        torch.distributed.all_reduce(t[:1], op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(u[1:], op=torch.distributed.ReduceOp.SUM)
+        mx, sm = float(t[0]), float(u[1])
+        bad_status, bad_tokens = float(u[2]) > 0, float(u[3]) > 0
+    else:
+        bad_status, bad_tokens = status != 0, tok_gpu != tok_ref
+    mean = sm / (len(errs_sum) * V)
+    ok = (mx <= PARITY_MAX_ABS and mean <= PARITY_MEAN_ABS and not bad_tokens
+          and not bad_status and min(gaps) >= PARITY_MAX_ABS)
+    return {"model": "2 layers, hidden 1024, 16 q / 8 kv heads, head_dim 64, intermediate 2048, "
+                     "vocab 8192, W8 tied head", "tp": world,
+            "window": f"last of {PARITY_PROMPT} prompt steps + {PARITY_STEPS} greedy steps",
+            "max_abs": mx, "mean_abs": mean, "tokens_equal": not bad_tokens,
+            "oracle_min_top2_gap": min(gaps), "device_status_ok": not bad_status,
+            "bar": {"max_abs": PARITY_MAX_ABS, "mean_abs": PARITY_MEAN_ABS}, "ok": bool(ok)}
+
+
 # --------------------------------------------------------------- our path
 
 def run_ours(args, rank, world, local_rank):
@@ -203,8 +345,8 @@ def run_ours(args, rank, world, local_rank):
     cfg = dict(CONFIG4)
     max_ctx = PROMPT + args.warmup + args.steps + 32
     b64 = 1 if args.no_batch64 else 64
-    # N > 1: one 8B model sharded tensor-parallel over the N GPUs (NCCL over
-    # NVLink), the same synthetic model at every N
+    # N > 1: one 8B model sharded tensor-parallel over the N GPUs, the same
+    # synthetic model at every N
     comm = None
     if world > 1:
         def share(data):
@@ -212,31 +354,37 @@ def run_ours(args, rank, world, local_rank):
             torch.distributed.broadcast_object_list(obj, src=0)
             return obj[0]
         comm = Comm(rank, world, local_rank, share)
+    parity = tp_parity(rank, world, local_rank, comm)
     dec = Decoder(**cfg, embedding_dtype="u8", max_batch=b64, max_context=max_ctx,
                   device=local_rank, comm=comm.handle if comm else None, tp_rank=rank,
                   tp_size=world)
     dec.init_synthetic(1234)
-
-    tin = ctypes.c_void_p(dec.tokens_in_ptr)
     tout = ctypes.c_void_p(dec.tokens_out_ptr)
-
-    def prompt_fill(batch):
-        dec.reset(sptr)
-        prompt = torch.randint(0, cfg["vocab"], (PROMPT, batch), dtype=torch.int32, device=dev,
-                               generator=torch.Generator(device=dev).manual_seed(1))
-        for t in range(PROMPT):
-            _lib.call("rxla_b200_decoder_step", dec.handle, ctypes.c_void_p(prompt[t].data_ptr()),
-                      batch, tout, None, sptr)
-        torch.cuda.synchronize()
-
-    def greedy(batch, n):
-        for _ in range(n):
-            _lib.call("rxla_b200_decoder_step", dec.handle, tout, batch, tout, None, sptr)
+    prompt = torch.randint(0, cfg["vocab"], (PROMPT,), dtype=torch.int32, device=dev,
+                           generator=torch.Generator(device=dev).manual_seed(1))
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world > 1:
+            t = torch.tensor([v], device=dev, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            v = float(t.item())
+        return v
+
+    # ---- config-4 prefill of the 2048-token prompt (also fills the context
+    # the decode steps run at)
+    prefill = run_prefill_timed(args, dec, prompt, dev, stream, world) if world == 1 else None
+    dec.reset(sptr)
+    dec.prefill(0, prompt, stream=sptr)
+    barrier()
+
+    def greedy(batch, n):
+        for _ in range(n):
+            _lib.call("rxla_b200_decoder_step", dec.handle, tout, batch, tout, None, sptr)
 
     def timed(batch, n):
         greedy(batch, args.warmup)
@@ -246,16 +394,10 @@ def run_ours(args, rank, world, local_rank):
         greedy(batch, n)
         e1.record(stream)
         barrier()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return max_over_ranks(e0.elapsed_time(e1))
 
     sampler = ClockSampler(local_rank)
     # ---- batch 1 (headline)
-    prompt_fill(1)
     sampler.start()
     ms1 = timed(1, args.steps)
     ctx_b1 = PROMPT + args.warmup + args.steps // 2
@@ -266,11 +408,7 @@ def run_ours(args, rank, world, local_rank):
     t0 = time.perf_counter()
     for _ in range(args.steps):
         host_tok = dec.step_host(host_tok)
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
     # ---- batch 64: every sequence at the 2048-token context (pages sized and
     # set by rxla_b200_decoder_set_context_lengths; the step's work does not
     # depend on the cached values)
@@ -282,15 +420,20 @@ def run_ours(args, rank, world, local_rank):
         ms64 = timed(64, n64)
         w, kv = step_bytes(cfg, 64, PROMPT + args.warmup + n64 // 2)
         res64 = {"value": 64 * n64 / (ms64 / 1e3), "ms_per_step": ms64 / n64, "steps": n64,
-                 "step_gbs": (w + kv) / (ms64 / n64 * 1e-3) / 1e9}
+                 "step_gbs": (w + kv) / (ms64 / n64 * 1e-3) / 1e9,
+                 "step_frac_of_hbm": (w + kv) / world / (ms64 / n64 * 1e-3) / 1e9 / measured_peaks()[0]}
     clocks = sampler.stop()
 
-    # ---- roofline of the dominant kernel: the W8 linear, all launches of one
-    # batch-1 step (qkv, o, gate/up, down per layer + tied head) replayed in a graph
-    roof = gemv_roofline(dec, cfg, dev, stream, lib, world)
-    status = lib.rxla_b200_device_status(local_rank)
+    # ---- roofline of the dominant kernel: the W8 linears of one batch-1 step
+    # of this rank's shard, the step's own instances, replayed in a graph
+    roof = gemv_roofline(dec, cfg, dev, stream, lib, world, rank)
+    status = lib.rxla_b200_device_status(0)
     dec.close()  # releases the captured graphs (they hold NCCL calls) before the comm
     res5 = None if args.no_config5 else run_config5(args, rank, world, local_rank, comm, barrier)
+    kernels = None
+    if world == 1 and not args.no_kernels:
+        kernels = {"config2_linear_sweep": config2_sweep(dev),
+                   "config3_attention": config3_attention(dev)}
     if comm:
         comm.close()
 
@@ -301,17 +444,14 @@ def run_ours(args, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": ms1 / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "u8 weights, bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded random W8 weights, random 2048-token prompt)",
-        "config": {"workload": "config4: 8B-shaped W8 decoder, batch 1 decode after a 2048-token prompt",
-                   "model": "qwen3-style-8B-shape", "layers": 36, "hidden": 4096, "vocab": 151936,
-                   "global_batch": 1, "seq_len": PROMPT,
-                   "parallelism": (f"tp{world} (" + ("NCCL" if os.environ.get("RXLA_B200_P2P") == "0"
-                                                      else "one-shot NVLink peer")
-                                   + " all-reduce after o_proj and down_proj)") if world > 1 else "single GPU",
-                   "l2": "inputs > L2 (7.6 GB of weights per step)"},
+        "config": workload_config(world),
         "step_gbs": (weights + kv1) / (ms1 / args.steps * 1e-3) / 1e9,
         "step_frac_of_hbm": (weights + kv1) / (ms1 / args.steps * 1e-3) / 1e9 / (world * measured_peaks()[0]),
+        "parity": parity,
         "batch64": res64,
         "config5": res5,
+        "prefill": prefill,
+        "kernels": kernels,
         "e2e": {"value": args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},
         "roofline": roof,
@@ -320,6 +460,47 @@ def run_ours(args, rank, world, local_rank):
         "device_status": status,
     }
     return out
+
+
+def run_prefill_timed(args, dec, prompt, dev, stream, world):
+    """Config-4 prefill of the PROMPT-token prompt through
+    rxla_b200_decoder_prefill (chunks of rows on the tcgen05 GEMM, causal
+    paged attention), from position 0 each time.  Tensor-bound: the roofline
+    is the measured bf16 GEMM peak."""
+    import torch
+    s = ctypes.c_void_p(stream.cuda_stream)
+    reps = 3
+    for _ in range(2):
+        dec.reset(s)
+        dec.prefill(0, prompt, stream=s)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(stream)
+    for _ in range(reps):
+        dec.reset(s)
+        dec.prefill(0, prompt, stream=s)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / reps
+    # end to end: the prompt from pinned host memory, the token back to the host
+    host_prompt = prompt.cpu().pin_memory()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        dec.reset(s)
+        prompt.copy_(host_prompt, non_blocking=True)
+        tok = dec.prefill(0, prompt, stream=s)
+        tok.cpu()
+    e2e_s = (time.perf_counter() - t0) / reps
+    flops = prefill_flops(CONFIG4, PROMPT)
+    _, peak, peak_sus, how = measured_peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    return {"workload": f"config4: {PROMPT}-token prompt, one sequence, prefill from position 0",
+            "value": PROMPT / (ms * 1e-3), "unit": "tokens/s", "ms_per_prefill": ms, "reps": reps,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": f"{how} (burst)",
+                         "frac_of_sustained": achieved / peak_sus, "flops_per_prefill": flops},
+            "e2e": {"value": PROMPT / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 4,
+                    "d2h_bytes_per_step": 4}}
 
 
 def run_config5(args, rank, world, local_rank, comm, barrier):
@@ -355,7 +536,7 @@ def run_config5(args, rank, world, local_rank, comm, barrier):
         t = torch.tensor([ms], device=torch.device("cuda", local_rank))
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-    status = _lib.load().rxla_b200_device_status(local_rank)
+    status = _lib.load().rxla_b200_device_status(0)
     dec.close()
     w, kv = step_bytes(CONFIG5, BATCH5, PROMPT5 + args.warmup + n // 2)
     sec = ms / n / 1e3
@@ -368,73 +549,104 @@ def run_config5(args, rank, world, local_rank, comm, barrier):
             "device_status": status}
 
 
-def gemv_roofline(dec, cfg, dev, stream, lib, tp=1):
-    """Time every W8 linear of one batch-1 step of this rank's shard, replayed as
-    one CUDA graph.
+def gemv_roofline(dec, cfg, dev, stream, lib, tp=1, rank=0):
+    """Time the W8 linears of one batch-1 decode step of this rank's shard as
+    the step runs them, replayed as one CUDA graph: qkv and gate/up with the
+    input RMSNorm fused (real norm weights, the evolving f32 residual h),
+    o_proj and down_proj adding into h (tp 1) or storing f32 partials (tp > 1),
+    the tied head with its norm fused (f32 logits; the step's head also picks
+    the greedy token in its epilogue).
 
-    Algorithmic bytes per launch = N·K weights + 4·N scales + 2·K (x) + output;
-    achieved = Σ bytes / Σ time of the launches (bytes-weighted mean)."""
+    Algorithmic bytes per launch = N·K weights + 4·N scales + x (2·K bf16 or
+    4·K f32 for the norm's h) + the output; achieved = Σ bytes / Σ time."""
     import torch
+    from rxla_b200 import _lib
     H, D = cfg["hidden"], cfg["head_dim"]
     I, V, hq = cfg["intermediate"] // tp, cfg["vocab"] // tp, cfg["q_heads"] // tp
     qkv_rows = (hq + 2 * cfg["kv_heads"] // tp) * D
-    x = torch.zeros(1, max(H, I, hq * D), dtype=torch.bfloat16, device=dev)
-    ybf = torch.empty(1, max(qkv_rows, I), dtype=torch.bfloat16, device=dev)
-    yf = torch.zeros(1, max(H, V), dtype=torch.float32, device=dev)
-    s = ctypes.c_void_p(stream.cuda_stream)
-    launches = []
+    g = torch.Generator(device=dev).manual_seed(5)
+    h = torch.randn(1, H, device=dev, generator=g)
+    att = torch.randn(1, hq * D, device=dev, generator=g).bfloat16()
+    act = torch.randn(1, I, device=dev, generator=g).bfloat16()
+    qkv = torch.empty(1, qkv_rows, dtype=torch.bfloat16, device=dev)
+    part = torch.zeros(1, H, dtype=torch.float32, device=dev)
+    logits = torch.empty(1, V, dtype=torch.float32, device=dev)
+    eps = ctypes.c_float(cfg["rms_eps"])
+    calls, total_bytes = [], 0
     for l in range(cfg["layers"]):
         p = f"layers.{l}."
-        launches.append((p + "self_attn.qkv", qkv_rows, H, ybf, 1, 0))
-        launches.append((p + "self_attn.o_proj", H, hq * D, yf, 0, 1))
-        launches.append((p + "mlp.gate_up", I, H, ybf, 1, 2))
-        launches.append((p + "mlp.down_proj", H, I, yf, 0, 1))
-    launches.append(("embed_tokens", V, H, yf, 0, 0))
-    total_bytes = 0
-    calls = []
-    rank = int(os.environ.get("RANK", "0"))
-    for name, n, k, y, ybf16, epi in launches:
-        w, _, _ = dec.parameter(name + ".weight")
-        sc, _, _ = dec.parameter(name + ".scale")
-        if name == "embed_tokens":  # the rank's vocab slice of the tied head
-            w, sc = w + rank * V * k, sc + rank * V * 4
-        rows = 2 * n if epi == 2 else n
-        total_bytes += rows * k + 4 * rows + 2 * k + (2 if ybf16 else 4) * n * (2 if epi == 1 else 1)
-        calls.append((x.data_ptr(), w, sc, k, n, k, y.data_ptr(), 1 if ybf16 else 0, epi))
+        ln1, _, _ = dec.parameter(p + "input_layernorm.weight")
+        ln2, _, _ = dec.parameter(p + "post_attention_layernorm.weight")
+        wqkv, _, _ = dec.parameter(p + "self_attn.qkv.weight")
+        sqkv, _, _ = dec.parameter(p + "self_attn.qkv.scale")
+        wo, _, _ = dec.parameter(p + "self_attn.o_proj.weight")
+        so, _, _ = dec.parameter(p + "self_attn.o_proj.scale")
+        wgu, _, _ = dec.parameter(p + "mlp.gate_up.weight")
+        sgu, _, _ = dec.parameter(p + "mlp.gate_up.scale")
+        wd, _, _ = dec.parameter(p + "mlp.down_proj.weight")
+        sd, _, _ = dec.parameter(p + "mlp.down_proj.scale")
+        res_ptr, res_epi = (h.data_ptr(), _lib.EPI_RESIDUAL_ADD) if tp == 1 else \
+            (part.data_ptr(), _lib.EPI_STORE)
+        calls.append(("norm", h.data_ptr(), ln1, wqkv, sqkv, H, qkv_rows, H, qkv.data_ptr(),
+                      _lib.BF16, _lib.EPI_STORE))
+        total_bytes += qkv_rows * H + 4 * qkv_rows + 4 * H + 2 * qkv_rows
+        calls.append(("lin", att.data_ptr(), 0, wo, so, hq * D, H, hq * D, res_ptr, _lib.F32,
+                      res_epi))
+        total_bytes += H * hq * D + 4 * H + 2 * hq * D + (8 if tp == 1 else 4) * H
+        calls.append(("norm", h.data_ptr(), ln2, wgu, sgu, H, I, H, act.data_ptr(), _lib.BF16,
+                      _lib.EPI_SWIGLU))
+        total_bytes += 2 * I * H + 8 * I + 4 * H + 2 * I
+        calls.append(("lin", act.data_ptr(), 0, wd, sd, I, H, I, res_ptr, _lib.F32, res_epi))
+        total_bytes += H * I + 4 * H + 2 * I + (8 if tp == 1 else 4) * H
+    fn, _, _ = dec.parameter("norm.weight")
+    we, _, _ = dec.parameter("embed_tokens.weight")
+    se, _, _ = dec.parameter("embed_tokens.scale")
+    calls.append(("norm", h.data_ptr(), fn, we + rank * V * H, se + rank * V * 4, H, V, H,
+                  logits.data_ptr(), _lib.F32, _lib.EPI_STORE))
+    total_bytes += V * H + 4 * V + 4 * H + 4 * V
 
     def run():
-        for xp, w, sc, g, n, k, yp, ybf16, epi in calls:
-            st = lib.rxla_b200_w8a16_linear(xp, 1, w, sc, g, 1, n, k, yp, ybf16, epi,
-                                            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-            assert st == 0
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for kind, x, nw, w, sc, group, n, k, y, ydt, epi in calls:
+            if kind == "norm":
+                st = lib.rxla_b200_w8a16_norm_linear(x, nw, eps, w, sc, group, 1, n, k, y, ydt,
+                                                     epi, s)
+            else:
+                st = lib.rxla_b200_w8a16_linear(x, _lib.BF16, w, sc, group, 1, n, k, y, ydt, epi, s)
+            assert st == 0, _lib.load().rxla_b200_last_error_message()
     run()
     torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
         run()
     for _ in range(3):
-        g.replay()
+        graph.replay()
     torch.cuda.synchronize()
     reps = 10
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(reps):
-        g.replay()
+        graph.replay()
     e1.record()
     torch.cuda.synchronize()
     sec = e0.elapsed_time(e1) / 1e3 / reps
-    peak, kind = measured_peaks()
+    peak, _, _, kind = measured_peaks()
     achieved = total_bytes / sec / 1e9
-    # DRAM bytes per launch: the algorithmic bytes scaled by the LM-head ncu
-    # capture's measured ratio (dram read + write 626.74 MB / algorithmic
-    # 623.25 MB, profiles/w8_gemv_lm_head_config4.md)
-    traffic = total_bytes / len(calls) * (626.74 / 623.25)
-    return {"bound": "hbm", "kernel": "w8_skinny_kernel (all W8 linears of one batch-1 step)",
+    del graph
+    return {"bound": "hbm", "kernel": "w8_skinny_kernel (the W8 linears of one batch-1 step: "
+                                      "fused-norm qkv / gate-up+SwiGLU / head, residual o / down)",
             "achieved": achieved, "peak": peak, "peak_kind": kind, "unit": "GB/s",
-            "frac": achieved / peak, "traffic": traffic,
-            "traffic_note": "per launch, scaled from the LM-head ncu capture",
-            "launches": len(calls), "avg_launch_us": sec / len(calls) * 1e6,
-            "bytes_per_step": total_bytes}
+            "frac": achieved / peak, "traffic": total_bytes / len(calls) * TRAFFIC_RATIO,
+            "traffic_note": TRAFFIC_NOTE, "launches": len(calls),
+            "avg_launch_us": sec / len(calls) * 1e6, "bytes_per_step": total_bytes,
+            "timing": "CUDA events around 10 replays of one graph of the step's linears"}
+
+
+# DRAM bytes (read + write) per algorithmic byte of the step's W8 linears, from
+# the ncu capture summarised in profiles/decode_step_launches_config4.md
+TRAFFIC_RATIO = 626.74 / 623.25
+TRAFFIC_NOTE = ("per launch: algorithmic bytes x the measured dram/algorithmic ratio of the "
+                "W8 linear ncu capture")
 
 
 def prefill_flops(cfg, tokens):
@@ -448,73 +660,101 @@ def prefill_flops(cfg, tokens):
     return lin + att + 2.0 * cfg["vocab"] * h
 
 
-def run_prefill(args):
-    """Config 4 prefill: a PROMPT-token prompt of one sequence through
-    rxla_b200_decoder_prefill (chunks of rows on the tcgen05 GEMM, causal
-    paged attention), from position 0 each step.  Tensor-bound: the roofline
-    is the measured bf16 GEMM peak.  Prints one JSON line."""
+def config2_sweep(dev):
+    """BASELINE config 2 through rxla_b200_w8a16_linear: x bf16 N(0,1) [M,K],
+    int8 weights U{-127..127} stored +128 [N,K], f32 per-row scales
+    U[1e-3,1e-2], bf16 out.  Each (N,K) cycles through enough weight copies to
+    exceed 2x L2 (126 MB) between launches; 3 warm-up launches, then 20 timed
+    with CUDA events.  Algorithmic bytes N·K + 4·N + 2·M·K + 2·M·N, FLOPs
+    2·M·N·K; frac = max(t_mem, t_flop) at the measured peaks / measured time."""
+    import torch
+    hbm, tf, _, how = measured_peaks()
+    g = torch.Generator(device=dev).manual_seed(2)
+    points = []
+    for n, k in ((4096, 4096), (12288, 4096), (4096, 12288), (6144, 4096)):
+        copies = max(2, -(-2 * 126 * 2**20 // (n * k)))
+        ws = [torch.randint(1, 256, (n, k), dtype=torch.uint8, device=dev, generator=g)
+              for _ in range(copies)]
+        sc = torch.rand(n, 1, device=dev, generator=g) * 9e-3 + 1e-3
+        for m in (1, 8, 32, 128, 512, 2048):
+            x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+            y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+            s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            from rxla_b200 import _lib
+            lib = _lib.load()
+
+            def launch(i):
+                st = lib.rxla_b200_w8a16_linear(x.data_ptr(), _lib.BF16, ws[i % copies].data_ptr(),
+                                                sc.data_ptr(), k, m, n, k, y.data_ptr(), _lib.BF16,
+                                                _lib.EPI_STORE, s)
+                assert st == 0
+            for i in range(3):
+                launch(i)
+            reps = 20
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(reps):
+                launch(i)
+            e1.record()
+            torch.cuda.synchronize()
+            sec = e0.elapsed_time(e1) / 1e3 / reps
+            byt = n * k + 4 * n + 2 * m * k + 2 * m * n
+            fl = 2.0 * m * n * k
+            t_mem, t_flop = byt / (hbm * 1e9), fl / (tf * 1e12)
+            points.append({"m": m, "n": n, "k": k, "us": sec * 1e6, "gbs": byt / sec / 1e9,
+                           "tflops": fl / sec / 1e12,
+                           "bound": "hbm" if t_mem >= t_flop else "tensor",
+                           "frac": max(t_mem, t_flop) / sec})
+            del x, y
+        del ws
+        torch.cuda.empty_cache()
+    return {"points": points, "peaks": {"hbm_gbs": hbm, "bf16_tflops": tf, "source": how},
+            "l2": "weight copies cycled, > 2x L2 between launches of one shape"}
+
+
+def config3_attention(dev):
+    """BASELINE config 3 through rxla_b200_paged_decode_attention: batch 64,
+    32 q / 8 kv heads, head_dim 128, page 16, contexts U[512, 8192) (seeded),
+    K/V/Q N(0,1) bf16, RoPE theta 1e6 on the new token, which is appended
+    before attending.  Bytes = Σ_b (L_b + 1)·Hkv·D·2·2 (K and V) + q / out +
+    the new K/V rows + the page table; ~1.1 GB per call, larger than L2."""
     import numpy as np
     import torch
-    from rxla_b200.decoder import Decoder
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    dec = Decoder(**CONFIG4, embedding_dtype="u8", max_batch=1, max_context=PROMPT + 16)
-    dec.init_synthetic(1)
-    stream = torch.cuda.current_stream()
-    s = ctypes.c_void_p(stream.cuda_stream)
-    prompt = torch.from_numpy(np.random.default_rng(5).integers(0, CONFIG4["vocab"], PROMPT)
-                              .astype(np.int32)).to(dev)
-    host_prompt = prompt.cpu().pin_memory()
-    for _ in range(args.warmup):
-        dec.reset(s)
-        dec.prefill(0, prompt, stream=s)
+    from rxla_b200 import nn
+    batch, hq, hkv, d, max_ctx = 64, 32, 8, 128, 8192
+    hbm, _, _, how = measured_peaks()
+    g = torch.Generator(device=dev).manual_seed(3)
+    cache = nn.PagedKvCache(batch=batch, kv_heads=hkv, head_dim=d, max_context=max_ctx + 16)
+    cache.k.normal_(generator=g)
+    cache.v.normal_(generator=g)
+    lens = torch.randint(512, 8192, (batch,), dtype=torch.int32, device=dev, generator=g)
+    cache.ctx_lens.copy_(lens)
+    qkv = torch.randn(batch, (hq + 2 * hkv) * d, device=dev, generator=g).bfloat16()
+    ws = torch.zeros(nn.paged_decode_workspace_size(batch, hq, hkv, d, cache.max_context),
+                     dtype=torch.uint8, device=dev)
+    inv = torch.from_numpy(nn.rope_inv_freq(1e6, d)).to(dev)
+
+    def launch():
+        nn.paged_decode_attention(qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d],
+                                  qkv[:, (hq + hkv) * d:], cache, q_heads=hq, inv_freq=inv,
+                                  rotary_dim=d, workspace=ws)
+    for _ in range(3):
+        launch()
     torch.cuda.synchronize()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    sampler = ClockSampler(0)
-    sampler.start()
-    t0 = time.perf_counter()
-    ev[0].record(stream)
-    for _ in range(args.steps):
-        dec.reset(s)
-        dec.prefill(0, prompt, stream=s)
-    ev[1].record(stream)
+    reps = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        launch()
+    e1.record()
     torch.cuda.synchronize()
-    wall = (time.perf_counter() - t0) / args.steps
-    ms = ev[0].elapsed_time(ev[1]) / args.steps
-    # end to end: the prompt from pinned host memory, the token back to the host
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        dec.reset(s)
-        prompt.copy_(host_prompt, non_blocking=True)
-        tok = dec.prefill(0, prompt, stream=s)
-        tok.cpu()
-    e2e_s = (time.perf_counter() - t0) / args.steps
-    clocks = sampler.stop()
-    flops = prefill_flops(CONFIG4, PROMPT)
-    try:
-        with open(ROOT / "MEASURED_PEAKS.json") as f:
-            peak, how = float(json.load(f)["bf16_tflops"]), "measured"
-    except Exception:
-        peak, how = 1590.0, "fallback"
-    achieved = flops / (ms * 1e-3) / 1e12
-    line = {"metric": "W8 prefill tokens/sec", "value": PROMPT / (ms * 1e-3), "unit": "tokens/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "wall_ms_per_step": wall * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "u8 weights, bf16 operands, f32 accumulate",
-            "data": "synthetic",
-            "config": {"workload": f"config4: 8B-shaped W8 decoder, {PROMPT}-token prompt, "
-                                   "one sequence, prefill from position 0",
-                       "l2": "weights 6.95 GB per pass, larger than L2"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": how,
-                         "flops_per_step": flops, "traffic": None},
-            "e2e": {"value": PROMPT / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 4,
-                    "d2h_bytes_per_step": 4},
-            "clocks": clocks}
-    dec.close()
-    if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_prefill_sample()
-    print(json.dumps(line), flush=True)
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    L = lens.cpu().numpy().astype(np.int64)
+    byt = int(((L + 1) * hkv * d * 2 * 2).sum() + 2 * batch * hq * d * 2 + batch * hkv * d * 2 * 2
+              + cache.page_table.numel() * 4)
+    return {"workload": "config3: batch 64, 32 q / 8 kv heads, head_dim 128, ctx U[512,8192)",
+            "us": sec * 1e6, "bytes_per_call": byt, "gbs": byt / sec / 1e9, "bound": "hbm",
+            "frac": byt / sec / 1e9 / hbm, "peak_gbs": hbm, "peak_source": how}
 
 
 def profile_case(what: str):
@@ -533,6 +773,7 @@ def profile_case(what: str):
                1024-row chunks) after one warm-up prompt
     attention: config-3 paged decode attention (batch 64, 32 q / 8 kv heads, d 128,
                ctx ~U[512, 8192]), 3 launches
+    attention1: the batch-1 decode attention of config 4 at a 2048-token context, 3 launches
     """
     import numpy as np
     import torch
@@ -612,6 +853,19 @@ def profile_case(what: str):
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
         dec.close()
+    elif what == "attention1":
+        # the batch-1 decode attention of config 4 at a 2048-token context, 3 launches
+        hq, hkv, d = 32, 8, 128
+        cache = nn.PagedKvCache(batch=1, kv_heads=hkv, head_dim=d, max_context=PROMPT + 16)
+        cache.k.normal_()
+        cache.v.normal_()
+        cache.ctx_lens.fill_(PROMPT)
+        qkv = torch.randn(1, (hq + 2 * hkv) * d, device=dev).bfloat16()
+        inv = torch.from_numpy(nn.rope_inv_freq(1e6, d)).to(dev)
+        for _ in range(3):
+            nn.paged_decode_attention(qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d],
+                                      qkv[:, (hq + hkv) * d:], cache, q_heads=hq, inv_freq=inv,
+                                      rotary_dim=d)
     elif what == "attention":
         batch, hq, hkv, d, max_ctx = 64, 32, 8, 128, 8192
         cache = nn.PagedKvCache(batch=batch, kv_heads=hkv, head_dim=d, max_context=max_ctx)
@@ -640,19 +894,17 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-batch64", action="store_true")
     ap.add_argument("--no-config5", action="store_true")
+    ap.add_argument("--no-kernels", action="store_true",
+                    help="skip the config-2 sweep and config-3 attention keys (N = 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--prefill", action="store_true",
-                    help="measure the config-4 prompt prefill instead of decode (one JSON line)")
-    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "gemmdec", "step", "step64", "step5", "prefill", "attention"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "gemmdec", "step", "step64", "step5",
+                                          "prefill", "attention", "attention1"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.profile:
         profile_case(args.profile)
         return
     args.warmup = max(args.warmup, 3)
-    if args.prefill:
-        run_prefill(args)
-        return
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -667,11 +919,12 @@ def main():
             res = cpu_decode_sample()
             steps.append(res["value"])
         value = statistics.median(steps)
-        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                "impl": "reference", "scaling": "weak", "vs_baseline": None,
+                "impl": "reference", "scaling": "strong", "vs_baseline": None,
                 "dtype": "u8 weights, f32 activations (CPU restatement)",
-                "data": "synthetic", "config": {"workload": "config4: 8B-shaped W8 decoder, batch 1 decode"},
+                "data": "synthetic (seeded random W8 weights, 2048-token context)",
+                "config": workload_config(world),
                 "cpu_baseline": {**res, "value": value},
                 "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
@@ -692,6 +945,9 @@ def main():
         torch.distributed.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
+    if not out["parity"]["ok"]:
+        sys.stderr.write(f"tensor-parallel parity failed: {json.dumps(out['parity'])}\n")
+        sys.exit(1)
 
 
 if __name__ == "__main__":

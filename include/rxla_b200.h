@@ -108,6 +108,15 @@ int32_t rxla_b200_device_info(int32_t device, int32_t* sm_count, int32_t* cc_maj
  * wait runs out (RXLA_B200_DEADLINE_EXCEEDED) — kernels return instead of
  * hanging.  0 when nothing went wrong; nonzero `reset` clears it. */
 int32_t rxla_b200_device_status(int32_t reset);
+/* Budget in nanoseconds of every bounded device-side wait in this library's
+ * kernels on the current device (mbarrier rings, split-K hand-offs, the peer
+ * all-reduce's flag waits); default 4 s, allowed range [1 ms, 60 s].  Kernels
+ * that start after the call (graph replays included) use the new value.  A
+ * wait that runs out records RXLA_B200_DEADLINE_EXCEEDED in the device status
+ * word and its kernel returns early; the context stays usable.  Replaces no
+ * reference interface (XLA's own kernels do not wait on peers). */
+int32_t rxla_b200_set_wait_timeout(int64_t ns);
+int32_t rxla_b200_get_wait_timeout(int64_t* ns);
 
 /* ------------------------------------------------------- W8A16 linear layer
  *
@@ -136,6 +145,22 @@ int32_t rxla_b200_w8a16_linear(const void* x, int32_t x_dtype, const uint8_t* we
                                const float* scale, int64_t group_size, int64_t m, int64_t n,
                                int64_t k, void* y, int32_t y_dtype, int32_t epilogue,
                                void* stream);
+
+/* The same linear with its input RMSNorm fused into the kernel's prologue, the
+ * decoder block's `linear(rms_norm(h))` for decode shapes (each pass of up to
+ * 8 tokens streams the weights once):
+ *
+ *   y = bf16(h * rsqrt(mean(h²) + eps) * norm_weight) · W_deqᵀ
+ *
+ * (crates/rxla-core/src/ops.rs:929-945, then the bf16 cast of the consuming
+ * QuantizedLinear, crates/rxla-nn/src/layers.rs:289-297).  h f32 [m, k] (a
+ * residual stream), norm_weight f32 [k]; weight / scale / y / epilogue as in
+ * rxla_b200_w8a16_linear.  Needs k % 64 == 0, group_size == k or a multiple
+ * of 64, 16-byte aligned h and weight; y must not overlap h. */
+int32_t rxla_b200_w8a16_norm_linear(const float* h, const float* norm_weight, float eps,
+                                    const uint8_t* weight, const float* scale,
+                                    int64_t group_size, int64_t m, int64_t n, int64_t k, void* y,
+                                    int32_t y_dtype, int32_t epilogue, void* stream);
 
 /* Dense bf16-weight linear y = bf16(x) · wᵀ (the tied bf16 LM head of a
  * decoder whose embedding stays bf16; crates/rxla-core/src/nn.rs:286-310).
@@ -220,7 +245,8 @@ int32_t rxla_b200_paged_decode_attention(const rxla_b200_paged_decode_args* args
  * whose rxla_b200_paged_decode_workspace_size exceeds it returns
  * RXLA_B200_OUT_OF_RANGE without launching.  The first call on a device looks
  * up the array's device address (make it before any stream capture); every
- * call clears the array's split counters on its stream.  All calls share the
+ * call clears the array's split counters on its stream, which must belong to
+ * the current device (else RXLA_B200_INVALID_ARGUMENT).  All calls share the
  * one array, so calls that can run at the same time on the GPU race. */
 #define RXLA_B200_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 int32_t rxla_b200_paged_decode_attention_noalloc(const rxla_b200_paged_decode_args* args,

@@ -85,6 +85,9 @@ def lib() -> ctypes.CDLL:
         "oracle_decoder_forward": (None, [_vp, _i32p, _i32, _f32p, _i32p]),
         "oracle_decoder_context": (_i32, [_vp, _i32]),
         "oracle_decoder_kv": (None, [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+        "oracle_decoder_prefill": (_i32, [_vp, _i32, _i32p, _i32, _f32p, _i32p]),
+        "oracle_decoder_set_context": (_i32, [_vp, _i32, _i32]),
+        "oracle_set_num_threads": (None, [_i32]),
         "oracle_num_threads": (_i32, []),
     }
     for name, (res, args) in sig.items():
@@ -353,6 +356,25 @@ class Decoder:
         lib().oracle_decoder_forward(self._h, prompt, prompt.shape[0], logits, nxt)
         return logits, int(nxt[0])
 
+    def prefill(self, seq: int, prompt):
+        """The full-sequence forward of `prompt` for the empty sequence `seq`
+        that also stores the prompt rows' K/V and sets its context to the
+        prompt length (decode steps then continue after the prompt; the same
+        state as stepping the prompt token by token).  Returns the last row's
+        logits [vocab] and greedy token."""
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        logits = np.empty(self.vocab, np.float32)
+        nxt = np.empty(1, np.int32)
+        if lib().oracle_decoder_prefill(self._h, seq, prompt, prompt.shape[0], logits, nxt) != 0:
+            raise ValueError("oracle prefill: sequence not empty or prompt longer than max_context")
+        return logits, int(nxt[0])
+
+    def set_context(self, seq: int, ctx: int):
+        """Set sequence `seq`'s context length directly (cached values stay as
+        they are), e.g. to time a step at a long context."""
+        if lib().oracle_decoder_set_context(self._h, seq, ctx) != 0:
+            raise ValueError("oracle set_context: out of range")
+
     def step(self, tokens):
         tokens = np.ascontiguousarray(tokens, np.int32)
         b = tokens.shape[0]
@@ -364,6 +386,12 @@ class Decoder:
 
 def num_threads() -> int:
     return int(lib().oracle_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    """OpenMP threads of the oracle from now on (overrides OMP_NUM_THREADS,
+    which torchrun sets to 1)."""
+    lib().oracle_set_num_threads(int(n))
 
 
 def library_path() -> str:

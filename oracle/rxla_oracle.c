@@ -126,17 +126,23 @@ void oracle_w8_linear(const float* x, int64_t m, int64_t k, const uint8_t* w,
 #pragma omp for schedule(static)
     for (int64_t r = 0; r < n; ++r) {
       if (mode == 2 || mode == 3) {
-        for (int64_t mm = 0; mm < m; ++mm) {
-          double acc = 0.0;
+        /* four tokens at a time: four independent sums, each in the same
+         * sequential order as a token alone (identical results, less time
+         * waiting on one dependent add chain) */
+        for (int64_t m0 = 0; m0 < m; m0 += 4) {
+          const int64_t nt = m - m0 < 4 ? m - m0 : 4;
+          double acc[4] = {0.0, 0.0, 0.0, 0.0};
           for (int64_t g = 0; g < groups; ++g) {
-            double part = 0.0;
+            double part[4] = {0.0, 0.0, 0.0, 0.0};
             for (int64_t j = 0; j < group; ++j) {
               int64_t c = g * group + j;
-              part += (double)xr[mm * k + c] * (double)((int32_t)w[r * k + c] - 128);
+              const double wq = (double)((int32_t)w[r * k + c] - 128);
+              for (int64_t u = 0; u < nt; ++u) part[u] += (double)xr[(m0 + u) * k + c] * wq;
             }
-            acc += part * (double)scale[r * groups + g];
+            for (int64_t u = 0; u < nt; ++u) acc[u] += part[u] * (double)scale[r * groups + g];
           }
-          y[mm * n + r] = mode == 3 ? oracle_bf16_round((float)acc) : (float)acc;
+          for (int64_t u = 0; u < nt; ++u)
+            y[(m0 + u) * n + r] = mode == 3 ? oracle_bf16_round((float)acc[u]) : (float)acc[u];
         }
         continue;
       }
@@ -145,7 +151,26 @@ void oracle_w8_linear(const float* x, int64_t m, int64_t k, const uint8_t* w,
         float wd = (float)((int32_t)w[r * k + c] - 128) * scale[r * groups + c / group];
         wrow[c] = (mode == 1 || mode == 4) ? oracle_bf16_round(wd) : wd;
       }
-      for (int64_t mm = 0; mm < m; ++mm) {
+      int64_t mm = 0;
+      if (mode != 4) {
+        /* four tokens at a time, each its own sequential f64 sum (identical
+         * results to one token at a time) */
+        for (; mm + 4 <= m; mm += 4) {
+          double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+          const float* x0 = xr + mm * k;
+          for (int64_t c = 0; c < k; ++c) {
+            const double wv = (double)wrow[c];
+            a0 += (double)x0[c] * wv;
+            a1 += (double)x0[k + c] * wv;
+            a2 += (double)x0[2 * k + c] * wv;
+            a3 += (double)x0[3 * k + c] * wv;
+          }
+          const double a[4] = {a0, a1, a2, a3};
+          for (int u = 0; u < 4; ++u)
+            y[(mm + u) * n + r] = mode == 1 ? oracle_bf16_round((float)a[u]) : (float)a[u];
+        }
+      }
+      for (; mm < m; ++mm) {
         float out;
         if (mode == 4) { /* mode 1 with an fp32 running sum (noise-floor probe) */
           float facc = 0.0f;
@@ -752,8 +777,8 @@ void oracle_decoder_step(oracle_decoder* dec, const int32_t* tokens, int32_t bat
  * attention of the whole [T, T] score matrix under the additive mask.  K and V
  * are rounded to bf16 as the paged cache stores them.  Writes the last row's
  * logits [V] and its greedy token; the decoder's state is not touched. */
-void oracle_decoder_forward(oracle_decoder* dec, const int32_t* tokens, int32_t T, float* logits,
-                            int32_t* next_token) {
+static void decoder_forward_impl(oracle_decoder* dec, int32_t seq, const int32_t* tokens,
+                                 int32_t T, float* logits, int32_t* next_token) {
   const oracle_decoder_config* c = &dec->cfg;
   int64_t H = c->hidden, D = c->head_dim, I = c->intermediate, V = c->vocab;
   int64_t HQ = c->q_heads, HKV = c->kv_heads;
@@ -820,6 +845,13 @@ void oracle_decoder_forward(oracle_decoder* dec, const int32_t* tokens, int32_t 
           kh[(hh * M + t) * D + i] = oracle_bf16_round(v[i]);
           vh[(hh * M + t) * D + i] = oracle_bf16_round(vv[t * HKV * D + hh * D + i]);
         }
+        if (seq >= 0) { /* prefill: the row's K/V into the sequence's cache slot t */
+          size_t base = ((((size_t)l * c->max_batch + seq) * HKV + hh) * c->max_context + t) * D;
+          for (int64_t i = 0; i < D; ++i) {
+            dec->k_cache[base + i] = oracle_f32_to_bf16(kh[(hh * M + t) * D + i]);
+            dec->v_cache[base + i] = oracle_f32_to_bf16(vh[(hh * M + t) * D + i]);
+          }
+        }
       }
     }
     oracle_gqa_attention(qh, kh, vh, mask, 0, 0, 1, HQ, HKV, M, M, D, D,
@@ -877,6 +909,43 @@ void oracle_decoder_forward(oracle_decoder* dec, const int32_t* tokens, int32_t 
   free(up);
   free(mask);
   free(pos);
+}
+
+void oracle_decoder_forward(oracle_decoder* dec, const int32_t* tokens, int32_t T, float* logits,
+                            int32_t* next_token) {
+  decoder_forward_impl(dec, -1, tokens, T, logits, next_token);
+}
+
+/* The same full-sequence forward for sequence `seq` of the decoder's state,
+ * which must be empty (context 0): the prompt rows' K/V (bf16, as a
+ * token-by-token decode writes them) land in the sequence's cache and its
+ * context becomes T, so decode steps continue after the prompt.  Returns 0,
+ * or -1 (nothing done) when the sequence is not empty or T does not fit. */
+int32_t oracle_decoder_prefill(oracle_decoder* dec, int32_t seq, const int32_t* tokens, int32_t T,
+                               float* logits, int32_t* next_token) {
+  if (seq < 0 || seq >= dec->cfg.max_batch || dec->ctx[seq] != 0 || T <= 0 ||
+      T > dec->cfg.max_context)
+    return -1;
+  decoder_forward_impl(dec, seq, tokens, T, logits, next_token);
+  dec->ctx[seq] = T;
+  return 0;
+}
+
+/* Context length of sequence `seq` set directly (the cached K/V values at
+ * positions below it are whatever the cache holds): for timing a decode step
+ * at a long context without decoding the prompt. */
+int32_t oracle_decoder_set_context(oracle_decoder* dec, int32_t seq, int32_t ctx) {
+  if (seq < 0 || seq >= dec->cfg.max_batch || ctx < 0 || ctx >= dec->cfg.max_context) return -1;
+  dec->ctx[seq] = ctx;
+  return 0;
+}
+
+void oracle_set_num_threads(int32_t n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
 }
 
 int32_t oracle_num_threads(void) {

@@ -148,6 +148,10 @@ int32_t oracle_decoder_context(oracle_decoder* dec, int32_t b);
 void oracle_decoder_kv(oracle_decoder* dec, int32_t layer, uint16_t** k, uint16_t** v);
 
 /* Number of OpenMP threads the oracle uses (for the CPU baseline report). */
+int32_t oracle_decoder_prefill(oracle_decoder* dec, int32_t seq, const int32_t* tokens, int32_t T,
+                               float* logits, int32_t* next_token);
+int32_t oracle_decoder_set_context(oracle_decoder* dec, int32_t seq, int32_t ctx);
+void oracle_set_num_threads(int32_t n);
 int32_t oracle_num_threads(void);
 
 #ifdef __cplusplus

@@ -87,8 +87,12 @@ SIGNATURES = {
     "rxla_b200_last_error_message": (ctypes.c_char_p, []),
     "rxla_b200_device_info": (_i32, [_i32, _vp, _vp, _vp]),
     "rxla_b200_device_status": (_i32, [_i32]),
+    "rxla_b200_set_wait_timeout": (_i32, [_i64]),
+    "rxla_b200_get_wait_timeout": (_i32, [ctypes.POINTER(_i64)]),
     "rxla_b200_w8a16_linear": (_i32, [_vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i32,
                                       _i32, _vp]),
+    "rxla_b200_w8a16_norm_linear": (_i32, [_vp, _vp, _f32, _vp, _vp, _i64, _i64, _i64, _i64, _vp,
+                                           _i32, _i32, _vp]),
     "rxla_b200_bf16_linear": (_i32, [_vp, _i32, _vp, _i64, _i64, _i64, _vp, _i32, _i32, _vp]),
     "rxla_b200_paged_decode_workspace_size": (_i32, [_i32, _i32, _i32, _i32, _i32,
                                                      ctypes.POINTER(_sz)]),

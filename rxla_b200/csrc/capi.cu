@@ -208,6 +208,24 @@ extern "C" int32_t rxla_b200_device_status(int32_t reset) {
   return rxla::read_device_status(reset != 0);
 }
 
+extern "C" int32_t rxla_b200_set_wait_timeout(int64_t ns) {
+  using namespace rxla;
+  RXLA_REQUIRE(ns >= kMinWaitTimeoutNs && ns <= kMaxWaitTimeoutNs,
+               "set_wait_timeout: the budget must lie in [1 ms, 60 s]");
+  const unsigned long long v = (unsigned long long)ns;
+  RXLA_CUDA_CHECK(cudaMemcpyToSymbol(g_rxla_wait_timeout_ns, &v, sizeof(v)));
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_get_wait_timeout(int64_t* ns) {
+  using namespace rxla;
+  RXLA_REQUIRE(ns, "get_wait_timeout: null argument");
+  unsigned long long v = 0;
+  RXLA_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_rxla_wait_timeout_ns, sizeof(v)));
+  *ns = (int64_t)v;
+  return RXLA_B200_OK;
+}
+
 extern "C" int32_t rxla_b200_rms_norm_bf16(const float* x, const float* weight, int64_t rows,
                                            int64_t width, float eps, uint16_t* y, void* stream) {
   using namespace rxla;

@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(const Args a) {
     if (ld_acquire_sys(flag) < e) {
       const uint64_t t0 = globaltimer();
       while (ld_acquire_sys(flag) < e) {
-        if (globaltimer() - t0 > kWaitTimeoutNs) {
+        if (globaltimer() - t0 > wait_timeout_ns()) {
           record_device_error(RXLA_B200_DEADLINE_EXCEEDED);
           ok = 0;
           break;
@@ -281,6 +281,28 @@ extern "C" int32_t rxla_b200_comm_init(const uint8_t id[RXLA_B200_COMM_ID_BYTES]
   return RXLA_B200_OK;
 }
 
+namespace rxla {
+namespace p2p {
+// What each rank contributes to the set-up exchange: its buffer's IPC handle
+// (zeroed when its own set-up failed) and whether that set-up succeeded.
+struct Offer {
+  cudaIpcMemHandle_t handle;
+  int32_t ok;
+  int32_t pad[3];
+};
+// Exchange area of the set-up collectives: [kMaxRanks] offers, then one int32
+// for the agreement.  A file-scope array, so the exchange itself allocates
+// nothing and cannot fail where a rank's own allocations did.
+static __device__ __align__(16) unsigned char g_xfer[kMaxRanks * sizeof(Offer) + 16];
+}  // namespace p2p
+}  // namespace rxla
+
+// Every rank runs the same two collectives in the same order whatever its own
+// result (the all-gather of offers, then a min-agreement), so a rank whose
+// cudaMalloc or cudaIpcGetMemHandle failed never leaves its peers waiting in a
+// collective it skipped.  A rank opens its peers' handles only when every
+// offer says ok; the agreement then tells every rank whether all openings
+// succeeded, and every rank keeps the buffers or releases them together.
 extern "C" int32_t rxla_b200_comm_p2p_enable(rxla_b200_comm* c, int64_t max_count) {
   RXLA_REQUIRE(c && c->nccl, "comm_p2p_enable: comm not initialised");
   RXLA_REQUIRE(max_count > 0, "comm_p2p_enable: max_count must be positive");
@@ -290,63 +312,70 @@ extern "C" int32_t rxla_b200_comm_p2p_enable(rxla_b200_comm* c, int64_t max_coun
     return RXLA_B200_OK;
   }
   RXLA_CUDA_CHECK(cudaSetDevice(c->device));
+  void* xfer_v = nullptr;
+  RXLA_CUDA_CHECK(cudaGetSymbolAddress(&xfer_v, p2p::g_xfer));
+  uint8_t* xfer = static_cast<uint8_t*>(xfer_v);
+  p2p::Offer* offers = reinterpret_cast<p2p::Offer*>(xfer);
+  int32_t* agree = reinterpret_cast<int32_t*>(xfer + p2p::kMaxRanks * sizeof(p2p::Offer));
   p2p::Layout L;
   L.cap = (max_count + 3) / 4 * 4;
   L.max_ctas = (int)((L.cap + p2p::kChunk - 1) / p2p::kChunk);
   uint8_t* local = nullptr;
   uint64_t* epoch = nullptr;
-  uint8_t* xfer = nullptr;
+  // 1. this rank's own set-up (no collective yet)
   cudaError_t e = cudaMalloc(&local, L.bytes());
   if (e == cudaSuccess) e = cudaMemset(local, 0, L.bytes());
   if (e == cudaSuccess) e = cudaMalloc(&epoch, (size_t)L.max_ctas * 8);
   if (e == cudaSuccess) e = cudaMemset(epoch, 0, (size_t)L.max_ctas * 8);
-  if (e == cudaSuccess) e = cudaMalloc(&xfer, (size_t)p2p::kMaxRanks * sizeof(cudaIpcMemHandle_t));
-  cudaIpcMemHandle_t mine{};
-  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine, local);
-  // every rank's handle, through the comm itself (no host store needed)
-  std::vector<cudaIpcMemHandle_t> all(c->world);
-  if (e == cudaSuccess) e = cudaMemcpy(xfer + c->rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
-  int32_t st = RXLA_B200_OK;
-  if (e == cudaSuccess) {
-    ncclResult_t r = comm::nccl().all_gather(xfer + c->rank * sizeof(mine), xfer, sizeof(mine),
-                                             ncclUint8, c->nccl, nullptr);
-    if (r != ncclSuccess) st = comm::nccl_fail(r, "comm_p2p_enable: handle exchange");
+  p2p::Offer mine{};
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine.handle, local);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    std::memset(&mine, 0, sizeof(mine));
   }
-  if (e == cudaSuccess && !st) e = cudaDeviceSynchronize();
-  if (e == cudaSuccess && !st) e = cudaMemcpy(all.data(), xfer, c->world * sizeof(mine), cudaMemcpyDeviceToHost);
+  mine.ok = e == cudaSuccess ? 1 : 0;
+  cudaError_t local_err = e;
+  // 2. all-gather of the offers: always called
+  bool ok = cudaMemcpy(offers + c->rank, &mine, sizeof(mine), cudaMemcpyHostToDevice) == cudaSuccess;
+  int32_t st = RXLA_B200_OK;
+  ncclResult_t r = comm::nccl().all_gather(offers + c->rank, offers, sizeof(mine), ncclUint8,
+                                           c->nccl, nullptr);
+  if (r != ncclSuccess) st = comm::nccl_fail(r, "comm_p2p_enable: handle exchange");
+  std::vector<p2p::Offer> all(c->world);
+  ok = ok && !st && cudaDeviceSynchronize() == cudaSuccess &&
+       cudaMemcpy(all.data(), offers, c->world * sizeof(mine), cudaMemcpyDeviceToHost) == cudaSuccess;
+  for (int q = 0; q < c->world && ok; ++q) ok = all[q].ok == 1;
+  // 3. open the peers' buffers only if every rank offered one
   uint8_t* peer[p2p::kMaxRanks] = {};
-  for (int q = 0; q < c->world && e == cudaSuccess && !st; ++q) {
+  for (int q = 0; q < c->world && ok; ++q) {
     if (q == c->rank) {
       peer[q] = local;
       continue;
     }
     void* ptr = nullptr;
-    e = cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess);
+    ok = cudaIpcOpenMemHandle(&ptr, all[q].handle, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
     peer[q] = static_cast<uint8_t*>(ptr);
   }
-  // every rank must take the same path: agree on success (min over ranks)
-  if (!st) {
-    const int32_t mine_ok = e == cudaSuccess ? 1 : 0;
-    cudaGetLastError();
-    int32_t* flag = reinterpret_cast<int32_t*>(xfer);
-    cudaError_t e2 = cudaMemcpy(flag, &mine_ok, 4, cudaMemcpyHostToDevice);
-    ncclResult_t r = e2 == cudaSuccess ? comm::nccl().all_reduce(flag, flag, 1, ncclInt32, ncclMin,
-                                                                 c->nccl, nullptr)
-                                       : ncclInternalError;
-    int32_t all_ok = 0;
-    if (r == ncclSuccess && cudaDeviceSynchronize() == cudaSuccess &&
-        cudaMemcpy(&all_ok, flag, 4, cudaMemcpyDeviceToHost) == cudaSuccess && !all_ok &&
-        e == cudaSuccess)
-      e = cudaErrorPeerAccessUnsupported;  // a peer failed: nobody uses the buffers
-    if (r != ncclSuccess) st = comm::nccl_fail(r, "comm_p2p_enable: agreement");
-  }
-  if (xfer) cudaFree(xfer);
-  if (e != cudaSuccess || st) {
+  if (!ok) cudaGetLastError();
+  // 4. min-agreement over the ranks: always called
+  const int32_t opened = ok ? 1 : 0;
+  int32_t all_ok = 0;
+  const bool sent = cudaMemcpy(agree, &opened, 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  r = comm::nccl().all_reduce(agree, agree, 1, ncclInt32, ncclMin, c->nccl, nullptr);
+  if (r != ncclSuccess && !st) st = comm::nccl_fail(r, "comm_p2p_enable: agreement");
+  if (!(sent && r == ncclSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+        cudaMemcpy(&all_ok, agree, 4, cudaMemcpyDeviceToHost) == cudaSuccess))
+    all_ok = 0;
+  if (!all_ok || st) {
     for (int q = 0; q < c->world; ++q)
       if (q != c->rank && peer[q]) cudaIpcCloseMemHandle(peer[q]);
     if (local) cudaFree(local);
     if (epoch) cudaFree(epoch);
-    return st ? st : cuda_fail(e, "comm_p2p_enable");
+    cudaGetLastError();
+    if (st) return st;
+    if (local_err != cudaSuccess) return cuda_fail(local_err, "comm_p2p_enable: local set-up");
+    return fail(RXLA_B200_UNAVAILABLE,
+                "comm_p2p_enable: a rank could not set up or map the peer buffers; no rank uses them");
   }
   c->p2p = L;
   c->p2p_local = local;

@@ -65,14 +65,20 @@ int32_t read_device_status(bool reset);
 
 // ------------------------------------------------------------------ device
 
-// Bounded-wait budget.  Kernels here last microseconds; a wait this long means
-// a lost arrival, never a slow peer.
+// Default bounded-wait budget.  Kernels here last microseconds; a wait this
+// long means a lost arrival, never a slow peer.  rxla_b200_set_wait_timeout
+// changes it per device.
 constexpr unsigned long long kWaitTimeoutNs = 4000000000ull;
+constexpr int64_t kMinWaitTimeoutNs = 1000000;      // 1 ms
+constexpr int64_t kMaxWaitTimeoutNs = 60000000000;  // 60 s
 
 }  // namespace rxla
 
 // Device status word of this library on each device (single translation unit).
 __device__ int g_rxla_device_status = 0;
+// Bounded-wait budget of every spin in this library's kernels on each device
+// (ns of %globaltimer); set by rxla_b200_set_wait_timeout.
+__device__ unsigned long long g_rxla_wait_timeout_ns = rxla::kWaitTimeoutNs;
 
 namespace rxla {
 
@@ -80,6 +86,11 @@ __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// The current wait budget (read only once a wait has spun for a while).
+__device__ __forceinline__ unsigned long long wait_timeout_ns() {
+  return *reinterpret_cast<volatile unsigned long long*>(&g_rxla_wait_timeout_ns);
 }
 
 __device__ __forceinline__ void record_device_error(int code) {
@@ -130,7 +141,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
+    if (globaltimer() - t0 > wait_timeout_ns()) {
       record_device_error(RXLA_B200_DEADLINE_EXCEEDED);
       return false;
     }

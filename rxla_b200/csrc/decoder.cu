@@ -106,12 +106,9 @@ __global__ void fill_bf16_kernel(__nv_bfloat16* w, int64_t n, uint64_t seed) {
 __global__ void embed_kernel(const int32_t* __restrict__ tokens, const uint8_t* __restrict__ w8,
                              const float* __restrict__ scale, const __nv_bfloat16* __restrict__ wb,
                              int64_t vocab, int64_t hidden, int64_t groups, int64_t group,
-                             float* __restrict__ h, uint32_t* __restrict__ zero, int nzero) {
+                             float* __restrict__ h) {
   pdl_wait();
   pdl_launch_dependents();
-  // the step's grid-wide phase counters start at zero (fused layer chains)
-  if (blockIdx.x == 0)
-    for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0u;
   int64_t t = tokens[blockIdx.x];
   t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
   float* out = h + blockIdx.x * hidden;
@@ -270,11 +267,6 @@ struct Layer {
   float* sd;
   uint16_t* kc;
   uint16_t* vc;
-  // stream-order copies for the fused layer chain (w8_chain_pack)
-  uint8_t* pqkv;
-  uint8_t* po;
-  uint8_t* pgu;
-  uint8_t* pd;
 };
 
 }  // namespace dec
@@ -324,15 +316,6 @@ struct rxla_b200_decoder {
   float* arg_val = nullptr;
   int32_t* arg_idx = nullptr;
   uint32_t* arg_count = nullptr;
-  // phase arrival counters of the fused layer chains, [layers][kChainMaxPhases]
-  uint32_t* chain_bar = nullptr;
-  // fused layer chain: stage width (-1 not planned yet, 0 off), grid, and the
-  // stream-order weight copies (rebuilt after parameters were handed out)
-  int chain_kc = -1;
-  int chain_grid = 0;
-  uint8_t* packed = nullptr;
-  uint8_t* pemb = nullptr;
-  bool packed_valid = false;
   int32_t* host_pinned = nullptr;
   std::map<int, cudaGraphExec_t> graphs;
   // multi-token prefill: chunk buffers (rows = tokens of one prompt chunk),
@@ -605,184 +588,18 @@ static int32_t enqueue_gemm_layers(rxla_b200_decoder* d, int batch, cudaStream_t
 }
 
 // One decode step for `batch` sequences, enqueued on `s` (graph-capturable).
-// Stage width of the fused layer chain, or 0 when the chain is off or does
-// not apply.  The chain is opt-in (environment RXLA_B200_CHAIN=1, read when a
-// decoder plans its first small-batch step): on one B200 it measured slower
-// than the per-kernel path (its phases stream no faster than the skinny
-// kernel and each grid-wide phase boundary costs about a kernel boundary).
-// It applies with no tensor parallelism, a W8 tied head, per-channel scales
-// everywhere, a stage width that divides every input width and a
-// shared-memory plan that fits the largest chain batch;
-// RXLA_B200_CHAIN_KC sets the largest stage width tried.
-static int chain_kc(rxla_b200_decoder* d) {
-  if (d->chain_kc >= 0) return d->chain_kc;
-  const char* ev = getenv("RXLA_B200_CHAIN");
-  const int enabled = ev ? atoi(ev) : 0;
-  const char* kv = getenv("RXLA_B200_CHAIN_KC");
-  const int want = kv ? atoi(kv) : 4096;
-  d->chain_kc = 0;
-  if (!enabled || want <= 0 || want % 64 || d->cfg.tp_size > 1 || !d->emb_w8) return 0;
-  if (d->groups_h != 1 || d->groups_i != 1 || d->groups_o != 1) return 0;
-  const int64_t H = d->cfg.hidden, qd = (int64_t)d->hq * d->cfg.head_dim, I = d->inter;
-  if (H > 4 * 4 * 512) return 0;  // the normalised inputs' register plan
-  const int mb = std::min(d->cfg.max_batch, kChainMaxTokens);
-  for (int kc = want; kc >= 256; kc /= 2) {
-    if (kc % 64 || H % kc || qd % kc || I % kc) continue;
-    if (w8_chain_smem(mb, std::max({H, qd, I}), kc, nullptr) == 0) continue;
-    d->chain_kc = kc;
-    d->chain_grid = sm_count(d->device);
-    break;
-  }
-  return d->chain_kc;
-}
-
-// (Re)build the stream-order weight copies the chain reads.
-static int32_t pack_chain_weights(rxla_b200_decoder* d, cudaStream_t s) {
-  const auto& c = d->cfg;
-  const int64_t H = c.hidden, qd = (int64_t)d->hq * c.head_dim, I = d->inter;
-  const size_t per_layer = (size_t)(d->qkv_rows * H + H * qd + 2 * I * H + H * I);
-  if (!d->packed) {
-    const size_t bytes = per_layer * c.layers + (size_t)d->vocab * H + 256;
-    cudaError_t e = cudaMalloc(&d->packed, bytes);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      d->packed = nullptr;
-      d->chain_kc = 0;  // not enough memory for the copies: per-kernel path
-      return RXLA_B200_OK;
-    }
-    uint8_t* p = d->packed;
-    for (auto& L : d->layers) {
-      L.pqkv = p;
-      p += d->qkv_rows * H;
-      L.po = p;
-      p += H * qd;
-      L.pgu = p;
-      p += 2 * I * H;
-      L.pd = p;
-      p += H * I;
-    }
-    d->pemb = p;
-  }
-  const int kc = d->chain_kc, G = d->chain_grid;
-  for (auto& L : d->layers) {
-    int32_t st = w8_chain_pack(L.wqkv, L.pqkv, d->qkv_rows, H, false, kc, G, s);
-    if (!st) st = w8_chain_pack(L.wo, L.po, H, qd, false, kc, G, s);
-    if (!st) st = w8_chain_pack(L.wgu, L.pgu, I, H, true, kc, G, s);
-    if (!st) st = w8_chain_pack(L.wd, L.pd, H, I, false, kc, G, s);
-    if (st) return st;
-  }
-  int32_t st = w8_chain_pack(d->emb_w8, d->pemb, d->vocab, H, false, kc, G, s);
-  if (st) return st;
-  d->packed_valid = true;
-  return RXLA_B200_OK;
-}
-
-// Batch <= kChainMaxTokens without tensor parallelism: per layer the
-// attention kernel, then ONE persistent launch for o_proj (+ residual),
-// gate/up (post-attention RMSNorm, SwiGLU), down_proj (+ residual) and the
-// next layer's qkv (input RMSNorm) — or, after the last layer, the tied head
-// with its greedy argmax.  Layer 0's qkv runs as its own kernel after the
-// embedding.
-static int32_t enqueue_chain_layers(rxla_b200_decoder* d, int batch, cudaStream_t s) {
-  const auto& c = d->cfg;
-  const int64_t H = c.hidden, D = c.head_dim;
-  const int64_t qd = (int64_t)d->hq * D;
-  const int kc = d->chain_kc;
-  // bytes each CTA keeps requested into L2 ahead of its shared-memory ring
-  // (environment RXLA_B200_CHAIN_L2_KB overrides the default)
-  static const int64_t l2_ahead = [] {
-    const char* v = getenv("RXLA_B200_CHAIN_L2_KB");
-    const long kb = v ? atol(v) : 0;
-    return (int64_t)std::min<long>(std::max<long>(kb, 0), 1 << 16) * 1024;
-  }();
-  int32_t st = RXLA_B200_OK;
-  if (c.layers > 0) {
-    NormLinearArgs na{};
-    na.h = d->h;
-    na.norm_w = d->layers[0].ln1;
-    na.eps = c.rms_eps;
-    na.w = d->layers[0].wqkv;
-    na.scale = d->layers[0].sqkv;
-    na.group = d->group_h;
-    na.m = batch;
-    na.n = d->qkv_rows;
-    na.k = H;
-    na.y = d->qkv;
-    na.y_dtype = RXLA_B200_BF16;
-    na.epilogue = RXLA_B200_EPI_STORE;
-    st = w8_norm_linear(na, s);
-    if (st) return st;
-  }
-  for (int l = 0; l < c.layers; ++l) {
-    const Layer& L = d->layers[l];
-    rxla_b200_paged_decode_args a = attention_args(d, L, batch);
-    L2Prefetch to_o{};  // the chain's first weights, pulled into L2 while attention drains
-    to_o.seg[0] = L.po;
-    to_o.bytes[0] = H * qd;
-    to_o.nseg = 1;
-    to_o.per_cta = 256 * 1024;
-    st = attn::launch(&a, s, true, &to_o);
-    if (st) return st;
-    ChainParams p{};
-    p.m = batch;
-    p.kc = kc;
-    p.grid = d->chain_grid;
-    p.l2_ahead = l2_ahead;
-    p.bar = d->chain_bar + (size_t)l * kChainMaxPhases;
-    auto add = [&](const uint8_t* w, const float* scale, int64_t n, int64_t k, const void* x,
-                   const float* norm_w, int32_t epi, void* y, bool y_f32) -> ChainPhase& {
-      ChainPhase& ph = p.ph[p.nphases++];
-      ph.w = w;
-      ph.scale = scale;
-      ph.n = (int32_t)n;
-      ph.k = (int32_t)k;
-      ph.x = x;
-      ph.norm_w = norm_w;
-      ph.norm_eps = c.rms_eps;
-      ph.x_norm = norm_w != nullptr;
-      ph.epilogue = epi;
-      ph.y = y;
-      ph.y_f32 = y_f32;
-      ph.packed = 1;
-      return ph;
-    };
-    add(L.po, L.so, H, qd, d->att, nullptr, RXLA_B200_EPI_RESIDUAL_ADD, d->h, true);
-    add(L.pgu, L.sgu, d->inter, H, d->h, L.ln2, RXLA_B200_EPI_SWIGLU, d->act, false);
-    add(L.pd, L.sd, H, d->inter, d->act, nullptr, RXLA_B200_EPI_RESIDUAL_ADD, d->h, true);
-    if (l + 1 < c.layers) {
-      const Layer& N = d->layers[l + 1];
-      add(N.pqkv, N.sqkv, d->qkv_rows, H, d->h, N.ln1, RXLA_B200_EPI_STORE, d->qkv, false);
-    } else {
-      // tied W8 head: logits (f32), greedy token and the position advance
-      ChainPhase& ph = add(d->pemb, d->emb_scale, d->vocab, H, d->h, d->final_norm,
-                           kArgmaxEpilogue, d->logits, true);
-      ph.arg_val = d->arg_val;
-      ph.arg_idx = d->arg_idx;
-      ph.arg_count = d->arg_count;
-      ph.arg_out = d->tok_out;
-      ph.arg_advance = d->ctx;
-    }
-    st = w8_chain(p, s);
-    if (st) return st;
-  }
-  return RXLA_B200_OK;
-}
-
 static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
   const auto& c = d->cfg;
   const int64_t H = c.hidden, D = c.head_dim;
   cudaError_t e = launch_pdl(embed_kernel, dim3(batch), dim3(256), 0, s, (const int32_t*)d->tok_in,
                              (const uint8_t*)d->emb_w8, (const float*)d->emb_scale,
                              (const __nv_bfloat16*)d->emb_bf16, (int64_t)c.vocab, H,
-                             (int64_t)d->groups_h, (int64_t)d->group_h, d->h, d->chain_bar,
-                             c.layers * kChainMaxPhases);
+                             (int64_t)d->groups_h, (int64_t)d->group_h, d->h);
   if (e != cudaSuccess) return cuda_fail(e, "embed launch");
   const bool tp = c.tp_size > 1;
   if (batch > kSkinnyTokens && d->gws_bytes > 0 && d->group_h % 64 == 0 &&
       d->group_o % 64 == 0 && d->group_i % 64 == 0)
     return enqueue_gemm_layers(d, batch, s);
-  if (batch <= kChainMaxTokens && chain_kc(d) > 0 && d->packed_valid)
-    return enqueue_chain_layers(d, batch, s);
   const int64_t qd = (int64_t)d->hq * D;
   // each kernel pulls the start of the next weight matrix into L2 while it drains
   auto pf = [](const void* w, int64_t bytes, int32_t per_cta) {
@@ -1113,7 +930,6 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
       {(void**)&d->arg_val, (size_t)1024 * 8 * 4},
       {(void**)&d->arg_idx, (size_t)1024 * 8 * 4},
       {(void**)&d->arg_count, 256},
-      {(void**)&d->chain_bar, (size_t)std::max(c.layers, 1) * kChainMaxPhases * 4},
   };
   for (auto& a : acts) {
     st = dec::alloc_dev(a.p, std::max<size_t>(a.bytes, 256));
@@ -1170,7 +986,7 @@ extern "C" int32_t rxla_b200_decoder_destroy(rxla_b200_decoder* d) {
   void* ptrs[] = {d->arena, d->page_table, d->ctx, d->h, d->xn, d->qkv, d->att, d->act,
                   d->part, d->logits, d->tok_in, d->tok_out, d->inv_freq, d->ws,
                   d->gws, d->arg_val, d->arg_idx, d->arg_count, d->cand, d->cand_all,
-                  d->chain_bar, d->packed, d->pf_mem};
+                  d->pf_mem};
   for (void* p : ptrs) cudaFree(p);
   if (d->host_pinned) cudaFreeHost(d->host_pinned);
   delete d;
@@ -1180,7 +996,6 @@ extern "C" int32_t rxla_b200_decoder_destroy(rxla_b200_decoder* d) {
 extern "C" int32_t rxla_b200_decoder_parameter(rxla_b200_decoder* d, const char* name,
                                                void** ptr, int64_t* bytes, int32_t* dtype) {
   RXLA_REQUIRE(d && name && ptr, "decoder_parameter: null argument");
-  d->packed_valid = false;  // the caller may write through the pointer
   const std::string n(name);
   const auto& c = d->cfg;
   const int64_t H = c.hidden, D = c.head_dim;
@@ -1238,7 +1053,6 @@ extern "C" int32_t rxla_b200_decoder_set_parameter(rxla_b200_decoder* d, const c
 }
 
 extern "C" int32_t rxla_b200_decoder_init_synthetic(rxla_b200_decoder* d, uint64_t seed) {
-  if (d) d->packed_valid = false;
   RXLA_REQUIRE(d, "decoder_init_synthetic: null decoder");
   RXLA_CUDA_CHECK(cudaSetDevice(d->device));
   const int grid = sm_count(d->device) * 8;
@@ -1352,12 +1166,6 @@ extern "C" int32_t rxla_b200_decoder_step(rxla_b200_decoder* d, const int32_t* t
   if (tokens != d->tok_in)
     RXLA_CUDA_CHECK(cudaMemcpyAsync(d->tok_in, tokens, (size_t)batch * 4,
                                     cudaMemcpyDeviceToDevice, s));
-  if (batch <= kChainMaxTokens && dec::chain_kc(d) > 0 && !d->packed_valid) {
-    // the chain's weight copies are stale (parameters were handed out): the
-    // captured graphs keep pointing at the same buffers
-    int32_t st = dec::pack_chain_weights(d, s);
-    if (st) return st;
-  }
   // RXLA_B200_NO_GRAPH=1: launch the step's kernels directly on `stream`
   // (for profilers that attribute work per kernel launch)
   static const bool no_graph = [] {
@@ -1505,7 +1313,7 @@ extern "C" int32_t rxla_b200_decoder_prefill(rxla_b200_decoder* d, int32_t seq,
       e = launch_pdl(dec::embed_kernel, dim3(n), dim3(256), 0, s, tokens + c0,
                      (const uint8_t*)d->emb_w8, (const float*)d->emb_scale,
                      (const __nv_bfloat16*)d->emb_bf16, (int64_t)c.vocab, H,
-                     (int64_t)d->groups_h, (int64_t)d->group_h, d->pf_h, (uint32_t*)nullptr, 0);
+                     (int64_t)d->groups_h, (int64_t)d->group_h, d->pf_h);
     if (e != cudaSuccess) return cuda_fail(e, "prefill rows launch");
     const dec::Rows r{n,         d->pf_h,         d->pf_xn, d->pf_qkv, d->pf_att,
                       d->pf_act, d->pf_part,      d->pf_gws, d->pf_gws_bytes, d->pf_pt,

@@ -46,52 +46,6 @@ struct GemmArgs {
   size_t ws_bytes;
 };
 
-// Several dependent W8 linears of a decode step in one persistent launch
-// (one CTA per SM): phase p starts once every CTA has finished phase p-1,
-// counted in bar[p-1] (zero before the launch).  A phase's x is bf16 [m, k],
-// or the f32 residual h [m, k] normalised in the CTA (x_norm); its epilogue
-// is STORE / RESIDUAL_ADD / SWIGLU / argmax with per-channel scales.
-constexpr int kChainMaxPhases = 8;
-constexpr int kChainMaxTokens = 4;
-
-struct ChainPhase {
-  const uint8_t* w;
-  const float* scale;  // per output row
-  const void* x;
-  const float* norm_w;
-  float norm_eps;
-  int32_t x_norm;
-  int32_t n, k, k_chunks;
-  int32_t epilogue, y_f32;
-  int32_t packed;  // w is in the chain's stream order (w8_chain_pack), else [rows, k]
-  void* y;
-  float* arg_val;
-  int32_t* arg_idx;
-  uint32_t* arg_count;
-  int32_t* arg_out;
-  int32_t* arg_advance;
-};
-
-struct ChainParams {
-  ChainPhase ph[kChainMaxPhases];
-  int32_t nphases, m;
-  int32_t grid;   // CTAs (0: one per SM); packed weights need the grid they were packed for
-  uint32_t* bar;  // [nphases] arrival counters
-  int64_t l2_ahead;  // bytes of its weight stream each CTA keeps prefetched into L2
-  // shared-memory plan: stage width (divides every phase's k), set by the caller;
-  // the rest by w8_chain
-  int32_t kc, stages, stage_bytes, x_pitch;
-};
-
-int32_t w8_chain(ChainParams p, cudaStream_t stream);
-// Rewrites W8 weights [rows, k] (rows = 2n for SwiGLU: gate rows, then up
-// rows) into the order a chain of `grid` CTAs with stage width kc streams
-// them, so that every stage is one contiguous copy.  Same size as w.
-int32_t w8_chain_pack(const uint8_t* w, uint8_t* packed, int64_t n, int64_t k, bool swiglu,
-                      int kc, int grid, cudaStream_t stream);
-// dynamic shared memory of a chain launch (0: does not fit)
-size_t w8_chain_smem(int m, int64_t max_k, int64_t kc, int* stages);
-
 int32_t w8_norm_linear(const NormLinearArgs& a, cudaStream_t stream);
 // rxla_b200_w8a16_linear with an L2 prefetch of the next kernel's first bytes
 int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const float* scale,

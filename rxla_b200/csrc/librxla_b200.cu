@@ -6,7 +6,6 @@
 #include "w8_linear.cu"
 #include "w8_gemm.cu"
 #include "w8_gemm_dec.cu"
-#include "w8_chain.cu"
 #include "dense_linear.cu"
 #include "attention.cu"
 #include "decoder.cu"

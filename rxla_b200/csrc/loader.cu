@@ -341,8 +341,9 @@ static int32_t read_block(const rxla_b200_safetensors* f, const Tensor& t, int64
                           int64_t rows, int64_t col0, int64_t cols, uint8_t* dst) {
   int64_t R, C;
   as_matrix(t, R, C);
-  RXLA_REQUIRE(row0 >= 0 && rows >= 0 && col0 >= 0 && cols >= 0 && row0 + rows <= R &&
-                   col0 + cols <= C,
+  // overflow-safe: rows <= R and row0 <= R - rows (never forms row0 + rows)
+  RXLA_REQUIRE(row0 >= 0 && rows >= 0 && col0 >= 0 && cols >= 0 && rows <= R &&
+                   row0 <= R - rows && cols <= C && col0 <= C - cols,
                "safetensors_read: block outside tensor " + t.name);
   const int64_t rb = C * t.elem, cb = cols * t.elem;
   auto pread_all = [&](uint8_t* d, int64_t n, int64_t off) -> bool {
@@ -377,7 +378,10 @@ extern "C" int32_t rxla_b200_safetensors_read(const rxla_b200_safetensors* f, in
   RXLA_REQUIRE(index >= 0 && index < (int32_t)f->tensors.size(),
                "safetensors_read: index out of range");
   const st::Tensor& t = f->tensors[(size_t)index];
-  RXLA_REQUIRE(rows >= 0 && cols >= 0 && dst_bytes == rows * cols * t.elem,
+  // checked product: rows * cols * elem must not wrap before it is compared
+  int64_t want = 0;
+  RXLA_REQUIRE(rows >= 0 && cols >= 0 && !__builtin_mul_overflow(rows, cols, &want) &&
+                   !__builtin_mul_overflow(want, (int64_t)t.elem, &want) && dst_bytes == want,
                "safetensors_read: destination must hold exactly rows * cols elements");
   return st::read_block(f, t, row0, rows, col0, cols, static_cast<uint8_t*>(dst));
 }
@@ -484,7 +488,6 @@ extern "C" int32_t rxla_b200_decoder_load_safetensors(rxla_b200_decoder* d, cons
                   "decoder_load_safetensors: the checkpoint does not fill parameter " + p.name +
                       " (" + std::to_string(covered[p.name]) + " of " + std::to_string(p.bytes) +
                       " bytes)");
-  d->packed_valid = false;
   if (loaded) *loaded = n_loaded;
   if (skipped) *skipped = n_skipped;
   return RXLA_B200_OK;

@@ -34,10 +34,9 @@ static __device__ __align__(256) unsigned char g_scratch[kNoallocScratchBytes];
 static std::mutex g_mu;
 static void* g_ptr[64] = {};
 
-// Device address of g_scratch on the current device (looked up once per device).
-static int32_t scratch_address(void** out) {
-  int dev = 0;
-  RXLA_CUDA_CHECK(cudaGetDevice(&dev));
+// Device address of g_scratch on device `dev`, which must be current (looked
+// up once per device).
+static int32_t scratch_address(int dev, void** out) {
   if (dev < 0 || dev >= 64) return fail(RXLA_B200_OUT_OF_RANGE, "noalloc: device index >= 64");
   std::lock_guard<std::mutex> lock(g_mu);
   if (!g_ptr[dev]) {
@@ -69,12 +68,22 @@ extern "C" int32_t rxla_b200_paged_decode_attention_noalloc(const rxla_b200_page
                     std::to_string(noalloc::kNoallocScratchBytes) +
                     "; use rxla_b200_paged_decode_attention with a caller workspace");
   if (a->batch == 0) return RXLA_B200_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the array used is the current device's: a stream of another device would
+  // clear that device's counters under a call it may have in flight
+  int dev = 0, sdev = 0;
+  RXLA_CUDA_CHECK(cudaGetDevice(&dev));
+  sdev = dev;
+  if (s) RXLA_CUDA_CHECK(cudaStreamGetDevice(s, &sdev));
+  if (sdev != dev)
+    return fail(RXLA_B200_INVALID_ARGUMENT,
+                "paged_decode_noalloc: the stream belongs to device " + std::to_string(sdev) +
+                    " but device " + std::to_string(dev) + " is current");
   void* scratch = nullptr;
-  st = noalloc::scratch_address(&scratch);
+  st = noalloc::scratch_address(dev, &scratch);
   if (st != RXLA_B200_OK) return st;
   // the split counters (the first bytes of the workspace) must start at zero
   const size_t counters = ((size_t)a->batch * a->kv_heads + 1) * 4;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   RXLA_CUDA_CHECK(cudaMemsetAsync(scratch, 0, counters, s));
   rxla_b200_paged_decode_args b = *a;
   b.workspace = scratch;

@@ -971,6 +971,47 @@ int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const f
 }
 }  // namespace rxla
 
+extern "C" int32_t rxla_b200_w8a16_norm_linear(const float* h, const float* norm_weight,
+                                               float eps, const uint8_t* weight,
+                                               const float* scale, int64_t group_size, int64_t m,
+                                               int64_t n, int64_t k, void* y, int32_t y_dtype,
+                                               int32_t epilogue, void* stream) {
+  using namespace rxla;
+  RXLA_REQUIRE(m >= 0 && n >= 0 && k > 0 && k <= INT32_MAX && n <= INT32_MAX,
+               "w8a16_norm_linear: m, n must be >= 0 and k > 0");
+  RXLA_REQUIRE(eps > 0.0f && eps == eps && eps < INFINITY,
+               "w8a16_norm_linear: epsilon must be finite and positive (ops.rs:930)");
+  RXLA_REQUIRE(group_size > 0 && k % group_size == 0,
+               "w8a16_norm_linear: group_size must be positive and divide k (layers.rs:266-275)");
+  RXLA_REQUIRE(y_dtype == RXLA_B200_BF16 || y_dtype == RXLA_B200_F32,
+               "w8a16_norm_linear: y must be BF16 or F32");
+  RXLA_REQUIRE(epilogue >= RXLA_B200_EPI_STORE && epilogue <= RXLA_B200_EPI_SWIGLU,
+               "w8a16_norm_linear: unknown epilogue");
+  RXLA_REQUIRE(epilogue != RXLA_B200_EPI_RESIDUAL_ADD || y_dtype == RXLA_B200_F32,
+               "w8a16_norm_linear: the residual epilogue adds into an F32 y");
+  if (m == 0 || n == 0) return RXLA_B200_OK;
+  RXLA_REQUIRE(h && norm_weight && weight && scale && y, "w8a16_norm_linear: null pointer");
+  // every CTA reads all of h while the epilogue writes y: they must not overlap
+  const uintptr_t h0 = reinterpret_cast<uintptr_t>(h), h1 = h0 + (uintptr_t)(m * k * 4);
+  const uintptr_t y0 = reinterpret_cast<uintptr_t>(y);
+  const uintptr_t y1 = y0 + (uintptr_t)(m * n * (y_dtype == RXLA_B200_F32 ? 4 : 2));
+  RXLA_REQUIRE(y1 <= h0 || h1 <= y0, "w8a16_norm_linear: y must not overlap h");
+  NormLinearArgs a{};
+  a.h = h;
+  a.norm_w = norm_weight;
+  a.eps = eps;
+  a.w = weight;
+  a.scale = scale;
+  a.group = group_size;
+  a.m = m;
+  a.n = n;
+  a.k = k;
+  a.y = y;
+  a.y_dtype = y_dtype;
+  a.epilogue = epilogue;
+  return w8_norm_linear(a, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int32_t rxla_b200_w8a16_linear(const void* x, int32_t x_dtype, const uint8_t* weight,
                                           const float* scale, int64_t group_size, int64_t m,
                                           int64_t n, int64_t k, void* y, int32_t y_dtype,

@@ -80,6 +80,39 @@ def quantized_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
     return out
 
 
+def quantized_norm_linear(h: torch.Tensor, norm_weight: torch.Tensor, epsilon: float,
+                          weight: torch.Tensor, scale: torch.Tensor,
+                          group_size: int | None = None, *, out_dtype=torch.bfloat16,
+                          epilogue: int = _lib.EPI_STORE, out: torch.Tensor | None = None,
+                          stream=None) -> torch.Tensor:
+    """QuantizedLinear of bf16(rms_norm(h) * norm_weight), the norm fused into
+    the linear's prologue (rxla_b200_w8a16_norm_linear): h f32 [..., K], the
+    other arguments as for quantized_linear."""
+    if h.dtype != torch.float32 or norm_weight.dtype != torch.float32:
+        raise InvalidLayerInput("the fused norm needs an F32 h and norm weight")
+    if not (epsilon > 0 and math.isfinite(epsilon)):
+        raise InvalidLayerInput("RMSNorm requires a finite positive epsilon")
+    k = h.shape[-1]
+    rows = weight.shape[0]
+    if weight.dim() != 2 or weight.shape[1] != k or norm_weight.numel() != k:
+        raise InvalidLayerInput("weight must be [out_features, in_features], norm [in_features]")
+    group = k if group_size is None else int(group_size)
+    if group <= 0 or k % group != 0 or scale.numel() != rows * (k // group):
+        raise InvalidLayerInput("scale must be [out_features, in_features / group_size]")
+    n = rows // 2 if epilogue == _lib.EPI_SWIGLU else rows
+    lead = h.shape[:-1]
+    m = int(np.prod(lead)) if len(lead) else 1
+    h2 = h.reshape(m, k).contiguous()
+    if out is None:
+        if epilogue == _lib.EPI_RESIDUAL_ADD:
+            raise InvalidLayerInput("the residual epilogue needs `out` (f32) to add into")
+        out = torch.empty(*lead, n, dtype=out_dtype, device=h.device)
+    _lib.call("rxla_b200_w8a16_norm_linear", _ptr(h2), _ptr(norm_weight), ctypes.c_float(epsilon),
+              _ptr(weight), _ptr(scale), group, m, n, k, _ptr(out), _DT[out.dtype], epilogue,
+              _stream(stream))
+    return out
+
+
 class QuantizedLinear:
     """rxla_nn::QuantizedLinear::new(out_features, group_size) (layers.rs:231-256).
 

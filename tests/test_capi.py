@@ -133,3 +133,26 @@ def test_python_constants_match_header_enums():
     enums = {m.group(1): int(m.group(2)) for m in re.finditer(r"RXLA_B200_(\w+)\s*=\s*(-?\d+)", text)}
     for name in ("F32", "BF16", "U8", "I32", "F16", "OK", "INVALID_ARGUMENT", "NOT_FOUND"):
         assert getattr(_lib, name) == enums[name], name
+
+
+def test_python_noalloc_limit_matches_header():
+    """The allocation-free attention's scratch limit the binding and its tests
+    use is the header's RXLA_B200_NOALLOC_SCRATCH_BYTES."""
+    text = HEADER.read_text()
+    m = re.search(r"#define\s+RXLA_B200_NOALLOC_SCRATCH_BYTES\s+\(([^)]*)\)", text)
+    assert m, "RXLA_B200_NOALLOC_SCRATCH_BYTES not found"
+    expr = re.sub(r"(\d+)u\b", r"\1", m.group(1))
+    assert re.fullmatch(r"[\d\s*+()]+", expr), expr
+    assert eval(expr) == _lib.NOALLOC_SCRATCH_BYTES
+    m = re.search(r"#define\s+RXLA_B200_COMM_ID_BYTES\s+(\d+)", text)
+    assert m and int(m.group(1)) == _lib.COMM_ID_BYTES
+
+
+def test_wait_timeout_range_is_checked_without_cuda():
+    """rxla_b200_set_wait_timeout refuses budgets outside [1 ms, 60 s] before
+    any CUDA call."""
+    lib = _lib.load()
+    assert lib.rxla_b200_set_wait_timeout(999_999) == _lib.INVALID_ARGUMENT
+    assert lib.rxla_b200_set_wait_timeout(60_000_000_001) == _lib.INVALID_ARGUMENT
+    assert "[1 ms, 60 s]" in lib.rxla_b200_last_error_message().decode()
+    assert lib.rxla_b200_get_wait_timeout(None) == _lib.INVALID_ARGUMENT

@@ -1,0 +1,197 @@
+"""Decoder parity at the benchmarked model widths (BASELINE configs 4 and 5).
+
+The tiny config-1 decoder (hidden 512) never reaches the kernel instances the
+8B- and 32B-shaped decode steps spend their time in: the skinny GEMV with
+x held in registers and the RMSNorm fused in its prologue (K = 4096: qkv,
+gate/up with SwiGLU, the tied LM head with its greedy argmax), down_proj at
+K = 12288, the decode-batch tcgen05 GEMM at 32 and 64 token columns, and the
+paged attention with 32 or 64 query heads over 8 kv heads at head_dim 128.
+These tests run 2-layer decoders with exactly those layer shapes (hidden,
+heads, head_dim, intermediate, the 151936-token W8 tied head) against the CPU
+oracle decoder holding the same weights:
+
+* config 4 at batch 1: a 128-token prompt through the prefill on both sides,
+  then 32 greedy decode steps (teacher forcing: both consume the oracle's
+  tokens);
+* config 4 at batch 64 and config 5 at batch 32: short prompts stepped as a
+  batch, then greedy decode steps.
+
+Acceptance (north star): logits within max-abs 2e-2 and mean-abs 2e-3 over
+the window of the last prompt row and the decode steps, and identical greedy
+tokens.  Token identity is only meaningful where the oracle's own choice is
+not a tie within that tolerance: a top-1 logit that beats the top-2 by less
+than the max-abs bar (2e-2) may legitimately go either way for any
+implementation inside the bar.  With random N(0, 0.02) weights and 151936
+logits of standard deviation ~1.3, the top-2 gap is below 2e-2 for roughly
+one token in ten, so:
+
+* batch 1 uses weights and a prompt whose 33 oracle tokens all have a gap of
+  at least 2e-2 (asserted on the oracle side, so the comparison is
+  well-posed) and requires all 32 decode tokens and the prompt's token to be
+  identical;
+* the batched tests require identical tokens wherever the oracle's gap is at
+  least 2e-2 and report how many tokens fell below it.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from rxla_b200 import _lib
+from rxla_b200.decoder import Decoder
+
+pytestmark = pytest.mark.gpu
+
+CONFIG4_2L = dict(layers=2, hidden=4096, q_heads=32, kv_heads=8, head_dim=128,
+                  intermediate=12288, vocab=151936, rms_eps=1e-6, rope_theta=1e6)
+CONFIG5_2L = dict(layers=2, hidden=5120, q_heads=64, kv_heads=8, head_dim=128,
+                  intermediate=25600, vocab=151936, rms_eps=1e-6, rope_theta=1e6)
+MAX_ABS, MEAN_ABS, TIE = 2e-2, 2e-3, 2e-2
+# weights seed and prompt seed of the batch-1 case (every oracle token's
+# top-2 gap >= TIE; chosen by running the oracle, asserted below)
+B1_WEIGHTS_SEED, B1_PROMPT_SEED = 11, 1006
+
+
+def _names(layers):
+    names = ["embed_tokens.weight", "embed_tokens.scale", "norm.weight"]
+    for l in range(layers):
+        p = f"layers.{l}."
+        names += [p + "input_layernorm.weight", p + "post_attention_layernorm.weight",
+                  p + "self_attn.q_norm.weight", p + "self_attn.k_norm.weight"]
+        names += [f"{p}self_attn.{pr}.{k}" for pr in ("q_proj", "k_proj", "v_proj", "o_proj")
+                  for k in ("weight", "scale")]
+        names += [f"{p}mlp.{pr}.{k}" for pr in ("gate_proj", "up_proj", "down_proj")
+                  for k in ("weight", "scale")]
+    return names
+
+
+def _pair(cfg, batch, max_context, seed):
+    ref = oracle.Decoder(**cfg, embedding_bf16=False, group_size=0, max_batch=batch,
+                         max_context=max_context)
+    ref.init_synthetic(seed)
+    gpu = Decoder(**cfg, embedding_dtype="u8", group_size=0, max_batch=batch,
+                  max_context=max_context)
+    for n in _names(cfg["layers"]):
+        gpu.set_parameter(n, ref.parameter(n))
+    return ref, gpu
+
+
+class _Stepper:
+    """Device buffers for teacher-forced GPU decode steps with logits."""
+
+    def __init__(self, gpu, batch):
+        self.gpu, self.batch = gpu, batch
+        self.lg = torch.empty(batch, gpu.vocab, dtype=torch.float32, device="cuda")
+        self.tin = torch.empty(batch, dtype=torch.int32, device="cuda")
+        self.tout = torch.empty(batch, dtype=torch.int32, device="cuda")
+
+    def step(self, tokens):
+        self.tin.copy_(torch.from_numpy(np.ascontiguousarray(tokens, np.int32)))
+        _lib.call("rxla_b200_decoder_step", self.gpu.handle, ctypes.c_void_p(self.tin.data_ptr()),
+                  self.batch, ctypes.c_void_p(self.tout.data_ptr()),
+                  ctypes.c_void_p(self.lg.data_ptr()),
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        return self.lg.cpu().numpy(), self.tout.cpu().numpy()
+
+
+def _gap(logits):
+    top2 = np.sort(logits, axis=-1)[..., -2:]
+    return top2[..., 1] - top2[..., 0]
+
+
+def _batched_decode(cfg, batch, prompt_len, steps, seed):
+    """Prompts stepped as one batch, then greedy decode steps; returns the
+    window's per-step max/mean errors, tokens and the oracle's gaps."""
+    ref, gpu = _pair(cfg, batch, prompt_len + steps + 8, seed)
+    st = _Stepper(gpu, batch)
+    prompt = oracle.randint(batch * prompt_len, seed + 500, 0, cfg["vocab"]).reshape(batch, prompt_len)
+    emax, emean, gref, ggpu, gaps = [], [], [], [], []
+    cur = prompt[:, 0].copy()
+    for t in range(prompt_len + steps):
+        l_ref, n_ref = ref.step(cur)
+        l_gpu, n_gpu = st.step(cur)
+        if t + 1 >= prompt_len:  # the last prompt row and the decode steps
+            d = np.abs(l_gpu - l_ref)
+            emax.append(d.max())
+            emean.append(d.mean())
+            gref.append(n_ref.copy())
+            ggpu.append(n_gpu.copy())
+            gaps.append(_gap(l_ref))
+            cur = n_ref.astype(np.int32)
+        else:
+            cur = prompt[:, t + 1].copy()
+    status = _lib.load().rxla_b200_device_status(0)
+    gpu.close()
+    ref.close()
+    return (np.array(emax), np.array(emean), np.stack(gref), np.stack(ggpu), np.stack(gaps),
+            status)
+
+
+def test_config4_batch1_prefill_then_32_greedy_steps(cuda):
+    """Config-4 widths at batch 1: prefill of a 128-token prompt (the tcgen05
+    prefill GEMM, K/V append, causal prefill attention, fused-argmax head) and
+    32 decode steps on the fused-norm x-in-register GEMVs, down_proj at
+    K = 12288 and the split-K paged attention."""
+    ref, gpu = _pair(CONFIG4_2L, 1, 256, B1_WEIGHTS_SEED)
+    prompt = oracle.randint(128, B1_PROMPT_SEED, 0, CONFIG4_2L["vocab"])
+    l_ref, n_ref = ref.prefill(0, prompt)
+    lg = torch.empty(gpu.vocab, dtype=torch.float32, device="cuda")
+    tok = gpu.prefill(0, prompt, logits_ptr=ctypes.c_void_p(lg.data_ptr()))
+    torch.cuda.synchronize()
+    d = np.abs(lg.cpu().numpy() - l_ref)
+    emax, emean, gaps = [d.max()], [d.mean()], [_gap(l_ref)]
+    gref, ggpu = [n_ref], [int(tok.item())]
+    st = _Stepper(gpu, 1)
+    cur = np.array([n_ref], np.int32)
+    for _ in range(32):
+        l_ref, n_ref = ref.step(cur)
+        l_gpu, n_gpu = st.step(cur)
+        d = np.abs(l_gpu - l_ref)
+        emax.append(d.max())
+        emean.append(d.mean())
+        gaps.append(float(_gap(l_ref)[0]))
+        gref.append(int(n_ref[0]))
+        ggpu.append(int(n_gpu[0]))
+        cur = n_ref.astype(np.int32)
+    status = _lib.load().rxla_b200_device_status(0)
+    gpu.close()
+    ref.close()
+    emax, emean = np.array(emax), np.array(emean)
+    print(f"config4 batch 1: window max-abs {emax.max():.4g}, mean-abs {emean.mean():.4g} "
+          f"(prefill row: {emax[0]:.4g} / {emean[0]:.4g}); oracle min top-2 gap {min(gaps):.4g}; "
+          f"tokens {gref}")
+    assert status == 0
+    assert min(gaps) >= TIE, "precondition: the oracle's tokens of this case are not near-ties"
+    assert emax.max() <= MAX_ABS, f"max-abs logits error {emax.max()}"
+    assert emean.mean() <= MEAN_ABS, f"mean-abs logits error {emean.mean()}"
+    assert ggpu == gref, "greedy tokens differ"
+
+
+def test_config4_batch64(cuda):
+    """Config-4 widths at batch 64: every linear on the decode-batch tcgen05
+    GEMM (64 token columns, split-K), the attention at batch 64."""
+    emax, emean, gref, ggpu, gaps, status = _batched_decode(CONFIG4_2L, 64, 6, 6, seed=21)
+    clear = gaps >= TIE
+    print(f"config4 batch 64: max-abs {emax.max():.4g}, mean-abs {emean.mean():.4g}; "
+          f"{int((~clear).sum())} of {clear.size} oracle tokens within the tie tolerance, "
+          f"{int((ggpu != gref).sum())} tokens differ")
+    assert status == 0
+    assert emax.max() <= MAX_ABS and emean.mean() <= MEAN_ABS
+    assert (ggpu[clear] == gref[clear]).all(), "a token differs where the oracle is not tied"
+
+
+def test_config5_batch32(cuda):
+    """Config-5 widths (hidden 5120, 64 q / 8 kv heads, intermediate 25600) at
+    batch 32: the decode-batch GEMM at 32 token columns with K = 5120, 8192
+    and 25600, attention with 8 query heads per kv head."""
+    emax, emean, gref, ggpu, gaps, status = _batched_decode(CONFIG5_2L, 32, 4, 5, seed=31)
+    clear = gaps >= TIE
+    print(f"config5 batch 32: max-abs {emax.max():.4g}, mean-abs {emean.mean():.4g}; "
+          f"{int((~clear).sum())} of {clear.size} oracle tokens within the tie tolerance, "
+          f"{int((ggpu != gref).sum())} tokens differ")
+    assert status == 0
+    assert emax.max() <= MAX_ABS and emean.mean() <= MEAN_ABS
+    assert (ggpu[clear] == gref[clear]).all(), "a token differs where the oracle is not tied"

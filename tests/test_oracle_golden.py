@@ -330,3 +330,27 @@ def test_stepped_decoder_equals_full_sequence_causal_forward(emb_bf16, group):
     np.testing.assert_array_equal(full_logits, step_logits[0])
     assert full_tok == int(step_tok[0])
     dec.close()
+
+
+def test_oracle_prefill_equals_stepping_bit_for_bit():
+    """Decoder.prefill (the full-sequence forward that also fills the cache)
+    leaves the same state as stepping the prompt token by token: the last
+    prompt row's logits and every later decode step are bit-identical."""
+    import numpy as np
+    cfg = dict(layers=2, hidden=256, q_heads=4, kv_heads=2, head_dim=64, intermediate=512,
+               vocab=1024)
+    a = oracle.Decoder(**cfg, max_batch=1, max_context=64)
+    b = oracle.Decoder(**cfg, max_batch=1, max_context=64)
+    a.init_synthetic(2)
+    b.init_synthetic(2)
+    prompt = oracle.randint(24, 3, 0, 1024)
+    for t in prompt:
+        la, _ = a.step(np.array([t], np.int32))
+    lb, _ = b.prefill(0, prompt)
+    assert np.array_equal(la[0].view(np.uint32), lb.view(np.uint32))
+    for t in (5, 17, 900):
+        la, _ = a.step(np.array([t], np.int32))
+        lb, _ = b.step(np.array([t], np.int32))
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    a.close()
+    b.close()

@@ -315,3 +315,149 @@ def test_tp2_checkpoint_load_and_prefill(tmp_path):
         assert counts == (len(names), 0)
         assert max(errs) <= 2e-2
         assert flip_ok
+
+
+def _spawn(target, world, *args):
+    """Run `target(rank, world, port, *args, q)` in `world` spawned processes
+    (NVLS off, as every multi-rank failure test here runs) and collect one
+    result per rank."""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    old = os.environ.get("NCCL_NVLS_ENABLE")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        procs = [ctx.Process(target=target, args=(r, world, port, *args, q)) for r in range(world)]
+        for p in procs:
+            p.start()
+        results = [q.get(timeout=300) for _ in range(world)]
+        for p in procs:
+            p.join(timeout=60)
+    finally:
+        if old is None:
+            del os.environ["NCCL_NVLS_ENABLE"]
+        else:
+            os.environ["NCCL_NVLS_ENABLE"] = old
+    return sorted(results, key=lambda r: r[0])
+
+
+def _comm_for(rank, world, port):
+    import torch.distributed as dist
+    from rxla_b200.decoder import Comm
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+
+    def share(data):
+        obj = [data]
+        dist.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    return Comm(rank, world, rank, share)
+
+
+def _p2p_setup_fail_main(rank, world, port, q):
+    import ctypes
+    import torch.distributed as dist
+    from rxla_b200 import _lib
+    try:
+        comm = _comm_for(rank, world, port)
+        lib = _lib.load()
+        # rank 1 asks for a buffer no GPU holds (its cudaMalloc fails); rank 0
+        # for an ordinary one.  Both must come back with an error, having run
+        # the same collectives, and neither may keep the buffers.
+        first = lib.rxla_b200_comm_p2p_enable(comm.handle, (1 << 36) if rank == 1 else 4096)
+        msg = lib.rxla_b200_last_error_message().decode()
+        # the communicator still works: an NCCL all-reduce, then a successful
+        # enable and one peer all-reduce on every rank
+        t = torch.full((16,), float(rank + 1), device="cuda")
+        _lib.call("rxla_b200_allreduce", comm.handle, ctypes.c_void_p(t.data_ptr()), 16, _lib.F32,
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        nccl_ok = bool((t == float(sum(range(1, world + 1)))).all())
+        second = lib.rxla_b200_comm_p2p_enable(comm.handle, 4096)
+        part = torch.full((4096,), float(rank + 1), device="cuda")
+        _lib.call("rxla_b200_p2p_allreduce_f32", comm.handle, ctypes.c_void_p(part.data_ptr()),
+                  None, 4096, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        p2p_ok = bool((part == float(sum(range(1, world + 1)))).all())
+        status = lib.rxla_b200_device_status(1)
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, first, msg, nccl_ok, second, p2p_ok, status, None))
+    except Exception as e:
+        q.put((rank, None, None, None, None, None, None, repr(e)))
+
+
+def test_p2p_enable_when_one_rank_fails():
+    """rxla_b200_comm_p2p_enable when one rank's own set-up fails: every rank
+    still runs the same collectives (handle all-gather, agreement), so none is
+    left waiting; every rank reports an error and keeps no peer buffers, and
+    the communicator stays usable (NCCL all-reduce, a later enable and a peer
+    all-reduce succeed)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from rxla_b200 import _lib
+    for rank, first, msg, nccl_ok, second, p2p_ok, status, err in _spawn(_p2p_setup_fail_main, 2):
+        assert err is None, f"rank {rank}: {err}"
+        print(f"rank {rank}: first enable {first} ({msg})")
+        assert first != _lib.OK, f"rank {rank}: enable should fail when a peer failed"
+        assert nccl_ok and second == _lib.OK and p2p_ok and status == 0, f"rank {rank}"
+
+
+def _wait_timeout_main(rank, world, port, q):
+    import ctypes
+    import time as _time
+    import torch.distributed as dist
+    from rxla_b200 import _lib
+    try:
+        comm = _comm_for(rank, world, port)
+        lib = _lib.load()
+        _lib.call("rxla_b200_comm_p2p_enable", comm.handle, 4096)
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        part = torch.ones(4096, device="cuda")
+        _lib.call("rxla_b200_p2p_allreduce_f32", comm.handle, ctypes.c_void_p(part.data_ptr()),
+                  None, 4096, s)  # both ranks: an ordinary all-reduce first
+        torch.cuda.synchronize()
+        before = lib.rxla_b200_device_status(0)
+        waited, status, answers = 0.0, 0, False
+        if rank == 0:
+            # rank 1 never joins this one: rank 0's flag waits must give up
+            # after the 50 ms budget and the kernel return
+            _lib.call("rxla_b200_set_wait_timeout", 50_000_000)
+            t0 = _time.perf_counter()
+            _lib.call("rxla_b200_p2p_allreduce_f32", comm.handle, ctypes.c_void_p(part.data_ptr()),
+                      None, 4096, s)
+            torch.cuda.synchronize()
+            waited = _time.perf_counter() - t0
+            status = lib.rxla_b200_device_status(1)  # read and clear
+            x = torch.arange(1024, device="cuda", dtype=torch.float32)
+            answers = float((x * 2).sum().item()) == float(1023 * 1024)  # the GPU still runs work
+            _lib.call("rxla_b200_set_wait_timeout", 4_000_000_000)
+        dist.barrier()  # rank 1 leaves its step only here, with nothing in flight
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, before, waited, status, answers, None))
+    except Exception as e:
+        q.put((rank, None, None, None, None, repr(e)))
+
+
+def test_bounded_wait_runs_out_and_reports_deadline_exceeded():
+    """The failure path of the bounded device waits, made on the host: rank 1
+    skips a peer all-reduce that rank 0 enters.  With the wait budget set to
+    50 ms (rxla_b200_set_wait_timeout), rank 0's kernel gives up, records
+    RXLA_B200_DEADLINE_EXCEEDED in the device status word and returns; the
+    GPU keeps running work and the communicator is torn down collectively."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from rxla_b200 import _lib
+    res = _spawn(_wait_timeout_main, 2)
+    for rank, before, waited, status, answers, err in res:
+        assert err is None, f"rank {rank}: {err}"
+        assert before == 0
+    rank, before, waited, status, answers, err = res[0]
+    print(f"rank 0: waited {waited * 1e3:.1f} ms, status {status}")
+    assert status == _lib.DEADLINE_EXCEEDED
+    assert 0.04 <= waited < 2.0
+    assert answers

@@ -71,9 +71,11 @@ def test_config2_shapes(cuda, n, k, m):
     _check(_run(x, w, s, k), x, w, s, k)
 
 
-@pytest.mark.parametrize("m,n,k", [(512, 4096, 4096), (2048, 4096, 4096), (512, 12288, 4096)])
+@pytest.mark.parametrize("n,k", [(4096, 4096), (12288, 4096), (4096, 12288), (6144, 4096)])
+@pytest.mark.parametrize("m", [512, 2048])
 def test_config2_prefill_shapes(cuda, m, n, k):
-    """Config 2's tensor-bound rows (M = 512, 2048) on the tcgen05 GEMM."""
+    """Config 2's tensor-bound rows (M = 512, 2048) on the tcgen05 GEMM: all
+    eight (N,K) x M combinations."""
     x, w, s = oracle.linear_sweep_case(m, n, k, seed=n + k + m)
     _check(_run(x, w, s, k), x, w, s, k)
 
@@ -183,12 +185,23 @@ def test_residual_epilogue(cuda):
 
 
 @pytest.mark.parametrize("m,n,k,group", [(1, 1536, 512, 512), (8, 3000, 1024, 128), (20, 700, 2048, 2048),
-                                         (64, 1024, 1024, 1024)])
+                                         (64, 1024, 1024, 1024),
+                                         # x fragments held in registers (per-channel
+                                         # scales, K a multiple of 1024 up to 4096): the
+                                         # gate/up instance of the 8B decode step
+                                         (1, 12288, 4096, 4096), (8, 6144, 4096, 4096),
+                                         (3, 2000, 3072, 3072), (5, 777, 1024, 1024)])
 def test_swiglu_epilogue(cuda, m, n, k, group):
     x, w, s = _case(m, 2 * n, k, group, seed=m + n)
     xt = torch.from_numpy(x).cuda().bfloat16()
     y = nn.quantized_linear(xt, torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda(), group,
                             epilogue=_lib.EPI_SWIGLU).float().cpu().numpy()
+    _check_swiglu(y, x, w, s, group, n)
+
+
+def _check_swiglu(y, x, w, s, group, n):
+    """silu(bf16(gate)) * bf16(up) within one bf16 ulp of each half plus the
+    fp32 accumulation error, propagated through silu and the product."""
     ref = oracle.w8_linear(x, w, s, group, mode=1).astype(np.float64)
     bound = _bound(x, w, s, group)
     g_ex, u_ex = ref[:, :n], ref[:, n:]
@@ -236,4 +249,41 @@ def test_invalid_sizes_rejected_without_launch(cuda):
     assert b"group_size" in lib.rxla_b200_last_error_message()
     assert lib.rxla_b200_w8a16_linear(None, _lib.BF16, None, None, 64, 0, 8, 64, None, _lib.BF16,
                                       0, None) == _lib.OK  # m == 0 is a no-op
+    assert nn.device_status() == 0
+
+
+@pytest.mark.parametrize("m,n,k,epi", [(1, 6144, 4096, "store"), (1, 12288, 4096, "swiglu"),
+                                       (8, 4096, 4096, "swiglu"), (3, 151936, 4096, "f32"),
+                                       (2, 10240, 5120, "store"), (5, 512, 2048, "residual"),
+                                       (1, 300, 12288, "store")])
+def test_fused_norm_linear(cuda, m, n, k, epi):
+    """rxla_b200_w8a16_norm_linear: the RMSNorm of the f32 residual fused into
+    the linear's prologue, the instances a decode step runs (qkv, gate/up with
+    SwiGLU, the tied head's f32 logits at K = 4096 with x in registers; K = 5120
+    and 12288 through shared memory).  Against the oracle's rms_norm, the bf16
+    cast and the reference-rounding linear."""
+    rows = 2 * n if epi == "swiglu" else n
+    h = oracle.normal(m * k, 300 + m + k, 0.0, 3.0).reshape(m, k)
+    nw = oracle.bf16_round(oracle.normal(k, 301 + k, 1.0, 0.02))
+    w = (oracle.randint(rows * k, 302 + n, -127, 128).reshape(rows, k) + 128).astype(np.uint8)
+    s = oracle.uniform(rows, 303 + n, 1e-3, 1e-2).reshape(rows, 1)
+    x = oracle.bf16_round(oracle.rms_norm(h, nw, 1e-6))
+    ht, nwt = torch.from_numpy(h).cuda(), torch.from_numpy(nw).cuda()
+    wt, st = torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda()
+    if epi == "store":
+        y = nn.quantized_norm_linear(ht, nwt, 1e-6, wt, st, k).float().cpu().numpy()
+        _check(y, x, w, s, k)
+    elif epi == "f32":
+        y = nn.quantized_norm_linear(ht, nwt, 1e-6, wt, st, k, out_dtype=torch.float32).cpu().numpy()
+        _check(y, x, w, s, k, bf16_out=False)
+    elif epi == "residual":
+        r0 = oracle.normal(m * n, 304, 0.0, 1.0).reshape(m, n)
+        rt = torch.from_numpy(r0).cuda()
+        nn.quantized_norm_linear(ht, nwt, 1e-6, wt, st, k, epilogue=_lib.EPI_RESIDUAL_ADD, out=rt)
+        yb = nn.quantized_norm_linear(ht, nwt, 1e-6, wt, st, k).float().cpu().numpy()
+        _check(yb, x, w, s, k)
+        np.testing.assert_array_equal(rt.cpu().numpy(), (r0 + yb).astype(np.float32))
+    else:
+        y = nn.quantized_norm_linear(ht, nwt, 1e-6, wt, st, k, epilogue=_lib.EPI_SWIGLU)
+        _check_swiglu(y.float().cpu().numpy(), x, w, s, k, n)
     assert nn.device_status() == 0
