@@ -430,6 +430,88 @@ int32_t rxla_b200_comm_p2p_enable(rxla_b200_comm* comm, int64_t max_count);
 int32_t rxla_b200_p2p_allreduce_f32(rxla_b200_comm* comm, float* partial, float* residual,
                                     int64_t count, void* stream);
 
+/* ------------------------------------------------- XLA custom-call adapters
+ *
+ * The linear and the decode attention as XLA GPU custom calls with XLA's
+ * legacy untyped ABI, for registration through PJRT's GPU custom-call
+ * extension with api_version 0:
+ *   Plugin::register_gpu_custom_call(name, GpuCustomCallApi::Legacy,
+ *       GpuCustomCallHandlers::execute_only(handler))
+ * (crates/rxla-pjrt/src/runtime.rs:265-270, :395-436), `name` being the
+ * function's own name.  XLA calls a handler with its stream, the device
+ * pointers of the custom call's operands followed by its results, and the
+ * call's backend_config bytes (`opaque`), which must be one of the config
+ * structs below byte for byte (little-endian, this layout, version 1).
+ * The *_status forms take XLA's status-returning signature (custom-call
+ * api_version 2) and report a failure with XlaCustomCallStatusSetFailure,
+ * resolved in the process at run time; the plain forms (api_version 1) have
+ * no failure channel and only set the calling thread's error message.
+ * Handlers allocate nothing: the attention uses the fixed scratch of
+ * rxla_b200_paged_decode_attention_noalloc (same size limit; its first call
+ * on a device should come before any stream capture).
+ */
+#define RXLA_B200_XLA_LINEAR_MAGIC 0x4E4C3852u    /* "R8LN" */
+#define RXLA_B200_XLA_ATTENTION_MAGIC 0x54413852u /* "R8AT" */
+
+/* backend_config of rxla_b200_xla_w8a16_linear(_status) — 64 bytes.
+ * Operands: fused_norm == 0: x [m, k] (x_dtype), weight u8 [n_rows, k],
+ *           scale f32 [n_rows, k / group_size];
+ *           fused_norm != 0: h f32 [m, k], norm_weight f32 [k], weight, scale
+ *           (rxla_b200_w8a16_norm_linear);
+ *           then, for RXLA_B200_EPI_RESIDUAL_ADD only, the residual f32 [m, n].
+ * Result:  y [m, n] (y_dtype).  With the residual epilogue y = residual +
+ *          bf16(dot); y may alias the residual operand (it is copied first
+ *          when it does not). */
+typedef struct rxla_b200_xla_linear_config {
+  uint32_t magic;   /* RXLA_B200_XLA_LINEAR_MAGIC */
+  uint32_t version; /* 1 */
+  int64_t m, n, k, group_size;
+  int32_t x_dtype, y_dtype, epilogue, fused_norm;
+  float eps; /* RMSNorm epsilon (fused_norm) */
+  int32_t reserved;
+} rxla_b200_xla_linear_config;
+
+/* backend_config of rxla_b200_xla_paged_decode_attention(_status) — 64 bytes.
+ * Operands: q bf16 [batch, q_heads*D], k_new / v_new bf16 [batch, kv_heads*D],
+ *           (has_qk_norm) q_norm_weight f32 [D], k_norm_weight f32 [D],
+ *           (rotary_dim > 0) inv_freq f32 [rotary_dim / 2],
+ *           page_table i32 [batch, max_pages_per_seq], ctx_lens i32 [batch],
+ *           k_pages, v_pages bf16 [num_pages, kv_heads, 16, D].
+ * Results:  out bf16 [batch, q_heads*D], ctx_lens i32 [batch] (each advanced
+ *           by the accepted token), k_pages, v_pages (the new row appended).
+ *           The state results should alias their operands (donated buffers,
+ *           KvCache semantics of crates/rxla-core/src/kv_cache.rs:53-112);
+ *           when they do not, the operands are copied into them first. */
+typedef struct rxla_b200_xla_attention_config {
+  uint32_t magic;   /* RXLA_B200_XLA_ATTENTION_MAGIC */
+  uint32_t version; /* 1 */
+  int32_t batch, q_heads, kv_heads, head_dim;
+  int32_t page_size; /* 16 */
+  int32_t max_pages_per_seq;
+  int64_t num_pages;
+  int32_t max_context;
+  int32_t has_qk_norm;
+  int32_t rotary_dim; /* 0: no RoPE */
+  int32_t kv_update;  /* rxla_b200_kv_update */
+  float norm_eps;
+  float scale; /* 0 => 1/sqrt(head_dim) */
+} rxla_b200_xla_attention_config;
+
+void rxla_b200_xla_w8a16_linear(void* stream, void** buffers, const char* opaque,
+                                size_t opaque_len);
+void rxla_b200_xla_w8a16_linear_status(void* stream, void** buffers, const char* opaque,
+                                       size_t opaque_len, void* status);
+void rxla_b200_xla_paged_decode_attention(void* stream, void** buffers, const char* opaque,
+                                          size_t opaque_len);
+void rxla_b200_xla_paged_decode_attention_status(void* stream, void** buffers,
+                                                 const char* opaque, size_t opaque_len,
+                                                 void* status);
+/* Validate a backend_config for the named target before emitting it (the
+ * lowering's compile-time check): RXLA_B200_OK, RXLA_B200_INVALID_ARGUMENT /
+ * RXLA_B200_UNIMPLEMENTED for a bad blob, RXLA_B200_NOT_FOUND for an unknown
+ * target.  No CUDA call. */
+int32_t rxla_b200_xla_check_config(const char* target, const void* opaque, size_t opaque_len);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

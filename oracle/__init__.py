@@ -298,8 +298,12 @@ class Decoder:
     def __init__(self, *, layers, hidden, q_heads, kv_heads, head_dim, intermediate, vocab,
                  rms_eps=1e-6, rope_theta=1e6, embedding_bf16=False, group_size=0,
                  max_batch=1, max_context=256, linear_mode=1):
-        """linear_mode 1: the reference's QuantizedLinear rounding (bf16(W_deq));
-        3: exact q with the scale on the fp32 dot (the CUDA kernel's algebra)."""
+        """linear_mode 1: the reference's QuantizedLinear rounding (bf16(W_deq)),
+        f64 sums, and the reference's F32 tied head (f32 hidden · f32 W_deq);
+        3: exact q with the scale on the fp32 dot;
+        4: the noise-floor model of a bf16-activation, fp32-accumulation
+        implementation: mode 1's rounding points with fp32 running sums, and
+        the tied head on bf16 operands with an fp32 sum."""
         self.cfg = _DecCfg(layers, hidden, q_heads, kv_heads, head_dim, intermediate, vocab,
                            rms_eps, rope_theta, int(embedding_bf16), group_size, max_batch,
                            max_context, linear_mode)

@@ -149,10 +149,10 @@ void oracle_w8_linear(const float* x, int64_t m, int64_t k, const uint8_t* w,
       /* layers.rs:277-288: cast(F32) -> add(-128) -> mul(scale) in f32 */
       for (int64_t c = 0; c < k; ++c) {
         float wd = (float)((int32_t)w[r * k + c] - 128) * scale[r * groups + c / group];
-        wrow[c] = (mode == 1 || mode == 4) ? oracle_bf16_round(wd) : wd;
+        wrow[c] = (mode == 1 || mode == 4 || mode == 5) ? oracle_bf16_round(wd) : wd;
       }
       int64_t mm = 0;
-      if (mode != 4) {
+      if (mode != 4 && mode != 5) {
         /* four tokens at a time, each its own sequential f64 sum (identical
          * results to one token at a time) */
         for (; mm + 4 <= m; mm += 4) {
@@ -172,7 +172,8 @@ void oracle_w8_linear(const float* x, int64_t m, int64_t k, const uint8_t* w,
       }
       for (; mm < m; ++mm) {
         float out;
-        if (mode == 4) { /* mode 1 with an fp32 running sum (noise-floor probe) */
+        if (mode == 4 || mode == 5) { /* mode 1 with an fp32 running sum (noise-floor
+                                         * probe); mode 5 leaves the sum unrounded */
           float facc = 0.0f;
           for (int64_t c = 0; c < k; ++c) facc += xr[mm * k + c] * wrow[c];
           out = facc;
@@ -622,6 +623,43 @@ static void dec_w8(oracle_decoder* dec, const char* prefix, const float* x, int6
                    y);
 }
 
+/* Tied LM head: logits [M, V] of the final-norm output xn [M, H].
+ * The reference (crates/rxla-models/src/qwen3_5/mod.rs:157-173) is an F32
+ * linear: hidden(f32) · ((q - 128) · s in f32)ᵀ with no bf16 cast of either
+ * operand — restated with an f64 sum (mode 0).  linear_mode 4 (the
+ * noise-floor model of a bf16-activation, fp32-accumulation implementation)
+ * rounds both operands to bf16 and sums in fp32 instead (mode 5). */
+static void dec_head(oracle_decoder* dec, const float* xn, int64_t M, float* logits) {
+  const oracle_decoder_config* c = &dec->cfg;
+  int64_t H = c->hidden, V = c->vocab;
+  oracle_param* emb = find_param(dec, "embed_tokens.weight");
+  oracle_param* embs = find_param(dec, "embed_tokens.scale");
+  const int bf16_model = c->linear_mode == 4;
+  if (c->embedding_bf16) {
+    uint16_t* e = (uint16_t*)emb->data;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < V; ++r) {
+      for (int64_t b = 0; b < M; ++b) {
+        if (bf16_model) {
+          float acc = 0.0f;
+          for (int64_t j = 0; j < H; ++j)
+            acc += oracle_bf16_round(xn[b * H + j]) * oracle_bf16_to_f32(e[r * H + j]);
+          logits[b * V + r] = acc;
+        } else {
+          double acc = 0.0;
+          for (int64_t j = 0; j < H; ++j)
+            acc += (double)xn[b * H + j] * (double)oracle_bf16_to_f32(e[r * H + j]);
+          logits[b * V + r] = (float)acc;
+        }
+      }
+    }
+  } else {
+    int64_t group = c->group_size > 0 ? c->group_size : H;
+    oracle_w8_linear(xn, M, H, (const uint8_t*)emb->data, (const float*)embs->data, V, group,
+                     bf16_model ? 5 : 0, logits);
+  }
+}
+
 void oracle_decoder_step(oracle_decoder* dec, const int32_t* tokens, int32_t batch,
                          float* logits, int32_t* next_tokens) {
   const oracle_decoder_config* c = &dec->cfg;
@@ -731,23 +769,7 @@ void oracle_decoder_step(oracle_decoder* dec, const int32_t* tokens, int32_t bat
     for (int64_t i = 0; i < M * H; ++i) h[i] = h[i] + o[i];
   }
   oracle_rms_norm(h, M, H, (float*)find_param(dec, "norm.weight")->data, c->rms_eps, xn);
-  /* tied LM head: bf16(x) · W, fp32 logits (no rounding of the logits) */
-  if (c->embedding_bf16) {
-    uint16_t* e = (uint16_t*)emb->data;
-#pragma omp parallel for schedule(static)
-    for (int64_t r = 0; r < V; ++r) {
-      for (int64_t b = 0; b < M; ++b) {
-        double acc = 0.0;
-        for (int64_t j = 0; j < H; ++j)
-          acc += (double)oracle_bf16_round(xn[b * H + j]) * (double)oracle_bf16_to_f32(e[r * H + j]);
-        logits[b * V + r] = (float)acc;
-      }
-    }
-  } else {
-    int64_t group = c->group_size > 0 ? c->group_size : H;
-    oracle_w8_linear(xn, M, H, (const uint8_t*)emb->data, (const float*)embs->data, V, group, 2,
-                     logits);
-  }
+  dec_head(dec, xn, M, logits);
   for (int64_t b = 0; b < M; ++b) {
     int32_t best = 0;
     float bv = logits[b * V];
@@ -876,20 +898,7 @@ static void decoder_forward_impl(oracle_decoder* dec, int32_t seq, const int32_t
   /* the head on the last row */
   const float* hl = h + (M - 1) * H;
   oracle_rms_norm(hl, 1, H, (float*)find_param(dec, "norm.weight")->data, c->rms_eps, xn);
-  if (c->embedding_bf16) {
-    uint16_t* e = (uint16_t*)emb->data;
-#pragma omp parallel for schedule(static)
-    for (int64_t r = 0; r < V; ++r) {
-      double acc = 0.0;
-      for (int64_t j = 0; j < H; ++j)
-        acc += (double)oracle_bf16_round(xn[j]) * (double)oracle_bf16_to_f32(e[r * H + j]);
-      logits[r] = (float)acc;
-    }
-  } else {
-    int64_t group = c->group_size > 0 ? c->group_size : H;
-    oracle_w8_linear(xn, 1, H, (const uint8_t*)emb->data, (const float*)embs->data, V, group, 2,
-                     logits);
-  }
+  dec_head(dec, xn, 1, logits);
   int32_t best = 0;
   for (int64_t r = 1; r < V; ++r)
     if (logits[r] > logits[best]) best = (int32_t)r;

@@ -49,7 +49,9 @@ void oracle_quantize_w8(const float* w, int64_t n, int64_t k, int64_t group, uin
  *         f64 throughout, f32 out (used to bound the kernel's accumulation error).
  * mode 3: mode 2 with the output rounded to bf16.
  * mode 4: mode 1 with an fp32 running sum in index order (a second valid
- *         implementation of the reference's arithmetic: the noise floor). */
+ *         implementation of the reference's arithmetic: the noise floor).
+ * mode 5: mode 4 without the output rounding (f32 out): bf16 operands, fp32
+ *         sum — the precision of a bf16-activation tied head. */
 void oracle_w8_linear(const float* x, int64_t m, int64_t k, const uint8_t* w,
                       const float* scale, int64_t n, int64_t group, int32_t mode, float* y);
 

@@ -79,6 +79,28 @@ class DecoderConfig(ctypes.Structure):
                                        "max_context", "tp_rank", "tp_size")]
 
 
+XLA_LINEAR_MAGIC = 0x4E4C3852  # RXLA_B200_XLA_LINEAR_MAGIC
+XLA_ATTENTION_MAGIC = 0x54413852  # RXLA_B200_XLA_ATTENTION_MAGIC
+
+
+class XlaLinearConfig(ctypes.Structure):
+    """rxla_b200_xla_linear_config: the custom call's backend_config bytes."""
+    _fields_ = [("magic", ctypes.c_uint32), ("version", ctypes.c_uint32)] + \
+        [(n, ctypes.c_int64) for n in ("m", "n", "k", "group_size")] + \
+        [(n, ctypes.c_int32) for n in ("x_dtype", "y_dtype", "epilogue", "fused_norm")] + \
+        [("eps", ctypes.c_float), ("reserved", ctypes.c_int32)]
+
+
+class XlaAttentionConfig(ctypes.Structure):
+    """rxla_b200_xla_attention_config: the custom call's backend_config bytes."""
+    _fields_ = [("magic", ctypes.c_uint32), ("version", ctypes.c_uint32)] + \
+        [(n, ctypes.c_int32) for n in ("batch", "q_heads", "kv_heads", "head_dim", "page_size",
+                                       "max_pages_per_seq")] + \
+        [("num_pages", ctypes.c_int64)] + \
+        [(n, ctypes.c_int32) for n in ("max_context", "has_qk_norm", "rotary_dim", "kv_update")] + \
+        [("norm_eps", ctypes.c_float), ("scale", ctypes.c_float)]
+
+
 # name -> (restype, argtypes); every symbol declared in include/rxla_b200.h
 _vp, _i32, _i64, _u64, _f32, _sz = (ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                     ctypes.c_uint64, ctypes.c_float, ctypes.c_size_t)
@@ -129,6 +151,11 @@ SIGNATURES = {
     "rxla_b200_decoder_set_context_lengths": (_i32, [_vp, _vp, _i32, _vp]),
     "rxla_b200_decoder_kv_cache": (_i32, [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                           ctypes.POINTER(_i64)]),
+    "rxla_b200_xla_w8a16_linear": (None, [_vp, _vp, _vp, _sz]),
+    "rxla_b200_xla_w8a16_linear_status": (None, [_vp, _vp, _vp, _sz, _vp]),
+    "rxla_b200_xla_paged_decode_attention": (None, [_vp, _vp, _vp, _sz]),
+    "rxla_b200_xla_paged_decode_attention_status": (None, [_vp, _vp, _vp, _sz, _vp]),
+    "rxla_b200_xla_check_config": (_i32, [ctypes.c_char_p, _vp, _sz]),
     "rxla_b200_comm_unique_id": (_i32, [_vp]),
     "rxla_b200_comm_init": (_i32, [_vp, _i32, _i32, _i32, ctypes.POINTER(_vp)]),
     "rxla_b200_comm_destroy": (_i32, [_vp]),

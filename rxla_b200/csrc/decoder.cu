@@ -953,6 +953,9 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
       cudaMemcpy(d->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemset(d->ctx, 0, (size_t)B * 4) != cudaSuccess ||
       cudaMemset(d->ws, 0, need_ws) != cudaSuccess ||
+      // the split-K GEMMs' arrival counters sit at the head of gws and must
+      // start at zero (every launch leaves them zero again)
+      (d->gws && cudaMemset(d->gws, 0, std::max<size_t>(d->gws_bytes, 256)) != cudaSuccess) ||
       cudaMemset(d->arg_count, 0, 256) != cudaSuccess ||
       cudaMemset(d->arena, 0, d->arena_bytes) != cudaSuccess) {
     rxla_b200_decoder_destroy(d);

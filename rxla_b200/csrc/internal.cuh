@@ -52,6 +52,10 @@ int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const f
                   int64_t group_size, int64_t m, int64_t n, int64_t k, void* y, int32_t y_dtype,
                   int32_t epilogue, cudaStream_t stream, const L2Prefetch* next);
 int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream);
+// split-K workspace: a fixed counter region (the same for every shape, so
+// GEMMs sharing a workspace never overlap one another's counters), then the
+// [splits][m][n_rows] f32 partials
+constexpr size_t kGemmCounterBytes = 1u << 20;
 size_t w8_gemm_workspace_bytes(int64_t m, int64_t n_rows, int splits);
 // Decode batches (m <= kGemmDecMaxTokens) run the weights-on-M variant.
 constexpr int64_t kGemmDecMaxTokens = 128;
@@ -62,8 +66,6 @@ bool w8_gemm_dec_applies(int64_t m, int64_t k, int64_t group);
 int64_t w8_gemm_tiles(int64_t m, int64_t n, int64_t k, int64_t group, bool swiglu);
 // split-K depth w8_gemm should be given for this shape (decoder workspace plan)
 int w8_gemm_splits(int64_t m, int64_t n, int64_t k, int64_t group, bool swiglu);
-// split-K arrival counters reserved at the head of the workspace
-int64_t w8_gemm_counter_slots(int64_t m, int64_t n_rows);
 int32_t comm_allreduce_f32(rxla_b200_comm* comm, float* buf, int64_t count, cudaStream_t s);
 // every rank's `bytes` from `in`, concatenated in rank order into `out`
 int32_t comm_allgather_bytes(rxla_b200_comm* comm, const void* in, void* out, int64_t bytes,

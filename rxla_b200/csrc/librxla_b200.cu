@@ -12,3 +12,4 @@
 #include "loader.cu"
 #include "comm.cu"
 #include "noalloc.cu"
+#include "xla_custom_call.cu"

@@ -551,15 +551,14 @@ bool gemm_dec_enabled() {
   return on;
 }
 
-// enough counters for either GEMM's tiles (128-token × 256-row or 128-row)
-int64_t w8_gemm_counter_slots(int64_t m, int64_t n_rows) {
-  return ((m + 31) / 32) * ((n_rows + 127) / 128);
-}
-
+// A split-K workspace is [kGemmCounterBytes of tile counters][partials].  The
+// counter region has the same size for every shape: a decoder's GEMMs share
+// one workspace, and a region sized by the current shape let a GEMM with few
+// tiles write its partials over the counters of one with many tiles (which
+// must stay zero between launches).
 size_t w8_gemm_workspace_bytes(int64_t m, int64_t n_rows, int splits) {
   if (splits <= 1) return 0;
-  const size_t counters = ((size_t)w8_gemm_counter_slots(m, n_rows) * 4 + 255) / 256 * 256;
-  return counters + (size_t)splits * m * n_rows * 4;
+  return kGemmCounterBytes + (size_t)splits * m * n_rows * 4;
 }
 
 int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream) {
@@ -625,9 +624,10 @@ int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.epilogue = a.epilogue;
   p.k_per_split = (int32_t)(kb_per * kBK);
   if (splits > 1) {
-    const size_t counters = ((size_t)w8_gemm_counter_slots(a.m, n_rows) * 4 + 255) / 256 * 256;
+    RXLA_REQUIRE(tiles_m * tiles_n <= (int64_t)(kGemmCounterBytes / 4),
+                 "w8 gemm: too many tiles for the split-K counters");
     p.counters = static_cast<uint32_t*>(a.ws);
-    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(a.ws) + counters);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(a.ws) + kGemmCounterBytes);
   }
   const size_t smem = 1024 /*align*/ + 1024 /*barriers*/ + (size_t)kXStages * kXTile +
                       (size_t)kBStages * kBTile + (size_t)kWStages * kWTile;

@@ -572,9 +572,10 @@ int32_t w8_gemm_dec(const GemmArgs& a, cudaStream_t stream) {
   p.epilogue = a.epilogue;
   p.k_per_split = (int32_t)(kb_per * kBK);
   if (splits > 1) {
-    const size_t counters = ((size_t)w8_gemm_counter_slots(a.m, n_rows) * 4 + 255) / 256 * 256;
+    RXLA_REQUIRE(tiles_n <= (int64_t)(kGemmCounterBytes / 4),
+                 "w8 gemm (decode): too many tiles for the split-K counters");
     p.counters = static_cast<uint32_t*>(a.ws);
-    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(a.ws) + counters);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(a.ws) + kGemmCounterBytes);
   }
   const dim3 grid(1, (unsigned)tiles_n, (unsigned)splits);
   cudaError_t e = N == 32 ? launch<32>(xmap, wmap, p, grid, stream)

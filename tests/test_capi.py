@@ -156,3 +156,84 @@ def test_wait_timeout_range_is_checked_without_cuda():
     assert lib.rxla_b200_set_wait_timeout(60_000_000_001) == _lib.INVALID_ARGUMENT
     assert "[1 ms, 60 s]" in lib.rxla_b200_last_error_message().decode()
     assert lib.rxla_b200_get_wait_timeout(None) == _lib.INVALID_ARGUMENT
+
+
+def _linear_cfg(**kw):
+    c = _lib.XlaLinearConfig()
+    c.magic, c.version = _lib.XLA_LINEAR_MAGIC, 1
+    c.m, c.n, c.k, c.group_size = 4, 64, 128, 128
+    c.x_dtype, c.y_dtype, c.epilogue, c.fused_norm, c.eps = _lib.BF16, _lib.BF16, 0, 0, 1e-6
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def _attn_cfg(**kw):
+    c = _lib.XlaAttentionConfig()
+    c.magic, c.version = _lib.XLA_ATTENTION_MAGIC, 1
+    c.batch, c.q_heads, c.kv_heads, c.head_dim = 2, 8, 2, 64
+    c.page_size, c.max_pages_per_seq, c.num_pages, c.max_context = 16, 4, 8, 64
+    c.has_qk_norm, c.rotary_dim, c.kv_update, c.norm_eps, c.scale = 1, 64, 0, 1e-6, 0.0
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def test_xla_config_layout_matches_header():
+    """The backend_config structs are a wire format: 64 bytes each, the
+    header's field order (checked against the C++ static_asserts' offsets)."""
+    assert ctypes.sizeof(_lib.XlaLinearConfig) == 64
+    assert ctypes.sizeof(_lib.XlaAttentionConfig) == 64
+    assert _lib.XlaLinearConfig.m.offset == 8 and _lib.XlaLinearConfig.x_dtype.offset == 40
+    assert _lib.XlaLinearConfig.eps.offset == 56
+    assert _lib.XlaAttentionConfig.num_pages.offset == 32
+    assert _lib.XlaAttentionConfig.max_context.offset == 40
+    assert _lib.XlaAttentionConfig.scale.offset == 60
+    text = HEADER.read_text()
+    for name, value in (("RXLA_B200_XLA_LINEAR_MAGIC", _lib.XLA_LINEAR_MAGIC),
+                        ("RXLA_B200_XLA_ATTENTION_MAGIC", _lib.XLA_ATTENTION_MAGIC)):
+        m = re.search(rf"#define\s+{name}\s+0x([0-9A-Fa-f]+)u", text)
+        assert m and int(m.group(1), 16) == value
+
+
+def test_xla_check_config_without_cuda():
+    """rxla_b200_xla_check_config: the lowering's compile-time validation of
+    the backend_config bytes (size, magic, version, shape), no CUDA call."""
+    lib = _lib.load()
+    lin, att = b"rxla_b200_xla_w8a16_linear_status", b"rxla_b200_xla_paged_decode_attention"
+    c = _linear_cfg()
+    assert lib.rxla_b200_xla_check_config(lin, ctypes.byref(c), ctypes.sizeof(c)) == _lib.OK
+    assert lib.rxla_b200_xla_check_config(lin, ctypes.byref(c), 56) == _lib.INVALID_ARGUMENT
+    assert "expected 64" in lib.rxla_b200_last_error_message().decode()
+    bad = _linear_cfg(magic=1)
+    assert lib.rxla_b200_xla_check_config(lin, ctypes.byref(bad), 64) == _lib.INVALID_ARGUMENT
+    newer = _linear_cfg(version=2)
+    assert lib.rxla_b200_xla_check_config(lin, ctypes.byref(newer), 64) == _lib.UNIMPLEMENTED
+    for kw in ({"group_size": 48}, {"epilogue": 9}, {"epilogue": _lib.EPI_RESIDUAL_ADD},
+               {"fused_norm": 1}, {"y_dtype": _lib.U8}):
+        c = _linear_cfg(**kw)
+        assert lib.rxla_b200_xla_check_config(lin, ctypes.byref(c), 64) == _lib.INVALID_ARGUMENT, kw
+    c = _linear_cfg(fused_norm=1, x_dtype=_lib.F32)
+    assert lib.rxla_b200_xla_check_config(lin, ctypes.byref(c), 64) == _lib.OK
+    a = _attn_cfg()
+    assert lib.rxla_b200_xla_check_config(att, ctypes.byref(a), 64) == _lib.OK
+    for kw in ({"q_heads": 7}, {"page_size": 32}, {"max_context": 65}, {"rotary_dim": 128},
+               {"kv_update": 5}):
+        a = _attn_cfg(**kw)
+        assert lib.rxla_b200_xla_check_config(att, ctypes.byref(a), 64) == _lib.INVALID_ARGUMENT, kw
+    assert lib.rxla_b200_xla_check_config(b"other_target", ctypes.byref(a), 64) == _lib.NOT_FOUND
+
+
+def test_xla_handler_reports_a_bad_config_without_cuda():
+    """A handler given a bad backend_config launches nothing and leaves the
+    reason as the thread's error message (the status form would also pass it
+    to XlaCustomCallStatusSetFailure when XLA is in the process)."""
+    lib = _lib.load()
+    c = _linear_cfg(magic=7)
+    lib.rxla_b200_xla_w8a16_linear_status(None, None, ctypes.cast(ctypes.byref(c), ctypes.c_void_p),
+                                          64, None)
+    assert "magic" in lib.rxla_b200_last_error_message().decode()
+    a = _attn_cfg(version=3)
+    lib.rxla_b200_xla_paged_decode_attention(None, None, ctypes.cast(ctypes.byref(a), ctypes.c_void_p),
+                                             64)
+    assert "version 3" in lib.rxla_b200_last_error_message().decode()
