@@ -35,7 +35,7 @@ random N(0, 0.02) weights and 151936 logits of standard deviation ~1.3, such
 near-ties are common, so:
 
 * batch 1 uses weights and a prompt whose 33 oracle tokens all have a gap of
-  at least 0.04 (asserted on the oracle side, so the comparison is
+  at least 0.03 (asserted on the oracle side, so the comparison is
   well-posed) and requires all 32 decode tokens and the prompt's token to be
   identical;
 * the batched tests require identical tokens wherever the oracle's gap is at
@@ -58,7 +58,7 @@ CONFIG4_2L = dict(layers=2, hidden=4096, q_heads=32, kv_heads=8, head_dim=128,
                   intermediate=12288, vocab=151936, rms_eps=1e-6, rope_theta=1e6)
 CONFIG5_2L = dict(layers=2, hidden=5120, q_heads=64, kv_heads=8, head_dim=128,
                   intermediate=25600, vocab=151936, rms_eps=1e-6, rope_theta=1e6)
-MAX_ABS, MEAN_ABS, TIE = 2e-2, 2e-3, 4e-2
+MAX_ABS, MEAN_ABS, TIE = 2e-2, 2e-3, 3e-2
 FLOOR_MARGIN = 1.25
 # weights seed and prompt seed of the batch-1 case (every oracle token's
 # top-2 gap >= TIE; chosen by running the oracle, asserted below)
