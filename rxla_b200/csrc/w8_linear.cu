@@ -52,6 +52,7 @@ constexpr int kMaxStages = 8;
 constexpr int kMaxTokens = 8;       // tokens per pass (one n-tile)
 constexpr int kRedFloats = kConsumerWarps * kTileRows * kMaxTokens;
 constexpr int kHeader = 1024;       // barriers + norm partials
+constexpr int kEarlyBytes = 64 * 1024;  // weights requested before griddepcontrol.wait
 
 // Where x comes from.
 enum XMode : int {
@@ -95,7 +96,7 @@ struct Params {
 struct Bars {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
-  uint64_t x_full;
+  uint64_t x_issued;  // every consumer warp has issued its loads of x
   uint64_t grp[2];
   uint64_t ss_free;  // norm: every warp has read a round's sums
   uint64_t epi_full[2];
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       mbar_init(&bars.full[s], 1);
       mbar_init(&bars.empty[s], kConsumerWarps);
     }
-    mbar_init(&bars.x_full, 1);
+    mbar_init(&bars.x_issued, kConsumerWarps);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars.grp[i], kConsumerWarps);
       if (i == 0) mbar_init(&bars.ss_free, kConsumerWarps);
@@ -280,9 +281,18 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
         }
       }
     };
-    // weights do not depend on the previous kernel: fill the ring first
+    // Weights do not depend on the previous kernel: up to kEarlyBytes of them
+    // are requested before griddepcontrol.wait, so the stream starts while
+    // the previous kernel drains.  The rest of the ring waits until every
+    // consumer warp has issued its loads of x (the previous kernel's output,
+    // read after the wait): loads issued behind a full ring of this SM's
+    // weight copies wait for those copies first (~190 KB at this SM's share
+    // of HBM bandwidth is ~4 µs).
     const int pre = min(S, total);
-    for (int it = 0; it < pre; ++it) issue(it, it);
+    const int early = min(pre, max(1, kEarlyBytes / p.stage_bytes));
+    for (int it = 0; it < early; ++it) issue(it, it);
+    if (!mbar_wait(&bars.x_issued, 0)) return;
+    for (int it = early; it < pre; ++it) issue(it, it);
     // bf16 x is copied by the consumers after griddepcontrol.wait: a bulk
     // copy issued here would queue behind the ring's weight copies in this
     // SM's TMA engine (down_proj's 48 row copies delayed x by ~1.7 µs)
@@ -380,9 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
         }
       }
       if (lane == 0) {
-        for (int t = 0; t < p.m; ++t) {
-          p.arg_val[blockIdx.x * kMaxTokens + t] = best_v[t];
-          p.arg_idx[blockIdx.x * kMaxTokens + t] = best_i[t];
+#pragma unroll
+        for (int t = 0; t < kMaxTokens; ++t) {  // compile-time t: best_v / best_i stay in registers
+          if (t < p.m) {
+            p.arg_val[blockIdx.x * kMaxTokens + t] = best_v[t];
+            p.arg_idx[blockIdx.x * kMaxTokens + t] = best_i[t];
+          }
         }
         __threadfence();
       }
@@ -462,6 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       uint4* dst = reinterpret_cast<uint4*>(xs + t * p.x_pitch);
       for (int c = ctid; c < chunks; c += kConsumerWarps * 32) dst[c] = __ldcg(src + c);
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars.x_issued);
     if (!consumer_sync(&bars.grp[1], 0)) return;
   } else {
     const float* xf = static_cast<const float*>(p.x);
@@ -484,6 +499,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     }
     pdl_wait();  // x / h come from the previous kernel
     int round = 0;
+    if (!regs) {  // strided loads below: let the ring fill right away
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.x_issued);
+    }
     for (int t0 = 0; t0 < p.m; t0 += 2, ++round) {
       const int nt = min(2, p.m - t0);
       float4 hv[2][kXV];
@@ -497,9 +516,17 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
             hv[u][i] = (u < nt && c < p.k)
                            ? __ldg(reinterpret_cast<const float4*>(xf + (int64_t)(t0 + u) * p.ldx + c))
                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          }
+        if (round == 0) {  // the first tokens' loads are in flight: the ring may fill up
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.x_issued);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int i = 0; i < kXV; ++i)
             ss[u] += hv[u][i].x * hv[u][i].x + hv[u][i].y * hv[u][i].y +
                      hv[u][i].z * hv[u][i].z + hv[u][i].w * hv[u][i].w;
-          }
       } else if (XMODE == kXNorm) {
         for (int u = 0; u < nt; ++u) {
           const float* row = xf + (int64_t)(t0 + u) * p.ldx;
@@ -531,7 +558,11 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
         // every warp has read the sums before the next round overwrites them
         if (t0 + 2 < p.m && !consumer_sync(&bars.ss_free, round & 1)) return;
       }
-      for (int u = 0; u < nt; ++u) {
+      // u is a compile-time index (a runtime one would move hv to local memory,
+      // which misses the small L1 left beside a full shared-memory carve-out)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (u >= nt) break;
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(xs + (t0 + u) * p.x_pitch);
         if (regs) {
 #pragma unroll
