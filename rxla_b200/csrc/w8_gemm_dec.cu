@@ -52,7 +52,6 @@ constexpr int kHalf = kRows / 2;       // rows per weight TMA box; SwiGLU output
 constexpr int kBK = 128;               // k per stage
 constexpr int kAColsPerStage = kBK / 2;
 constexpr int kWTile = kRows * kBK;    // 16 KB
-constexpr int kACol = 128;             // first TMEM column of the A stages
 
 // Per token width: N = 32 runs two CTAs per SM (8 dequant warps, 256 TMEM
 // columns and ~90 KB of rings each), so that one CTA's pipeline fill and
@@ -64,12 +63,17 @@ struct Shape {
   static constexpr int kCtasPerSm = N <= 32 ? 2 : 1;
   static constexpr int kDeqWarps = N <= 32 ? 8 : 16;
   static constexpr int kThreads = (3 + kDeqWarps) * 32;
-  static constexpr int kAStages = N <= 32 ? 2 : 4;   // bf16 A stages in TMEM, 64 columns each
+  // bf16 A stages in TMEM, 64 columns each, after the N accumulator columns:
+  // as many as the allocation holds (dequant warps waited ~300 cycles per
+  // k-block for a free stage with 2 / 4)
+  static constexpr int kAStages = N <= 32 ? 3 : (N <= 64 ? 6 : 4);
   static constexpr int kTmemCols = N <= 32 ? 256 : 512;
+  static constexpr int kACol = N;  // first TMEM column of the A stages
   // kXStages >= kAStages: a dequant warp waits on the commit barrier of the
   // x slot of k-block it - kAStages, which must not have moved two phases on
-  static constexpr int kXStages = N <= 32 ? 3 : 4;
-  static constexpr int kWStages = N <= 32 ? 4 : (N <= 64 ? 8 : 5);  // u8 tiles, 16 KB each
+  static constexpr int kXStages = N <= 32 ? 3 : (N <= 64 ? 6 : 4);
+  static constexpr int kWStages = N <= 32 ? 4 : (N <= 64 ? 6 : 5);  // u8 tiles, 16 KB each
+  static_assert(kACol + kAStages * kBK / 2 <= kTmemCols, "A stages fit the TMEM allocation");
   static constexpr int kXHalf = N * 64 * 2;          // one 64-column half, bf16 SW128
   static constexpr int kXTile = 2 * kXHalf;
   // kind::f16, bf16 A and B (K-major), f32 accumulate, M = 128, N tokens
@@ -229,7 +233,7 @@ __global__ void __launch_bounds__(Shape<N>::kThreads, Shape<N>::kCtasPerSm)
         const uint64_t bd1 = sw128_desc(x_ring + (size_t)xs * kXTile + kXHalf);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)  // A: 8 TMEM columns per K = 16; B: +32 bytes
-          mma_ts<Shape<N>::kIdesc>(tmem, tmem + kACol + as * kAColsPerStage + 8 * kk,
+          mma_ts<Shape<N>::kIdesc>(tmem, tmem + Shape<N>::kACol + as * kAColsPerStage + 8 * kk,
                                    (kk < 4 ? bd0 : bd1) + 2 * (kk & 3), it > 0 || kk > 0);
         mma_commit(&sm.mma_done[xs]);
       }
@@ -298,7 +302,7 @@ __global__ void __launch_bounds__(Shape<N>::kThreads, Shape<N>::kCtasPerSm)
         deq4<false>(wv1.z, rs, o1[4], o1[5]);
         deq4<false>(wv1.w, rs, o1[6], o1[7]);
       }
-      const uint32_t adst = tmem + lane_base + kACol + as * kAColsPerStage + 8 * u0;
+      const uint32_t adst = tmem + lane_base + Shape<N>::kACol + as * kAColsPerStage + 8 * u0;
       tmem_st8(adst, o0);
       tmem_st8(adst + 8, o1);
       }
