@@ -374,11 +374,14 @@ def run_ours(args, rank, world, local_rank):
             torch.distributed.broadcast_object_list(obj, src=0)
             return obj[0]
         comm = Comm(rank, world, local_rank, share)
-    parity = tp_parity(rank, world, local_rank, comm)
+    # the 8B decoder first: the first decoder on a comm reserves the peer
+    # all-reduce buffers, sized for its own batch x hidden (the parity model's
+    # and config 5's all-reduces fit in them)
     dec = Decoder(**cfg, embedding_dtype="u8", max_batch=b64, max_context=max_ctx,
                   device=local_rank, comm=comm.handle if comm else None, tp_rank=rank,
                   tp_size=world)
     dec.init_synthetic(1234)
+    parity = tp_parity(rank, world, local_rank, comm)
     tout = ctypes.c_void_p(dec.tokens_out_ptr)
     prompt = torch.randint(0, cfg["vocab"], (PROMPT,), dtype=torch.int32, device=dev,
                            generator=torch.Generator(device=dev).manual_seed(1))

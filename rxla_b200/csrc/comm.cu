@@ -201,6 +201,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(const Args a) {
 // (residual false) or out += bf16(Σ partial) (residual true).  Falls back to
 // NCCL + a residual kernel when the comm has no peer buffers.
 bool comm_has_p2p(const rxla_b200_comm* c) { return c && c->p2p_local != nullptr; }
+int64_t comm_p2p_capacity(const rxla_b200_comm* c) { return comm_has_p2p(c) ? c->p2p.cap : 0; }
 
 int32_t comm_p2p_allreduce(rxla_b200_comm* c, const float* partial, float* out, int64_t count,
                            bool residual, cudaStream_t s) {

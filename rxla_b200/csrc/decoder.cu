@@ -276,6 +276,7 @@ struct rxla_b200_decoder {
   rxla_b200_decoder_config cfg;
   int device = 0;
   rxla_b200_comm* comm = nullptr;
+  bool use_p2p = false;  // row-parallel all-reduces over the comm's peer buffers
   // shard sizes
   int hq = 0, hkv = 0, inter = 0, vocab = 0, groups_h = 1, groups_i = 1, groups_o = 1;
   int64_t qkv_rows = 0;
@@ -459,7 +460,7 @@ static int32_t tp_residual(rxla_b200_decoder* d, int batch, cudaStream_t s, floa
   const int64_t H = d->cfg.hidden;
   // one-shot peer all-reduce fused with the residual add (its buffers hold
   // max_batch rows), else NCCL + a kernel
-  if (p2p && comm_has_p2p(d->comm)) return comm_p2p_allreduce(d->comm, part, h, batch * H, true, s);
+  if (p2p && d->use_p2p) return comm_p2p_allreduce(d->comm, part, h, batch * H, true, s);
   int32_t st = comm_allreduce_f32(d->comm, part, batch * H, s);
   if (st) return st;
   cudaError_t e = launch_pdl(residual_add_kernel, dim3(std::max(1, (int)((batch * H + 1023) / 1024))),
@@ -973,6 +974,11 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
     if (!(pv && pv[0] == '0') &&
         rxla_b200_comm_p2p_enable(comm, (int64_t)c.max_batch * H) != RXLA_B200_OK)
       cudaGetLastError();  // NCCL path
+    // the peer buffers may have been enabled earlier, by a decoder with a
+    // smaller batch or width: this decoder uses them only when its
+    // all-reduces fit (the same answer on every rank, whose decoders and
+    // comm capacity are the same)
+    d->use_p2p = comm_p2p_capacity(comm) >= (int64_t)c.max_batch * H;
   }
   *out = d;
   return RXLA_B200_OK;

@@ -72,6 +72,8 @@ int32_t comm_allgather_bytes(rxla_b200_comm* comm, const void* in, void* out, in
                              cudaStream_t s);
 int32_t comm_world(const rxla_b200_comm* comm);
 bool comm_has_p2p(const rxla_b200_comm* comm);
+// f32 elements the comm's peer buffers hold per rank (0: not enabled)
+int64_t comm_p2p_capacity(const rxla_b200_comm* comm);
 // out = Σ partial over ranks (residual false) or out += bf16(Σ partial)
 int32_t comm_p2p_allreduce(rxla_b200_comm* comm, const float* partial, float* out, int64_t count,
                            bool residual, cudaStream_t s);
