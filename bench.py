@@ -788,6 +788,8 @@ def profile_case(what: str):
     gemm:      config-2 tensor-bound row, M=2048 N=4096 K=4096 on the tcgen05 GEMM, 3 launches
     step:      the config-4 decoder after a 256-token prompt, 2 decode steps inside
                the NVTX range "profile"
+    step2l:    a 2-layer config-4-shaped decoder at batch 1, 256-token context, 2 steps
+               inside "profile"
     step64:    config 4 at batch 64 (2048 context), 1 step inside "profile"
     step5:     config 5 (32B shape) at batch 32 (4096 context), 1 step inside "profile"
     gemmdec:   a 2-layer config-4-shaped decoder at batch 64, 1 step (the decode-batch
@@ -825,6 +827,24 @@ def profile_case(what: str):
         s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         tout = ctypes.c_void_p(dec.tokens_out_ptr)
         for _ in range(256):
+            _lib.call("rxla_b200_decoder_step", dec.handle, tout, 1, tout, None, s)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("profile")
+        for _ in range(2):
+            _lib.call("rxla_b200_decoder_step", dec.handle, tout, 1, tout, None, s)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        dec.close()
+    elif what == "step2l":
+        # a 2-layer config-4-shaped decoder at batch 1 (256-token context),
+        # 2 decode steps inside the NVTX range "profile" (~1 GB on the device)
+        from rxla_b200.decoder import Decoder
+        dec = Decoder(**dict(CONFIG4, layers=2), embedding_dtype="u8", max_batch=1, max_context=320)
+        dec.init_synthetic(1)
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        dec.set_context_lengths([256], s)
+        tout = ctypes.c_void_p(dec.tokens_out_ptr)
+        for _ in range(3):
             _lib.call("rxla_b200_decoder_step", dec.handle, tout, 1, tout, None, s)
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("profile")
@@ -920,8 +940,8 @@ def main():
     ap.add_argument("--no-kernels", action="store_true",
                     help="skip the config-2 sweep and config-3 attention keys (N = 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "gemmdec", "step", "step64", "step5",
-                                          "prefill", "attention", "attention1"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "head", "gemm", "gemmdec", "step", "step2l", "step64",
+                                          "step5", "prefill", "attention", "attention1"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.profile:
