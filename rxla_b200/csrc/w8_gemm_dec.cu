@@ -136,6 +136,86 @@ __device__ __forceinline__ void tmem_ld8(uint32_t addr, float (&v)[8]) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// The tile's last split CTA: y[m0 + t, out0 + c] = epilogue(Σ_s partial_s)
+// for its tt_n tokens and 4·nq columns, the sums in split order.  Thread d of
+// `stride` takes EU float4 elements per round with SU splits of each (and the
+// residual row) in flight, so a round costs one L2 round trip.
+template <int EU, int SU, bool SWIGLU>
+__device__ __forceinline__ void split_reduce(const Params& p, int d, int stride, int m0, int tt_n,
+                                             int nq, int out0, bool vec_y, int nsplit) {
+  const int total = tt_n * nq;
+  const bool resid = !SWIGLU && p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD;
+  for (int e0 = d; e0 < total; e0 += EU * stride) {
+    float4 g[EU], u[EU], hres[EU];
+    int64_t off[EU], src[EU];
+#pragma unroll
+    for (int uu = 0; uu < EU; ++uu) {
+      const int e = min(e0 + uu * stride, total - 1);
+      const int tt = m0 + e / nq, c4 = (e % nq) * 4;
+      off[uu] = (int64_t)tt * p.ldy + out0 + c4;
+      src[uu] = (int64_t)tt * p.n_rows + out0 + c4;
+      g[uu] = make_float4(0.f, 0.f, 0.f, 0.f);
+      u[uu] = g[uu];
+      if (resid && vec_y) hres[uu] = *reinterpret_cast<const float4*>(static_cast<float*>(p.y) + off[uu]);
+    }
+    for (int sp0 = 0; sp0 < nsplit; sp0 += SU) {
+      float4 gv[EU][SU], uv[EU][SWIGLU ? SU : 1];
+#pragma unroll
+      for (int uu = 0; uu < EU; ++uu)
+#pragma unroll
+        for (int jj = 0; jj < SU; ++jj)
+          if (sp0 + jj < nsplit) {
+            const float* row = p.ws + (int64_t)(sp0 + jj) * p.m * p.n_rows + src[uu];
+            gv[uu][jj] = __ldcg(reinterpret_cast<const float4*>(row));
+            if (SWIGLU) uv[uu][jj] = __ldcg(reinterpret_cast<const float4*>(row + p.n));
+          }
+#pragma unroll
+      for (int uu = 0; uu < EU; ++uu)
+#pragma unroll
+        for (int jj = 0; jj < SU; ++jj)
+          if (sp0 + jj < nsplit) {
+            g[uu].x += gv[uu][jj].x; g[uu].y += gv[uu][jj].y;
+            g[uu].z += gv[uu][jj].z; g[uu].w += gv[uu][jj].w;
+            if (SWIGLU) {
+              u[uu].x += uv[uu][jj].x; u[uu].y += uv[uu][jj].y;
+              u[uu].z += uv[uu][jj].z; u[uu].w += uv[uu][jj].w;
+            }
+          }
+    }
+#pragma unroll
+    for (int uu = 0; uu < EU; ++uu) {
+      if (e0 + uu * stride >= total) break;
+      const float gg[4] = {g[uu].x, g[uu].y, g[uu].z, g[uu].w};
+      if (SWIGLU) {
+        const float ug[4] = {u[uu].x, u[uu].y, u[uu].z, u[uu].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float rr = silu(bf16_round(gg[i])) * bf16_round(ug[i]);
+          if (p.y_f32) static_cast<float*>(p.y)[off[uu] + i] = rr;
+          else static_cast<__nv_bfloat16*>(p.y)[off[uu] + i] = __float2bfloat16_rn(rr);
+        }
+      } else if (resid) {
+        float* yy = static_cast<float*>(p.y) + off[uu];
+        if (vec_y) {
+          float4 h4 = hres[uu];
+          h4.x += bf16_round(gg[0]); h4.y += bf16_round(gg[1]);
+          h4.z += bf16_round(gg[2]); h4.w += bf16_round(gg[3]);
+          *reinterpret_cast<float4*>(yy) = h4;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) yy[i] = yy[i] + bf16_round(gg[i]);
+        }
+      } else if (p.y_f32) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) static_cast<float*>(p.y)[off[uu] + i] = gg[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) static_cast<__nv_bfloat16*>(p.y)[off[uu] + i] = __float2bfloat16_rn(gg[i]);
+      }
+    }
+  }
+}
+
 template <int N>
 __global__ void __launch_bounds__(Shape<N>::kThreads, Shape<N>::kCtasPerSm)
     w8_gemm_dec_kernel(const __grid_constant__ CUtensorMap xmap,
@@ -352,55 +432,10 @@ __global__ void __launch_bounds__(Shape<N>::kThreads, Shape<N>::kCtasPerSm)
         const int nout = swiglu ? min(kHalf, p.n - out0) : min(kRows, p.n - out0);
         const int nq = nout / 4;  // split-K runs only for n % 64 == 0
         const bool vec_y = (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && p.ldy % 4 == 0;
-        for (int e = d; e < tt_n * nq; e += kDeqWarps * 32) {
-          const int tt = m0 + e / nq, c4 = (e % nq) * 4;
-          float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
-          for (int sp0 = 0; sp0 < nsplit; sp0 += 4) {
-            float4 gv[4], uv[4];
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              if (sp0 + jj < nsplit) {
-                const float* row = p.ws + ((int64_t)(sp0 + jj) * p.m + tt) * p.n_rows;
-                gv[jj] = __ldcg(reinterpret_cast<const float4*>(row + out0 + c4));
-                if (swiglu) uv[jj] = __ldcg(reinterpret_cast<const float4*>(row + p.n + out0 + c4));
-              }
-            }
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              if (sp0 + jj < nsplit) {
-                g.x += gv[jj].x; g.y += gv[jj].y; g.z += gv[jj].z; g.w += gv[jj].w;
-                if (swiglu) { u.x += uv[jj].x; u.y += uv[jj].y; u.z += uv[jj].z; u.w += uv[jj].w; }
-              }
-            }
-          }
-          const float gg[4] = {g.x, g.y, g.z, g.w}, uu[4] = {u.x, u.y, u.z, u.w};
-          const int64_t off = (int64_t)tt * p.ldy + out0 + c4;
-          if (swiglu) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float rr = silu(bf16_round(gg[i])) * bf16_round(uu[i]);
-              if (p.y_f32) static_cast<float*>(p.y)[off + i] = rr;
-              else static_cast<__nv_bfloat16*>(p.y)[off + i] = __float2bfloat16_rn(rr);
-            }
-          } else if (p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD) {
-            float* yy = static_cast<float*>(p.y) + off;
-            if (vec_y) {
-              float4 h4 = *reinterpret_cast<float4*>(yy);
-              h4.x += bf16_round(gg[0]); h4.y += bf16_round(gg[1]);
-              h4.z += bf16_round(gg[2]); h4.w += bf16_round(gg[3]);
-              *reinterpret_cast<float4*>(yy) = h4;
-            } else {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) yy[i] = yy[i] + bf16_round(gg[i]);
-            }
-          } else if (p.y_f32) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) static_cast<float*>(p.y)[off + i] = gg[i];
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) static_cast<__nv_bfloat16*>(p.y)[off + i] = __float2bfloat16_rn(gg[i]);
-          }
-        }
+        if (swiglu)
+          split_reduce<(N <= 32 ? 1 : 2), 2, true>(p, d, kDeqWarps * 32, m0, tt_n, nq, out0, vec_y, nsplit);
+        else
+          split_reduce<(N <= 32 ? 1 : 2), 4, false>(p, d, kDeqWarps * 32, m0, tt_n, nq, out0, vec_y, nsplit);
         if (d == 0) p.counters[blockIdx.y * gridDim.x + blockIdx.x] = 0u;
       }
     } else if (swiglu) {
