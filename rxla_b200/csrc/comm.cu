@@ -20,6 +20,7 @@ namespace p2p {
 constexpr int kMaxRanks = 8;
 constexpr int kChunk = 2048;  // floats of the all-reduce per CTA
 constexpr int kThreads = 256;
+constexpr int kFusedCtas = 1024;  // flag slots for grids of one CTA per SM
 
 // One rank's IPC-shared all-reduce buffer: two slots of [world][cap] f32
 // partials (alternating per call, so a rank may start the next all-reduce
@@ -95,16 +96,6 @@ static int32_t nccl_fail(ncclResult_t r, const char* what) {
 }  // namespace comm
 
 namespace p2p {
-
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 
 // CTA c owns floats [c·kChunk, (c+1)·kChunk): it pushes this rank's partial of
 // that range into slot (e & 1), row `rank`, of every rank's buffer (NVLink
@@ -202,6 +193,19 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(const Args a) {
 // NCCL + a residual kernel when the comm has no peer buffers.
 bool comm_has_p2p(const rxla_b200_comm* c) { return c && c->p2p_local != nullptr; }
 int64_t comm_p2p_capacity(const rxla_b200_comm* c) { return comm_has_p2p(c) ? c->p2p.cap : 0; }
+
+bool comm_p2p_view(const rxla_b200_comm* c, P2pView* out) {
+  static_assert(kP2pMaxRanks == p2p::kMaxRanks, "peer buffer layout");
+  if (!comm_has_p2p(c) || !out) return false;
+  *out = P2pView{};
+  for (int q = 0; q < c->world; ++q) out->peer[q] = c->p2p_peer[q];
+  out->epoch = c->p2p_epoch;
+  out->cap = c->p2p.cap;
+  out->rank = c->rank;
+  out->world = c->world;
+  out->max_ctas = c->p2p.max_ctas;
+  return true;
+}
 
 int32_t comm_p2p_allreduce(rxla_b200_comm* c, const float* partial, float* out, int64_t count,
                            bool residual, cudaStream_t s) {
@@ -320,7 +324,9 @@ extern "C" int32_t rxla_b200_comm_p2p_enable(rxla_b200_comm* c, int64_t max_coun
   int32_t* agree = reinterpret_cast<int32_t*>(xfer + p2p::kMaxRanks * sizeof(p2p::Offer));
   p2p::Layout L;
   L.cap = (max_count + 3) / 4 * 4;
-  L.max_ctas = (int)((L.cap + p2p::kChunk - 1) / p2p::kChunk);
+  // flags for the all-reduce kernel's CTAs and for the row-parallel GEMV
+  // epilogue's (one CTA per SM)
+  L.max_ctas = std::max((int)((L.cap + p2p::kChunk - 1) / p2p::kChunk), p2p::kFusedCtas);
   uint8_t* local = nullptr;
   uint64_t* epoch = nullptr;
   // 1. this rank's own set-up (no collective yet)

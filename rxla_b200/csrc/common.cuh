@@ -206,6 +206,18 @@ __device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int cta,
   }
 }
 
+// System-scope flag accesses of the peer all-reduces (flags live in
+// IPC-mapped memory that other GPUs write over NVLink).
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // Programmatic dependent launch: wait for the previous grid's results, and
 // allow the next grid to start its prologue.  Every kernel of this library
 // triggers its dependents only after its own griddepcontrol.wait, so when a

@@ -277,6 +277,10 @@ struct rxla_b200_decoder {
   int device = 0;
   rxla_b200_comm* comm = nullptr;
   bool use_p2p = false;  // row-parallel all-reduces over the comm's peer buffers
+  // batch <= 8: the all-reduce runs in the o_proj / down_proj GEMV epilogue
+  // (RXLA_B200_TP_FUSED=1; otherwise a separate all-reduce kernel after each)
+  bool tp_fused = false;
+  rxla::P2pView p2p{};
   // shard sizes
   int hq = 0, hkv = 0, inter = 0, vocab = 0, groups_h = 1, groups_i = 1, groups_o = 1;
   int64_t qkv_rows = 0;
@@ -654,6 +658,11 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
       st = w8_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd, d->h,
                      RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s, &to_gu);
       if (st) return st;
+    } else if (d->tp_fused) {
+      // o_proj partials all-reduced in the GEMV's epilogue, added to h
+      st = w8_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd, d->h,
+                     RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s, &to_gu, &d->p2p);
+      if (st) return st;
     } else {
       st = rxla_b200_w8a16_linear(d->att, RXLA_B200_BF16, L.wo, L.so, d->group_o, batch, H, qd,
                                   d->part, RXLA_B200_F32, RXLA_B200_EPI_STORE, s);
@@ -674,6 +683,10 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
     if (!tp) {
       st = w8_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H, d->inter, d->h,
                      RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s, &to_next);
+      if (st) return st;
+    } else if (d->tp_fused) {
+      st = w8_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H, d->inter, d->h,
+                     RXLA_B200_F32, RXLA_B200_EPI_RESIDUAL_ADD, s, &to_next, &d->p2p);
       if (st) return st;
     } else {
       st = rxla_b200_w8a16_linear(d->act, RXLA_B200_BF16, L.wd, L.sd, d->group_i, batch, H,
@@ -979,6 +992,8 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
     // all-reduces fit (the same answer on every rank, whose decoders and
     // comm capacity are the same)
     d->use_p2p = comm_p2p_capacity(comm) >= (int64_t)c.max_batch * H;
+    const char* fv = getenv("RXLA_B200_TP_FUSED");
+    d->tp_fused = d->use_p2p && comm_p2p_view(comm, &d->p2p) && fv && fv[0] == '1';
   }
   *out = d;
   return RXLA_B200_OK;

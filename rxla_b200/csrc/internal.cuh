@@ -47,10 +47,29 @@ struct GemmArgs {
 };
 
 int32_t w8_norm_linear(const NormLinearArgs& a, cudaStream_t stream);
-// rxla_b200_w8a16_linear with an L2 prefetch of the next kernel's first bytes
+
+// A comm's one-shot peer all-reduce buffers as a kernel sees them: every
+// rank's buffer mapped here (two slots of [8][cap] f32 partials, then
+// [8][max_ctas] u64 arrival flags) and this rank's per-CTA epoch counters.
+constexpr int kP2pMaxRanks = 8;
+struct P2pView {
+  uint8_t* peer[kP2pMaxRanks];
+  uint64_t* epoch;  // [max_ctas]
+  int64_t cap;      // floats per (slot, rank)
+  int32_t rank, world, max_ctas;
+};
+// false when the comm has no peer buffers
+bool comm_p2p_view(const rxla_b200_comm* c, P2pView* out);
+
+// rxla_b200_w8a16_linear with an L2 prefetch of the next kernel's first bytes.
+// With `tp` (a row-parallel linear of a tensor-parallel decoder: epilogue
+// RESIDUAL_ADD, f32 y = the residual, one pass of at most 8 tokens) the
+// kernel's epilogue all-reduces the partial dot across the ranks through the
+// peer buffers and adds bf16(Σ over ranks, in rank order) into y.
 int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const float* scale,
                   int64_t group_size, int64_t m, int64_t n, int64_t k, void* y, int32_t y_dtype,
-                  int32_t epilogue, cudaStream_t stream, const L2Prefetch* next);
+                  int32_t epilogue, cudaStream_t stream, const L2Prefetch* next,
+                  const P2pView* tp = nullptr);
 int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream);
 // split-K workspace: a fixed counter region (the same for every shape, so
 // GEMMs sharing a workspace never overlap one another's counters), then the

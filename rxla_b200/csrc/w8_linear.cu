@@ -91,6 +91,10 @@ struct Params {
   int32_t x_pitch;      // bytes of one resident bf16 token row of x
   int32_t stage_bytes;  // 16 rows × kc
   L2Prefetch next;      // the following kernel's first bytes (last pass only)
+  // row-parallel all-reduce in the epilogue (tp.world > 1, RESIDUAL_ADD into
+  // the f32 residual y): partials to every rank's peer buffer, then the sum
+  // over ranks in rank order once the same CTA of every rank has pushed
+  P2pView tp;
 };
 
 struct Bars {
@@ -314,6 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
     pdl_wait();  // y (or the residual it adds into) may be used by the previous kernel
     pdl_launch_dependents();
     const bool argmax = p.epilogue == kEpiArgmax;
+    // tensor parallelism: this CTA's call number on its flag slot, read after
+    // the wait (the previous user of the slot, two row-parallel linears ago,
+    // has completed), and the data slot it selects
+    const bool tp = p.tp.world > 1;
+    const uint64_t tp_e = tp ? p.tp.epoch[blockIdx.x] + 1 : 0;
+    const int64_t tp_off = tp ? ((int64_t)(tp_e & 1) * kP2pMaxRanks + p.tp.rank) * p.tp.cap : 0;
     float best_v[kMaxTokens];
     int best_i[kMaxTokens];
 #pragma unroll
@@ -333,7 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       for (int tt = 0; tt < kPerLane; ++tt) {
         const int idx = lane + 32 * tt;
         const int row = idx % out_rows, tok = idx / out_rows;
-        resid[tt] = (!SWIGLU && p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD && row < nr && tok < p.m)
+        resid[tt] = (!SWIGLU && !tp && p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD && row < nr &&
+                     tok < p.m)
                         ? static_cast<const float*>(p.y)[(int64_t)tok * p.ldy + r0 + row]
                         : 0.0f;
       }
@@ -365,7 +376,13 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
               best_i[t] = out_col;
             }
         } else if (p.epilogue == RXLA_B200_EPI_RESIDUAL_ADD) {
-          static_cast<float*>(p.y)[o] = resid[tt] + bf16_round(v);
+          if (tp) {
+            // this rank's partial of (token, column) into every rank's slot
+            for (int q2 = 0; q2 < p.tp.world; ++q2)
+              reinterpret_cast<float*>(p.tp.peer[q2])[tp_off + o] = v;
+          } else {
+            static_cast<float*>(p.y)[o] = resid[tt] + bf16_round(v);
+          }
         } else if (p.y_f32) {
           static_cast<float*>(p.y)[o] = v;
         } else {
@@ -374,6 +391,52 @@ __global__ void __launch_bounds__(kThreads, 1) w8_skinny_kernel(const Params p) 
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.epi_free[b2]);
+    }
+    if (tp) {
+      // Every partial of this CTA's rows is in every rank's slot: publish the
+      // call number in each rank's flag [rank][cta] (a system-scope fence
+      // first, cumulative over the warp's stores), wait (bounded) until every
+      // rank's flag [q][cta] here reached it, then sum the ranks' rows in rank
+      // order 0..world-1 — the same bits on every rank — and add bf16(sum) to
+      // the residual.  The same CTA index covers the same rows on every rank
+      // (same grid, same row split).
+      const size_t data_bytes = (size_t)2 * kP2pMaxRanks * p.tp.cap * 4;
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_system();
+        for (int q2 = 0; q2 < p.tp.world; ++q2)
+          st_relaxed_sys(reinterpret_cast<uint64_t*>(p.tp.peer[q2] + data_bytes) +
+                             (int64_t)p.tp.rank * p.tp.max_ctas + blockIdx.x,
+                         tp_e);
+      }
+      bool arrived = true;
+      if (lane < p.tp.world) {
+        const uint64_t* flag = reinterpret_cast<const uint64_t*>(p.tp.peer[p.tp.rank] + data_bytes) +
+                               (int64_t)lane * p.tp.max_ctas + blockIdx.x;
+        if (ld_acquire_sys(flag) < tp_e) {
+          const unsigned long long limit = wait_timeout_ns();
+          const uint64_t t0 = globaltimer();
+          while (ld_acquire_sys(flag) < tp_e) {
+            if (globaltimer() - t0 > limit) {
+              record_device_error(RXLA_B200_DEADLINE_EXCEEDED);
+              arrived = false;
+              break;
+            }
+          }
+        }
+      }
+      if (!__all_sync(0xffffffffu, arrived)) return;
+      const float* rows = reinterpret_cast<const float*>(p.tp.peer[p.tp.rank]) +
+                          (int64_t)(tp_e & 1) * kP2pMaxRanks * p.tp.cap;
+      const int nrow = r_end - r_begin;
+      for (int idx = lane; idx < nrow * p.m; idx += 32) {
+        const int64_t o = (int64_t)(idx / nrow) * p.ldy + r_begin + idx % nrow;
+        float acc = __ldcv(rows + o);
+        for (int q2 = 1; q2 < p.tp.world; ++q2) acc += __ldcv(rows + (int64_t)q2 * p.tp.cap + o);
+        float* hh = static_cast<float*>(p.y) + o;
+        *hh = *hh + bf16_round(acc);
+      }
+      if (lane == 0) p.tp.epoch[blockIdx.x] = tp_e;
     }
     if (argmax) {
       // per-CTA best of each row, then the last CTA to arrive picks the token
@@ -936,7 +999,8 @@ static_assert(kArgmaxEpilogue == w8::kEpiArgmax, "argmax epilogue code");
 namespace rxla {
 int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const float* scale,
                   int64_t group_size, int64_t m, int64_t n, int64_t k, void* y, int32_t y_dtype,
-                  int32_t epilogue, cudaStream_t stream, const L2Prefetch* next) {
+                  int32_t epilogue, cudaStream_t stream, const L2Prefetch* next,
+                  const P2pView* tp) {
   RXLA_REQUIRE(m >= 0 && n >= 0 && k > 0, "w8a16_linear: m, n must be >= 0 and k > 0");
   RXLA_REQUIRE(group_size > 0 && k % group_size == 0,
                "w8a16_linear: group_size must be positive and divide k (layers.rs:266-275)");
@@ -990,6 +1054,15 @@ int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const f
   }
   const int xmode = p.x_f32 ? w8::kXF32 : w8::kXBf16;
   const int64_t step = fast ? per_pass : 32;
+  if (tp && tp->world > 1) {
+    // the row-parallel all-reduce runs in the epilogue of one fast pass; the
+    // flags are per CTA of the grid, the same grid on every rank
+    RXLA_REQUIRE(fast && m <= per_pass && epilogue == RXLA_B200_EPI_RESIDUAL_ADD &&
+                     tp->world <= kP2pMaxRanks && tp->rank >= 0 && tp->rank < tp->world &&
+                     m * n <= tp->cap && w8::grid_for(p) <= tp->max_ctas,
+                 "w8a16_linear: the fused all-reduce needs one fast pass within the peer buffers");
+    p.tp = *tp;
+  }
   for (int64_t m0 = 0; m0 < m; m0 += step) {
     p.m = (int32_t)std::min<int64_t>(step, m - m0);
     p.x = static_cast<const uint8_t*>(x) + m0 * k * xe;
