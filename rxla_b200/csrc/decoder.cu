@@ -278,7 +278,8 @@ struct rxla_b200_decoder {
   rxla_b200_comm* comm = nullptr;
   bool use_p2p = false;  // row-parallel all-reduces over the comm's peer buffers
   // batch <= 8: the all-reduce runs in the o_proj / down_proj GEMV epilogue
-  // (RXLA_B200_TP_FUSED=1; otherwise a separate all-reduce kernel after each)
+  // (RXLA_B200_TP_FUSED=0: a separate all-reduce kernel after each; TP-2
+  // batch-1 decode 419.6 -> 435.9 tok/s fused)
   bool tp_fused = false;
   rxla::P2pView p2p{};
   // shard sizes
@@ -993,7 +994,7 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
     // comm capacity are the same)
     d->use_p2p = comm_p2p_capacity(comm) >= (int64_t)c.max_batch * H;
     const char* fv = getenv("RXLA_B200_TP_FUSED");
-    d->tp_fused = d->use_p2p && comm_p2p_view(comm, &d->p2p) && fv && fv[0] == '1';
+    d->tp_fused = d->use_p2p && comm_p2p_view(comm, &d->p2p) && !(fv && fv[0] == '0');
   }
   *out = d;
   return RXLA_B200_OK;
