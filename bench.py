@@ -665,11 +665,14 @@ def gemv_roofline(dec, cfg, dev, stream, lib, tp=1, rank=0):
             "timing": "CUDA events around 10 replays of one graph of the step's linears"}
 
 
-# DRAM bytes (read + write) per algorithmic byte of the step's W8 linears, from
-# the ncu capture summarised in profiles/decode_step_launches_config4.md
-TRAFFIC_RATIO = 626.74 / 623.25
-TRAFFIC_NOTE = ("per launch: algorithmic bytes x the measured dram/algorithmic ratio of the "
-                "W8 linear ncu capture")
+# DRAM bytes (read + write) per algorithmic byte of the W8 linears of a decode
+# step, from the ncu capture without cache flushing summarised in
+# profiles/w8_linear_dram_config4_b1.md (2-layer config-4-width decoder, the
+# second of two steps: 946.5 MB over 1010.1 MB of algorithmic bytes; each
+# kernel's count includes the next kernel's weights it pulls into L2)
+TRAFFIC_RATIO = 946.5 / 1010.1
+TRAFFIC_NOTE = ("per launch: algorithmic bytes x the measured DRAM / algorithmic ratio of the "
+                "step's W8 linears (ncu, caches not flushed)")
 
 
 def prefill_flops(cfg, tokens):
