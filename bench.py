@@ -687,12 +687,14 @@ def prefill_flops(cfg, tokens):
 
 
 def config2_sweep(dev):
-    """BASELINE config 2 through rxla_b200_w8a16_linear: x bf16 N(0,1) [M,K],
-    int8 weights U{-127..127} stored +128 [N,K], f32 per-row scales
-    U[1e-3,1e-2], bf16 out.  Each (N,K) cycles through enough weight copies to
-    exceed 2x L2 (126 MB) between launches; 3 warm-up launches, then 20 timed
-    with CUDA events.  Algorithmic bytes N·K + 4·N + 2·M·K + 2·M·N, FLOPs
-    2·M·N·K; frac = max(t_mem, t_flop) at the measured peaks / measured time."""
+    """BASELINE config 2 through rxla_b200_w8a16_linear_ws (the linear with a
+    split-K workspace sized by rxla_b200_w8a16_linear_workspace_size; no
+    workspace for the shapes that do not split): x bf16 N(0,1) [M,K], int8
+    weights U{-127..127} stored +128 [N,K], f32 per-row scales U[1e-3,1e-2],
+    bf16 out.  Each (N,K) cycles through enough weight copies to exceed 2x L2
+    (126 MB) between launches; 3 warm-up launches, then 20 timed with CUDA
+    events.  Algorithmic bytes N·K + 4·N + 2·M·K + 2·M·N, FLOPs 2·M·N·K;
+    frac = max(t_mem, t_flop) at the measured peaks / measured time."""
     import torch
     hbm, tf, _, how = measured_peaks()
     g = torch.Generator(device=dev).manual_seed(2)
@@ -706,14 +708,16 @@ def config2_sweep(dev):
             x = torch.randn(m, k, device=dev, generator=g).bfloat16()
             y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
             s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-            from rxla_b200 import _lib
+            from rxla_b200 import _lib, nn
             lib = _lib.load()
+            wsb = nn.linear_workspace_size(m, n, k, k)
+            wsp = torch.zeros(max(wsb, 16), dtype=torch.uint8, device=dev)
 
             def launch(i):
-                st = lib.rxla_b200_w8a16_linear(x.data_ptr(), _lib.BF16, ws[i % copies].data_ptr(),
-                                                sc.data_ptr(), k, m, n, k, y.data_ptr(), _lib.BF16,
-                                                _lib.EPI_STORE, s)
-                assert st == 0
+                st = lib.rxla_b200_w8a16_linear_ws(x.data_ptr(), _lib.BF16, ws[i % copies].data_ptr(),
+                                                   sc.data_ptr(), k, m, n, k, y.data_ptr(), _lib.BF16,
+                                                   _lib.EPI_STORE, wsp.data_ptr(), wsb, s)
+                assert st == 0, _lib.load().rxla_b200_last_error_message()
             for i in range(3):
                 launch(i)
             reps = 20
@@ -727,11 +731,12 @@ def config2_sweep(dev):
             byt = n * k + 4 * n + 2 * m * k + 2 * m * n
             fl = 2.0 * m * n * k
             t_mem, t_flop = byt / (hbm * 1e9), fl / (tf * 1e12)
-            points.append({"m": m, "n": n, "k": k, "us": sec * 1e6, "gbs": byt / sec / 1e9,
+            points.append({"m": m, "n": n, "k": k, "workspace_bytes": wsb,
+                           "us": sec * 1e6, "gbs": byt / sec / 1e9,
                            "tflops": fl / sec / 1e12,
                            "bound": "hbm" if t_mem >= t_flop else "tensor",
                            "frac": max(t_mem, t_flop) / sec})
-            del x, y
+            del x, y, wsp
         del ws
         torch.cuda.empty_cache()
     return {"points": points, "peaks": {"hbm_gbs": hbm, "bf16_tflops": tf, "source": how},

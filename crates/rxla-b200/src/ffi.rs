@@ -164,6 +164,14 @@ extern "C" {
         x: *const c_void, x_dtype: i32, weight: *const u8, scale: *const f32, group_size: i64,
         m: i64, n: i64, k: i64, y: *mut c_void, y_dtype: i32, epilogue: i32, stream: *mut c_void,
     ) -> i32;
+    pub fn rxla_b200_w8a16_linear_workspace_size(
+        m: i64, n: i64, k: i64, group_size: i64, epilogue: i32, bytes: *mut usize,
+    ) -> i32;
+    pub fn rxla_b200_w8a16_linear_ws(
+        x: *const c_void, x_dtype: i32, weight: *const u8, scale: *const f32, group_size: i64,
+        m: i64, n: i64, k: i64, y: *mut c_void, y_dtype: i32, epilogue: i32,
+        workspace: *mut c_void, workspace_bytes: usize, stream: *mut c_void,
+    ) -> i32;
     pub fn rxla_b200_w8a16_norm_linear(
         h: *const f32, norm_weight: *const f32, eps: f32, weight: *const u8, scale: *const f32,
         group_size: i64, m: i64, n: i64, k: i64, y: *mut c_void, y_dtype: i32, epilogue: i32,

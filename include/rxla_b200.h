@@ -146,6 +146,21 @@ int32_t rxla_b200_w8a16_linear(const void* x, int32_t x_dtype, const uint8_t* we
                                int64_t k, void* y, int32_t y_dtype, int32_t epilogue,
                                void* stream);
 
+/* The same linear with a caller-owned workspace, which lets the tensor-core
+ * GEMM (more than 8 tokens) split K across more CTAs than it has output
+ * tiles — the depth the decoder's own GEMMs use.  Size it with
+ * rxla_b200_w8a16_linear_workspace_size for the shape (0 bytes: no split
+ * for this shape on this device; then workspace may be null).  The
+ * workspace must be 16-byte aligned and zero-filled before its first use;
+ * every call leaves its counters zero again.  Calls sharing one workspace
+ * must be stream-ordered. */
+int32_t rxla_b200_w8a16_linear_workspace_size(int64_t m, int64_t n, int64_t k, int64_t group_size,
+                                              int32_t epilogue, size_t* bytes);
+int32_t rxla_b200_w8a16_linear_ws(const void* x, int32_t x_dtype, const uint8_t* weight,
+                                  const float* scale, int64_t group_size, int64_t m, int64_t n,
+                                  int64_t k, void* y, int32_t y_dtype, int32_t epilogue,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* The same linear with its input RMSNorm fused into the kernel's prologue, the
  * decoder block's `linear(rms_norm(h))` for decode shapes (each pass of up to
  * 8 tokens streams the weights once):

@@ -113,6 +113,10 @@ SIGNATURES = {
     "rxla_b200_get_wait_timeout": (_i32, [ctypes.POINTER(_i64)]),
     "rxla_b200_w8a16_linear": (_i32, [_vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i32,
                                       _i32, _vp]),
+    "rxla_b200_w8a16_linear_workspace_size": (_i32, [_i64, _i64, _i64, _i64, _i32,
+                                                     ctypes.POINTER(ctypes.c_size_t)]),
+    "rxla_b200_w8a16_linear_ws": (_i32, [_vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i32,
+                                         _i32, _vp, _sz, _vp]),
     "rxla_b200_w8a16_norm_linear": (_i32, [_vp, _vp, _f32, _vp, _vp, _i64, _i64, _i64, _i64, _vp,
                                            _i32, _i32, _vp]),
     "rxla_b200_bf16_linear": (_i32, [_vp, _i32, _vp, _i64, _i64, _i64, _vp, _i32, _i32, _vp]),

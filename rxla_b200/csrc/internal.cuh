@@ -69,7 +69,7 @@ bool comm_p2p_view(const rxla_b200_comm* c, P2pView* out);
 int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const float* scale,
                   int64_t group_size, int64_t m, int64_t n, int64_t k, void* y, int32_t y_dtype,
                   int32_t epilogue, cudaStream_t stream, const L2Prefetch* next,
-                  const P2pView* tp = nullptr);
+                  const P2pView* tp = nullptr, void* ws = nullptr, size_t ws_bytes = 0);
 int32_t w8_gemm(const GemmArgs& a, cudaStream_t stream);
 // split-K workspace: a fixed counter region (the same for every shape, so
 // GEMMs sharing a workspace never overlap one another's counters), then the

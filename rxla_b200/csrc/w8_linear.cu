@@ -1000,7 +1000,7 @@ namespace rxla {
 int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const float* scale,
                   int64_t group_size, int64_t m, int64_t n, int64_t k, void* y, int32_t y_dtype,
                   int32_t epilogue, cudaStream_t stream, const L2Prefetch* next,
-                  const P2pView* tp) {
+                  const P2pView* tp, void* ws, size_t ws_bytes) {
   RXLA_REQUIRE(m >= 0 && n >= 0 && k > 0, "w8a16_linear: m, n must be >= 0 and k > 0");
   RXLA_REQUIRE(group_size > 0 && k % group_size == 0,
                "w8a16_linear: group_size must be positive and divide k (layers.rs:266-275)");
@@ -1050,6 +1050,20 @@ int32_t w8_linear(const void* x, int32_t x_dtype, const uint8_t* weight, const f
     g.y_dtype = y_dtype;
     g.epilogue = epilogue;
     g.splits = 1;
+    if (ws) {
+      // split-K over the caller's workspace, the depth the decoder's GEMMs use
+      const bool swiglu = epilogue == RXLA_B200_EPI_SWIGLU;
+      const int sp = w8_gemm_splits(m, n, k, group_size, swiglu);
+      if (sp > 1) {
+        RXLA_REQUIRE(reinterpret_cast<uintptr_t>(ws) % 16 == 0 &&
+                         ws_bytes >= w8_gemm_workspace_bytes(m, swiglu ? 2 * n : n, sp),
+                     "w8a16_linear: workspace smaller than rxla_b200_w8a16_linear_workspace_size "
+                     "or not 16-byte aligned");
+        g.splits = sp;
+        g.ws = ws;
+        g.ws_bytes = ws_bytes;
+      }
+    }
     return w8_gemm(g, stream);
   }
   const int xmode = p.x_f32 ? w8::kXF32 : w8::kXBf16;
@@ -1122,4 +1136,33 @@ extern "C" int32_t rxla_b200_w8a16_linear(const void* x, int32_t x_dtype, const 
                                           int32_t epilogue, void* stream) {
   return rxla::w8_linear(x, x_dtype, weight, scale, group_size, m, n, k, y, y_dtype, epilogue,
                          static_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" int32_t rxla_b200_w8a16_linear_workspace_size(int64_t m, int64_t n, int64_t k,
+                                                         int64_t group_size, int32_t epilogue,
+                                                         size_t* bytes) {
+  using namespace rxla;
+  RXLA_REQUIRE(bytes && m >= 0 && n >= 0 && k > 0 && group_size > 0 && k % group_size == 0,
+               "w8a16_linear_workspace_size: bad arguments");
+  RXLA_REQUIRE(epilogue >= RXLA_B200_EPI_STORE && epilogue <= RXLA_B200_EPI_SWIGLU,
+               "w8a16_linear_workspace_size: unknown epilogue");
+  *bytes = 0;
+  // only the tcgen05 GEMM (more tokens than one skinny pass) splits K
+  if (m <= w8::kMaxTokens || n == 0 || k % 64 != 0 || group_size % 64 != 0) return RXLA_B200_OK;
+  const bool swiglu = epilogue == RXLA_B200_EPI_SWIGLU;
+  const int sp = w8_gemm_splits(m, n, k, group_size, swiglu);
+  *bytes = w8_gemm_workspace_bytes(m, swiglu ? 2 * n : n, sp);
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_w8a16_linear_ws(const void* x, int32_t x_dtype,
+                                             const uint8_t* weight, const float* scale,
+                                             int64_t group_size, int64_t m, int64_t n, int64_t k,
+                                             void* y, int32_t y_dtype, int32_t epilogue,
+                                             void* workspace, size_t workspace_bytes,
+                                             void* stream) {
+  RXLA_REQUIRE(workspace || workspace_bytes == 0, "w8a16_linear_ws: null workspace");
+  return rxla::w8_linear(x, x_dtype, weight, scale, group_size, m, n, k, y, y_dtype, epilogue,
+                         static_cast<cudaStream_t>(stream), nullptr, nullptr, workspace,
+                         workspace_bytes);
 }

@@ -44,13 +44,15 @@ _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
 def quantized_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
                      group_size: int | None = None, *, out_dtype=torch.bfloat16,
                      epilogue: int = _lib.EPI_STORE, out: torch.Tensor | None = None,
-                     stream=None) -> torch.Tensor:
+                     workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """W8A16 linear through rxla_b200_w8a16_linear.
 
     x [..., K] bf16/f32, weight u8 [N, K] (value + 128; [2N, K] = [gate; up] for
     EPI_SWIGLU), scale f32 [N_rows, K / group].  Returns y [..., N] in out_dtype
     (bf16: the bf16 dot; f32: the unrounded fp32 dot), or accumulates into the
-    f32 `out` for EPI_RESIDUAL_ADD.
+    f32 `out` for EPI_RESIDUAL_ADD.  With `workspace` (a zero-filled u8 device
+    tensor of at least linear_workspace_size bytes) the call goes through
+    rxla_b200_w8a16_linear_ws, whose tensor-core GEMM may split K.
     """
     if x.dtype not in _DT or weight.dtype != torch.uint8 or scale.dtype != torch.float32:
         raise InvalidLayerInput("QuantizedLinear needs bf16/f32 x, u8 weight, f32 scale")
@@ -75,9 +77,25 @@ def quantized_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
         if epilogue == _lib.EPI_RESIDUAL_ADD:
             raise InvalidLayerInput("the residual epilogue needs `out` (f32) to add into")
         out = torch.empty(*lead, n, dtype=out_dtype, device=x.device)
+    if workspace is not None:
+        _lib.call("rxla_b200_w8a16_linear_ws", _ptr(x2), _DT[x.dtype], _ptr(weight),
+                  _ptr(scale), group, m, n, k, _ptr(out), _DT[out.dtype], epilogue,
+                  _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(stream))
+        return out
     _lib.call("rxla_b200_w8a16_linear", _ptr(x2), _DT[x.dtype], _ptr(weight),
               _ptr(scale), group, m, n, k, _ptr(out), _DT[out.dtype], epilogue, _stream(stream))
     return out
+
+
+def linear_workspace_size(m: int, n: int, k: int, group_size: int | None = None,
+                          epilogue: int = _lib.EPI_STORE) -> int:
+    """Bytes of the split-K workspace of quantized_linear for an [m, k] x
+    [n, k] call on the current device (rxla_b200_w8a16_linear_workspace_size;
+    0: this shape does not split)."""
+    size = ctypes.c_size_t(0)
+    _lib.call("rxla_b200_w8a16_linear_workspace_size", int(m), int(n), int(k),
+              int(k if group_size is None else group_size), int(epilogue), ctypes.byref(size))
+    return int(size.value)
 
 
 def quantized_norm_linear(h: torch.Tensor, norm_weight: torch.Tensor, epsilon: float,

@@ -287,3 +287,54 @@ def test_fused_norm_linear(cuda, m, n, k, epi):
         y = nn.quantized_norm_linear(ht, nwt, 1e-6, wt, st, k, epilogue=_lib.EPI_SWIGLU)
         _check_swiglu(y.float().cpu().numpy(), x, w, s, k, n)
     assert nn.device_status() == 0
+
+
+@pytest.mark.parametrize("m,n,k,group,epi", [(32, 4096, 4096, 4096, _lib.EPI_STORE),
+                                             (64, 6144, 4096, 128, _lib.EPI_STORE),
+                                             (100, 4096, 12288, 12288, _lib.EPI_RESIDUAL_ADD),
+                                             (64, 1024, 4096, 4096, _lib.EPI_SWIGLU),
+                                             (9, 768, 2048, 2048, _lib.EPI_STORE)])
+def test_linear_with_split_k_workspace(cuda, m, n, k, group, epi):
+    """rxla_b200_w8a16_linear_ws: the GEMM splits K over the caller's
+    workspace (sized by rxla_b200_w8a16_linear_workspace_size); same results
+    as the oracle, the workspace's counters left zero, and a second call on
+    the same workspace gives the same bits."""
+    rows = 2 * n if epi == _lib.EPI_SWIGLU else n
+    x, w, s = _case(m, rows, k, group, seed=700 + m)
+    xt = torch.from_numpy(x).cuda().bfloat16()
+    wt, st = torch.from_numpy(w).cuda(), torch.from_numpy(np.ascontiguousarray(s)).cuda()
+    size = nn.linear_workspace_size(m, n, k, group, epi)
+    ws = torch.zeros(max(size, 16), dtype=torch.uint8, device="cuda")
+    if epi == _lib.EPI_RESIDUAL_ADD:
+        # into a zero residual: y = 0 + bf16(dot) = the bf16 dot exactly
+        outs = []
+        for _ in range(2):
+            y = torch.zeros(m, n, device="cuda")
+            nn.quantized_linear(xt, wt, st, group, epilogue=epi, out=y, workspace=ws)
+            outs.append(y)
+        _check(outs[0].cpu().numpy(), x, w, s, group)
+    else:
+        outs = [nn.quantized_linear(xt, wt, st, group, epilogue=epi, workspace=ws)
+                for _ in range(2)]
+        y = outs[0].float().cpu().numpy()
+        if epi == _lib.EPI_SWIGLU:
+            _check_swiglu(y, x, w, s, group, n)
+        else:
+            _check(y, x, w, s, group)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    if size > 0:  # the split counters are zero again after every call
+        assert int(ws[:1 << 20].count_nonzero()) == 0
+    assert _lib.load().rxla_b200_device_status(0) == 0
+
+
+def test_linear_workspace_too_small_is_rejected(cuda):
+    m, n, k = 64, 4096, 4096
+    size = nn.linear_workspace_size(m, n, k)
+    if size == 0:
+        pytest.skip("this shape does not split on this device")
+    x, w, s = _case(m, n, k, k, seed=760)
+    ws = torch.zeros(size // 2, dtype=torch.uint8, device="cuda")
+    with pytest.raises(Exception, match="workspace"):
+        nn.quantized_linear(torch.from_numpy(x).cuda().bfloat16(), torch.from_numpy(w).cuda(),
+                            torch.from_numpy(s).cuda(), k, workspace=ws)
