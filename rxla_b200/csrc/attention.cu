@@ -191,6 +191,37 @@ __device__ __forceinline__ void prep_new_kv(float (&kn)[DL], float (&vn)[DL], in
 }
 
 constexpr int kComputeWarps = 4;
+
+// Thread-block cluster helpers: a full cluster barrier (release / acquire),
+// this CTA's rank, and loads from another CTA's shared memory at the address
+// `p` has in this CTA.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, int rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ float ld_dsmem_f32(const float* p, int rank) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(dsmem_addr(p, rank)) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_dsmem_f32x4(const float* p, int rank) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(dsmem_addr(p, rank))
+               : "memory");
+  return v;
+}
 // Ring depth and occupancy: small batches (few CTAs, latency-bound) use a
 // deep ring; large batches fit three CTAs per SM with a shallower ring.  The
 // page iterations of a split go round-robin to the compute warps, so a stage
@@ -200,11 +231,11 @@ constexpr int kComputeWarps = 4;
 constexpr int kStagesSmall = 8, kStagesLarge = 4;
 constexpr int kMergeBatch = 16;  // split partials in flight per thread in the final merge
 
-template <int D, int kStagesV2, int kMinBlocks>
-__global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
+template <int D, int kStagesV2, int kMinBlocks, int CW = kComputeWarps, bool CLUSTER = false>
+__global__ void __launch_bounds__((CW + 1) * 32, kMinBlocks)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const Params p) {
-  static_assert(kStagesV2 % kComputeWarps == 0, "ring depth must be a multiple of the warps");
+  static_assert(kStagesV2 % CW == 0, "ring depth must be a multiple of the warps");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   constexpr int DL = D / 32;     // dims per lane for the new k / v and the merges
   constexpr int KS = D / 16;     // k-steps of q·kᵀ
@@ -221,8 +252,8 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
   uint8_t* ring = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u) + 2048;
   // per-warp softmax states for the in-CTA merge: O [warp][8][D], m/l [warp][8][2]
   float* st_o = reinterpret_cast<float*>(ring + kStagesV2 * kStage);
-  float* st_ml = st_o + kComputeWarps * 8 * D;
-  float* wts = st_ml + kComputeWarps * 8 * 2;  // cross-split maxima [max_splits][8]
+  float* st_ml = st_o + CW * 8 * D;
+  float* wts = st_ml + CW * 8 * 2;  // cross-split maxima [max_splits][8]
   float* wls = wts + p.max_splits * 8;           // cross-split sums [max_splits][8]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -245,7 +276,9 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
 
   const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   const int ctas = gridDim.x * gridDim.y * gridDim.z;
-  if (split >= n_splits) {  // nothing of this sequence in this split (exit = trigger)
+  // nothing of this sequence in this split (exit = trigger); a cluster's CTAs
+  // all stay for the cluster barriers, with no pages
+  if (!CLUSTER && split >= n_splits) {
     if (threadIdx.x == 0) {
       if (p.next.nseg > 0) l2_prefetch_share(p.next, cta, ctas);
       finish_cta(p);
@@ -262,7 +295,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
   }
   __syncthreads();
 
-  if (warp == kComputeWarps) {
+  if (warp == CW) {
     // ------------------------------------------------------------ producer
     // Pages hold rows appended by earlier kernels only (the new row is patched
     // in from registers); with a stable ctx_lens they are fetched before
@@ -320,7 +353,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
       }
     }
     const int slot_pg = slot / kPage;
-    const bool appender = owner && warp == (slot_pg - pg0) % kComputeWarps;
+    const bool appender = owner && warp == (slot_pg - pg0) % CW;
     float kn[DL], vn[DL];
     if (appender) {
       const __nv_bfloat16* kr = p.k_new + (int64_t)b * p.kv_stride + (int64_t)h * D;
@@ -331,7 +364,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
         vn[i] = __bfloat162float(vr[DL * lane + i]);
       }
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");  // tables ready
+    asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");  // tables ready
 
     if (appender) {
       // k: RMSNorm over the head, RoPE, bf16; appended at the slot and patched
@@ -398,7 +431,7 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
       for (int i = 0; i < 4; ++i) o[mt][i] = 0.0f;
 
     const int mi = lane >> 3, rr = lane & 7;
-    for (int it = warp; it < n_it; it += kComputeWarps) {
+    for (int it = warp; it < n_it; it += CW) {
       const int s = it % kStagesV2;
       if (!mbar_wait(&full[s], (it / kStagesV2) & 1)) break;
       const int pg = pg0 + it;
@@ -499,20 +532,20 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
         }
       }
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
 
     // ---- merge the 4 warps (in-CTA) -> this split's (O, m, l) per head;
     // a thread takes 4 consecutive dims of one head
     const int64_t seg = (((int64_t)b * hkv + h) * p.max_splits + split) * G;
-    for (int e = tid; e < G * D / 4; e += kComputeWarps * 32) {
+    for (int e = tid; e < G * D / 4; e += CW * 32) {
       const int j = (4 * e) / D, d = (4 * e) % D;
       float m = -INFINITY;
 #pragma unroll
-      for (int w2 = 0; w2 < kComputeWarps; ++w2) m = fmaxf(m, st_ml[(w2 * 8 + j) * 2]);
+      for (int w2 = 0; w2 < CW; ++w2) m = fmaxf(m, st_ml[(w2 * 8 + j) * 2]);
       float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       float l = 0.0f;
 #pragma unroll
-      for (int w2 = 0; w2 < kComputeWarps; ++w2) {
+      for (int w2 = 0; w2 < CW; ++w2) {
         const float mw = st_ml[(w2 * 8 + j) * 2];
         const float wgt = mw == -INFINITY ? 0.0f : expf(mw - m);
         const float4 x = *reinterpret_cast<const float4*>(st_o + ((size_t)w2 * 8 + j) * D + d);
@@ -522,7 +555,16 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
         acc.w += wgt * x.w;
         l += wgt * st_ml[(w2 * 8 + j) * 2 + 1];
       }
-      if (n_splits == 1) {
+      if (CLUSTER) {
+        // this split's partial stays in shared memory for the cluster's
+        // leader: O over warp slot 0 (only this thread reads these four
+        // floats of every slot), (m, l) in the cross-split area
+        *reinterpret_cast<float4*>(st_o + (size_t)j * D + d) = acc;
+        if (d == 0) {
+          wts[j * 2] = m;
+          wts[j * 2 + 1] = l;
+        }
+      } else if (n_splits == 1) {
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
         uint2 pk;
         pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
@@ -533,28 +575,28 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
         if (d == 0) *reinterpret_cast<float2*>(p.ws_ml + (seg + j) * 2) = make_float2(m, l);
       }
     }
-    if (n_splits > 1) {
+    if (!CLUSTER && n_splits > 1) {
       __threadfence();
-      asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
       if (tid == 0) {
         const uint32_t prev = atomicAdd(&p.ws_counter[b * hkv + h], 1u);
         misc[0] = prev == (uint32_t)(n_splits - 1) ? 1.0f : 0.0f;
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
       if (misc[0] != 0.0f) {
         // the last split of (b, h) merges all splits' partials: (m, l) of
         // every split in one round of loads, then up to 8 partial rows in flight
         __threadfence();
         const int64_t base = ((int64_t)b * hkv + h) * p.max_splits * G;
-        for (int e = tid; e < n_splits * G; e += kComputeWarps * 32) {
+        for (int e = tid; e < n_splits * G; e += CW * 32) {
           const int sp = e / G, j = e % G;
           const float2 ml =
               __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (base + (int64_t)sp * G + j) * 2));
           wts[sp * 8 + j] = ml.x;
           wls[sp * 8 + j] = ml.y;
         }
-        asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
-        for (int e = tid; e < G * D / 4; e += kComputeWarps * 32) {
+        asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+        for (int e = tid; e < G * D / 4; e += CW * 32) {
           const int j = (4 * e) / D, d = (4 * e) % D;
           float m = -INFINITY;
           for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, wts[sp * 8 + j]);
@@ -592,6 +634,55 @@ __global__ void __launch_bounds__((kComputeWarps + 1) * 32, kMinBlocks)
     }
   }
   __syncthreads();
+  if constexpr (CLUSTER) {
+    // The cluster is the (sequence, kv head): CTA rank r holds split r.  Once
+    // every CTA's partial is in its shared memory, rank 0 merges them through
+    // distributed shared memory with log-sum-exp weights (splits in order)
+    // and writes the output; the second barrier keeps every CTA's shared
+    // memory alive until the leader has read it.  Every thread of every CTA
+    // reaches both barriers (no early exit in this variant).
+    cluster_sync();
+    if (cluster_rank() == 0 && warp < CW) {
+      const int tid = threadIdx.x;
+      const int ns = min(n_splits, (int)gridDim.x);
+      for (int e = tid; e < G * D / 4; e += CW * 32) {
+        const int j = (4 * e) / D, d = (4 * e) % D;
+        float mr[8], lr[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          mr[r] = -INFINITY;
+          lr[r] = 0.0f;
+          if (r < ns) {
+            mr[r] = ld_dsmem_f32(wts + j * 2, r);
+            lr[r] = ld_dsmem_f32(wts + j * 2 + 1, r);
+          }
+        }
+        float m = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) m = fmaxf(m, mr[r]);
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float l = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          if (r < ns && mr[r] != -INFINITY) {
+            const float wgt = expf(mr[r] - m);
+            const float4 x = ld_dsmem_f32x4(st_o + (size_t)j * D + d, r);
+            acc.x += wgt * x.x;
+            acc.y += wgt * x.y;
+            acc.z += wgt * x.z;
+            acc.w += wgt * x.w;
+            l += wgt * lr[r];
+          }
+        }
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        uint2 pk;
+        pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+        pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+        *reinterpret_cast<uint2*>(p.out + (int64_t)b * p.hq * D + (int64_t)(h * G + j) * D + d) = pk;
+      }
+    }
+    cluster_sync();
+  }
   if (threadIdx.x == 0) finish_cta(p);
 }
 
@@ -1002,7 +1093,23 @@ static int32_t make_page_map(CUtensorMap* map, void* base, int64_t num_pages, in
 // (RXLA_B200_ATTN_PPS_CAP: longer splits cost a fuller last wave but fewer
 // merges; batch 64 at 2048 context: 111.4 µs with 32, 105.8 with 48, 109.7
 // with 64).
+// Small grids — fewer than 16 sequences and at most 32 (sequence, kv head)
+// pairs — run one thread-block cluster of kClusterSplits CTAs per pair, each
+// with kClusterWarps compute warps, and merge the splits through distributed
+// shared memory instead of a workspace round trip (RXLA_B200_ATTN_CLUSTER=0:
+// off).
+constexpr int kClusterSplits = 8, kClusterWarps = 8, kStagesCluster = 16;
+static bool use_cluster(int batch, int kv_heads) {
+  static const bool on = [] {
+    const char* v = getenv("RXLA_B200_ATTN_CLUSTER");
+    return !(v && v[0] == '0');
+  }();
+  return on && batch < 16 && (int64_t)batch * kv_heads <= 32;
+}
+
 static int pages_per_split(int batch, int kv_heads, int max_pages) {
+  if (use_cluster(batch, kv_heads))
+    return std::max(1, (max_pages + kClusterSplits - 1) / kClusterSplits);
   static const int64_t cap = [] {
     const char* v = getenv("RXLA_B200_ATTN_PPS_CAP");
     return v ? (int64_t)std::max(1, atoi(v)) : (int64_t)48;
@@ -1028,7 +1135,9 @@ extern "C" int32_t rxla_b200_paged_decode_workspace_size(int32_t batch, int32_t 
                "paged_decode_workspace_size: bad arguments");
   const int max_pages = (max_context + attn::kPage - 1) / attn::kPage;
   const int pps = attn::pages_per_split(batch, kv_heads, max_pages);
-  const int64_t splits = std::max(1, (max_pages + pps - 1) / pps);
+  const int64_t splits = attn::use_cluster(batch, kv_heads)
+                             ? attn::kClusterSplits
+                             : std::max(1, (max_pages + pps - 1) / pps);
   const int64_t G = q_heads / kv_heads;
   const int64_t part = (int64_t)batch * kv_heads * splits * G;
   const int64_t counters = ((int64_t)batch * kv_heads + 1) * 4;
@@ -1110,7 +1219,10 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   p.group = a->q_heads / a->kv_heads;
   const int max_pages = (a->max_context + attn::kPage - 1) / attn::kPage;
   p.pps = attn::pages_per_split(a->batch, a->kv_heads, max_pages);
-  p.max_splits = std::max(1, (max_pages + p.pps - 1) / p.pps);
+  // a cluster holds all kClusterSplits CTAs of a (sequence, kv head), some
+  // possibly without pages
+  const bool cluster = !append_only && attn::use_cluster(a->batch, a->kv_heads);
+  p.max_splits = cluster ? attn::kClusterSplits : std::max(1, (max_pages + p.pps - 1) / p.pps);
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   const size_t cnt_bytes = (((size_t)a->batch * a->kv_heads + 1) * 4 + 255) / 256 * 256;
   p.ws_counter = reinterpret_cast<uint32_t*>(ws);
@@ -1130,7 +1242,8 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
     return RXLA_B200_OK;
   }
   const bool large = a->batch >= 16;  // enough CTAs to fill the SMs several times
-  p.stages = large ? attn::kStagesLarge : attn::kStagesSmall;
+  p.stages = cluster ? attn::kStagesCluster : (large ? attn::kStagesLarge : attn::kStagesSmall);
+  const int cw = cluster ? attn::kClusterWarps : attn::kComputeWarps;
   if (next) p.next = *next;
 
   CUtensorMap kmap, vmap;
@@ -1139,26 +1252,29 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   st = attn::make_page_map(&vmap, a->v_pages, a->num_pages, a->kv_heads, D);
   if (st != RXLA_B200_OK) return st;
 
-  const size_t smem = 3072 + (size_t)p.stages * p.stage_bytes +
-                      (size_t)attn::kComputeWarps * 8 * (D + 2) * 4 +
+  const size_t smem = 3072 + (size_t)p.stages * p.stage_bytes + (size_t)cw * 8 * (D + 2) * 4 +
                       (size_t)p.max_splits * 8 * 2 * 4;
   const dim3 grid(p.max_splits, a->kv_heads, a->batch);
-  const dim3 block((attn::kComputeWarps + 1) * 32);
+  const dim3 block((cw + 1) * 32);
   cudaStream_t s = s_in;
   auto go = [&](auto kernel) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
-    if (e == cudaSuccess) e = launch_pdl(kernel, grid, block, smem, s, kmap, vmap, p);
-    return e;
+    if (e != cudaSuccess) return e;
+    return cluster ? launch_pdl_cluster(kernel, grid, block, smem, s, attn::kClusterSplits, kmap,
+                                        vmap, p)
+                   : launch_pdl(kernel, grid, block, smem, s, kmap, vmap, p);
   };
   using namespace attn;
   cudaError_t e;
   if (D == 128)
-    e = large ? go(paged_decode_kernel<128, kStagesLarge, 3>)
-              : go(paged_decode_kernel<128, kStagesSmall, 1>);
+    e = cluster ? go(paged_decode_kernel<128, kStagesCluster, 1, kClusterWarps, true>)
+        : large ? go(paged_decode_kernel<128, kStagesLarge, 3>)
+                : go(paged_decode_kernel<128, kStagesSmall, 1>);
   else
-    e = large ? go(paged_decode_kernel<64, kStagesLarge, 3>)
-              : go(paged_decode_kernel<64, kStagesSmall, 1>);
+    e = cluster ? go(paged_decode_kernel<64, kStagesCluster, 1, kClusterWarps, true>)
+        : large ? go(paged_decode_kernel<64, kStagesLarge, 3>)
+                : go(paged_decode_kernel<64, kStagesSmall, 1>);
   if (e != cudaSuccess) return cuda_fail(e, "paged decode attention launch");
   return RXLA_B200_OK;
 }

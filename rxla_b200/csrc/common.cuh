@@ -60,6 +60,28 @@ cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaSt
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// The same launch with a thread-block cluster of `cluster_x` CTAs along x
+// (gridDim.x a multiple of it).
+template <typename Kernel, typename... Args>
+cudaError_t launch_pdl_cluster(Kernel kernel, dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, unsigned cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Device status word (per device): 0 = fine, else a negative rxla_b200_status.
 int32_t read_device_status(bool reset);
 
