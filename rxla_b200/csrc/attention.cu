@@ -1096,28 +1096,17 @@ static int32_t make_page_map(CUtensorMap* map, void* base, int64_t num_pages, in
 // Small grids — fewer than 16 sequences and at most 32 (sequence, kv head)
 // pairs — run one thread-block cluster of kClusterSplits CTAs per pair, each
 // with kClusterWarps compute warps, and merge the splits through distributed
-// shared memory instead of a workspace round trip (RXLA_B200_ATTN_CLUSTER=0:
-// off).
+// shared memory instead of a workspace round trip.
 constexpr int kClusterSplits = 8, kClusterWarps = 8, kStagesCluster = 16;
 static bool use_cluster(int batch, int kv_heads) {
-  static const bool on = [] {
-    const char* v = getenv("RXLA_B200_ATTN_CLUSTER");
-    return !(v && v[0] == '0');
-  }();
-  return on && batch < 16 && (int64_t)batch * kv_heads <= 32;
+  return batch < 16 && (int64_t)batch * kv_heads <= 32;
 }
 
 static int pages_per_split(int batch, int kv_heads, int max_pages) {
   if (use_cluster(batch, kv_heads))
     return std::max(1, (max_pages + kClusterSplits - 1) / kClusterSplits);
-  static const int64_t cap = [] {
-    const char* v = getenv("RXLA_B200_ATTN_PPS_CAP");
-    return v ? (int64_t)std::max(1, atoi(v)) : (int64_t)48;
-  }();
-  static const int64_t most = [] {  // splits per (sequence, kv head) at most
-    const char* v = getenv("RXLA_B200_ATTN_MAX_SPLITS");
-    return v ? (int64_t)std::max(1, atoi(v)) : (int64_t)16;
-  }();
+  constexpr int64_t cap = 48;   // pages per split at most
+  constexpr int64_t most = 16;  // splits per (sequence, kv head) at most
   const int64_t want = ((int64_t)batch * kv_heads * max_pages + 4 * 148 - 1) / (4 * 148);
   const int64_t depth = ((int64_t)max_pages + most - 1) / most;
   return (int)std::max<int64_t>(1, std::max(depth, std::min<int64_t>(cap, want)));

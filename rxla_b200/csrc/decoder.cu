@@ -616,14 +616,10 @@ static int32_t enqueue_step(rxla_b200_decoder* d, int batch, cudaStream_t s) {
     f.per_cta = per_cta;
     return f;
   };
-  // bytes of the next kernel's weights each CTA pulls into L2 (environment
-  // RXLA_B200_L2_AHEAD_KB overrides the default; batch-1 step at 2048 context:
-  // 0 KB 2.49 ms, 96 KB 2.40, 192 KB 2.41, 384 KB 2.50, 768 KB 2.61)
-  static const int32_t kRingShare = [] {
-    const char* v = getenv("RXLA_B200_L2_AHEAD_KB");
-    const long kb = v ? atol(v) : 96;
-    return (int32_t)std::min<long>(std::max<long>(kb, 0), 1 << 20) * 1024;
-  }();
+  // bytes of the next kernel's weights each CTA pulls into L2 (measured on
+  // the batch-1 step at 2048 context: 0 KB 2.49 ms, 96 KB 2.40, 192 KB 2.41,
+  // 384 KB 2.50, 768 KB 2.61)
+  constexpr int32_t kRingShare = 96 * 1024;
   for (int l = 0; l < c.layers; ++l) {
     const Layer& L = d->layers[l];
     const L2Prefetch to_o = pf(L.wo, H * qd, 256 * 1024);

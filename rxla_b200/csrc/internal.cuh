@@ -79,7 +79,6 @@ size_t w8_gemm_workspace_bytes(int64_t m, int64_t n_rows, int splits);
 // Decode batches (m <= kGemmDecMaxTokens) run the weights-on-M variant.
 constexpr int64_t kGemmDecMaxTokens = 128;
 int32_t w8_gemm_dec(const GemmArgs& a, cudaStream_t stream);
-bool gemm_dec_enabled();
 bool w8_gemm_dec_applies(int64_t m, int64_t k, int64_t group);
 // CTAs per split of the GEMM w8_gemm runs for this shape (m tokens, n outputs)
 int64_t w8_gemm_tiles(int64_t m, int64_t n, int64_t k, int64_t group, bool swiglu);

@@ -542,15 +542,6 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace gemm
 
-// Decode batches run w8_gemm_dec unless RXLA_B200_GEMM_DEC=0.
-bool gemm_dec_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("RXLA_B200_GEMM_DEC");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
 // A split-K workspace is [kGemmCounterBytes of tile counters][partials].  The
 // counter region has the same size for every shape: a decoder's GEMMs share
 // one workspace, and a region sized by the current shape let a GEMM with few

@@ -501,7 +501,7 @@ static cudaError_t launch(const CUtensorMap& xmap, const CUtensorMap& wmap, cons
 }  // namespace gemmdec
 
 bool w8_gemm_dec_applies(int64_t m, int64_t k, int64_t group) {
-  return gemm_dec_enabled() && m <= kGemmDecMaxTokens && k % gemmdec::kBK == 0 &&
+  return m <= kGemmDecMaxTokens && k % gemmdec::kBK == 0 &&
          group % gemmdec::kBK == 0;
 }
 
@@ -531,9 +531,6 @@ int w8_gemm_splits(int64_t m, int64_t n, int64_t k, int64_t group, bool swiglu) 
   const int64_t rows = dec ? gemmdec::kRows : gemm::kBN;  // weight rows per tile
   const int64_t kb = (k + kblock - 1) / kblock;
   const int64_t smax = std::max<int64_t>(1, std::min<int64_t>(16, kb / 2));
-  const char* pv = getenv("RXLA_B200_SPLIT_POLICY");
-  if (pv && pv[0] == '0')
-    return (int)std::max<int64_t>(1, std::min<int64_t>({(sms + tiles - 1) / tiles, 16, k / 128}));
   // a split's partial tile (m × rows f32) in units of one k-block of weights
   const double pu = (double)std::min<int64_t>(m, 128) * rows * 4 / (double)(rows * kblock);
   int64_t best = 1;

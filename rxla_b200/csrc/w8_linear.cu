@@ -856,24 +856,10 @@ __global__ void w8_generic_kernel(const Params p) {
 // Shared-memory plan.  K is cut into k_chunks of kc columns so that one
 // stage (16 rows × kc) stays within 64 KB (80 KB if that avoids a split);
 // x (m tokens, bf16) is resident; the ring takes the rest, 2..8 stages.
-static size_t env_size(const char* name, size_t dflt) {
-  const char* v = getenv(name);
-  return v ? (size_t)strtoull(v, nullptr, 10) : dflt;
-}
-
-// x fragments in registers for rows of at most 4096 (RXLA_B200_GEMV_XREG=0: off)
-static bool xreg_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("RXLA_B200_GEMV_XREG");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
 static int32_t plan_skinny(Params& p, size_t& smem) {
-  // tuning knobs (bytes): largest stage, shared-memory budget of one CTA
-  static const size_t max_stage = env_size("RXLA_B200_GEMV_STAGE", 80 * 1024);
-  static const size_t budget = env_size("RXLA_B200_GEMV_SMEM", 227 * 1024);
+  // largest stage and shared-memory budget of one CTA (bytes)
+  constexpr size_t max_stage = 80 * 1024;
+  constexpr size_t budget = 227 * 1024;
   int chunks = (int)(((int64_t)kTileRows * p.k + max_stage - 1) / max_stage);
   int kc = (int)((((int64_t)p.k + chunks - 1) / chunks + 63) / 64 * 64);
   p.kc = kc;
@@ -891,7 +877,7 @@ template <bool SWIGLU, bool GROUPED, int XMODE>
 static cudaError_t launch_variant(const Params& p, int grid, size_t smem, cudaStream_t stream) {
   auto k = w8_skinny_kernel<SWIGLU, GROUPED, XMODE, false>;
   if (!GROUPED && p.k_chunks == 1 && p.k % (kConsumerWarps * 64) == 0 &&
-      p.k <= kXRegBoxes * kConsumerWarps * 64 && xreg_enabled())
+      p.k <= kXRegBoxes * kConsumerWarps * 64)
     k = w8_skinny_kernel<SWIGLU, GROUPED, XMODE, !GROUPED>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
