@@ -456,7 +456,8 @@ def run_ours(args, rank, world, local_rank):
     kernels = None
     if world == 1 and not args.no_kernels:
         kernels = {"config2_linear_sweep": config2_sweep(dev),
-                   "config3_attention": config3_attention(dev)}
+                   "config3_attention": config3_attention(dev),
+                   "gated_delta": gated_delta_bench(dev)}
     if comm:
         comm.close()
 
@@ -788,6 +789,107 @@ def config3_attention(dev):
             "frac": byt / sec / 1e9 / hbm, "peak_gbs": hbm, "peak_source": how}
 
 
+def gated_delta_bench(dev):
+    """Qwen3.5-0.8B linear-attention mixer widths (16 heads of 128, conv 4)
+    through rxla_b200_gated_delta (crates/rxla-models/src/qwen3_5/layers.rs:114-268).
+
+    decode_b64: 64 sequences, one token each, continuing their states.  HBM
+      bound: algorithmic bytes = the recurrent state read and written
+      (64·16·128·128·4·2 = 134 MB) + the projections in, the conv history
+      read and written, the bf16 output; two state sets are cycled (268 MB,
+      > 2x L2) between timed calls.
+    prefill_2048: one sequence, a 2048-token prompt from a zero state: the
+      recurrence is sequential in the tokens (latency bound), reported as
+      tokens/s and µs per token.
+    layer_decode_b64: the whole mixer at batch 64 (fused W8 in-projection,
+      the three kernels, W8 out_proj added into the residual)."""
+    import torch
+    from rxla_b200.gated_delta import (GatedDeltaAttention, GatedDeltaState, gated_delta,
+                                       workspace_size)
+    hbm, _, _, how = measured_peaks()
+    H, D, K = 16, 128, 4
+    W = H * D
+    g = torch.Generator(device=dev).manual_seed(11)
+    conv_w = torch.randn(3 * W, K, device=dev, generator=g) * 0.5
+    a_log = torch.rand(H, device=dev, generator=g) * 2.7
+    dt_bias = torch.randn(H, device=dev, generator=g) * 0.5
+    norm_w = 1 + 0.1 * torch.randn(D, device=dev, generator=g)
+
+    def timed(fn, reps):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    out = {"workload": "Qwen3.5-0.8B linear-attention widths: 16 heads x 128, conv 4, hidden 1024"}
+    # decode, batch 64
+    B = 64
+    proj = torch.randn(B, 4 * W + 2 * H, device=dev, generator=g).bfloat16()
+    states = []
+    for _ in range(2):
+        st = GatedDeltaState(B, H, D, K, device=dev)
+        st.state.normal_(generator=g).mul_(0.05)
+        st.started = True
+        states.append(st)
+    y = torch.empty(B, W, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(workspace_size(B, 1, H, D), dtype=torch.uint8, device=dev)
+
+    def dec(i):
+        gated_delta(proj[:, :3 * W], proj[:, 3 * W:4 * W], proj[:, 4 * W:4 * W + H],
+                    proj[:, 4 * W + H:], conv_w, a_log, dt_bias, norm_w, state=states[i % 2],
+                    out=y, workspace=ws)
+    sec = timed(dec, 20)
+    byt = B * H * D * D * 4 * 2 + B * (4 * W + 2 * H) * 2 + B * (K - 1) * 3 * W * 2 * 2 + B * W * 2
+    out["decode_b64"] = {"us": sec * 1e6, "bytes_per_call": byt, "gbs": byt / sec / 1e9,
+                         "bound": "hbm", "frac": byt / sec / 1e9 / hbm, "peak_gbs": hbm,
+                         "peak_source": how, "launches_per_call": 3,
+                         "l2": "two state sets cycled (268 MB > 2x L2)"}
+    # prefill of one 2048-token sequence
+    T = 2048
+    proj = torch.randn(T, 4 * W + 2 * H, device=dev, generator=g).bfloat16()
+    st = GatedDeltaState(1, H, D, K, device=dev)
+    y = torch.empty(T, W, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(workspace_size(1, T, H, D), dtype=torch.uint8, device=dev)
+
+    def pre(i):
+        st.started = False
+        gated_delta(proj[:, :3 * W], proj[:, 3 * W:4 * W], proj[:, 4 * W:4 * W + H],
+                    proj[:, 4 * W + H:], conv_w, a_log, dt_bias, norm_w, state=st, out=y,
+                    workspace=ws)
+    sec = timed(pre, 5)
+    out["prefill_2048"] = {"us": sec * 1e6, "tokens_per_s": T / sec, "us_per_token": sec * 1e6 / T,
+                           "bound": "latency (sequential recurrence over the tokens)"}
+    # the whole mixer at batch 64 (W8 projections included)
+    hidden, G = 1024, 128
+    params = {}
+    for name, (n, k) in {"in_proj_qkv": (3 * W, hidden), "in_proj_z": (W, hidden),
+                         "in_proj_b": (H, hidden), "in_proj_a": (H, hidden),
+                         "out_proj": (hidden, W)}.items():
+        params[f"{name}.weight"] = torch.randint(1, 256, (n, k), dtype=torch.uint8, device=dev,
+                                                 generator=g)
+        params[f"{name}.scale"] = torch.rand(n, k // G, device=dev, generator=g) * 1e-3
+    params.update({"conv1d.weight": conv_w.reshape(3 * W, 1, K), "A_log": a_log,
+                   "dt_bias": dt_bias, "norm.weight": norm_w})
+    layer = GatedDeltaAttention(params, hidden_size=hidden, linear_heads=H, linear_head_dim=D,
+                                conv_kernel=K, quant_group_size=G)
+    x = torch.randn(B, 1, hidden, device=dev, generator=g)
+    res = torch.zeros(B, 1, hidden, device=dev)
+    lst = [layer.new_state(B) for _ in range(2)]
+    sec = timed(lambda i: layer.apply(x, lst[i % 2], residual=res), 20)
+    wbytes = sum(params[f"{n}.weight"].numel() + params[f"{n}.scale"].numel() * 4
+                 for n in GatedDeltaAttention.NAMES)
+    lbyt = wbytes + byt
+    out["layer_decode_b64"] = {"us": sec * 1e6, "bytes_per_call": lbyt, "gbs": lbyt / sec / 1e9,
+                               "frac": lbyt / sec / 1e9 / hbm, "launches_per_call": 5}
+    return out
+
+
 def profile_case(what: str):
     """Small, self-contained cases for ncu captures (no JSON line).
 
@@ -933,6 +1035,23 @@ def profile_case(what: str):
             nn.paged_decode_attention(qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d],
                                       qkv[:, (hq + hkv) * d:], cache, q_heads=hq, inv_freq=inv,
                                       rotary_dim=d, workspace=ws)
+    elif what in ("gdn_decode", "gdn_prefill"):
+        # the gated-delta mixer at the Qwen3.5-0.8B widths: 64 sequences x 1
+        # token (state 134 MB > L2) or one 2048-token prompt; 3 calls
+        from rxla_b200.gated_delta import GatedDeltaState, gated_delta
+        H, D, K = 16, 128, 4
+        W = H * D
+        B, T = (64, 1) if what == "gdn_decode" else (1, 2048)
+        proj = torch.randn(B * T, 4 * W + 2 * H, device=dev).bfloat16()
+        st = GatedDeltaState(B, H, D, K, device=dev)
+        st.state.normal_().mul_(0.05)
+        args = (proj[:, :3 * W], proj[:, 3 * W:4 * W], proj[:, 4 * W:4 * W + H],
+                proj[:, 4 * W + H:], torch.randn(3 * W, K, device=dev) * 0.5,
+                torch.rand(H, device=dev) * 2.7, torch.randn(H, device=dev) * 0.5,
+                torch.ones(D, device=dev))
+        for _ in range(3):
+            st.started = what == "gdn_decode"
+            gated_delta(*args, state=st)
     torch.cuda.synchronize()
     print("profile case done:", what)
 
@@ -946,10 +1065,11 @@ def main():
     ap.add_argument("--no-batch64", action="store_true")
     ap.add_argument("--no-config5", action="store_true")
     ap.add_argument("--no-kernels", action="store_true",
-                    help="skip the config-2 sweep and config-3 attention keys (N = 1)")
+                    help="skip the config-2 sweep, config-3 attention and gated-delta keys (N = 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["gemv", "head", "gemm", "gemmdec", "step", "step2l", "step64",
-                                          "step5", "prefill", "attention", "attention1"], default=None,
+                                          "step5", "prefill", "attention", "attention1", "gdn_decode",
+                                          "gdn_prefill"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     args = ap.parse_args()
     if args.profile:

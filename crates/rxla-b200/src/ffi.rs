@@ -77,6 +77,37 @@ pub struct rxla_b200_paged_decode_args {
     pub max_context: i32,
 }
 
+/// `rxla_b200_gated_delta_args`
+#[repr(C)]
+#[derive(Clone, Copy, Debug)]
+pub struct rxla_b200_gated_delta_args {
+    pub struct_size: u32,
+    pub batch: i32,
+    pub tokens: i32,
+    pub heads: i32,
+    pub head_dim: i32,
+    pub conv_kernel: i32,
+    pub mixed: *const u16,
+    pub z: *const u16,
+    pub beta_logits: *const u16,
+    pub a: *const u16,
+    pub mixed_row_stride: i64,
+    pub z_row_stride: i64,
+    pub b_row_stride: i64,
+    pub a_row_stride: i64,
+    pub conv_weight: *const f32,
+    pub a_log: *const f32,
+    pub dt_bias: *const f32,
+    pub norm_weight: *const f32,
+    pub eps: f32,
+    pub has_state: i32,
+    pub conv_state: *mut u16,
+    pub state: *mut f32,
+    pub out: *mut u16,
+    pub workspace: *mut c_void,
+    pub workspace_bytes: usize,
+}
+
 /// `rxla_b200_decoder_config`
 #[repr(C)]
 #[derive(Clone, Copy, Debug, Default)]
@@ -195,6 +226,11 @@ extern "C" {
         stream: *mut c_void,
     ) -> i32;
     pub fn rxla_b200_argmax(logits: *const f32, rows: i64, vocab: i64, out: *mut i32, stream: *mut c_void) -> i32;
+
+    pub fn rxla_b200_gated_delta_workspace_size(
+        batch: i32, tokens: i32, heads: i32, head_dim: i32, bytes: *mut usize,
+    ) -> i32;
+    pub fn rxla_b200_gated_delta(args: *const rxla_b200_gated_delta_args, stream: *mut c_void) -> i32;
 
     pub fn rxla_b200_decoder_create(
         config: *const rxla_b200_decoder_config, device: i32, comm: *mut rxla_b200_comm,

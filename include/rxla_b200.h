@@ -279,6 +279,62 @@ int32_t rxla_b200_rms_norm_bf16(const float* x, const float* weight, int64_t row
 int32_t rxla_b200_argmax(const float* logits, int64_t rows, int64_t vocab, int32_t* out,
                          void* stream);
 
+/* ------------------------------------------- gated-delta linear attention
+ *
+ * The mixer of Qwen3.5's linear-attention layers between its input
+ * projections and its out_proj (gated_delta_attention,
+ * crates/rxla-models/src/qwen3_5/layers.rs:114-268), for `tokens` new tokens
+ * of each of `batch` sequences, continuing each sequence's state:
+ *
+ *   x    = silu(causal depthwise conv_K(mixed))        (layers.rs:131-145)
+ *   q, k = l2_norm per head (x·rsqrt(Σx²+1e-6)); q ·= 1/sqrt(D)   (:103-160)
+ *   beta = sigmoid(b);  g = exp(softplus(a + dt_bias) · -exp(A_log)) (:179-212)
+ *   per token:  S = g·S;  S += k ⊗ beta·(v − Sᵀk);  o = Sᵀq          (:205-242)
+ *   out  = bf16(o · rsqrt(mean(o²) + eps) · norm_weight · silu(z))   (:243-259)
+ *
+ * with H = heads, D = head_dim (key and value heads alike, D ∈ {32, 64,
+ * 128}), W = H·D.  Inputs are the bf16 projections of the tokens, row r =
+ * b·tokens + t: mixed [rows, 3W] (q | k | v channels), z [rows, W], b and a
+ * [rows, H], each with its own row stride in elements (a fused projection
+ * passes offsets into one row).  conv_weight f32 [3W, K] (the reference's
+ * [3W, 1, K]), a_log / dt_bias f32 [H], norm_weight f32 [D].
+ * State (in place): conv_state bf16 [batch, K-1, 3W], the last K-1 mixed rows
+ * of each sequence, oldest first; state f32 [batch, H, D, D] with S[:, j]
+ * (column j of the reference's [Dk, Dv] state) contiguous at [b, h, j, :].
+ * has_state == 0 starts every sequence from zero state and zero history (the
+ * reference's full-sequence forward); nonzero continues from the stored
+ * state, so a prompt prefilled in one call or in several, then decoded one
+ * token per call, gives the full forward's outputs.  Output out bf16
+ * [rows, W] (the input of out_proj).  The workspace (256-byte aligned, size
+ * from rxla_b200_gated_delta_workspace_size, no zero-fill needed) holds the
+ * normalised q/k/v, the gates and o.  Calls on one state must be
+ * stream-ordered.
+ */
+typedef struct rxla_b200_gated_delta_args {
+  uint32_t struct_size; /* sizeof(rxla_b200_gated_delta_args) */
+  int32_t batch, tokens, heads, head_dim, conv_kernel;
+  const uint16_t* mixed;
+  const uint16_t* z;
+  const uint16_t* beta_logits;
+  const uint16_t* a;
+  int64_t mixed_row_stride, z_row_stride, b_row_stride, a_row_stride;
+  const float* conv_weight;
+  const float* a_log;
+  const float* dt_bias;
+  const float* norm_weight;
+  float eps;
+  int32_t has_state;
+  uint16_t* conv_state;
+  float* state;
+  uint16_t* out;
+  void* workspace;
+  size_t workspace_bytes;
+} rxla_b200_gated_delta_args;
+
+int32_t rxla_b200_gated_delta_workspace_size(int32_t batch, int32_t tokens, int32_t heads,
+                                             int32_t head_dim, size_t* bytes);
+int32_t rxla_b200_gated_delta(const rxla_b200_gated_delta_args* args, void* stream);
+
 /* ---------------------------------------------------------- decoder runner
  *
  * A Qwen3-style W8 decoder (plain q_proj, per-head q_norm / k_norm, full

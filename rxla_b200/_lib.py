@@ -79,6 +79,19 @@ class DecoderConfig(ctypes.Structure):
                                        "max_context", "tp_rank", "tp_size")]
 
 
+class GatedDeltaArgs(ctypes.Structure):
+    """rxla_b200_gated_delta_args."""
+    _fields_ = [("struct_size", ctypes.c_uint32)] + \
+        [(n, ctypes.c_int32) for n in ("batch", "tokens", "heads", "head_dim", "conv_kernel")] + \
+        [(n, ctypes.c_void_p) for n in ("mixed", "z", "beta_logits", "a")] + \
+        [(n, ctypes.c_int64) for n in ("mixed_row_stride", "z_row_stride", "b_row_stride",
+                                       "a_row_stride")] + \
+        [(n, ctypes.c_void_p) for n in ("conv_weight", "a_log", "dt_bias", "norm_weight")] + \
+        [("eps", ctypes.c_float), ("has_state", ctypes.c_int32)] + \
+        [(n, ctypes.c_void_p) for n in ("conv_state", "state", "out", "workspace")] + \
+        [("workspace_bytes", ctypes.c_size_t)]
+
+
 XLA_LINEAR_MAGIC = 0x4E4C3852  # RXLA_B200_XLA_LINEAR_MAGIC
 XLA_ATTENTION_MAGIC = 0x54413852  # RXLA_B200_XLA_ATTENTION_MAGIC
 
@@ -126,6 +139,8 @@ SIGNATURES = {
     "rxla_b200_paged_decode_attention_noalloc": (_i32, [ctypes.POINTER(PagedDecodeArgs), _vp]),
     "rxla_b200_rms_norm_bf16": (_i32, [_vp, _vp, _i64, _i64, _f32, _vp, _vp]),
     "rxla_b200_argmax": (_i32, [_vp, _i64, _i64, _vp, _vp]),
+    "rxla_b200_gated_delta_workspace_size": (_i32, [_i32, _i32, _i32, _i32, ctypes.POINTER(_sz)]),
+    "rxla_b200_gated_delta": (_i32, [ctypes.POINTER(GatedDeltaArgs), _vp]),
     "rxla_b200_decoder_create": (_i32, [ctypes.POINTER(DecoderConfig), _i32, _vp,
                                         ctypes.POINTER(_vp)]),
     "rxla_b200_decoder_destroy": (_i32, [_vp]),

@@ -1,0 +1,570 @@
+// gated_delta.cu — Qwen3.5 gated-delta linear attention (the "linear_attn"
+// mixer of crates/rxla-models/src/qwen3_5/layers.rs:114-268), between its
+// input projections and its out_proj.
+//
+// Three kernels per call, stream-ordered (programmatic dependent launch):
+//  1. gdn_prep_kernel — CTA = (channel block of D channels, 16 tokens,
+//     sequence), thread = channel: the causal depthwise conv of the mixed
+//     q/k/v projection over the last `conv_kernel` rows (rows before the
+//     call come from the sequence's conv state; each input row is loaded once
+//     per CTA and slid over the 16 tokens), SiLU, the L2 norm of every q and
+//     k head (q then scaled by 1/sqrt(D)); one extra channel block computes
+//     the gates beta = sigmoid(b) and exp(-exp(A_log) * softplus(a + dt_bias)).
+//  2. gdn_recurrence_kernel — the delta rule over the call's tokens, in
+//     order, with the state on chip.  Column j of a head's state S [Dk, Dv]
+//     evolves on its own:  S[:,j] = g S[:,j] + k δ_j,
+//     δ_j = beta (v_j − k·(g S[:,j])),  o_j = q·S[:,j].  Sixteen lanes hold
+//     one column (eight for D = 32), a warp two columns, a CTA a block of
+//     columns of one (sequence, head), so a 2048-token prompt of 16 heads
+//     still spreads over ~1000 warps.  One pass over a lane's rows per token
+//     updates S and forms both o_t = q_t·S_t and the next token's
+//     k_{t+1}·S_t, so one shuffle reduction of two values per token is the
+//     only cross-lane step on the recurrence's critical path.  Token rows of q, k,
+//     v and the gates stream through a double-buffered shared-memory stage
+//     (cp.async).  f32 throughout, as the reference's F32 graph.
+//  3. gdn_gated_norm_kernel — CTA = token row, warp = head: RMSNorm of each
+//     head's output over Dv, times norm.weight and silu(z), rounded to bf16
+//     for out_proj; the last row of each sequence also writes the new conv
+//     state.
+//
+// State layout (session state; the reference recomputes the whole sequence
+// each call and keeps none): the recurrent state f32 [batch, heads, Dv, Dk],
+// i.e. column j of S contiguous, and the conv state bf16
+// [batch, conv_kernel - 1, 3·heads·D] holding the last conv_kernel - 1 mixed
+// rows, oldest first.
+#include "common.cuh"
+
+namespace rxla {
+namespace gdn {
+
+constexpr int kMaxConvKernel = 8;
+constexpr int kPrepTokens = 16;  // tokens per prep CTA
+constexpr int kChunk = 16;       // tokens per shared-memory stage of the recurrence
+constexpr int kRecWarps = 4;     // warps per recurrence CTA
+
+__device__ __forceinline__ float sigmoid_f(float x) {
+  // logistic with a nonpositive exponent argument (crates/rxla-core/src/ops.rs:332-337)
+  const float e = __expf(-fabsf(x));
+  const float r = __fdividef(1.0f, 1.0f + e);
+  return x >= 0.0f ? r : e * r;
+}
+
+__device__ __forceinline__ float softplus_f(float x) {
+  // max(x, 0) + log1p(exp(-|x|)), the stable form the reference emits
+  // (crates/rxla-core/src/ops.rs:256-262)
+  return fmaxf(x, 0.0f) + log1pf(__expf(-fabsf(x)));
+}
+
+__device__ __forceinline__ float ld_bf16(const uint16_t* p) {
+  return __uint_as_float(((uint32_t)*p) << 16);
+}
+
+struct PrepArgs {
+  const uint16_t* mixed;
+  const uint16_t* b;
+  const uint16_t* a;
+  int64_t mixed_ld, b_ld, a_ld;
+  const float* conv_w;  // [3W, K]
+  const float* a_log;
+  const float* dt_bias;
+  const uint16_t* conv_state;  // [B, K-1, 3W] or null (zero history)
+  float* qkv;                  // [B*T, 3W]
+  float2* gb;                  // [B*T, H]: (exp(decay), beta)
+  int32_t T, H, K;
+  float q_scale;
+};
+
+// grid (3H + 1 channel blocks, ceil(T / kPrepTokens), B); block D threads.
+template <int D>
+__global__ void __launch_bounds__(D) gdn_prep_kernel(PrepArgs p) {
+  constexpr int TB = kPrepTokens, WIN = TB + kMaxConvKernel - 1;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int u = blockIdx.x, t0 = blockIdx.y * TB, b = blockIdx.z;
+  const int n = min(TB, p.T - t0);
+  const int W = p.H * D, C3 = 3 * W;
+  const int c = threadIdx.x;
+  const int64_t row0 = (int64_t)b * p.T + t0;
+  if (u == 3 * p.H) {
+    // gates (layers.rs:179-197, :205-212): beta = sigmoid(b);
+    // decay = softplus(a + dt_bias) * -exp(A_log), applied as exp(decay)
+    for (int i = c; i < n * p.H; i += D) {
+      const int tt = i / p.H, h = i % p.H;
+      const int64_t row = row0 + tt;
+      const float bl = ld_bf16(p.b + row * p.b_ld + h);
+      const float al = ld_bf16(p.a + row * p.a_ld + h);
+      const float decay = softplus_f(al + p.dt_bias[h]) * -__expf(p.a_log[h]);
+      p.gb[row * p.H + h] = make_float2(__expf(decay), sigmoid_f(bl));
+    }
+    return;
+  }
+  const int gc = u * D + c;  // global channel
+  // input rows t0 - (K-1) .. t0 + n - 1 of this channel (history from the
+  // conv state), each loaded once
+  float x[WIN];
+#pragma unroll
+  for (int w = 0; w < WIN; ++w) {
+    x[w] = 0.0f;
+    const int tau = t0 - (p.K - 1) + w;
+    if (w < n + p.K - 1) {
+      if (tau >= 0)
+        x[w] = ld_bf16(p.mixed + ((int64_t)b * p.T + tau) * p.mixed_ld + gc);
+      else if (p.conv_state)
+        x[w] = ld_bf16(p.conv_state + ((int64_t)b * (p.K - 1) + (p.K - 1 + tau)) * C3 + gc);
+    }
+  }
+  float wk[kMaxConvKernel];
+#pragma unroll
+  for (int j = 0; j < kMaxConvKernel; ++j) wk[j] = j < p.K ? p.conv_w[(int64_t)gc * p.K + j] : 0.0f;
+  // causal depthwise conv: out_t = Σ_j w[c, j] x[t - (K-1) + j] (padding
+  // [[K-1, 0]], no kernel reversal), then SiLU (layers.rs:131-145)
+  float y[TB];
+#pragma unroll
+  for (int tt = 0; tt < TB; ++tt) {
+    y[tt] = 0.0f;
+    if (tt < n) {  // n is uniform across the CTA: decode calls skip the rest
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kMaxConvKernel; ++j)
+        if (j < p.K) acc = fmaf(wk[j], x[tt + j], acc);
+      y[tt] = acc * sigmoid_f(acc);
+    }
+  }
+  float* out = p.qkv + row0 * C3 + gc;
+  if (u >= 2 * p.H) {  // v channels: conv + SiLU only
+#pragma unroll
+    for (int tt = 0; tt < TB; ++tt)
+      if (tt < n) out[(int64_t)tt * C3] = y[tt];
+    return;
+  }
+  // q / k heads: L2 norm over the head's D channels (l2_norm of
+  // layers.rs:103-112: x * rsqrt(Σx² + 1e-6)); q also times the f32 constant
+  // 1/sqrt(D) (layers.rs:146-152)
+  __shared__ float red[TB][D / 32];
+  const int lane = c & 31, warp = c >> 5;
+#pragma unroll
+  for (int tt = 0; tt < TB; ++tt) {
+    if (tt < n) {
+      float ss = y[tt] * y[tt];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) red[tt][warp] = ss;
+    }
+  }
+  __syncthreads();
+  const float scale = u < p.H ? p.q_scale : 1.0f;
+#pragma unroll
+  for (int tt = 0; tt < TB; ++tt) {
+    if (tt < n) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int w = 0; w < D / 32; ++w) ss += red[tt][w];
+      float v = y[tt] * rsqrtf(ss + 1e-6f);
+      if (u < p.H) v *= scale;
+      out[(int64_t)tt * C3] = v;
+    }
+  }
+}
+
+struct RecArgs {
+  const float* qkv;  // [B*T, 3W]
+  const float2* gb;  // [B*T, H]
+  float* state;      // [B, H, D(v), D(k)]
+  int32_t has_state;
+  float* o;  // [B*T, W]
+  int32_t T, H;
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Shared-memory stage of kChunk tokens: q [kChunk][D], k [kChunk + 1][D]
+// (the first row of the next chunk too: a token needs the next token's k),
+// v [kChunk][CPB], gates [kChunk], o [kChunk][CPB].
+template <int D, int CPB>
+struct Stage {
+  float q[kChunk][D];
+  float k[kChunk + 1][D];
+  float v[kChunk][CPB];
+  float2 g[kChunk];
+  float o[kChunk][CPB];
+};
+
+// Sum over the LPC lanes of a column (the low lane bits), two values at once.
+template <int LPC>
+__device__ __forceinline__ void reduce_col2(float& a, float& b) {
+#pragma unroll
+  for (int o = 1; o < LPC; o <<= 1) {
+    const float ta = __shfl_xor_sync(0xffffffffu, a, o);
+    const float tb = __shfl_xor_sync(0xffffffffu, b, o);
+    a += ta;
+    b += tb;
+  }
+}
+
+// Thread layout of the recurrence for head_dim D: LPC lanes hold a column,
+// R rows each, as float4 groups at rows 4·LPC·i + 4·part + e (conflict-free
+// shared-memory reads, 16-byte state accesses).
+template <int D>
+struct RecShape {
+  static constexpr int LPC = D >= 64 ? 16 : 8;  // lanes per column
+  static constexpr int R = D / LPC;             // rows per lane
+  static constexpr int NI = R / 4;              // float4 groups per lane
+  static constexpr int CPW = 32 / LPC;          // columns per warp
+  static constexpr int CPB = kRecWarps * CPW;   // columns per CTA
+  static_assert(R % 4 == 0, "rows per lane must be whole float4 groups");
+};
+
+// grid (D / CPB column blocks, H, B); block kRecWarps warps.
+template <int D>
+__global__ void __launch_bounds__(kRecWarps * 32) gdn_recurrence_kernel(RecArgs p) {
+  using Sh = RecShape<D>;
+  constexpr int LPC = Sh::LPC, R = Sh::R, NI = Sh::NI, CPB = Sh::CPB;
+  constexpr int NT = kRecWarps * 32;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Stage<D, CPB>* st = reinterpret_cast<Stage<D, CPB>*>(smem_raw);
+  const int cb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int W = p.H * D, C3 = 3 * W;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int part = lane & (LPC - 1);
+  const int col_local = warp * Sh::CPW + lane / LPC;
+  const int j = cb * CPB + col_local;
+  float s[R];
+  float* sp = p.state + (((int64_t)b * p.H + h) * D + j) * D;
+  pdl_wait();
+  if (p.has_state) {
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const float4 v = *reinterpret_cast<const float4*>(sp + 4 * LPC * i + 4 * part);
+      s[4 * i] = v.x;
+      s[4 * i + 1] = v.y;
+      s[4 * i + 2] = v.z;
+      s[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; ++r) s[r] = 0.0f;
+  }
+  const int64_t row0 = (int64_t)b * p.T;
+  const int nchunks = (p.T + kChunk - 1) / kChunk;
+  auto load = [&](int c, int buf) {
+    Stage<D, CPB>& S = st[buf];
+    const int t0 = c * kChunk;
+    const int n = min(kChunk, p.T - t0);
+    const int nk = min(kChunk + 1, p.T - t0);  // k rows: this chunk's and the next one's first
+    for (int i = tid; i < n * (D / 4); i += NT) {
+      const int tt = i / (D / 4), piece = i % (D / 4);
+      cp_async16(&S.q[tt][piece * 4], p.qkv + (row0 + t0 + tt) * C3 + h * D + piece * 4);
+    }
+    for (int i = tid; i < nk * (D / 4); i += NT) {
+      const int tt = i / (D / 4), piece = i % (D / 4);
+      cp_async16(&S.k[tt][piece * 4], p.qkv + (row0 + t0 + tt) * C3 + W + h * D + piece * 4);
+    }
+    for (int i = tid; i < n * (CPB / 4); i += NT) {
+      const int tt = i / (CPB / 4), piece = i % (CPB / 4);
+      cp_async16(&S.v[tt][piece * 4],
+                 p.qkv + (row0 + t0 + tt) * C3 + 2 * W + h * D + cb * CPB + piece * 4);
+    }
+    for (int tt = tid; tt < n; tt += NT) S.g[tt] = p.gb[(row0 + t0 + tt) * p.H + h];
+    cp_async_commit();
+  };
+  auto ld_rows = [&](const float* src, float (&dst)[R]) {
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const float4 v = *reinterpret_cast<const float4*>(src + 4 * LPC * i + 4 * part);
+      dst[4 * i] = v.x;
+      dst[4 * i + 1] = v.y;
+      dst[4 * i + 2] = v.z;
+      dst[4 * i + 3] = v.w;
+    }
+  };
+  float a = 0.0f;  // k_t · S_{t-1}[:, j] of the token about to be processed
+  // One token: S_t = g S + k_t δ (the reference's state.mul(decay) then
+  // add(k ⊗ δ)), δ = beta (v - g (k_t·S)), o_t = q_t · S_t, and the next
+  // token's k_{t+1} · S_t — one pass over the rows.  Row tt + 1 of the k
+  // stage exists for every tt; after the sequence's last token it holds
+  // stale values whose dot is never used.
+  auto step = [&](Stage<D, CPB>& S, int tt, const float (&kc)[R], float (&kn)[R]) {
+    const float2 g = S.g[tt];
+    const float vj = S.v[tt][col_local];
+    float qv[R];
+    ld_rows(&S.q[tt][0], qv);
+    ld_rows(&S.k[tt + 1][0], kn);
+    const float delta = (vj - g.x * a) * g.y;
+    float o0 = 0.f, o1 = 0.f, n0 = 0.f, n1 = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; r += 2) {
+      s[r] = fmaf(kc[r], delta, s[r] * g.x);
+      s[r + 1] = fmaf(kc[r + 1], delta, s[r + 1] * g.x);
+      o0 = fmaf(s[r], qv[r], o0);
+      o1 = fmaf(s[r + 1], qv[r + 1], o1);
+      n0 = fmaf(s[r], kn[r], n0);
+      n1 = fmaf(s[r + 1], kn[r + 1], n1);
+    }
+    float o = o0 + o1;
+    a = n0 + n1;
+    reduce_col2<LPC>(o, a);
+    if (part == 0) S.o[tt][col_local] = o;
+  };
+  float kA[R], kB[R];  // this token's k and the next one's, alternating
+  load(0, 0);
+  for (int c = 0; c < nchunks; ++c) {
+    const int buf = c & 1;
+    if (c + 1 < nchunks) {
+      load(c + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    Stage<D, CPB>& S = st[buf];
+    const int t0 = c * kChunk;
+    const int n = min(kChunk, p.T - t0);
+    if (c == 0) {
+      ld_rows(&S.k[0][0], kA);
+      if (p.has_state) {
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int r = 0; r < R; r += 2) {
+          a0 = fmaf(s[r], kA[r], a0);
+          a1 = fmaf(s[r + 1], kA[r + 1], a1);
+        }
+        a = a0 + a1;
+        float unused = 0.0f;
+        reduce_col2<LPC>(a, unused);
+      }
+    }
+    // two tokens per iteration, so the k registers alternate without copies
+    int tt = 0;
+    for (; tt + 1 < n; tt += 2) {
+      step(S, tt, kA, kB);
+      step(S, tt + 1, kB, kA);
+    }
+    if (tt < n) {
+      step(S, tt, kA, kB);
+#pragma unroll
+      for (int r = 0; r < R; ++r) kA[r] = kB[r];
+    }
+    __syncthreads();
+    // the chunk's outputs, CPB contiguous floats per token
+    for (int i = tid; i < n * (CPB / 4); i += NT) {
+      const int tt = i / (CPB / 4), piece = i % (CPB / 4);
+      *reinterpret_cast<float4*>(p.o + (row0 + t0 + tt) * W + h * D + cb * CPB + piece * 4) =
+          *reinterpret_cast<const float4*>(&S.o[tt][piece * 4]);
+    }
+    // buffer reuse: the load of chunk c + 2 into this buffer is issued at
+    // the top of the next iteration, after the __syncthreads above, when no
+    // thread reads this chunk's q, k, v or gates any more; S.o is written
+    // again only after that iteration's own __syncthreads, when every thread
+    // has finished the stores here
+  }
+  pdl_launch_dependents();
+#pragma unroll
+  for (int i = 0; i < NI; ++i)
+    *reinterpret_cast<float4*>(sp + 4 * LPC * i + 4 * part) =
+        make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+}
+
+struct NormArgs {
+  const float* o;  // [B*T, W]
+  const uint16_t* z;
+  int64_t z_ld;
+  const float* norm_w;  // [D]
+  float eps;
+  uint16_t* out;  // [B*T, W] bf16
+  // conv-state update (done by the last row of each sequence)
+  const uint16_t* mixed;
+  int64_t mixed_ld;
+  uint16_t* conv_state;  // [B, K-1, 3W]
+  int32_t has_state;
+  int32_t T, H, K;
+};
+
+constexpr int kNormWarps = 16;
+
+// grid B*T (one token row per CTA); warp = head.
+template <int D>
+__global__ void __launch_bounds__(kNormWarps * 32) gdn_gated_norm_kernel(NormArgs p) {
+  constexpr int E = D / 32;  // consecutive elements per lane
+  pdl_wait();
+  pdl_launch_dependents();
+  const int row = blockIdx.x;
+  const int W = p.H * D;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // output norm (layers.rs:243-259): o * rsqrt(mean(o²) + eps) * w * silu(z)
+  for (int h = warp; h < p.H; h += kNormWarps) {
+    const int64_t base = (int64_t)row * W + h * D + lane * E;
+    float v[E], z[E], w[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      v[e] = p.o[base + e];
+      z[e] = ld_bf16(p.z + (int64_t)row * p.z_ld + h * D + lane * E + e);
+      w[e] = p.norm_w[lane * E + e];
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss = fmaf(v[e], v[e], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float ns = rsqrtf(ss / (float)D + p.eps);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float y = ((v[e] * ns) * w[e]) * (z[e] * sigmoid_f(z[e]));
+      p.out[base + e] = __bfloat16_as_ushort(__float2bfloat16_rn(y));
+    }
+  }
+  // new conv state of sequence b: its last K-1 mixed rows (older rows from
+  // the previous state when the call has fewer than K-1 tokens).  Each
+  // channel belongs to one thread, which reads all of its new slots into
+  // registers before writing any, so an in-place move never overwrites an
+  // old slot it has still to read.
+  const int t = row % p.T, b = row / p.T;
+  if (t != p.T - 1 || p.K <= 1) return;
+  const int C3 = 3 * W, hist = p.K - 1;
+  uint16_t* cs = p.conv_state + (int64_t)b * hist * C3;
+  for (int c = threadIdx.x; c < C3; c += blockDim.x) {
+    uint16_t v[kMaxConvKernel - 1];
+#pragma unroll
+    for (int s = 0; s < kMaxConvKernel - 1; ++s) {
+      v[s] = 0;
+      if (s < hist) {
+        const int tau = p.T - hist + s;  // call-relative position of slot s
+        if (tau >= 0)
+          v[s] = p.mixed[((int64_t)b * p.T + tau) * p.mixed_ld + c];
+        else if (p.has_state)
+          v[s] = cs[(int64_t)(hist + tau) * C3 + c];
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < kMaxConvKernel - 1; ++s)
+      if (s < hist) cs[(int64_t)s * C3 + c] = v[s];
+  }
+}
+
+template <int D>
+int32_t launch_all(const PrepArgs& pa, const RecArgs& ra, const NormArgs& na, int B, int T,
+                   cudaStream_t s) {
+  cudaError_t e = launch_pdl(gdn_prep_kernel<D>,
+                             dim3(3 * pa.H + 1, (T + kPrepTokens - 1) / kPrepTokens, B), dim3(D),
+                             0, s, pa);
+  if (e != cudaSuccess) return cuda_fail(e, "gated_delta prep launch");
+  constexpr int CPB = RecShape<D>::CPB;
+  const size_t smem = 2 * sizeof(Stage<D, CPB>);
+  auto rec = gdn_recurrence_kernel<D>;
+  RXLA_CUDA_CHECK(cudaFuncSetAttribute(rec, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  e = launch_pdl(rec, dim3(D / CPB, ra.H, B), dim3(kRecWarps * 32), smem, s, ra);
+  if (e != cudaSuccess) return cuda_fail(e, "gated_delta recurrence launch");
+  e = launch_pdl(gdn_gated_norm_kernel<D>, dim3((unsigned)(B * T)), dim3(kNormWarps * 32), 0, s, na);
+  if (e != cudaSuccess) return cuda_fail(e, "gated_delta norm launch");
+  return RXLA_B200_OK;
+}
+
+size_t workspace_bytes(int64_t rows, int64_t H, int64_t D) {
+  // qkv [rows, 3W] f32, gates [rows, H] float2, o [rows, W] f32; each region
+  // 256-byte aligned
+  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+  const int64_t W = H * D;
+  return al((size_t)rows * 3 * W * 4) + al((size_t)rows * H * 8) + al((size_t)rows * W * 4);
+}
+
+}  // namespace gdn
+}  // namespace rxla
+
+extern "C" int32_t rxla_b200_gated_delta_workspace_size(int32_t batch, int32_t tokens,
+                                                        int32_t heads, int32_t head_dim,
+                                                        size_t* bytes) {
+  using namespace rxla;
+  RXLA_REQUIRE(bytes, "gated_delta_workspace_size: null argument");
+  RXLA_REQUIRE(batch >= 0 && tokens >= 0 && heads > 0 && head_dim > 0,
+               "gated_delta_workspace_size: bad shape");
+  *bytes = gdn::workspace_bytes((int64_t)batch * tokens, heads, head_dim);
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_gated_delta(const rxla_b200_gated_delta_args* a, void* stream) {
+  using namespace rxla;
+  RXLA_REQUIRE(a && a->struct_size == sizeof(rxla_b200_gated_delta_args),
+               "gated_delta: args null or struct_size mismatch");
+  const int64_t B = a->batch, T = a->tokens, H = a->heads, D = a->head_dim, K = a->conv_kernel;
+  RXLA_REQUIRE(B >= 0 && T >= 0, "gated_delta: batch and tokens must be >= 0");
+  RXLA_REQUIRE(D == 32 || D == 64 || D == 128, "gated_delta: head_dim must be 32, 64 or 128");
+  RXLA_REQUIRE(H > 0 && H <= 4096, "gated_delta: heads must lie in [1, 4096]");
+  RXLA_REQUIRE(K >= 1 && K <= gdn::kMaxConvKernel, "gated_delta: conv_kernel must lie in [1, 8]");
+  RXLA_REQUIRE(a->eps > 0.0f && a->eps == a->eps && a->eps < INFINITY,
+               "gated_delta: epsilon must be finite and positive");
+  if (B == 0 || T == 0) return RXLA_B200_OK;
+  RXLA_REQUIRE(B * T <= INT32_MAX && B <= 65535 && (T + gdn::kPrepTokens - 1) / gdn::kPrepTokens <= 65535,
+               "gated_delta: batch or tokens too large");
+  const int64_t W = H * D;
+  RXLA_REQUIRE(a->mixed && a->z && a->beta_logits && a->a && a->conv_weight && a->a_log &&
+                   a->dt_bias && a->norm_weight && a->state && a->out && a->workspace,
+               "gated_delta: null pointer");
+  RXLA_REQUIRE(K == 1 || a->conv_state, "gated_delta: conv_state is required for conv_kernel > 1");
+  RXLA_REQUIRE(a->mixed_row_stride >= 3 * W && a->z_row_stride >= W &&
+                   a->b_row_stride >= H && a->a_row_stride >= H,
+               "gated_delta: a row stride is shorter than its row");
+  RXLA_REQUIRE(reinterpret_cast<uintptr_t>(a->state) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(a->workspace) % 256 == 0,
+               "gated_delta: state must be 16-byte and workspace 256-byte aligned");
+  const size_t need = gdn::workspace_bytes(B * T, H, D);
+  RXLA_REQUIRE(a->workspace_bytes >= need, "gated_delta: workspace too small (see workspace_size)");
+  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  float* qkv = reinterpret_cast<float*>(ws);
+  float2* gb = reinterpret_cast<float2*>(ws + al((size_t)B * T * 3 * W * 4));
+  float* o = reinterpret_cast<float*>(ws + al((size_t)B * T * 3 * W * 4) + al((size_t)B * T * H * 8));
+
+  gdn::PrepArgs pa;
+  pa.mixed = a->mixed;
+  pa.b = a->beta_logits;
+  pa.a = a->a;
+  pa.mixed_ld = a->mixed_row_stride;
+  pa.b_ld = a->b_row_stride;
+  pa.a_ld = a->a_row_stride;
+  pa.conv_w = a->conv_weight;
+  pa.a_log = a->a_log;
+  pa.dt_bias = a->dt_bias;
+  pa.conv_state = (a->has_state && K > 1) ? a->conv_state : nullptr;
+  pa.qkv = qkv;
+  pa.gb = gb;
+  pa.T = (int32_t)T;
+  pa.H = (int32_t)H;
+  pa.K = (int32_t)K;
+  pa.q_scale = 1.0f / sqrtf((float)D);
+
+  gdn::RecArgs ra;
+  ra.qkv = qkv;
+  ra.gb = gb;
+  ra.state = a->state;
+  ra.has_state = a->has_state;
+  ra.o = o;
+  ra.T = (int32_t)T;
+  ra.H = (int32_t)H;
+
+  gdn::NormArgs na;
+  na.o = o;
+  na.z = a->z;
+  na.z_ld = a->z_row_stride;
+  na.norm_w = a->norm_weight;
+  na.eps = a->eps;
+  na.out = a->out;
+  na.mixed = a->mixed;
+  na.mixed_ld = a->mixed_row_stride;
+  na.conv_state = a->conv_state;
+  na.has_state = a->has_state;
+  na.T = (int32_t)T;
+  na.H = (int32_t)H;
+  na.K = (int32_t)K;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (D == 128) return gdn::launch_all<128>(pa, ra, na, (int)B, (int)T, s);
+  if (D == 64) return gdn::launch_all<64>(pa, ra, na, (int)B, (int)T, s);
+  return gdn::launch_all<32>(pa, ra, na, (int)B, (int)T, s);
+}

@@ -13,3 +13,4 @@
 #include "comm.cu"
 #include "noalloc.cu"
 #include "xla_custom_call.cu"
+#include "gated_delta.cu"

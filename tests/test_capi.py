@@ -237,3 +237,27 @@ def test_xla_handler_reports_a_bad_config_without_cuda():
     lib.rxla_b200_xla_paged_decode_attention(None, None, ctypes.cast(ctypes.byref(a), ctypes.c_void_p),
                                              64)
     assert "version 3" in lib.rxla_b200_last_error_message().decode()
+
+
+def test_gated_delta_validation_without_cuda():
+    """rxla_b200_gated_delta checks its shape before any CUDA call; an empty
+    call (no tokens) succeeds without launching."""
+    lib = _lib.load()
+    a = _lib.GatedDeltaArgs()
+    a.struct_size = ctypes.sizeof(a)
+    a.batch, a.tokens, a.heads, a.head_dim, a.conv_kernel, a.eps = 1, 4, 2, 96, 4, 1e-6
+    assert lib.rxla_b200_gated_delta(ctypes.byref(a), None) == _lib.INVALID_ARGUMENT
+    assert "head_dim" in lib.rxla_b200_last_error_message().decode()
+    a.head_dim, a.conv_kernel = 64, 9
+    assert lib.rxla_b200_gated_delta(ctypes.byref(a), None) == _lib.INVALID_ARGUMENT
+    a.conv_kernel, a.eps = 4, 0.0
+    assert lib.rxla_b200_gated_delta(ctypes.byref(a), None) == _lib.INVALID_ARGUMENT
+    a.eps, a.tokens = 1e-6, 0
+    assert lib.rxla_b200_gated_delta(ctypes.byref(a), None) == _lib.OK
+    a.tokens = 4  # null pointers
+    assert lib.rxla_b200_gated_delta(ctypes.byref(a), None) == _lib.INVALID_ARGUMENT
+    n = ctypes.c_size_t()
+    assert lib.rxla_b200_gated_delta_workspace_size(2, 3, 4, 64, ctypes.byref(n)) == _lib.OK
+    W = 4 * 64
+    al = lambda v: (v + 255) // 256 * 256
+    assert n.value == al(6 * 3 * W * 4) + al(6 * 4 * 8) + al(6 * W * 4)

@@ -67,7 +67,8 @@ def _rust_struct_fields(name):
 
 
 def test_structs_keep_the_header_field_order():
-    for name in ("rxla_b200_paged_decode_args", "rxla_b200_decoder_config",
+    for name in ("rxla_b200_paged_decode_args", "rxla_b200_gated_delta_args",
+                 "rxla_b200_decoder_config",
                  "rxla_b200_xla_linear_config", "rxla_b200_xla_attention_config"):
         assert _c_struct_fields(name) == _rust_struct_fields(name), name
 
