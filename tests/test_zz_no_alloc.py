@@ -103,6 +103,17 @@ def test_noalloc_matches_workspace_entry_point_twice(shape):
         assert (np.abs(got - ref_np) <= tol).all()
         assert torch.equal(cache.k, k_after)  # the same append
     assert lib.rxla_b200_device_status(0) == 0
+    # and both against the CPU oracle's restatement of the attention step,
+    # at the attention tests' tolerance
+    qkv_np = c["qkv"]
+    ora, _ = oracle.paged_decode_attention(
+        q=qkv_np[:, :hq * d], k_new=qkv_np[:, hq * d:(hq + hkv) * d],
+        v_new=qkv_np[:, (hq + hkv) * d:], k_pages=c["kp"].copy(), v_pages=c["vp"].copy(),
+        page_table=c["pt"], ctx_lens=c["ctx"].copy(), hq=hq, hkv=hkv, d=d,
+        q_norm_w=qn.cpu().numpy(), k_norm_w=kn.cpu().numpy(), eps=1e-6,
+        inv_freq=inv.cpu().numpy(), rotary_dim=d)
+    vmax = np.abs(oracle.bf16_bits_to_f32(c["vp"])).max()
+    assert (np.abs(got - ora) <= 2.0 ** -7 * np.abs(ora) + 2.0 ** -14 * vmax + 1e-6).all()
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
