@@ -75,10 +75,12 @@ struct PrepArgs {
   float q_scale;
 };
 
-// grid (3H + 1 channel blocks, ceil(T / kPrepTokens), B); block D threads.
-template <int D>
+// grid (3H + 1 channel blocks, ceil(T / TB), B); block D threads.  TB = 16
+// tokens per CTA, or 1 for single-token (decode) calls, whose unrolled loops
+// are then 16 times shorter.
+template <int D, int TB>
 __global__ void __launch_bounds__(D) gdn_prep_kernel(PrepArgs p) {
-  constexpr int TB = kPrepTokens, WIN = TB + kMaxConvKernel - 1;
+  constexpr int WIN = TB + kMaxConvKernel - 1;
   pdl_wait();
   pdl_launch_dependents();
   const int u = blockIdx.x, t0 = blockIdx.y * TB, b = blockIdx.z;
@@ -227,14 +229,16 @@ __device__ __forceinline__ void reduce_col2(float& a, float& b) {
 // stage; ACC independent partial sums per dot product.
 //  - PROMPT (long calls): 8 lanes per column, 64-token stages, 4 partial sums
 //    — fewer shuffle levels and fewer barriers on the sequential chain;
-//  - DECODE (a few tokens per sequence, many sequences): 16 lanes per column
-//    and 16-token stages — small CTAs, many resident, for the state stream.
-// (2048-token prompt, 16 heads of 128: 335 µs against 413 µs with the decode
-// shape; batch-64 decode: 35 µs against 86 µs with the prompt shape.)
+//  - DECODE (a few tokens per sequence, many sequences): 8 lanes per column
+//    and 8-token stages — small CTAs (~20 KB of shared memory), many
+//    resident, 64 bytes of state per thread in flight.
+// (2048-token prompt, 16 heads of 128: 335 µs against 413 µs with 16 lanes
+// and 16-token stages; batch-64 decode: 35 µs against 86 µs with the prompt
+// shape.)
 template <int D, bool PROMPT>
 struct RecShape {
-  static constexpr int LPC = (PROMPT || D < 64) ? 8 : 16;  // lanes per column
-  static constexpr int CH = PROMPT ? 64 : 16;              // tokens per stage
+  static constexpr int LPC = 8;               // lanes per column
+  static constexpr int CH = PROMPT ? 64 : 8;  // tokens per stage
   static constexpr int ACC = PROMPT ? 4 : 2;
   static constexpr int R = D / LPC;            // rows per lane
   static constexpr int NI = R / 4;             // float4 groups per lane
@@ -261,7 +265,11 @@ __global__ void __launch_bounds__(kRecWarps * 32) gdn_recurrence_kernel(RecArgs 
   const int j = cb * CPB + col_local;
   float s[R];
   float* sp = p.state + (((int64_t)b * p.H + h) * D + j) * D;
-  pdl_wait();
+  // The state is read before griddepcontrol.wait: its last writer is the
+  // previous call's recurrence kernel, two or more grids back on the stream,
+  // which has completed when this grid starts (every kernel of this library
+  // triggers its dependents only after its own wait), so the load overlaps
+  // the prep kernel that directly precedes this one.
   if (p.has_state) {
 #pragma unroll
     for (int i = 0; i < NI; ++i) {
@@ -275,6 +283,7 @@ __global__ void __launch_bounds__(kRecWarps * 32) gdn_recurrence_kernel(RecArgs 
 #pragma unroll
     for (int r = 0; r < R; ++r) s[r] = 0.0f;
   }
+  pdl_wait();
   const int64_t row0 = (int64_t)b * p.T;
   const int nchunks = (p.T + CH - 1) / CH;
   auto load = [&](int c, int buf) {
@@ -489,9 +498,10 @@ int32_t launch_recurrence(const RecArgs& ra, int B, cudaStream_t s) {
 template <int D>
 int32_t launch_all(const PrepArgs& pa, const RecArgs& ra, const NormArgs& na, int B, int T,
                    cudaStream_t s) {
-  cudaError_t e = launch_pdl(gdn_prep_kernel<D>,
-                             dim3(3 * pa.H + 1, (T + kPrepTokens - 1) / kPrepTokens, B), dim3(D),
-                             0, s, pa);
+  cudaError_t e = T == 1 ? launch_pdl(gdn_prep_kernel<D, 1>, dim3(3 * pa.H + 1, 1, B), dim3(D), 0, s, pa)
+                         : launch_pdl(gdn_prep_kernel<D, kPrepTokens>,
+                                      dim3(3 * pa.H + 1, (T + kPrepTokens - 1) / kPrepTokens, B),
+                                      dim3(D), 0, s, pa);
   if (e != cudaSuccess) return cuda_fail(e, "gated_delta prep launch");
   const int32_t rc = T > kLongCall ? launch_recurrence<D, true>(ra, B, s)
                                    : launch_recurrence<D, false>(ra, B, s);
