@@ -75,14 +75,53 @@ struct PrepArgs {
   float q_scale;
 };
 
+// Per-token sums of squares of a warp's 32 channels for TB tokens: a
+// reduce-scatter butterfly (TB = 16: 16 shuffles instead of 16 × 5); lane l
+// ends with the full sum of token `tok`; lanes with tok_owner true write it.
+template <int TB>
+__device__ __forceinline__ void token_sums(const float (&y)[TB], int lane, float& sum, int& tok,
+                                           bool& tok_owner) {
+  if constexpr (TB == 16) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = y[i] * y[i];
+    tok = 0;
+#pragma unroll
+    for (int half = 8; half >= 1; half >>= 1) {
+      const int off = 2 * half;  // lane distance 16, 8, 4, 2
+      const bool up = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = up ? v[i] : v[i + half];
+        const float keep = up ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+      tok += up ? half : 0;
+    }
+    sum = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+    tok_owner = (lane & 1) == 0;
+  } else {
+    static_assert(TB == 1, "token blocks of 1 or 16");
+    float ss = y[0] * y[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    sum = ss;
+    tok = 0;
+    tok_owner = lane == 0;
+  }
+}
+
 // grid (3H + 1 channel blocks, ceil(T / TB), B); block D threads.  TB = 16
 // tokens per CTA, or 1 for single-token (decode) calls, whose unrolled loops
-// are then 16 times shorter.
-template <int D, int TB>
+// are then 16 times shorter.  KC = 4: the conv width as a constant (Qwen3.5's
+// conv_kernel, weights read as one float4); KC = 0: the runtime width (<= 8).
+template <int D, int TB, int KC>
 __global__ void __launch_bounds__(D) gdn_prep_kernel(PrepArgs p) {
-  constexpr int WIN = TB + kMaxConvKernel - 1;
+  constexpr int KM = KC > 0 ? KC : kMaxConvKernel;  // taps unrolled
+  constexpr int WIN = TB + KM - 1;
   pdl_wait();
   pdl_launch_dependents();
+  const int K = KC > 0 ? KC : p.K;
   const int u = blockIdx.x, t0 = blockIdx.y * TB, b = blockIdx.z;
   const int n = min(TB, p.T - t0);
   const int W = p.H * D, C3 = 3 * W;
@@ -105,15 +144,21 @@ __global__ void __launch_bounds__(D) gdn_prep_kernel(PrepArgs p) {
   // input rows t0 - (K-1) .. t0 + n - 1 of this channel (history from the
   // conv state), each loaded once
   float x[WIN];
+  if (t0 >= K - 1) {  // every row inside this call: one strided walk
+    const uint16_t* mp = p.mixed + (row0 - (K - 1)) * p.mixed_ld + gc;
 #pragma unroll
-  for (int w = 0; w < WIN; ++w) {
-    x[w] = 0.0f;
-    const int tau = t0 - (p.K - 1) + w;
-    if (w < n + p.K - 1) {
-      if (tau >= 0)
-        x[w] = ld_bf16(p.mixed + ((int64_t)b * p.T + tau) * p.mixed_ld + gc);
-      else if (p.conv_state)
-        x[w] = ld_bf16(p.conv_state + ((int64_t)b * (p.K - 1) + (p.K - 1 + tau)) * C3 + gc);
+    for (int w = 0; w < WIN; ++w) x[w] = w < n + K - 1 ? ld_bf16(mp + (int64_t)w * p.mixed_ld) : 0.0f;
+  } else {
+#pragma unroll
+    for (int w = 0; w < WIN; ++w) {
+      x[w] = 0.0f;
+      const int tau = t0 - (K - 1) + w;
+      if (w < n + K - 1) {
+        if (tau >= 0)
+          x[w] = ld_bf16(p.mixed + ((int64_t)b * p.T + tau) * p.mixed_ld + gc);
+        else if (p.conv_state)
+          x[w] = ld_bf16(p.conv_state + ((int64_t)b * (K - 1) + (K - 1 + tau)) * C3 + gc);
+      }
     }
   }
   // A call of at most 16 tokens per sequence has one token block: this
@@ -121,26 +166,34 @@ __global__ void __launch_bounds__(D) gdn_prep_kernel(PrepArgs p) {
   // it holds the channel's new history (inputs n .. n + K - 2) in registers,
   // so it writes it (longer calls: the last row's gdn_gated_norm_kernel CTA)
   if (gridDim.y == 1 && p.conv_state_out) {
-    uint16_t* cs = p.conv_state_out + (int64_t)b * (p.K - 1) * C3 + gc;
+    uint16_t* cs = p.conv_state_out + (int64_t)b * (K - 1) * C3 + gc;
 #pragma unroll
     for (int w = 0; w < WIN; ++w)  // slot w - n holds x[w] (static register indices)
-      if (w >= n && w < n + p.K - 1)
+      if (w >= n && w < n + K - 1)
         cs[(int64_t)(w - n) * C3] = __bfloat16_as_ushort(__float2bfloat16_rn(x[w]));
   }
-  float wk[kMaxConvKernel];
+  float wk[KM];
+  if constexpr (KC == 4) {
+    const float4 w4 = *reinterpret_cast<const float4*>(p.conv_w + (int64_t)gc * 4);
+    wk[0] = w4.x;
+    wk[1] = w4.y;
+    wk[2] = w4.z;
+    wk[3] = w4.w;
+  } else {
 #pragma unroll
-  for (int j = 0; j < kMaxConvKernel; ++j) wk[j] = j < p.K ? p.conv_w[(int64_t)gc * p.K + j] : 0.0f;
+    for (int j = 0; j < KM; ++j) wk[j] = j < K ? p.conv_w[(int64_t)gc * K + j] : 0.0f;
+  }
   // causal depthwise conv: out_t = Σ_j w[c, j] x[t - (K-1) + j] (padding
   // [[K-1, 0]], no kernel reversal), then SiLU (layers.rs:131-145)
   float y[TB];
 #pragma unroll
   for (int tt = 0; tt < TB; ++tt) {
     y[tt] = 0.0f;
-    if (tt < n) {  // n is uniform across the CTA: decode calls skip the rest
+    if (tt < n) {  // n is uniform across the CTA
       float acc = 0.0f;
 #pragma unroll
-      for (int j = 0; j < kMaxConvKernel; ++j)
-        if (j < p.K) acc = fmaf(wk[j], x[tt + j], acc);
+      for (int j = 0; j < KM; ++j)
+        if (KC > 0 || j < K) acc = fmaf(wk[j], x[tt + j], acc);
       y[tt] = acc * sigmoid_f(acc);
     }
   }
@@ -156,14 +209,12 @@ __global__ void __launch_bounds__(D) gdn_prep_kernel(PrepArgs p) {
   // 1/sqrt(D) (layers.rs:146-152)
   __shared__ float red[TB][D / 32];
   const int lane = c & 31, warp = c >> 5;
-#pragma unroll
-  for (int tt = 0; tt < TB; ++tt) {
-    if (tt < n) {
-      float ss = y[tt] * y[tt];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) red[tt][warp] = ss;
-    }
+  {
+    float sum;
+    int tok;
+    bool owner;
+    token_sums<TB>(y, lane, sum, tok, owner);
+    if (owner) red[tok][warp] = sum;
   }
   __syncthreads();
   const float scale = u < p.H ? p.q_scale : 1.0f;
@@ -421,6 +472,7 @@ struct NormArgs {
   uint16_t* conv_state;  // [B, K-1, 3W]
   int32_t has_state;
   int32_t T, H, K;
+  int32_t vec;  // z rows and norm_w allow 8- / 16-byte loads (D = 128)
 };
 
 constexpr int kNormWarps = 16;
@@ -437,12 +489,35 @@ __global__ void __launch_bounds__(kNormWarps * 32) gdn_gated_norm_kernel(NormArg
   // output norm (layers.rs:243-259): o * rsqrt(mean(o²) + eps) * w * silu(z)
   for (int h = warp; h < p.H; h += kNormWarps) {
     const int64_t base = (int64_t)row * W + h * D + lane * E;
+    const uint16_t* zr = p.z + (int64_t)row * p.z_ld + h * D + lane * E;
     float v[E], z[E], w[E];
+    if constexpr (E == 4) {
+      const float4 o4 = *reinterpret_cast<const float4*>(p.o + base);
+      v[0] = o4.x;
+      v[1] = o4.y;
+      v[2] = o4.z;
+      v[3] = o4.w;
+    } else {
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      v[e] = p.o[base + e];
-      z[e] = ld_bf16(p.z + (int64_t)row * p.z_ld + h * D + lane * E + e);
-      w[e] = p.norm_w[lane * E + e];
+      for (int e = 0; e < E; ++e) v[e] = p.o[base + e];
+    }
+    if (E == 4 && p.vec) {
+      const uint2 z4 = *reinterpret_cast<const uint2*>(zr);
+      z[0] = bf16_lo(z4.x);
+      z[1] = bf16_hi(z4.x);
+      z[2] = bf16_lo(z4.y);
+      z[3] = bf16_hi(z4.y);
+      const float4 w4 = *reinterpret_cast<const float4*>(p.norm_w + lane * E);
+      w[0] = w4.x;
+      w[1] = w4.y;
+      w[2] = w4.z;
+      w[3] = w4.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        z[e] = ld_bf16(zr + e);
+        w[e] = p.norm_w[lane * E + e];
+      }
     }
     float ss = 0.0f;
 #pragma unroll
@@ -450,10 +525,14 @@ __global__ void __launch_bounds__(kNormWarps * 32) gdn_gated_norm_kernel(NormArg
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float ns = rsqrtf(ss / (float)D + p.eps);
+    float y[E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const float y = ((v[e] * ns) * w[e]) * (z[e] * sigmoid_f(z[e]));
-      p.out[base + e] = __bfloat16_as_ushort(__float2bfloat16_rn(y));
+    for (int e = 0; e < E; ++e) y[e] = ((v[e] * ns) * w[e]) * (z[e] * sigmoid_f(z[e]));
+    if (E == 4 && p.vec) {
+      *reinterpret_cast<uint2*>(p.out + base) = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) p.out[base + e] = __bfloat16_as_ushort(__float2bfloat16_rn(y[e]));
     }
   }
   // new conv state of sequence b: its last K-1 mixed rows (older rows from
@@ -498,10 +577,15 @@ int32_t launch_recurrence(const RecArgs& ra, int B, cudaStream_t s) {
 template <int D>
 int32_t launch_all(const PrepArgs& pa, const RecArgs& ra, const NormArgs& na, int B, int T,
                    cudaStream_t s) {
-  cudaError_t e = T == 1 ? launch_pdl(gdn_prep_kernel<D, 1>, dim3(3 * pa.H + 1, 1, B), dim3(D), 0, s, pa)
-                         : launch_pdl(gdn_prep_kernel<D, kPrepTokens>,
-                                      dim3(3 * pa.H + 1, (T + kPrepTokens - 1) / kPrepTokens, B),
-                                      dim3(D), 0, s, pa);
+  const bool k4 = pa.K == 4 && reinterpret_cast<uintptr_t>(pa.conv_w) % 16 == 0;
+  const dim3 g1(3 * pa.H + 1, 1, B), gt(3 * pa.H + 1, (T + kPrepTokens - 1) / kPrepTokens, B);
+  cudaError_t e;
+  if (T == 1)
+    e = k4 ? launch_pdl(gdn_prep_kernel<D, 1, 4>, g1, dim3(D), 0, s, pa)
+           : launch_pdl(gdn_prep_kernel<D, 1, 0>, g1, dim3(D), 0, s, pa);
+  else
+    e = k4 ? launch_pdl(gdn_prep_kernel<D, kPrepTokens, 4>, gt, dim3(D), 0, s, pa)
+           : launch_pdl(gdn_prep_kernel<D, kPrepTokens, 0>, gt, dim3(D), 0, s, pa);
   if (e != cudaSuccess) return cuda_fail(e, "gated_delta prep launch");
   const int32_t rc = T > kLongCall ? launch_recurrence<D, true>(ra, B, s)
                                    : launch_recurrence<D, false>(ra, B, s);
@@ -608,6 +692,9 @@ extern "C" int32_t rxla_b200_gated_delta(const rxla_b200_gated_delta_args* a, vo
   na.T = (int32_t)T;
   na.H = (int32_t)H;
   na.K = (int32_t)K;
+  na.vec = D == 128 && reinterpret_cast<uintptr_t>(a->z) % 8 == 0 && a->z_row_stride % 4 == 0 &&
+           reinterpret_cast<uintptr_t>(a->norm_weight) % 16 == 0 &&
+           reinterpret_cast<uintptr_t>(a->out) % 8 == 0;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (D == 128) return gdn::launch_all<128>(pa, ra, na, (int)B, (int)T, s);
