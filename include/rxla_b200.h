@@ -279,6 +279,16 @@ int32_t rxla_b200_rms_norm_bf16(const float* x, const float* weight, int64_t row
 int32_t rxla_b200_argmax(const float* logits, int64_t rows, int64_t vocab, int32_t* out,
                          void* stream);
 
+/* Output gate of Qwen3.5's full-attention layers
+ * (crates/rxla-models/src/qwen3_5/layers.rs:50-55, 94-95):
+ * y[r, c] = bf16(x[r, c] · sigmoid(gate[r, c])) for bf16 x (the attended
+ * values) and gate (the gate half of q_proj), rows × width, each with its
+ * own row stride in elements (a fused projection passes an offset into its
+ * rows).  y may alias x. */
+int32_t rxla_b200_sigmoid_gate(const uint16_t* x, int64_t x_row_stride, const uint16_t* gate,
+                               int64_t gate_row_stride, int64_t rows, int64_t width, uint16_t* y,
+                               int64_t y_row_stride, void* stream);
+
 /* ------------------------------------------- gated-delta linear attention
  *
  * The mixer of Qwen3.5's linear-attention layers between its input

@@ -188,6 +188,28 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int64_t vocab,
   }
 }
 
+// ------------------------------------------------------ sigmoid output gate
+// y[r, c] = bf16(x[r, c] · sigmoid(gate[r, c])), the output gate of Qwen3.5's
+// full-attention layers (crates/rxla-models/src/qwen3_5/layers.rs:50-55,
+// 94-95): the gate half of q_proj, through the logistic, times the attended
+// values, in f32, rounded once for o_proj's bf16 input.
+__global__ void sigmoid_gate_kernel(const uint16_t* __restrict__ x, int64_t x_ld,
+                                    const uint16_t* __restrict__ g, int64_t g_ld, int64_t width,
+                                    uint16_t* __restrict__ y, int64_t y_ld) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t r = blockIdx.y;
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < width;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    const float xv = __uint_as_float((uint32_t)x[r * x_ld + c] << 16);
+    const float gv = __uint_as_float((uint32_t)g[r * g_ld + c] << 16);
+    // logistic with a nonpositive exponent argument (crates/rxla-core/src/ops.rs:332-337)
+    const float e = expf(-fabsf(gv));
+    const float sig = gv >= 0.0f ? 1.0f / (1.0f + e) : e / (1.0f + e);
+    y[r * y_ld + c] = __bfloat16_as_ushort(__float2bfloat16_rn(xv * sig));
+  }
+}
+
 }  // namespace rxla
 
 extern "C" int32_t rxla_b200_abi_version(void) { return RXLA_B200_ABI_VERSION; }
@@ -251,5 +273,23 @@ extern "C" int32_t rxla_b200_argmax(const float* logits, int64_t rows, int64_t v
                              static_cast<cudaStream_t>(stream), logits, vocab, out,
                              (int32_t*)nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_sigmoid_gate(const uint16_t* x, int64_t x_row_stride,
+                                          const uint16_t* gate, int64_t gate_row_stride,
+                                          int64_t rows, int64_t width, uint16_t* y,
+                                          int64_t y_row_stride, void* stream) {
+  using namespace rxla;
+  RXLA_REQUIRE(rows >= 0 && width >= 0 && rows <= 65535, "sigmoid_gate: bad shape");
+  if (rows == 0 || width == 0) return RXLA_B200_OK;
+  RXLA_REQUIRE(x && gate && y, "sigmoid_gate: null pointer");
+  RXLA_REQUIRE(x_row_stride >= width && gate_row_stride >= width && y_row_stride >= width,
+               "sigmoid_gate: a row stride is shorter than the row");
+  const unsigned bx = (unsigned)std::min<int64_t>((width + 255) / 256, 64);
+  cudaError_t e = launch_pdl(sigmoid_gate_kernel, dim3(bx, (unsigned)rows), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), x, x_row_stride, gate,
+                             gate_row_stride, width, y, y_row_stride);
+  if (e != cudaSuccess) return cuda_fail(e, "sigmoid_gate launch");
   return RXLA_B200_OK;
 }

@@ -285,10 +285,25 @@ def paged_decode_attention(q, k_new, v_new, cache: PagedKvCache, *, q_heads: int
     return out
 
 
+def sigmoid_gate(x: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None,
+                 stream=None) -> torch.Tensor:
+    """bf16(x · sigmoid(gate)) through rxla_b200_sigmoid_gate: Qwen3.5's
+    attention output gate (crates/rxla-models/src/qwen3_5/layers.rs:50-55,
+    94-95).  x, gate: bf16 [rows, width] views with unit inner stride."""
+    if x.dtype != torch.bfloat16 or gate.dtype != torch.bfloat16 or x.shape != gate.shape \
+            or x.dim() != 2 or x.stride(1) != 1 or gate.stride(1) != 1:
+        raise InvalidLayerInput("sigmoid_gate needs bf16 [rows, width] x and gate")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    _lib.call("rxla_b200_sigmoid_gate", _ptr(x), x.stride(0), _ptr(gate), gate.stride(0),
+              x.shape[0], x.shape[1], _ptr(out), out.stride(0), _stream(stream))
+    return out
+
+
 def device_status(reset: bool = False) -> int:
     return int(_lib.load().rxla_b200_device_status(int(reset)))
 
 
 __all__ = ["QuantizedLinear", "quantized_linear", "bf16_linear", "rms_norm_bf16", "argmax",
            "rope_inv_freq", "device_status", "InvalidLayerInput", "RxlaError", "PagedKvCache",
-           "paged_decode_attention", "paged_decode_workspace_size"]
+           "paged_decode_attention", "paged_decode_workspace_size", "sigmoid_gate"]

@@ -261,3 +261,10 @@ def test_gated_delta_validation_without_cuda():
     W = 4 * 64
     al = lambda v: (v + 255) // 256 * 256
     assert n.value == al(6 * 3 * W * 4) + al(6 * 4 * 8) + al(6 * W * 4)
+
+
+def test_sigmoid_gate_validation_without_cuda():
+    lib = _lib.load()
+    assert lib.rxla_b200_sigmoid_gate(None, 8, None, 8, -1, 8, None, 8, None) == _lib.INVALID_ARGUMENT
+    assert lib.rxla_b200_sigmoid_gate(None, 8, None, 8, 0, 8, None, 8, None) == _lib.OK
+    assert lib.rxla_b200_sigmoid_gate(None, 4, None, 8, 2, 8, None, 8, None) == _lib.INVALID_ARGUMENT
