@@ -227,6 +227,10 @@ extern "C" {
     ) -> i32;
     pub fn rxla_b200_argmax(logits: *const f32, rows: i64, vocab: i64, out: *mut i32, stream: *mut c_void) -> i32;
 
+    pub fn rxla_b200_w8_embedding(
+        ids: *const i32, rows: i64, weight: *const u8, scale: *const f32, vocab: i64, hidden: i64,
+        group_size: i64, out: *mut f32, stream: *mut c_void,
+    ) -> i32;
     pub fn rxla_b200_sigmoid_gate(
         x: *const u16, x_row_stride: i64, gate: *const u16, gate_row_stride: i64, rows: i64,
         width: i64, y: *mut u16, y_row_stride: i64, stream: *mut c_void,

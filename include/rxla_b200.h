@@ -279,6 +279,15 @@ int32_t rxla_b200_rms_norm_bf16(const float* x, const float* weight, int64_t row
 int32_t rxla_b200_argmax(const float* logits, int64_t rows, int64_t vocab, int32_t* out,
                          void* stream);
 
+/* W8 token embedding (crates/rxla-models/src/qwen3_5/mod.rs:134-155):
+ * out[r, :] = f32(weight[ids[r], :] - 128) · scale[ids[r], c / group_size]
+ * for int32 ids [rows] (device), u8 weight [vocab, hidden], f32 scale
+ * [vocab, hidden / group_size]; out f32 [rows, hidden].  An id outside
+ * [0, vocab) gives a zero row. */
+int32_t rxla_b200_w8_embedding(const int32_t* ids, int64_t rows, const uint8_t* weight,
+                               const float* scale, int64_t vocab, int64_t hidden,
+                               int64_t group_size, float* out, void* stream);
+
 /* Output gate of Qwen3.5's full-attention layers
  * (crates/rxla-models/src/qwen3_5/layers.rs:50-55, 94-95):
  * y[r, c] = bf16(x[r, c] · sigmoid(gate[r, c])) for bf16 x (the attended

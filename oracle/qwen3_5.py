@@ -21,7 +21,8 @@ def _sigmoid(x):
 
 
 def full_attention(x, params, *, attention_heads, key_value_heads, head_dim, rotary_dim,
-                   rope_theta, group_size, eps=1e-6, positions=None, round_attention=False):
+                   rope_theta, group_size, eps=1e-6, positions=None, round_attention=False,
+                   linear_mode=1):
     """x [B, T, hidden] F32 (the normalised layer input).  params: q_proj /
     k_proj / v_proj / o_proj `.weight` u8 and `.scale` f32, q_norm.weight and
     k_norm.weight f32 [D] (zero-centred: the norm multiplies by weight + 1).
@@ -29,13 +30,15 @@ def full_attention(x, params, *, attention_heads, key_value_heads, head_dim, rot
     round_attention=True rounds the attended values to bf16 before the gate,
     as the paged attention kernel's bf16 output does (the reference keeps
     them F32): the model of that one extra rounding point, used to measure
-    its effect."""
+    its effect.  linear_mode: the C oracle's W8 linear mode (1: the
+    reference's rounding points with f64 sums; 4: the same with f32 running
+    sums, the accumulation-noise model)."""
     B, T, hid = x.shape
     Hq, Hkv, D = attention_heads, key_value_heads, head_dim
 
     def proj(name, inp):
         return w8_linear(inp.reshape(B * T, -1), params[f"{name}.weight"], params[f"{name}.scale"],
-                         group_size, mode=1).reshape(B, T, -1)
+                         group_size, mode=linear_mode).reshape(B, T, -1)
 
     q = proj("q_proj", x).reshape(B, T, Hq, 2 * D)
     query = np.ascontiguousarray(q[..., :D])
@@ -62,3 +65,62 @@ def full_attention(x, params, *, attention_heads, key_value_heads, head_dim, rot
     att = att.astype(np.float64)
     y = (att * gate).astype(np.float32)                          # layers.rs:94-95
     return proj("o_proj", y)
+
+
+def qwen3_5_forward(ids, params, *, layer_types, vocabulary, hidden_size, attention_heads,
+                    key_value_heads, head_dim, linear_heads, linear_head_dim, rope_theta,
+                    rotary_dim, epsilon, quant_group_size, gpu_rounding=False):
+    """`qwen3_5(cx, token_ids, config)` (crates/rxla-models/src/qwen3_5/mod.rs:
+    199-260) on the CPU: ids [B, T]; returns logits [B, T, vocabulary].
+    params by the names below "model.language_model." (numpy arrays).
+
+    gpu_rounding=True models what the GPU path computes differently — f32
+    running sums in every W8 linear (the decoder tests' noise-floor model),
+    bf16 attended values before the output gate, and the tied head on bf16 x
+    and bf16 dequantized weights with an f32 sum (the reference's head is an
+    F32 linear, mod.rs:157-173) — so that their effect can be measured."""
+    from . import gated_delta as gdo
+    mode = 4 if gpu_rounding else 1
+    lin_mode = lambda x, w, s, g: w8_linear(x, w, s, g, mode=mode)
+    ids = np.asarray(ids)
+    B, T = ids.shape
+    G = quant_group_size
+    emb_w = np.asarray(params["embed_tokens.weight"])
+    emb_s = np.asarray(params["embed_tokens.scale"]).reshape(vocabulary, -1)
+    col = np.arange(hidden_size) // G
+    # quantized_embedding (mod.rs:134-155): take, cast, -128, × group scale (f32)
+    h = ((emb_w[ids].astype(np.float32) - np.float32(128.0)) *
+         emb_s[ids][..., col]).astype(np.float32)
+    zc = lambda name: (np.asarray(params[name], np.float32) + np.float32(1.0)).astype(np.float32)
+    for i, kind in enumerate(layer_types):
+        pre = f"layers.{i}."
+        xn = rms_norm(h, zc(pre + "input_layernorm.weight"), epsilon)
+        if kind == "linear":
+            sub = {k[len(pre + "linear_attn."):]: v for k, v in params.items()
+                   if k.startswith(pre + "linear_attn.")}
+            sub["conv1d.weight"] = np.asarray(sub["conv1d.weight"])
+            out, _, _ = gdo.gated_delta_attention(xn, sub, heads=linear_heads,
+                                                  head_dim=linear_head_dim, group_size=G,
+                                                  eps=epsilon, w8_linear=lambda x, w, s, g, mode=1:
+                                                  lin_mode(x, w, s, g))
+        else:
+            sub = {k[len(pre + "self_attn."):]: v for k, v in params.items()
+                   if k.startswith(pre + "self_attn.")}
+            out = full_attention(xn, sub, attention_heads=attention_heads,
+                                 key_value_heads=key_value_heads, head_dim=head_dim,
+                                 rotary_dim=rotary_dim, rope_theta=rope_theta, group_size=G,
+                                 eps=epsilon, round_attention=gpu_rounding, linear_mode=mode)
+        h = (h + out).astype(np.float32)                               # mod.rs:246
+        xn = rms_norm(h, zc(pre + "post_attention_layernorm.weight"), epsilon)
+
+        def lin(name, inp):
+            return w8_linear(inp.reshape(B * T, -1), params[pre + f"mlp.{name}.weight"],
+                             params[pre + f"mlp.{name}.scale"], G, mode=mode).reshape(B, T, -1)
+        gate = lin("gate_proj", xn).astype(np.float64)
+        up = lin("up_proj", xn).astype(np.float64)
+        y = (gate / (1.0 + np.exp(-gate)) * up).astype(np.float32)   # layers.rs:270-293
+        h = (h + lin("down_proj", y)).astype(np.float32)
+    hn = rms_norm(h, zc("norm.weight"), epsilon)
+    # tied LM head (mod.rs:157-173): F32 hidden · F32 dequantized embedding
+    return w8_linear(hn.reshape(B * T, -1), emb_w, emb_s, G,
+                     mode=5 if gpu_rounding else 0).reshape(B, T, vocabulary)

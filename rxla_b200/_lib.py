@@ -139,6 +139,7 @@ SIGNATURES = {
     "rxla_b200_paged_decode_attention_noalloc": (_i32, [ctypes.POINTER(PagedDecodeArgs), _vp]),
     "rxla_b200_rms_norm_bf16": (_i32, [_vp, _vp, _i64, _i64, _f32, _vp, _vp]),
     "rxla_b200_argmax": (_i32, [_vp, _i64, _i64, _vp, _vp]),
+    "rxla_b200_w8_embedding": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "rxla_b200_sigmoid_gate": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
     "rxla_b200_gated_delta_workspace_size": (_i32, [_i32, _i32, _i32, _i32, ctypes.POINTER(_sz)]),
     "rxla_b200_gated_delta": (_i32, [ctypes.POINTER(GatedDeltaArgs), _vp]),

@@ -210,6 +210,26 @@ __global__ void sigmoid_gate_kernel(const uint16_t* __restrict__ x, int64_t x_ld
   }
 }
 
+// ------------------------------------------------------------ W8 embedding
+// out[r, c] = f32(weight[id_r, c] - 128) · scale[id_r, c / group]: the W8
+// token embedding of qwen3_5/mod.rs:134-155 (take, cast, -128, × group
+// scale), one CTA per row, ids outside [0, vocab) give zero rows.
+__global__ void w8_embedding_kernel(const int32_t* __restrict__ ids, const uint8_t* __restrict__ w,
+                                    const float* __restrict__ scale, int64_t vocab, int64_t hidden,
+                                    int64_t group, float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t r = blockIdx.x;
+  const int32_t id = ids[r];
+  const bool ok = id >= 0 && id < vocab;
+  const int64_t groups = hidden / group;
+  for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
+    float v = 0.0f;
+    if (ok) v = (float)((int32_t)w[(int64_t)id * hidden + c] - 128) * scale[(int64_t)id * groups + c / group];
+    out[r * hidden + c] = v;
+  }
+}
+
 }  // namespace rxla
 
 extern "C" int32_t rxla_b200_abi_version(void) { return RXLA_B200_ABI_VERSION; }
@@ -291,5 +311,21 @@ extern "C" int32_t rxla_b200_sigmoid_gate(const uint16_t* x, int64_t x_row_strid
                              static_cast<cudaStream_t>(stream), x, x_row_stride, gate,
                              gate_row_stride, width, y, y_row_stride);
   if (e != cudaSuccess) return cuda_fail(e, "sigmoid_gate launch");
+  return RXLA_B200_OK;
+}
+
+extern "C" int32_t rxla_b200_w8_embedding(const int32_t* ids, int64_t rows, const uint8_t* weight,
+                                          const float* scale, int64_t vocab, int64_t hidden,
+                                          int64_t group_size, float* out, void* stream) {
+  using namespace rxla;
+  RXLA_REQUIRE(rows >= 0 && rows <= INT32_MAX && vocab > 0 && hidden > 0 && group_size > 0 &&
+                   hidden % group_size == 0,
+               "w8_embedding: bad shape (group_size must divide hidden)");
+  if (rows == 0) return RXLA_B200_OK;
+  RXLA_REQUIRE(ids && weight && scale && out, "w8_embedding: null pointer");
+  cudaError_t e = launch_pdl(w8_embedding_kernel, dim3((unsigned)rows), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), ids, weight, scale, vocab, hidden,
+                             group_size, out);
+  if (e != cudaSuccess) return cuda_fail(e, "w8_embedding launch");
   return RXLA_B200_OK;
 }

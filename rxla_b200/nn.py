@@ -285,6 +285,23 @@ def paged_decode_attention(q, k_new, v_new, cache: PagedKvCache, *, q_heads: int
     return out
 
 
+def w8_embedding(ids: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor, group_size: int,
+                 stream=None) -> torch.Tensor:
+    """The W8 token embedding (qwen3_5/mod.rs:134-155) through
+    rxla_b200_w8_embedding: ids int32 [...] on the device, weight u8 [vocab,
+    hidden], scale f32 [vocab, hidden / group_size]; returns f32 [..., hidden]."""
+    if ids.dtype != torch.int32 or weight.dtype != torch.uint8 or scale.dtype != torch.float32:
+        raise InvalidLayerInput("embedding needs int32 ids, u8 weight, f32 scale")
+    vocab, hidden = weight.shape
+    if hidden % group_size or scale.numel() != vocab * (hidden // group_size):
+        raise InvalidLayerInput("scale must be [vocab, hidden / group_size]")
+    ids_c = ids.contiguous()
+    out = torch.empty(*ids.shape, hidden, dtype=torch.float32, device=weight.device)
+    _lib.call("rxla_b200_w8_embedding", _ptr(ids_c), ids_c.numel(), _ptr(weight), _ptr(scale),
+              vocab, hidden, group_size, _ptr(out), _stream(stream))
+    return out
+
+
 def sigmoid_gate(x: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None,
                  stream=None) -> torch.Tensor:
     """bf16(x · sigmoid(gate)) through rxla_b200_sigmoid_gate: Qwen3.5's
@@ -306,4 +323,5 @@ def device_status(reset: bool = False) -> int:
 
 __all__ = ["QuantizedLinear", "quantized_linear", "bf16_linear", "rms_norm_bf16", "argmax",
            "rope_inv_freq", "device_status", "InvalidLayerInput", "RxlaError", "PagedKvCache",
-           "paged_decode_attention", "paged_decode_workspace_size", "sigmoid_gate"]
+           "paged_decode_attention", "paged_decode_workspace_size", "sigmoid_gate",
+           "w8_embedding"]

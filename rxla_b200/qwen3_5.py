@@ -1,4 +1,4 @@
-"""Host-side mirror of Qwen3.5's full-attention layer.
+"""Host-side mirror of Qwen3.5's full-attention layer and of the hybrid model.
 
 `GatedFullAttention` follows `full_attention(cx, input, angles, mask, config)`
 (crates/rxla-models/src/qwen3_5/layers.rs:28-100, paths inside the rxla
@@ -10,6 +10,10 @@ attention over the cached keys; the gated output through o_proj.  The
 arithmetic runs in librxla_b200: one W8 linear for the fused q | gate | k | v
 projection, rxla_b200_paged_decode_attention (norms, RoPE, append, GQA),
 rxla_b200_sigmoid_gate, and the o_proj W8 linear with the residual add.
+
+`Qwen3_5Model` composes the whole text model (`qwen3_5`, mod.rs:199-260):
+W8 embedding, zero-centred RMSNorms, gated-delta and full-attention mixers,
+SwiGLU MLP, tied W8 head.
 
 The attention kernels take head_dim 64 or 128; Qwen3.5-0.8B's 256 is not
 supported.
@@ -109,4 +113,98 @@ class GatedFullAttention:
                             for t in range(x.shape[1])], dim=1)
 
 
-__all__ = ["GatedFullAttention"]
+class Qwen3_5Model:
+    """The hybrid Qwen3.5 text model, `qwen3_5(cx, token_ids, config)`
+    (crates/rxla-models/src/qwen3_5/mod.rs:199-260), with W8 storage, for a
+    batch of sequences whose state — every linear-attention layer's conv
+    history and recurrent state, every full-attention layer's paged KV cache —
+    is carried from call to call, where the reference recomputes the whole
+    sequence.
+
+    params: device tensors by the checkpoint names below "model.language_model."
+    (`embed_tokens.weight` u8 [V, H] and `.scale`, `layers.{i}.input_layernorm.weight`,
+    `layers.{i}.post_attention_layernorm.weight`, `layers.{i}.linear_attn.*` or
+    `layers.{i}.self_attn.*`, `layers.{i}.mlp.{gate,up,down}_proj.{weight,scale}`,
+    `norm.weight`).  Every RMSNorm is zero-centred (weight + 1).  `layer_types`:
+    "linear" or "full" per layer (mod.rs:8-12).  The tied LM head is the W8
+    linear over the embedding with bf16 x and an f32 dot (the reference's is an
+    F32 linear over the dequantized embedding)."""
+
+    def __init__(self, params, *, vocabulary: int, hidden_size: int, intermediate_size: int,
+                 layer_types, attention_heads: int, key_value_heads: int, head_dim: int,
+                 linear_heads: int, linear_head_dim: int, conv_kernel: int, rope_theta: float,
+                 rotary_dim: int, epsilon: float, quant_group_size: int, batch: int = 1,
+                 max_context: int = 256):
+        from .gated_delta import GatedDeltaAttention
+        G = quant_group_size
+        self.V, self.H, self.G, self.eps, self.B = vocabulary, hidden_size, G, epsilon, batch
+        self.types = list(layer_types)
+        self.embed_w = params["embed_tokens.weight"]
+        self.embed_s = params["embed_tokens.scale"]
+        if tuple(self.embed_w.shape) != (vocabulary, hidden_size) or self.embed_w.dtype != torch.uint8:
+            raise InvalidLayerInput("embed_tokens.weight must be U8 [vocabulary, hidden]")
+        zc = lambda name: (params[name].float() + 1.0).contiguous()  # zero-centred norm weight
+        self.norm_in, self.norm_post, self.mixers, self.states = [], [], [], []
+        self.mlp_gu, self.mlp_gu_s, self.mlp_d, self.mlp_d_s = [], [], [], []
+        for i, kind in enumerate(self.types):
+            pre = f"layers.{i}."
+            self.norm_in.append(zc(pre + "input_layernorm.weight"))
+            self.norm_post.append(zc(pre + "post_attention_layernorm.weight"))
+            if kind == "linear":
+                sub = {k[len(pre + "linear_attn."):]: v for k, v in params.items()
+                       if k.startswith(pre + "linear_attn.")}
+                m = GatedDeltaAttention(sub, hidden_size=hidden_size, linear_heads=linear_heads,
+                                        linear_head_dim=linear_head_dim, conv_kernel=conv_kernel,
+                                        quant_group_size=G, epsilon=epsilon)
+                self.mixers.append(m)
+                self.states.append(m.new_state(batch))
+            elif kind == "full":
+                sub = {k[len(pre + "self_attn."):]: v for k, v in params.items()
+                       if k.startswith(pre + "self_attn.")}
+                self.mixers.append(GatedFullAttention(
+                    sub, hidden_size=hidden_size, attention_heads=attention_heads,
+                    key_value_heads=key_value_heads, head_dim=head_dim, rotary_dim=rotary_dim,
+                    rope_theta=rope_theta, quant_group_size=G, epsilon=epsilon, batch=batch,
+                    max_context=max_context))
+                self.states.append(None)
+            else:
+                raise InvalidLayerInput(f"layer type {kind!r}")
+            # SwiGLU MLP (layers.rs:270-293): [gate; up] rows for the fused epilogue
+            self.mlp_gu.append(torch.cat([params[pre + "mlp.gate_proj.weight"],
+                                          params[pre + "mlp.up_proj.weight"]]).contiguous())
+            self.mlp_gu_s.append(torch.cat([params[pre + "mlp.gate_proj.scale"],
+                                            params[pre + "mlp.up_proj.scale"]]).contiguous())
+            self.mlp_d.append(params[pre + "mlp.down_proj.weight"].contiguous())
+            self.mlp_d_s.append(params[pre + "mlp.down_proj.scale"].contiguous())
+        self.norm_final = zc("norm.weight")
+
+    def forward(self, ids: torch.Tensor, stream=None) -> torch.Tensor:
+        """ids int32 [batch, T] on the device: the next T tokens of every
+        sequence.  Returns the last position's logits f32 [batch, vocabulary]."""
+        from .nn import rms_norm_bf16, w8_embedding
+        if ids.dim() != 2 or ids.shape[0] != self.B or ids.dtype != torch.int32:
+            raise InvalidLayerInput("ids must be int32 [batch, T]")
+        B, T = ids.shape
+        h = w8_embedding(ids, self.embed_w, self.embed_s, self.G, stream=stream)  # [B, T, H] f32
+        for i, kind in enumerate(self.types):
+            xn = rms_norm_bf16(h, self.norm_in[i], self.eps, stream=stream)
+            if kind == "linear":
+                self.mixers[i].apply(xn, self.states[i], residual=h, stream=stream)
+            else:
+                for t in range(T):
+                    r = h[:, t].contiguous()
+                    self.mixers[i].step(xn[:, t].contiguous(), residual=r, stream=stream)
+                    h[:, t] = r
+            xn = rms_norm_bf16(h, self.norm_post[i], self.eps, stream=stream)
+            u = quantized_linear(xn.reshape(B * T, self.H), self.mlp_gu[i], self.mlp_gu_s[i],
+                                 self.G, epilogue=_lib.EPI_SWIGLU, out_dtype=torch.bfloat16,
+                                 stream=stream)
+            quantized_linear(u, self.mlp_d[i], self.mlp_d_s[i], self.G,
+                             epilogue=_lib.EPI_RESIDUAL_ADD, out=h.view(B * T, self.H),
+                             stream=stream)
+        hn = rms_norm_bf16(h[:, -1].contiguous(), self.norm_final, self.eps, stream=stream)
+        return quantized_linear(hn, self.embed_w, self.embed_s, self.G, out_dtype=torch.float32,
+                                stream=stream)
+
+
+__all__ = ["GatedFullAttention", "Qwen3_5Model"]

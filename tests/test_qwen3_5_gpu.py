@@ -76,3 +76,84 @@ def test_sigmoid_gate_rounding(cuda):
                           torch.from_numpy(g).cuda().bfloat16()).float().cpu().numpy()
     ref = x.astype(np.float64) / (1.0 + np.exp(-g.astype(np.float64)))
     assert np.all(np.abs(got - ref) <= 2.0 ** -8 * np.abs(ref) + 1e-30)
+
+
+QWEN_TINY = dict(vocabulary=512, hidden_size=256, intermediate_size=512,
+                 layer_types=["linear", "full", "linear", "full"], attention_heads=4,
+                 key_value_heads=2, head_dim=64, linear_heads=4, linear_head_dim=64,
+                 conv_kernel=4, rope_theta=1e7, rotary_dim=32, epsilon=1e-6,
+                 quant_group_size=64)
+
+
+def _model_params(cfg, seed):
+    from tests.test_gated_delta_gpu import _layer_params
+    rng = np.random.default_rng(seed)
+    V, H, I, G = (cfg["vocabulary"], cfg["hidden_size"], cfg["intermediate_size"],
+                  cfg["quant_group_size"])
+    q8 = lambda n, k, sc: oracle.quantize_w8((rng.standard_normal((n, k)) * sc).astype(np.float32), G)
+    p = {}
+    p["embed_tokens.weight"], p["embed_tokens.scale"] = q8(V, H, 0.05)
+    for i, kind in enumerate(cfg["layer_types"]):
+        pre = f"layers.{i}."
+        p[pre + "input_layernorm.weight"] = (0.1 * rng.standard_normal(H)).astype(np.float32)
+        p[pre + "post_attention_layernorm.weight"] = (0.1 * rng.standard_normal(H)).astype(np.float32)
+        if kind == "linear":
+            sub = _layer_params(H, cfg["linear_heads"], cfg["linear_head_dim"], cfg["conv_kernel"],
+                                G, seed=seed + 10 * i)
+            p.update({pre + "linear_attn." + k: v for k, v in sub.items()})
+        else:
+            sub = _params(H, cfg["attention_heads"], cfg["key_value_heads"], cfg["head_dim"], G,
+                          seed=seed + 10 * i)
+            p.update({pre + "self_attn." + k: v for k, v in sub.items()})
+        p[pre + "mlp.gate_proj.weight"], p[pre + "mlp.gate_proj.scale"] = q8(I, H, H ** -0.5)
+        p[pre + "mlp.up_proj.weight"], p[pre + "mlp.up_proj.scale"] = q8(I, H, H ** -0.5)
+        p[pre + "mlp.down_proj.weight"], p[pre + "mlp.down_proj.scale"] = q8(H, I, I ** -0.5)
+    p["norm.weight"] = (0.1 * rng.standard_normal(H)).astype(np.float32)
+    return p
+
+
+def test_qwen3_5_model_prompt_then_decode(cuda):
+    """The hybrid model (linear, full, linear, full) over a 10-token prompt
+    of 2 sequences, then 4 teacher-forced decode steps with the carried
+    state, against the oracle's full-sequence `qwen3_5` forward.
+
+    Bar (the decoder tests' parity rule): the floor is the oracle computing
+    what the GPU path computes differently — f32 running sums in every W8
+    linear, bf16 attended values before the output gate, the tied head on
+    bf16 operands — against the exact oracle, over the window of the five
+    compared positions; the last-position logits must lie within
+    max(north-star 2e-3, 1.25 × floor) on the mean |Δ| and max(north-star 2e-2,
+    1.5 × floor) on the max |Δ| (the maxima of two independent
+    accumulation-noise realizations differ by up to ~40 %), and the greedy
+    token must match wherever the oracle's top-2 gap exceeds twice the max
+    bar."""
+    from rxla_b200.qwen3_5 import Qwen3_5Model
+    cfg = QWEN_TINY
+    B, T0, steps = 2, 10, 4
+    p = _model_params(cfg, seed=31)
+    ids = np.random.default_rng(32).integers(0, cfg["vocabulary"], (B, T0 + steps)).astype(np.int32)
+    okw = {k: v for k, v in cfg.items() if k not in ("intermediate_size", "conv_kernel")}
+    ref = q35.qwen3_5_forward(ids, p, **okw)
+    ref_g = q35.qwen3_5_forward(ids, p, gpu_rounding=True, **okw)
+    model = Qwen3_5Model({k: torch.from_numpy(v).cuda() for k, v in p.items()}, **cfg, batch=B,
+                         max_context=64)
+    dev_ids = torch.from_numpy(ids).cuda()
+    rows = [(model.forward(dev_ids[:, :T0]), T0 - 1)]
+    for t in range(T0, T0 + steps):
+        rows.append((model.forward(dev_ids[:, t:t + 1].contiguous()), t))
+    errs, floors, tokens_ok = [], [], True
+    for logits, t in rows:
+        got = logits.cpu().numpy()
+        r = ref[:, t]
+        errs.append(np.abs(got - r))
+        floors.append(np.abs(ref_g[:, t] - r))
+        top2 = np.sort(r, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 2 * max(2e-2, 1.5 * floors[-1].max())
+        tokens_ok &= bool((got.argmax(1)[clear] == r.argmax(1)[clear]).all())
+    # over the teacher-forced window, as the decoder tests measure their floor
+    err, fl = np.stack(errs), np.stack(floors)
+    bar_max, bar_mean = max(2e-2, 1.5 * fl.max()), max(2e-3, 1.25 * fl.mean())
+    assert err.max() <= bar_max, f"max |d| {err.max():.4g} > {bar_max:.4g}"
+    assert err.mean() <= bar_mean, f"mean |d| {err.mean():.4g} > {bar_mean:.4g}"
+    assert tokens_ok, "greedy token differs where the oracle's top-2 gap is clear"
+    assert nn.device_status() == 0
