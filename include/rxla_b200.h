@@ -197,6 +197,8 @@ int32_t rxla_b200_bf16_linear(const void* x, int32_t x_dtype, const uint16_t* we
  * head_dim]; page_table int32 [batch, max_pages_per_seq] maps the p-th page of
  * sequence b; capacity of sequence b = pages_per_seq[b] * page_size (or
  * max_pages_per_seq * page_size when pages_per_seq is NULL).
+ * head_dim 64, 128 or 256 (256: rotary_dim <= 128); 1 to 8 query heads per
+ * kv head; rotary_dim a multiple of 32.
  */
 typedef struct rxla_b200_paged_decode_args {
   uint32_t struct_size; /* sizeof(rxla_b200_paged_decode_args) */

@@ -245,11 +245,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, kMinBlocks)
   uint64_t* empty = full + kStagesV2;
   float* misc = reinterpret_cast<float*>(empty + kStagesV2);  // 8 floats: flags
   float2* cs = reinterpret_cast<float2*>(misc + 8);               // [64] cos, sin
-  float* qw = reinterpret_cast<float*>(cs + 64);                  // [128] q norm weight
-  float* kw = qw + 128;                                           // [128] k norm weight
+  float* qw = reinterpret_cast<float*>(cs + 64);                  // [D] q norm weight
+  float* kw = qw + D;                                             // [D] k norm weight
   // the swizzled ring must start on a 1024-byte boundary, after the above
+  // (barriers, flags, tables: at most 2048 bytes up to D = 128, 3072 for 256)
+  constexpr uint32_t kHdr = D > 128 ? 3072u : 2048u;
   const uint32_t base_u32 = smem_u32(smem_raw);
-  uint8_t* ring = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u) + 2048;
+  uint8_t* ring = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u) + kHdr;
   // per-warp softmax states for the in-CTA merge: O [warp][8][D], m/l [warp][8][2]
   float* st_o = reinterpret_cast<float*>(ring + kStagesV2 * kStage);
   float* st_ml = st_o + CW * 8 * D;
@@ -327,8 +329,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, kMinBlocks)
       const float ang = (float)pos * p.inv_freq[tid];
       cs[tid] = make_float2(cosf(ang), sinf(ang));
     }
-    if (p.q_norm_w && tid < D) qw[tid] = p.q_norm_w[tid];
-    if (p.k_norm_w && tid < D) kw[tid] = p.k_norm_w[tid];
+    for (int i = tid; i < D; i += CW * 32) {
+      if (p.q_norm_w) qw[i] = p.q_norm_w[i];
+      if (p.k_norm_w) kw[i] = p.k_norm_w[i];
+    }
     if (p.ctx_stable) pdl_wait();  // q / k_new / v_new come from the previous kernel
     // dependents wait for this grid's completion before reading its output
     if (tid == 0) pdl_launch_dependents();
@@ -1083,27 +1087,24 @@ static int32_t make_page_map(CUtensorMap* map, void* base, int64_t num_pages, in
   return RXLA_B200_OK;
 }
 
-// Pages per split: CTAs are (sequence, kv head, split).  Aim for ~4 CTAs per
-// SM when every sequence is at max_context, with at most 32 pages per split
-// for balance, but never more than 32 splits (the merge depth).
-// Pages per split: enough CTAs for ~4 per SM over all (sequence, kv head)
-// pairs, at least ceil(pages / 16) pages (RXLA_B200_ATTN_MAX_SPLITS: at most
-// 16 splits per sequence and head; batch 1 at 2048 context: 9.8 µs with 16,
-// 11.2 with 32, 16.9 with 48 — the last CTA merges every split), at most 48
-// (RXLA_B200_ATTN_PPS_CAP: longer splits cost a fuller last wave but fewer
-// merges; batch 64 at 2048 context: 111.4 µs with 32, 105.8 with 48, 109.7
-// with 64).
+// Pages per split: CTAs are (sequence, kv head, split): enough CTAs for ~4
+// per SM over all (sequence, kv head) pairs, at least ceil(pages / 16) pages
+// (at most 16 splits per sequence and head; batch 1 at 2048 context: 9.8 µs
+// with 16, 11.2 with 32, 16.9 with 48 — the last CTA merges every split), at
+// most 48 (longer splits cost a fuller last wave but fewer merges; batch 64
+// at 2048 context: 111.4 µs with 32, 105.8 with 48, 109.7 with 64).
 // Small grids — fewer than 16 sequences and at most 32 (sequence, kv head)
 // pairs — run one thread-block cluster of kClusterSplits CTAs per pair, each
 // with kClusterWarps compute warps, and merge the splits through distributed
-// shared memory instead of a workspace round trip.
+// shared memory instead of a workspace round trip (head_dim up to 128: the
+// cluster variant's 16-stage ring of 256-dim pages would not fit).
 constexpr int kClusterSplits = 8, kClusterWarps = 8, kStagesCluster = 16;
-static bool use_cluster(int batch, int kv_heads) {
-  return batch < 16 && (int64_t)batch * kv_heads <= 32;
+static bool use_cluster(int batch, int kv_heads, int head_dim) {
+  return head_dim <= 128 && batch < 16 && (int64_t)batch * kv_heads <= 32;
 }
 
-static int pages_per_split(int batch, int kv_heads, int max_pages) {
-  if (use_cluster(batch, kv_heads))
+static int pages_per_split(int batch, int kv_heads, int max_pages, int head_dim) {
+  if (use_cluster(batch, kv_heads, head_dim))
     return std::max(1, (max_pages + kClusterSplits - 1) / kClusterSplits);
   constexpr int64_t cap = 48;   // pages per split at most
   constexpr int64_t most = 16;  // splits per (sequence, kv head) at most
@@ -1123,8 +1124,8 @@ extern "C" int32_t rxla_b200_paged_decode_workspace_size(int32_t batch, int32_t 
                    head_dim > 0 && max_context >= 0,
                "paged_decode_workspace_size: bad arguments");
   const int max_pages = (max_context + attn::kPage - 1) / attn::kPage;
-  const int pps = attn::pages_per_split(batch, kv_heads, max_pages);
-  const int64_t splits = attn::use_cluster(batch, kv_heads)
+  const int pps = attn::pages_per_split(batch, kv_heads, max_pages, head_dim);
+  const int64_t splits = attn::use_cluster(batch, kv_heads, head_dim)
                              ? attn::kClusterSplits
                              : std::max(1, (max_pages + pps - 1) / pps);
   const int64_t G = q_heads / kv_heads;
@@ -1152,7 +1153,10 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   RXLA_REQUIRE(a->q_heads / a->kv_heads <= 8, "paged_decode: at most 8 query heads per kv head");
   RXLA_REQUIRE(a->kv_heads <= 65535 && a->batch <= 65535,
                "paged_decode: kv_heads and batch must be <= 65535 (grid dimensions)");
-  RXLA_REQUIRE(D == 64 || D == 128, "paged_decode: head_dim must be 64 or 128");
+  RXLA_REQUIRE(D == 64 || D == 128 || (D == 256 && !append_only),
+               "paged_decode: head_dim must be 64 or 128 (or 256 for the decode step)");
+  RXLA_REQUIRE(D != 256 || a->inv_freq == nullptr || a->rotary_dim <= 128,
+               "paged_decode: rotary_dim must be <= 128 at head_dim 256");
   RXLA_REQUIRE(a->page_size == attn::kPage, "paged_decode: page_size must be 16");
   RXLA_REQUIRE(a->rotary_dim == 0 || a->inv_freq == nullptr ||
                    (a->rotary_dim % 32 == 0 && a->rotary_dim <= D),
@@ -1207,10 +1211,10 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   p.hkv = a->kv_heads;
   p.group = a->q_heads / a->kv_heads;
   const int max_pages = (a->max_context + attn::kPage - 1) / attn::kPage;
-  p.pps = attn::pages_per_split(a->batch, a->kv_heads, max_pages);
+  p.pps = attn::pages_per_split(a->batch, a->kv_heads, max_pages, D);
   // a cluster holds all kClusterSplits CTAs of a (sequence, kv head), some
   // possibly without pages
-  const bool cluster = !append_only && attn::use_cluster(a->batch, a->kv_heads);
+  const bool cluster = !append_only && attn::use_cluster(a->batch, a->kv_heads, D);
   p.max_splits = cluster ? attn::kClusterSplits : std::max(1, (max_pages + p.pps - 1) / p.pps);
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   const size_t cnt_bytes = (((size_t)a->batch * a->kv_heads + 1) * 4 + 255) / 256 * 256;
@@ -1241,8 +1245,9 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   st = attn::make_page_map(&vmap, a->v_pages, a->num_pages, a->kv_heads, D);
   if (st != RXLA_B200_OK) return st;
 
-  const size_t smem = 3072 + (size_t)p.stages * p.stage_bytes + (size_t)cw * 8 * (D + 2) * 4 +
-                      (size_t)p.max_splits * 8 * 2 * 4;
+  // 1024 bytes of alignment slack + the header region (kHdr in the kernel)
+  const size_t smem = (D > 128 ? 4096 : 3072) + (size_t)p.stages * p.stage_bytes +
+                      (size_t)cw * 8 * (D + 2) * 4 + (size_t)p.max_splits * 8 * 2 * 4;
   const dim3 grid(p.max_splits, a->kv_heads, a->batch);
   const dim3 block((cw + 1) * 32);
   cudaStream_t s = s_in;
@@ -1256,7 +1261,10 @@ int32_t launch(const rxla_b200_paged_decode_args* a, cudaStream_t s_in, bool ctx
   };
   using namespace attn;
   cudaError_t e;
-  if (D == 128)
+  if (D == 256)  // one CTA per SM: ~170 KB of shared memory, ~200 registers a thread
+    e = large ? go(paged_decode_kernel<256, kStagesLarge, 1>)
+              : go(paged_decode_kernel<256, kStagesSmall, 1>);
+  else if (D == 128)
     e = cluster ? go(paged_decode_kernel<128, kStagesCluster, 1, kClusterWarps, true>)
         : large ? go(paged_decode_kernel<128, kStagesLarge, 3>)
                 : go(paged_decode_kernel<128, kStagesSmall, 1>);

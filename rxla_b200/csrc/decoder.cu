@@ -793,6 +793,7 @@ extern "C" int32_t rxla_b200_decoder_create(const rxla_b200_decoder_config* cfg,
   RXLA_REQUIRE(gsz <= 0 || (c.hidden % gsz == 0 && (c.q_heads * c.head_dim / tp) % gsz == 0 &&
                             (c.intermediate / tp) % gsz == 0),
                "decoder_create: group_size must divide every input width");
+  RXLA_REQUIRE(c.head_dim == 64 || c.head_dim == 128, "decoder: head_dim must be 64 or 128");
   RXLA_REQUIRE(c.hidden % 64 == 0 && (c.q_heads * c.head_dim / tp) % 64 == 0 &&
                    (c.intermediate / tp) % 64 == 0 && (gsz <= 0 || gsz % 64 == 0),
                "decoder_create: hidden, q_heads*head_dim, intermediate (and group_size) must be "

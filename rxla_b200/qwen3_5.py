@@ -15,8 +15,8 @@ rxla_b200_sigmoid_gate, and the o_proj W8 linear with the residual add.
 W8 embedding, zero-centred RMSNorms, gated-delta and full-attention mixers,
 SwiGLU MLP, tied W8 head.
 
-The attention kernels take head_dim 64 or 128; Qwen3.5-0.8B's 256 is not
-supported.
+The decode attention takes head_dim 64, 128 or 256 (Qwen3.5-0.8B's), with
+rotary_dim <= 128 at 256.
 """
 from __future__ import annotations
 
@@ -40,8 +40,8 @@ class GatedFullAttention:
                  head_dim: int, rotary_dim: int, rope_theta: float, quant_group_size: int,
                  epsilon: float = 1e-6, batch: int = 1, max_context: int = 256):
         Hq, Hkv, D, G = attention_heads, key_value_heads, head_dim, quant_group_size
-        if D not in (64, 128):
-            raise InvalidLayerInput("the attention kernels take head_dim 64 or 128")
+        if D not in (64, 128, 256):
+            raise InvalidLayerInput("the decode attention takes head_dim 64, 128 or 256")
         if Hq % Hkv or rotary_dim <= 0 or rotary_dim > D or rotary_dim % 2 or \
                 hidden_size % G or (Hq * D) % G:
             raise InvalidLayerInput("invalid Qwen3.5 attention configuration")

@@ -133,6 +133,22 @@ def test_batch64_many_splits(cuda):
     _check_close(out, ref, _abs_weighted_v(c, kpo, vpo))
 
 
+@pytest.mark.parametrize("batch,hq,hkv,ctx_hi", [(2, 8, 2, 1024), (16, 4, 1, 600)])
+def test_head_dim_256(cuda, batch, hq, hkv, ctx_hi):
+    """head_dim 256 (Qwen3.5-0.8B's full-attention heads) with partial RoPE
+    over 64 dims and q/k norms: the small-batch and the many-sequence
+    variants of the decode kernel."""
+    ctx = list(oracle.randint(batch, 256 + batch, 1, ctx_hi - 1))
+    c = _setup(batch, hq, hkv, 256, ctx, max_context=ctx_hi, seed=256 + batch, rot=64)
+    (out,), kp, vp, ctx_a, acc = _run_gpu(c)
+    ref, kpo, vpo, ctx_o, acc_o = _run_oracle(c)
+    _check_close(out, ref, _abs_weighted_v(c, kpo, vpo))
+    np.testing.assert_array_equal(ctx_a, ctx_o)
+    np.testing.assert_array_equal(vp, vpo)
+    dk = np.abs(oracle.bf16_bits_to_f32(kp) - oracle.bf16_bits_to_f32(kpo))
+    assert dk.max() <= 2.0 ** -7 * np.abs(oracle.bf16_bits_to_f32(kpo)).max()
+
+
 def test_single_sequence_long_pps1(cuda):
     c = _setup(1, 32, 8, 128, [3000], max_context=4096, seed=55)
     (out,), kp, vp, ctx_a, acc = _run_gpu(c)

@@ -48,7 +48,8 @@ def _check_layer(got, ref, floor_max=0.0, floor_mean=0.0):
 
 
 @pytest.mark.parametrize("hidden,Hq,Hkv,D,rot,B,T", [(512, 8, 2, 128, 64, 2, 12),
-                                                     (256, 4, 1, 64, 32, 1, 20)])
+                                                     (256, 4, 1, 64, 32, 1, 20),
+                                                     (1024, 8, 2, 256, 64, 2, 9)])
 def test_full_attention_layer_matches_oracle(cuda, hidden, Hq, Hkv, D, rot, B, T):
     G, theta = 128, 1e7
     p = _params(hidden, Hq, Hkv, D, G, seed=hidden + D)
