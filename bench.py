@@ -457,7 +457,8 @@ def run_ours(args, rank, world, local_rank):
     if world == 1 and not args.no_kernels:
         kernels = {"config2_linear_sweep": config2_sweep(dev),
                    "config3_attention": config3_attention(dev),
-                   "gated_delta": gated_delta_bench(dev)}
+                   "gated_delta": gated_delta_bench(dev),
+                   "qwen3_5_08b": qwen3_5_bench(dev)}
     if comm:
         comm.close()
 
@@ -888,6 +889,131 @@ def gated_delta_bench(dev):
     out["layer_decode_b64"] = {"us": sec * 1e6, "bytes_per_call": lbyt, "gbs": lbyt / sec / 1e9,
                                "frac": lbyt / sec / 1e9 / hbm, "launches_per_call": 5}
     return out
+
+
+def qwen3_5_bench(dev, steps: int = 32):
+    """The Qwen3.5-0.8B-shaped hybrid model (crates/rxla-models/src/qwen3_5/
+    mod.rs:57-85: 24 layers, every 4th full attention with 8 q / 2 kv heads of
+    256 and rotary 64, the rest gated-delta with 16 heads of 128, hidden 1024,
+    intermediate 3584, vocab 248320, W8 with 128-wide groups) with random
+    weights through Qwen3_5Model: a 64-token prompt, then batch-1 decode steps
+    each replayed as one CUDA graph; and a 16-token prompt from a fresh state
+    as one graph (the sequence-16 forward the reference publishes).  Bytes per
+    decode step: every W8 weight and scale once (the tied head included), the
+    gated-delta states read and written, the KV rows of the full-attention
+    layers."""
+    import torch
+    from rxla_b200.qwen3_5 import Qwen3_5Model
+    hbm, _, _, how = measured_peaks()
+    types = ["full" if (i + 1) % 4 == 0 else "linear" for i in range(24)]
+    cfg = dict(vocabulary=248320, hidden_size=1024, intermediate_size=3584, layer_types=types,
+               attention_heads=8, key_value_heads=2, head_dim=256, linear_heads=16,
+               linear_head_dim=128, conv_kernel=4, rope_theta=1e7, rotary_dim=64, epsilon=1e-6,
+               quant_group_size=128)
+    g = torch.Generator(device=dev).manual_seed(21)
+    H, I, G, V = 1024, 3584, 128, 248320
+    params = {}
+
+    def w8(name, n, k):
+        params[name + ".weight"] = torch.randint(1, 256, (n, k), dtype=torch.uint8, device=dev,
+                                                 generator=g)
+        params[name + ".scale"] = torch.rand(n, k // G, device=dev, generator=g) * 2e-4
+
+    def vec(name, n, scale=0.1):
+        params[name] = torch.randn(n, device=dev, generator=g) * scale
+    w8("embed_tokens", V, H)
+    for i, kind in enumerate(types):
+        pre = f"layers.{i}."
+        vec(pre + "input_layernorm.weight", H)
+        vec(pre + "post_attention_layernorm.weight", H)
+        if kind == "linear":
+            W = 16 * 128
+            w8(pre + "linear_attn.in_proj_qkv", 3 * W, H)
+            w8(pre + "linear_attn.in_proj_z", W, H)
+            w8(pre + "linear_attn.in_proj_b", 16, H)
+            w8(pre + "linear_attn.in_proj_a", 16, H)
+            w8(pre + "linear_attn.out_proj", H, W)
+            params[pre + "linear_attn.conv1d.weight"] = torch.randn(3 * W, 1, 4, device=dev,
+                                                                    generator=g) * 0.5
+            params[pre + "linear_attn.A_log"] = torch.rand(16, device=dev, generator=g) * 2.7
+            vec(pre + "linear_attn.dt_bias", 16, 0.5)
+            params[pre + "linear_attn.norm.weight"] = torch.ones(128, device=dev)
+        else:
+            w8(pre + "self_attn.q_proj", 2 * 8 * 256, H)
+            w8(pre + "self_attn.k_proj", 2 * 256, H)
+            w8(pre + "self_attn.v_proj", 2 * 256, H)
+            w8(pre + "self_attn.o_proj", H, 8 * 256)
+            vec(pre + "self_attn.q_norm.weight", 256)
+            vec(pre + "self_attn.k_norm.weight", 256)
+        w8(pre + "mlp.gate_proj", I, H)
+        w8(pre + "mlp.up_proj", I, H)
+        w8(pre + "mlp.down_proj", H, I)
+    vec("norm.weight", H)
+    wbytes = sum(t.numel() for n, t in params.items()
+                 if n.endswith(".weight") and t.dtype == torch.uint8) + \
+        sum(t.numel() * 4 for n, t in params.items() if n.endswith(".scale"))
+    prompt = 64
+    model = Qwen3_5Model(params, **cfg, batch=1, max_context=prompt + 3 + steps + 16)
+    model.forward(torch.randint(0, V, (1, prompt), dtype=torch.int32, device=dev, generator=g))
+    ids = torch.zeros(1, 1, dtype=torch.int32, device=dev)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):  # warm-up steps (also the state the graph starts from)
+            model.forward(ids)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        model.forward(ids)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / steps
+    del graph
+    # a 16-token prompt from a fresh state, one graph: the context lengths are
+    # zeroed inside it and every gated-delta call starts from zero state
+    p16 = torch.randint(0, V, (1, 16), dtype=torch.int32, device=dev, generator=g)
+    caches = [m.cache for m in model.mixers if hasattr(m, "cache")]
+
+    def fresh():
+        for st in model.states:
+            if st is not None:
+                st.started = False
+    fresh()
+    with torch.cuda.stream(side):
+        for c in caches:
+            c.ctx_lens.zero_()
+        model.forward(p16)
+    torch.cuda.current_stream().wait_stream(side)
+    fresh()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for c in caches:
+            c.ctx_lens.zero_()
+        model.forward(p16)
+    torch.cuda.synchronize()
+    reps = 10
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    sec16 = e0.elapsed_time(e1) / 1e3 / reps
+    del graph
+    ctx = prompt + 3 + steps // 2
+    byt = wbytes + 18 * 16 * 128 * 128 * 4 * 2 + 6 * 2 * 256 * 2 * 2 * ctx
+    return {"workload": "Qwen3.5-0.8B-shaped hybrid model (18 gated-delta + 6 full-attention "
+                        "layers, vocab 248320), batch-1 decode after a 64-token prompt",
+            "tokens_per_s": 1.0 / sec, "ms_per_step": sec * 1e3, "steps": steps,
+            "bytes_per_step": byt, "gbs": byt / sec / 1e9, "frac": byt / sec / 1e9 / hbm,
+            "peak_source": how, "timing": "CUDA events around graph replays of the whole step",
+            "prompt16": {"ms": sec16 * 1e3, "tokens_per_s": 16 / sec16,
+                         "what": "16-token prompt from a fresh state, one graph"},
+            "l2": "0.8 GB of weights per step > L2"}
 
 
 def profile_case(what: str):
