@@ -102,15 +102,52 @@ class GatedFullAttention:
         return quantized_linear(y, self.w_out, self.s_out, self.G, out_dtype=torch.bfloat16,
                                 stream=stream).float()
 
-    def forward(self, x: torch.Tensor, stream=None) -> torch.Tensor:
-        """A prompt [batch, T, hidden] token by token from each sequence's
-        current position: the rows of the reference's causal full-sequence
-        forward (layers.rs:28-100 with the causal mask of qwen3_5/mod.rs:229).
-        Returns F32 [batch, T, hidden]."""
-        if x.dim() != 3:
-            raise InvalidLayerInput("input must be [batch, sequence, hidden]")
-        return torch.stack([self.step(x[:, t].contiguous(), stream=stream)
-                            for t in range(x.shape[1])], dim=1)
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None,
+                stream=None) -> torch.Tensor:
+        """T tokens per sequence, x [batch, T, hidden] (F32 or bf16, the
+        normalised layer input, contiguous) from each sequence's current
+        position: the rows of the reference's causal full-sequence forward
+        (layers.rs:28-100 with the causal mask of qwen3_5/mod.rs:229).  The
+        projections run once over all batch * T rows; the attention runs
+        token by token, each call appending its token's K/V and attending
+        over the positions before it.  Without `residual` returns F32
+        [batch, T, hidden]; with it (F32 [batch, T, hidden], contiguous) adds
+        bf16(o_proj) into it in place and returns it."""
+        B = self.cache.batch
+        if x.dim() != 3 or x.shape[0] != B or x.shape[2] != self.hidden or not x.is_contiguous():
+            raise InvalidLayerInput("input must be contiguous [batch, sequence, hidden]")
+        T = x.shape[1]
+        if residual is not None and (residual.dtype != torch.float32 or
+                                     tuple(residual.shape) != (B, T, self.hidden) or
+                                     not residual.is_contiguous()):
+            raise InvalidLayerInput("residual must be contiguous F32 [batch, sequence, hidden]")
+        Hq, Hkv, D = self.Hq, self.Hkv, self.D
+        qd, kd = Hq * D, Hkv * D
+        proj = quantized_linear(x.view(B * T, self.hidden), self.w_in, self.s_in, self.G,
+                                out_dtype=torch.bfloat16, stream=stream)
+        pv = proj.view(B, T, -1)
+        att = torch.empty(T, B, qd, dtype=torch.bfloat16, device=x.device)
+        for t in range(T):
+            paged_decode_attention(pv[:, t, :qd], pv[:, t, 2 * qd:2 * qd + kd],
+                                   pv[:, t, 2 * qd + kd:], self.cache, q_heads=Hq,
+                                   q_norm_weight=self.q_norm, k_norm_weight=self.k_norm,
+                                   eps=self.eps, inv_freq=self.inv_freq, rotary_dim=self.rot,
+                                   advance_ctx=True, out=att[t], workspace=self.workspace,
+                                   stream=stream)
+        if B == 1 or T == 1:  # token-major rows are batch-major rows
+            y = sigmoid_gate(att.view(T * B, qd), proj[:, qd:2 * qd], out=att.view(T * B, qd),
+                             stream=stream)
+        else:
+            y = torch.empty(B, T, qd, dtype=torch.bfloat16, device=x.device)
+            for t in range(T):
+                sigmoid_gate(att[t], pv[:, t, qd:2 * qd], out=y[:, t], stream=stream)
+            y = y.view(B * T, qd)
+        if residual is not None:
+            quantized_linear(y, self.w_out, self.s_out, self.G, epilogue=_lib.EPI_RESIDUAL_ADD,
+                             out=residual.view(B * T, self.hidden), stream=stream)
+            return residual
+        return quantized_linear(y, self.w_out, self.s_out, self.G, out_dtype=torch.bfloat16,
+                                stream=stream).float().view(B, T, self.hidden)
 
 
 class Qwen3_5Model:
@@ -191,10 +228,7 @@ class Qwen3_5Model:
             if kind == "linear":
                 self.mixers[i].apply(xn, self.states[i], residual=h, stream=stream)
             else:
-                for t in range(T):
-                    r = h[:, t].contiguous()
-                    self.mixers[i].step(xn[:, t].contiguous(), residual=r, stream=stream)
-                    h[:, t] = r
+                self.mixers[i].forward(xn, residual=h, stream=stream)
             xn = rms_norm_bf16(h, self.norm_post[i], self.eps, stream=stream)
             u = quantized_linear(xn.reshape(B * T, self.H), self.mlp_gu[i], self.mlp_gu_s[i],
                                  self.G, epilogue=_lib.EPI_SWIGLU, out_dtype=torch.bfloat16,
