@@ -190,6 +190,8 @@ extern "C" {
     pub fn rxla_b200_device_status(reset: i32) -> i32;
     pub fn rxla_b200_set_wait_timeout(ns: i64) -> i32;
     pub fn rxla_b200_get_wait_timeout(ns: *mut i64) -> i32;
+    pub fn rxla_b200_bounded_wait_check(kind: i32, flag: *const u64, target: u64,
+                                        stream: *mut c_void) -> i32;
 
     pub fn rxla_b200_w8a16_linear(
         x: *const c_void, x_dtype: i32, weight: *const u8, scale: *const f32, group_size: i64,

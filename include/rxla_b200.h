@@ -117,6 +117,16 @@ int32_t rxla_b200_device_status(int32_t reset);
  * reference interface (XLA's own kernels do not wait on peers). */
 int32_t rxla_b200_set_wait_timeout(int64_t ns);
 int32_t rxla_b200_get_wait_timeout(int64_t* ns);
+/* Diagnostic of the bounded device-side waits: one thread waits, under the
+ * current budget, either (kind 0) on a shared-memory mbarrier that nothing
+ * arrives on — the wait of every TMA ring here, so it always runs out — or
+ * (kind 1) for the device u64 at `flag` (8-byte aligned) to reach `target` —
+ * the peer all-reduce's flag wait.  A wait that runs out records
+ * RXLA_B200_DEADLINE_EXCEEDED in the device status word and the kernel
+ * returns.  Asynchronous on `stream`.  Replaces no reference interface; it
+ * lets a single GPU show the failure path of the waits. */
+int32_t rxla_b200_bounded_wait_check(int32_t kind, const uint64_t* flag, uint64_t target,
+                                     void* stream);
 
 /* ------------------------------------------------------- W8A16 linear layer
  *

@@ -124,6 +124,7 @@ SIGNATURES = {
     "rxla_b200_device_status": (_i32, [_i32]),
     "rxla_b200_set_wait_timeout": (_i32, [_i64]),
     "rxla_b200_get_wait_timeout": (_i32, [ctypes.POINTER(_i64)]),
+    "rxla_b200_bounded_wait_check": (_i32, [_i32, _vp, _u64, _vp]),
     "rxla_b200_w8a16_linear": (_i32, [_vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i32,
                                       _i32, _vp]),
     "rxla_b200_w8a16_linear_workspace_size": (_i32, [_i64, _i64, _i64, _i64, _i32,

@@ -268,6 +268,33 @@ extern "C" int32_t rxla_b200_get_wait_timeout(int64_t* ns) {
   return RXLA_B200_OK;
 }
 
+namespace rxla {
+// One thread waits through the library's bounded-wait helpers: kind 0 on a
+// fresh mbarrier that nothing arrives on, kind 1 for *flag >= target.
+__global__ void bounded_wait_check_kernel(int kind, const uint64_t* flag, uint64_t target) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  if (kind == 0) {
+    mbar_init(&bar, 1);
+    fence_mbarrier_init();
+    mbar_wait(&bar, 0);
+  } else {
+    flag_wait_geq(flag, target);
+  }
+}
+}  // namespace rxla
+
+extern "C" int32_t rxla_b200_bounded_wait_check(int32_t kind, const uint64_t* flag,
+                                                uint64_t target, void* stream) {
+  using namespace rxla;
+  RXLA_REQUIRE(kind == 0 || kind == 1, "bounded_wait_check: kind must be 0 or 1");
+  RXLA_REQUIRE(kind == 0 || (flag && (reinterpret_cast<uintptr_t>(flag) & 7) == 0),
+               "bounded_wait_check: kind 1 needs an 8-byte aligned device flag");
+  bounded_wait_check_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(kind, flag, target);
+  RXLA_CUDA_CHECK(cudaGetLastError());
+  return RXLA_B200_OK;
+}
+
 extern "C" int32_t rxla_b200_rms_norm_bf16(const float* x, const float* weight, int64_t rows,
                                            int64_t width, float eps, uint16_t* y, void* stream) {
   using namespace rxla;

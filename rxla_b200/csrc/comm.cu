@@ -139,16 +139,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(const Args a) {
   if (threadIdx.x < a.world) {
     const uint64_t* flag = reinterpret_cast<const uint64_t*>(a.peer[a.rank] + data_bytes) +
                            (int64_t)threadIdx.x * a.max_ctas + c;
-    if (ld_acquire_sys(flag) < e) {
-      const uint64_t t0 = globaltimer();
-      while (ld_acquire_sys(flag) < e) {
-        if (globaltimer() - t0 > wait_timeout_ns()) {
-          record_device_error(RXLA_B200_DEADLINE_EXCEEDED);
-          ok = 0;
-          break;
-        }
-      }
-    }
+    if (!flag_wait_geq(flag, e)) ok = 0;
   }
   __syncthreads();
   if (!ok) return;

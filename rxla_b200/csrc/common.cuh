@@ -240,6 +240,19 @@ __device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+// Wait until *flag >= target; false after the timeout (the status word is set).
+__device__ __forceinline__ bool flag_wait_geq(const uint64_t* flag, uint64_t target) {
+  if (ld_acquire_sys(flag) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_sys(flag) < target) {
+    if (globaltimer() - t0 > wait_timeout_ns()) {
+      record_device_error(RXLA_B200_DEADLINE_EXCEEDED);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Programmatic dependent launch: wait for the previous grid's results, and
 // allow the next grid to start its prologue.  Every kernel of this library
 // triggers its dependents only after its own griddepcontrol.wait, so when a

@@ -158,6 +158,16 @@ def test_wait_timeout_range_is_checked_without_cuda():
     assert lib.rxla_b200_get_wait_timeout(None) == _lib.INVALID_ARGUMENT
 
 
+def test_bounded_wait_check_validates_without_cuda():
+    """rxla_b200_bounded_wait_check refuses an unknown kind and a flag wait
+    without an aligned flag before any CUDA call."""
+    lib = _lib.load()
+    assert lib.rxla_b200_bounded_wait_check(2, None, 0, None) == _lib.INVALID_ARGUMENT
+    assert lib.rxla_b200_bounded_wait_check(1, None, 1, None) == _lib.INVALID_ARGUMENT
+    assert lib.rxla_b200_bounded_wait_check(1, 0x1004, 1, None) == _lib.INVALID_ARGUMENT
+    assert "8-byte aligned" in lib.rxla_b200_last_error_message().decode()
+
+
 def _linear_cfg(**kw):
     c = _lib.XlaLinearConfig()
     c.magic, c.version = _lib.XLA_LINEAR_MAGIC, 1
