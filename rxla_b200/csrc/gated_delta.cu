@@ -2,7 +2,9 @@
 // mixer of crates/rxla-models/src/qwen3_5/layers.rs:114-268), between its
 // input projections and its out_proj.
 //
-// Three kernels per call, stream-ordered (programmatic dependent launch):
+// Single-token calls of at most kFusedMaxCtas (sequence, head) pairs run
+// as one kernel, gdn_decode_fused_kernel (below); every other call as three
+// kernels, stream-ordered (programmatic dependent launch):
 //  1. gdn_prep_kernel — CTA = (channel block of D channels, 16 tokens,
 //     sequence), thread = channel: the causal depthwise conv of the mixed
 //     q/k/v projection over the last `conv_kernel` rows (rows before the
@@ -563,6 +565,202 @@ __global__ void __launch_bounds__(kNormWarps * 32) gdn_gated_norm_kernel(NormArg
   }
 }
 
+// ------------------------------------------------ single-token fused step
+//
+// Decode calls (one token per sequence) of few sequences: the three kernels
+// above would each be a handful of CTAs whose launch and dependency latency
+// is most of the call.  Here one CTA of 4·D threads is one (head, sequence)
+// and does the whole step on chip: the conv of the head's 3·D channels with
+// the conv-state shift (thread = channel), the gates (one extra thread), the
+// q / k L2 norms, the delta rule over the head's state (four lanes per
+// column, D / 4 rows each) and the gated RMSNorm.  Every sum is formed in the
+// order the three kernels use, except the column dots, whose lane split
+// differs (4 lanes of D / 4 rows against 8 of D / 8).
+struct FusedArgs {
+  PrepArgs prep;        // mixed / b / a, conv weights, gates, conv state
+  float* state;         // [B, H, D(v), D(k)]
+  int32_t has_state;
+  const uint16_t* z;
+  int64_t z_ld;
+  const float* norm_w;  // [D]
+  float eps;
+  uint16_t* out;        // [B, W] bf16
+};
+
+constexpr int kFusedMaxCtas = 2 * 148;  // (sequence, head) pairs up to which T = 1 calls fuse
+
+template <int D, int KC>
+__global__ void __launch_bounds__(4 * D) gdn_decode_fused_kernel(FusedArgs f) {
+  constexpr int KM = KC > 0 ? KC : kMaxConvKernel;
+  constexpr int NW = D / 32;  // warps per q / k / v part
+  constexpr int LPC = 4;      // lanes per state column
+  constexpr int R = D / LPC;  // rows per lane
+  constexpr int NI = R / 4;   // float4 groups per lane: rows 4·LPC·i + 4·pl + e
+  constexpr int E = D / 32;   // output elements per lane of the norm warp
+  const PrepArgs& p = f.prep;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int H = p.H, W = H * D, C3 = 3 * W;
+  const int K = KC > 0 ? KC : p.K;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ __align__(16) float qs[D];
+  __shared__ __align__(16) float ks[D];
+  __shared__ float vs[D];
+  __shared__ float os[D];
+  __shared__ float red[2 * NW];
+  __shared__ float2 gate;
+  // The state's last writer may be the grid just before this one (two calls
+  // in a row on one state), so it is read after the wait; its lines are
+  // pulled into L2 now.
+  float* sp = f.state + ((int64_t)b * H + h) * D * D;
+  if (f.has_state)
+    for (int i = tid; i < D * D / 32; i += 4 * D)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(sp + (int64_t)i * 32));
+  const int part = tid / D, c = tid % D;  // parts 0, 1, 2: q, k, v channel c of head h
+  const int gc = part * W + h * D + c;
+  float wk[KM];
+#pragma unroll
+  for (int j = 0; j < KM; ++j) wk[j] = 0.0f;
+  if (part < 3) {  // conv weights are constants: loaded before the wait
+    if constexpr (KC == 4) {
+      const float4 w4 = *reinterpret_cast<const float4*>(p.conv_w + (int64_t)gc * 4);
+      wk[0] = w4.x;
+      wk[1] = w4.y;
+      wk[2] = w4.z;
+      wk[3] = w4.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < KM; ++j) wk[j] = j < K ? p.conv_w[(int64_t)gc * K + j] : 0.0f;
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  float y = 0.0f;
+  if (part < 3) {
+    // window: history slots 0 .. K-2 (oldest first), then this token's row
+    float x[KM];
+#pragma unroll
+    for (int w = 0; w < KM; ++w) {
+      x[w] = 0.0f;
+      if (w < K - 1) {
+        if (p.conv_state) x[w] = ld_bf16(p.conv_state + ((int64_t)b * (K - 1) + w) * C3 + gc);
+      } else if (w == K - 1) {
+        x[w] = ld_bf16(p.mixed + (int64_t)b * p.mixed_ld + gc);
+      }
+    }
+    if (p.conv_state_out) {  // slot s takes x[s + 1]; this thread alone owns the channel
+      uint16_t* cs = p.conv_state_out + (int64_t)b * (K - 1) * C3 + gc;
+#pragma unroll
+      for (int w = 1; w < KM; ++w)
+        if (w < K) cs[(int64_t)(w - 1) * C3] = __bfloat16_as_ushort(__float2bfloat16_rn(x[w]));
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < KM; ++j)
+      if (KC > 0 || j < K) acc = fmaf(wk[j], x[j], acc);
+    y = acc * sigmoid_f(acc);
+  }
+  if (part == 2) vs[c] = y;
+  if (part < 2) {  // whole warps: the q and k sums of squares
+    float ss = y * y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+  }
+  if (part == 3 && c == 0) {  // gates, as gdn_prep_kernel
+    const float bl = ld_bf16(p.b + (int64_t)b * p.b_ld + h);
+    const float al = ld_bf16(p.a + (int64_t)b * p.a_ld + h);
+    const float decay = softplus_f(al + p.dt_bias[h]) * -__expf(p.a_log[h]);
+    gate = make_float2(__expf(decay), sigmoid_f(bl));
+  }
+  __syncthreads();
+  if (part < 2) {
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) tot += red[part * NW + w];
+    const float v = y * rsqrtf(tot + 1e-6f);
+    if (part == 0)
+      qs[c] = v * p.q_scale;
+    else
+      ks[c] = v;
+  }
+  __syncthreads();
+  // delta rule on column j of the head's state (gdn_recurrence_kernel's step
+  // for one token): a = k·S, δ = beta (v_j - g a), S = g S + k δ, o_j = q·S
+  const int j = warp * (32 / LPC) + lane / LPC, pl = lane & (LPC - 1);
+  float* colp = sp + (int64_t)j * D + 4 * pl;
+  float st[R];
+  if (f.has_state) {
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const float4 v = *reinterpret_cast<const float4*>(colp + 4 * LPC * i);
+      st[4 * i] = v.x;
+      st[4 * i + 1] = v.y;
+      st[4 * i + 2] = v.z;
+      st[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; ++r) st[r] = 0.0f;
+  }
+  const float2 g = gate;
+  float a = 0.0f;
+  if (f.has_state) {
+    float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const float4 k4 = *reinterpret_cast<const float4*>(&ks[4 * LPC * i + 4 * pl]);
+      a0 = fmaf(st[4 * i], k4.x, a0);
+      a1 = fmaf(st[4 * i + 1], k4.y, a1);
+      a0 = fmaf(st[4 * i + 2], k4.z, a0);
+      a1 = fmaf(st[4 * i + 3], k4.w, a1);
+    }
+    a = a0 + a1;
+#pragma unroll
+    for (int o = 1; o < LPC; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+  }
+  const float delta = (vs[j] - g.x * a) * g.y;
+  float o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    const float4 k4 = *reinterpret_cast<const float4*>(&ks[4 * LPC * i + 4 * pl]);
+    const float4 q4 = *reinterpret_cast<const float4*>(&qs[4 * LPC * i + 4 * pl]);
+    st[4 * i] = fmaf(k4.x, delta, st[4 * i] * g.x);
+    st[4 * i + 1] = fmaf(k4.y, delta, st[4 * i + 1] * g.x);
+    st[4 * i + 2] = fmaf(k4.z, delta, st[4 * i + 2] * g.x);
+    st[4 * i + 3] = fmaf(k4.w, delta, st[4 * i + 3] * g.x);
+    o0 = fmaf(st[4 * i], q4.x, o0);
+    o1 = fmaf(st[4 * i + 1], q4.y, o1);
+    o0 = fmaf(st[4 * i + 2], q4.z, o0);
+    o1 = fmaf(st[4 * i + 3], q4.w, o1);
+    *reinterpret_cast<float4*>(colp + 4 * LPC * i) =
+        make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+  }
+  float o = o0 + o1;
+#pragma unroll
+  for (int s = 1; s < LPC; s <<= 1) o += __shfl_xor_sync(0xffffffffu, o, s);
+  if (pl == 0) os[j] = o;
+  __syncthreads();
+  if (warp == 0) {  // gated RMSNorm over the head, as gdn_gated_norm_kernel
+    float v[E], ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      v[e] = os[lane * E + e];
+      ss = fmaf(v[e], v[e], ss);
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s);
+    const float ns = rsqrtf(ss / (float)D + f.eps);
+    const uint16_t* zr = f.z + (int64_t)b * f.z_ld + h * D + lane * E;
+    uint16_t* outp = f.out + (int64_t)b * W + h * D + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float z = ld_bf16(zr + e);
+      const float r = ((v[e] * ns) * f.norm_w[lane * E + e]) * (z * sigmoid_f(z));
+      outp[e] = __bfloat16_as_ushort(__float2bfloat16_rn(r));
+    }
+  }
+}
+
 template <int D, bool PROMPT>
 int32_t launch_recurrence(const RecArgs& ra, int B, cudaStream_t s) {
   using Sh = RecShape<D, PROMPT>;
@@ -580,6 +778,22 @@ int32_t launch_all(const PrepArgs& pa, const RecArgs& ra, const NormArgs& na, in
   const bool k4 = pa.K == 4 && reinterpret_cast<uintptr_t>(pa.conv_w) % 16 == 0;
   const dim3 g1(3 * pa.H + 1, 1, B), gt(3 * pa.H + 1, (T + kPrepTokens - 1) / kPrepTokens, B);
   cudaError_t e;
+  if (T == 1 && (int64_t)B * pa.H <= kFusedMaxCtas) {
+    FusedArgs f;
+    f.prep = pa;
+    f.state = ra.state;
+    f.has_state = ra.has_state;
+    f.z = na.z;
+    f.z_ld = na.z_ld;
+    f.norm_w = na.norm_w;
+    f.eps = na.eps;
+    f.out = na.out;
+    const dim3 gf(pa.H, B);
+    e = k4 ? launch_pdl(gdn_decode_fused_kernel<D, 4>, gf, dim3(4 * D), 0, s, f)
+           : launch_pdl(gdn_decode_fused_kernel<D, 0>, gf, dim3(4 * D), 0, s, f);
+    if (e != cudaSuccess) return cuda_fail(e, "gated_delta fused decode launch");
+    return RXLA_B200_OK;
+  }
   if (T == 1)
     e = k4 ? launch_pdl(gdn_prep_kernel<D, 1, 4>, g1, dim3(D), 0, s, pa)
            : launch_pdl(gdn_prep_kernel<D, 1, 0>, g1, dim3(D), 0, s, pa);

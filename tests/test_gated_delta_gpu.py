@@ -97,6 +97,21 @@ def test_prefill_then_decode_continues_the_state(cuda, D, pieces):
     _check_state(state, S_ref, hist, c)
 
 
+@pytest.mark.parametrize("D,K", [(32, 1), (32, 4), (64, 4), (128, 2)])
+def test_single_token_calls_from_zero_state(cuda, D, K):
+    """Every call one token per sequence from the first token on (the fused
+    single-token kernel for few sequences: conv history shifted in place,
+    the state started from zero by the first call), with the runtime conv
+    width (K = 1, 2) and the float4 one (K = 4)."""
+    B, H, T = 3, 2, 6
+    c = _inputs(B, T, H, D, K, seed=500 + D + K)
+    y_ref, hist, S_ref = gdo.gated_delta_core(**c, heads=H, head_dim=D)
+    state = GatedDeltaState(B, H, D, K)
+    for t in range(T):
+        _check_out(_gpu_call(c, t, t + 1, state, H, D), y_ref[:, t:t + 1])
+    _check_state(state, S_ref, hist, c)
+
+
 def test_decode_batch_64_continues_the_state(cuda):
     """The decode shape of a serving step: 64 sequences, one token each, after
     a short prompt (the wide-grid recurrence variant)."""
