@@ -22,7 +22,7 @@ def _sigmoid(x):
 
 def full_attention(x, params, *, attention_heads, key_value_heads, head_dim, rotary_dim,
                    rope_theta, group_size, eps=1e-6, positions=None, round_attention=False,
-                   linear_mode=1):
+                   linear_mode=1, round_keys=True):
     """x [B, T, hidden] F32 (the normalised layer input).  params: q_proj /
     k_proj / v_proj / o_proj `.weight` u8 and `.scale` f32, q_norm.weight and
     k_norm.weight f32 [D] (zero-centred: the norm multiplies by weight + 1).
@@ -32,7 +32,9 @@ def full_attention(x, params, *, attention_heads, key_value_heads, head_dim, rot
     them F32): the model of that one extra rounding point, used to measure
     its effect.  linear_mode: the C oracle's W8 linear mode (1: the
     reference's rounding points with f64 sums; 4: the same with f32 running
-    sums, the accumulation-noise model)."""
+    sums, the accumulation-noise model; 0: F32 compute).  round_keys=False
+    keeps the rotated keys F32 instead of rounding them to bf16 as the paged
+    cache stores them (the F32 form used to pin the layer's structure)."""
     B, T, hid = x.shape
     Hq, Hkv, D = attention_heads, key_value_heads, head_dim
 
@@ -55,7 +57,8 @@ def full_attention(x, params, *, attention_heads, key_value_heads, head_dim, rot
     query = rope_split_half(query.reshape(-1, D), pos_rows, inv, rotary_dim).reshape(B, T, Hq, D)
     pos_rows = np.broadcast_to(pos[None, :, None], (B, T, Hkv)).reshape(-1)
     key = rope_split_half(key.reshape(-1, D), pos_rows, inv, rotary_dim).reshape(B, T, Hkv, D)
-    key = bf16_round(key)  # the cache's storage
+    if round_keys:
+        key = bf16_round(key)  # the cache's storage
     mask = causal_mask(pos, pos)[None, None]
     att = gqa_attention(query.transpose(0, 2, 1, 3), key.transpose(0, 2, 1, 3),
                         value.transpose(0, 2, 1, 3), mask)       # [B, Hq, T, D]
