@@ -72,7 +72,8 @@ def full_attention(x, params, *, attention_heads, key_value_heads, head_dim, rot
 
 def qwen3_5_forward(ids, params, *, layer_types, vocabulary, hidden_size, attention_heads,
                     key_value_heads, head_dim, linear_heads, linear_head_dim, rope_theta,
-                    rotary_dim, epsilon, quant_group_size, gpu_rounding=False):
+                    rotary_dim, epsilon, quant_group_size, gpu_rounding=False,
+                    f32_compute=False):
     """`qwen3_5(cx, token_ids, config)` (crates/rxla-models/src/qwen3_5/mod.rs:
     199-260) on the CPU: ids [B, T]; returns logits [B, T, vocabulary].
     params by the names below "model.language_model." (numpy arrays).
@@ -81,9 +82,12 @@ def qwen3_5_forward(ids, params, *, layer_types, vocabulary, hidden_size, attent
     running sums in every W8 linear (the decoder tests' noise-floor model),
     bf16 attended values before the output gate, and the tied head on bf16 x
     and bf16 dequantized weights with an f32 sum (the reference's head is an
-    F32 linear, mod.rs:157-173) — so that their effect can be measured."""
+    F32 linear, mod.rs:157-173) — so that their effect can be measured.
+    f32_compute=True runs every linear in F32 and keeps keys F32 (no bf16
+    rounding point anywhere): the form that pins the composition against an
+    F32 implementation of the same model."""
     from . import gated_delta as gdo
-    mode = 4 if gpu_rounding else 1
+    mode = 0 if f32_compute else (4 if gpu_rounding else 1)
     lin_mode = lambda x, w, s, g: w8_linear(x, w, s, g, mode=mode)
     ids = np.asarray(ids)
     B, T = ids.shape
@@ -112,7 +116,8 @@ def qwen3_5_forward(ids, params, *, layer_types, vocabulary, hidden_size, attent
             out = full_attention(xn, sub, attention_heads=attention_heads,
                                  key_value_heads=key_value_heads, head_dim=head_dim,
                                  rotary_dim=rotary_dim, rope_theta=rope_theta, group_size=G,
-                                 eps=epsilon, round_attention=gpu_rounding, linear_mode=mode)
+                                 eps=epsilon, round_attention=gpu_rounding, linear_mode=mode,
+                                 round_keys=not f32_compute)
         h = (h + out).astype(np.float32)                               # mod.rs:246
         xn = rms_norm(h, zc(pre + "post_attention_layernorm.weight"), epsilon)
 
@@ -126,4 +131,4 @@ def qwen3_5_forward(ids, params, *, layer_types, vocabulary, hidden_size, attent
     hn = rms_norm(h, zc("norm.weight"), epsilon)
     # tied LM head (mod.rs:157-173): F32 hidden · F32 dequantized embedding
     return w8_linear(hn.reshape(B * T, -1), emb_w, emb_s, G,
-                     mode=5 if gpu_rounding else 0).reshape(B, T, vocabulary)
+                     mode=5 if gpu_rounding and not f32_compute else 0).reshape(B, T, vocabulary)
