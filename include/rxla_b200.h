@@ -120,7 +120,8 @@ int32_t rxla_b200_get_wait_timeout(int64_t* ns);
 /* Diagnostic of the bounded device-side waits: one thread waits, under the
  * current budget, either (kind 0) on a shared-memory mbarrier that nothing
  * arrives on — the wait of every TMA ring here, so it always runs out — or
- * (kind 1) for the device u64 at `flag` (8-byte aligned) to reach `target` —
+ * (kind 1) for the u64 at `flag` (8-byte aligned; device, managed or pinned
+ * host memory, else INVALID_ARGUMENT) to reach `target` —
  * the peer all-reduce's flag wait.  A wait that runs out records
  * RXLA_B200_DEADLINE_EXCEEDED in the device status word and the kernel
  * returns.  Asynchronous on `stream`.  Replaces no reference interface; it

@@ -290,6 +290,15 @@ extern "C" int32_t rxla_b200_bounded_wait_check(int32_t kind, const uint64_t* fl
   RXLA_REQUIRE(kind == 0 || kind == 1, "bounded_wait_check: kind must be 0 or 1");
   RXLA_REQUIRE(kind == 0 || (flag && (reinterpret_cast<uintptr_t>(flag) & 7) == 0),
                "bounded_wait_check: kind 1 needs an 8-byte aligned device flag");
+  if (kind == 1) {
+    // the kernel loads the flag: ordinary host memory would be an illegal
+    // address there, so refuse it here
+    cudaPointerAttributes pa{};
+    const cudaError_t e = cudaPointerGetAttributes(&pa, flag);
+    if (e != cudaSuccess) cudaGetLastError();
+    RXLA_REQUIRE(e == cudaSuccess && pa.type != cudaMemoryTypeUnregistered,
+                 "bounded_wait_check: the flag must be device, managed or pinned host memory");
+  }
   bounded_wait_check_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(kind, flag, target);
   RXLA_CUDA_CHECK(cudaGetLastError());
   return RXLA_B200_OK;
