@@ -339,8 +339,9 @@ int32_t rxla_b200_sigmoid_gate(const uint16_t* x, int64_t x_row_stride, const ui
  * token per call, gives the full forward's outputs.  Output out bf16
  * [rows, W] (the input of out_proj).  The workspace (256-byte aligned, size
  * from rxla_b200_gated_delta_workspace_size, no zero-fill needed) holds the
- * normalised q/k/v, the gates and o.  Calls on one state must be
- * stream-ordered.
+ * normalised q/k/v, the gates and o (single-token calls of at most 296
+ * sequence × head pairs run as one kernel and leave it untouched).  Calls on
+ * one state must be stream-ordered.
  */
 typedef struct rxla_b200_gated_delta_args {
   uint32_t struct_size; /* sizeof(rxla_b200_gated_delta_args) */
